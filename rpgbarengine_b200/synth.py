@@ -1,0 +1,202 @@
+"""Seeded synthetic Qwen3 weights in raw ggml blocks (no network, no checkpoints).
+
+Value distributions follow the benchmark configurations:
+  Q8_0  d = fp16(U[1e-4, 2e-4]), qs = U{-127..127}
+  Q4_K  d = fp16(U[1e-3, 4e-3]), dmin = fp16(U[0, 1e-3]), 12 random scale
+        bytes (uniform 6-bit sc/m), 128 random quant bytes
+  Q6_K  ql/qh random bytes, sc = U{-32..31} (int8), d = fp16(U[1e-3, 4e-3])
+  norms F32 = 1.0
+Block byte layouts are ggml's (reference src/quant.cc:207-217, 327-354,
+396-429).  Shapes follow Qwen3 naming (reference src/model.cc:229-269).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import gguf
+from .gguf import F32, Q4_K, Q6_K, Q8_0, Tensor
+
+
+@dataclass(frozen=True)
+class Qwen3Shape:
+    name: str
+    n_layers: int
+    hidden: int
+    intermediate: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int = 128
+    vocab: int = 151936
+    tied: bool = True
+    context_length: int = 8192
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    # ggml type per tensor role
+    t_q: int = Q4_K
+    t_k: int = Q4_K
+    t_v: int = Q6_K
+    t_o: int = Q4_K
+    t_gate: int = Q4_K
+    t_up: int = Q4_K
+    t_down: int = Q6_K
+    t_embd: int = Q6_K
+    t_out: int = Q8_0
+
+    @property
+    def q_dim(self):
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_dim(self):
+        return self.n_kv_heads * self.head_dim
+
+    def matrices(self):
+        """(name, ggml type, rows, cols) of every 2-D weight."""
+        out = [("token_embd.weight", self.t_embd, self.vocab, self.hidden)]
+        if not self.tied:
+            out.append(("output.weight", self.t_out, self.vocab, self.hidden))
+        for l in range(self.n_layers):
+            p = f"blk.{l}."
+            out += [
+                (p + "attn_q.weight", self.t_q, self.q_dim, self.hidden),
+                (p + "attn_k.weight", self.t_k, self.kv_dim, self.hidden),
+                (p + "attn_v.weight", self.t_v, self.kv_dim, self.hidden),
+                (p + "attn_output.weight", self.t_o, self.hidden, self.q_dim),
+                (p + "ffn_gate.weight", self.t_gate, self.intermediate, self.hidden),
+                (p + "ffn_up.weight", self.t_up, self.intermediate, self.hidden),
+                (p + "ffn_down.weight", self.t_down, self.hidden, self.intermediate),
+            ]
+        return out
+
+    def weight_bytes(self, per_token: bool = False) -> int:
+        """Raw block bytes of all 2-D weights; per_token=True counts what one
+        decode step streams (every layer matrix + lm_head, not the embedding
+        table, of which one row is read)."""
+        tot = 0
+        for name, ty, rows, cols in self.matrices():
+            nb = rows * gguf.row_bytes(ty, cols)
+            if per_token and name == "token_embd.weight":
+                nb = gguf.row_bytes(ty, cols) + (nb if self.tied else 0)
+            tot += nb
+        return tot
+
+
+# BASELINE configurations.
+QWEN3_1_7B_Q8_0 = Qwen3Shape("qwen3-1.7b-q8_0", 28, 2048, 6144, 16, 8,
+                             t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0, t_gate=Q8_0, t_up=Q8_0,
+                             t_down=Q8_0, t_embd=Q8_0)
+QWEN3_4B_Q4KM = Qwen3Shape("qwen3-4b-q4_k_m", 36, 2560, 9728, 32, 8)
+QWEN3_8B_Q8_0 = Qwen3Shape("qwen3-8b-q8_0", 36, 4096, 12288, 32, 8, tied=False,
+                           t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0, t_gate=Q8_0, t_up=Q8_0,
+                           t_down=Q8_0, t_embd=Q8_0, t_out=Q8_0)
+# Small shapes for parity tests (same block types and code paths).
+TINY_MIX = Qwen3Shape("tiny-mix", 2, 512, 768, 4, 2, vocab=1024, context_length=1024)
+TINY_Q8 = replace(QWEN3_1_7B_Q8_0, name="tiny-q8_0", n_layers=2, hidden=256, intermediate=512,
+                  n_heads=2, n_kv_heads=1, vocab=768, context_length=1024)
+TINY_UNTIED = replace(TINY_MIX, name="tiny-untied", tied=False, t_out=Q6_K)
+
+SHAPES = {s.name: s for s in (QWEN3_1_7B_Q8_0, QWEN3_4B_Q4KM, QWEN3_8B_Q8_0, TINY_MIX, TINY_Q8,
+                              TINY_UNTIED)}
+
+
+def _f16_bytes(x: np.ndarray) -> np.ndarray:
+    return x.astype("<f2").view(np.uint8).reshape(-1, 2)
+
+
+def q8_0_blocks(rng: np.random.Generator, n_blocks: int, d=(1e-4, 2e-4)) -> np.ndarray:
+    b = np.empty((n_blocks, 34), np.uint8)
+    b[:, 0:2] = _f16_bytes(rng.uniform(d[0], d[1], n_blocks))
+    b[:, 2:] = rng.integers(-127, 128, (n_blocks, 32), dtype=np.int8).view(np.uint8)
+    return b.reshape(-1)
+
+
+def q4_k_blocks(rng: np.random.Generator, n_blocks: int, d=(1e-3, 4e-3), dmin=(0.0, 1e-3)):
+    b = np.frombuffer(rng.bytes(n_blocks * 144), np.uint8).reshape(n_blocks, 144).copy()
+    b[:, 0:2] = _f16_bytes(rng.uniform(d[0], d[1], n_blocks))
+    b[:, 2:4] = _f16_bytes(rng.uniform(dmin[0], dmin[1], n_blocks))
+    return b.reshape(-1)
+
+
+def q6_k_blocks(rng: np.random.Generator, n_blocks: int, d=(1e-3, 4e-3)):
+    b = np.frombuffer(rng.bytes(n_blocks * 210), np.uint8).reshape(n_blocks, 210).copy()
+    b[:, 192:208] = rng.integers(-32, 32, (n_blocks, 16), dtype=np.int8).view(np.uint8)
+    b[:, 208:210] = _f16_bytes(rng.uniform(d[0], d[1], n_blocks))
+    return b.reshape(-1)
+
+
+def f32_values(values: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(values, dtype="<f4").view(np.uint8).reshape(-1)
+
+
+def random_blocks(rng: np.random.Generator, ggml_type: int, rows: int, cols: int) -> np.ndarray:
+    """rows x cols weights of one type as raw bytes (row-major blocks)."""
+    n = rows * cols
+    if ggml_type == Q8_0:
+        return q8_0_blocks(rng, n // 32)
+    if ggml_type == Q4_K:
+        return q4_k_blocks(rng, n // 256)
+    if ggml_type == Q6_K:
+        return q6_k_blocks(rng, n // 256)
+    if ggml_type == F32:
+        return f32_values(rng.standard_normal(n).astype(np.float32))
+    raise ValueError(f"no generator for ggml type {ggml_type}")
+
+
+def build_tensors(shape: Qwen3Shape, seed: int) -> list:
+    """All tensors of a synthetic model, in Qwen3/GGUF naming order."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, ty, rows, cols in shape.matrices():
+        out.append(Tensor(name, ty, (cols, rows), random_blocks(rng, ty, rows, cols)))
+    ones_h = f32_values(np.ones(shape.hidden, np.float32))
+    ones_d = f32_values(np.ones(shape.head_dim, np.float32))
+    out.append(Tensor("output_norm.weight", F32, (shape.hidden,), ones_h))
+    for l in range(shape.n_layers):
+        p = f"blk.{l}."
+        out.append(Tensor(p + "attn_norm.weight", F32, (shape.hidden,), ones_h))
+        out.append(Tensor(p + "ffn_norm.weight", F32, (shape.hidden,), ones_h))
+        out.append(Tensor(p + "attn_q_norm.weight", F32, (shape.head_dim,), ones_d))
+        out.append(Tensor(p + "attn_k_norm.weight", F32, (shape.head_dim,), ones_d))
+    return out
+
+
+def metadata(shape: Qwen3Shape, with_tokenizer: bool = True) -> dict:
+    """GGUF metadata the reference's Model::Load needs (src/model.cc:159-211,
+    src/tokenizer.cc:135-162): qwen3.* hyper-parameters plus a dummy BBPE
+    vocabulary of `vocab` tokens and one merge."""
+    a = "qwen3."
+    m = {
+        "general.architecture": "qwen3",
+        "general.name": shape.name,
+        "general.alignment": gguf.ALIGN,
+        a + "block_count": shape.n_layers,
+        a + "context_length": shape.context_length,
+        a + "embedding_length": shape.hidden,
+        a + "feed_forward_length": shape.intermediate,
+        a + "attention.head_count": shape.n_heads,
+        a + "attention.head_count_kv": shape.n_kv_heads,
+        a + "attention.key_length": shape.head_dim,
+        a + "attention.value_length": shape.head_dim,
+        a + "rope.freq_base": float(shape.rope_theta),
+        a + "attention.layer_norm_rms_epsilon": float(shape.rms_eps),
+    }
+    if with_tokenizer:
+        m["tokenizer.ggml.model"] = "gpt2"
+        m["tokenizer.ggml.pre"] = "qwen2"
+        m["tokenizer.ggml.tokens"] = [f"<t{i}>" for i in range(shape.vocab)]
+        m["tokenizer.ggml.token_type"] = [1] * shape.vocab
+        m["tokenizer.ggml.merges"] = ["< t"]
+    return m
+
+
+def write_model(path: str, shape: Qwen3Shape, seed: int) -> list:
+    tensors = build_tensors(shape, seed)
+    gguf.write(path, metadata(shape), tensors)
+    return tensors
+
+
+def prompt_ids(seed: int, n: int, vocab: int = 151936, hi: int = 151643) -> np.ndarray:
+    """Seeded uniform token ids in [0, min(hi, vocab))."""
+    return np.random.default_rng(seed).integers(0, min(hi, vocab), n).astype(np.int32)
