@@ -1,0 +1,167 @@
+/* rpgc.h -- the thin C-ABI CUDA layer under the RPGBarEngine host (B200, sm_100a).
+ *
+ * This is the drop-in boundary for the token loop: plain C types, handles and
+ * pointers, no C++ or torch types, no exceptions.  Every call returns a status
+ * (RPGC_OK = 0, negative = error) or a handle (< 0 = error); the message of
+ * the last failure on the calling thread is rpgc_last_error(), the same
+ * convention as the reference ABI (include/rpg_engine.h:48-52,
+ * src/engine.cc:175-191).
+ *
+ * The layer replaces the reference's internal C++ seam between the host and
+ * the token loop (src/qwen3.h:83-142, src/kv_cache.h:35-82,
+ * src/model.h:62-92, src/matmul.h:35-64, src/quant.h:65).  The host keeps the
+ * text side (tokenizer, chat template, tool parsing) and calls this layer with
+ * token ids.
+ *
+ * Ownership: the caller owns host buffers; the layer owns device memory.  A
+ * session owns one CUDA stream; calls on different sessions may run from
+ * different host threads, one call at a time per session
+ * (include/rpg_engine.h:13-14).  Kernel-level entry points take device
+ * pointers and a cudaStream_t passed as void* (NULL = the legacy default
+ * stream).
+ */
+#ifndef RPGC_H
+#define RPGC_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RPGC_API __attribute__((visibility("default")))
+#else
+#define RPGC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------- status codes */
+#define RPGC_OK 0
+#define RPGC_E_ARG (-1)          /* bad argument / unsupported type or shape */
+#define RPGC_E_CUDA (-2)         /* CUDA runtime error */
+#define RPGC_E_OOM (-3)          /* device allocation failed */
+#define RPGC_E_STATE (-4)        /* invalid handle or call order */
+#define RPGC_E_CONTEXT_FULL (-5) /* KV cache would overflow (src/qwen3.cc:341-344) */
+#define RPGC_E_TIMEOUT (-6)      /* a bounded device wait gave up */
+#define RPGC_E_IO (-7)           /* GGUF file could not be read */
+
+/* ggml type ids (src/quant.h:22-38); the kernels take F32, Q8_0, Q4_K, Q6_K. */
+#define RPGC_F32 0u
+#define RPGC_F16 1u
+#define RPGC_Q8_0 8u
+#define RPGC_Q4_K 12u
+#define RPGC_Q6_K 14u
+
+/* One GGUF tensor: raw block bytes, dims[0] fastest (src/gguf.h:30-42). */
+typedef struct rpgc_tensor {
+  const char* name;
+  uint32_t type;
+  int32_t n_dims;
+  int64_t dims[4];
+  const void* data; /* host pointer to the raw bytes */
+  int64_t n_bytes;
+} rpgc_tensor;
+
+/* Model hyper-parameters (src/model.h:30-58).  max_pos caps the RoPE table
+ * at min(max_pos, context_length) positions (src/model.cc:122-145). */
+typedef struct rpgc_model_config {
+  int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  int32_t context_length, max_pos;
+  float rope_theta, rms_eps;
+} rpgc_model_config;
+
+/* Decode-loop options (src/qwen3.h:113-126, src/sampler.h:35-44).
+ * temperature <= 0 is greedy; top_k only applies when 1 < top_k < vocab;
+ * top_p only when 0 < top_p < 1; at most RPGC_MAX_STOP stop ids. */
+#define RPGC_MAX_STOP 16
+typedef struct rpgc_gen_opts {
+  int32_t max_tokens;
+  const int32_t* stop_ids;
+  int32_t n_stop;
+  float temperature;
+  int32_t top_k;
+  float top_p;
+  uint64_t seed;
+} rpgc_gen_opts;
+
+/* ------------------------------------------------------------- library */
+RPGC_API const char* rpgc_version(void);
+/* Thread-local; valid until the next call on this thread; do not free
+ * (src/common.cc:11, 54-56). */
+RPGC_API const char* rpgc_last_error(void);
+RPGC_API int rpgc_device_count(void);
+
+/* --------------------------------------------------------------- model */
+/* Replaces Model::Load (src/model.cc:147-281): shape-checked Qwen3 tensor
+ * table, raw blocks copied to HBM unchanged, F32 norms, RoPE table built on
+ * the host in double and rounded to float.  Returns a model handle (>= 1). */
+RPGC_API int32_t rpgc_model_upload(int device, const rpgc_model_config* cfg,
+                                   const rpgc_tensor* tensors, int32_t n_tensors);
+/* Parses a GGUF v1-v3 file (src/gguf.cc:69-160), reads the qwen3.*
+ * hyper-parameters (src/model.cc:159-211) and uploads it. */
+RPGC_API int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos);
+RPGC_API int rpgc_model_get_config(int32_t model, rpgc_model_config* out);
+/* Raw weight bytes resident in HBM (src/model.h:139-143). */
+RPGC_API int64_t rpgc_model_weight_bytes(int32_t model);
+/* Frees the model and every session on it (src/engine.cc:246-257). */
+RPGC_API int rpgc_model_free(int32_t model);
+
+/* ------------------------------------------------------------- session */
+/* Device KV cache [n_layers][n_kv_heads][max_seq][head_dim] fp32 for K and
+ * V, zero-initialised (src/kv_cache.h:35-82, src/kv_cache.cc:5-33). */
+RPGC_API int32_t rpgc_session_create(int32_t model, int32_t max_seq);
+RPGC_API int rpgc_session_destroy(int32_t session);
+RPGC_API int64_t rpgc_session_len(int32_t session);
+/* Prefix reuse: positions [0, len) stay valid (src/engine.cc:425-431,
+ * src/kv_cache.h:63-69).  Invalidates the pending logits. */
+RPGC_API int rpgc_session_set_len(int32_t session, int64_t len);
+/* cudaStream_t of the session, as void* (for event timing). */
+RPGC_API void* rpgc_session_stream(int32_t session);
+/* Copies the cache to host arrays of n_layers*n_kv_heads*max_seq*head_dim
+ * floats each (either may be NULL). */
+RPGC_API int rpgc_session_read_kv(int32_t session, float* k, float* v);
+
+/* ForwardFull / ForwardStep (src/qwen3.cc:208-300): appends n tokens at
+ * pos0 = len, writes K/V, len += n.  last_logits (vocab floats) receives the
+ * last row; all_logits (n*vocab floats) every row; either may be NULL.  The
+ * last row also stays on the device as the next rpgc_generate's input. */
+RPGC_API int rpgc_forward(int32_t session, const int32_t* ids, int64_t n, float* last_logits,
+                          float* all_logits);
+/* Generate (src/qwen3.cc:302-355): device-resident decode loop starting from
+ * the pending last-row logits; each picked token (the stop token included) is
+ * forwarded, so len grows by *n_out.  u = CounterUniform(seed, len) per step
+ * (src/sampler.cc:24-34).  out_ids needs max_tokens slots. */
+RPGC_API int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids,
+                           int32_t* n_out);
+/* Same two calls with device-resident ids / results and no host transfer of
+ * logits (the benchmark's kernel-only leg).  ids_dev: n int32 on the device;
+ * out_ids_dev: max_tokens int32 on the device; n_out stays on the device too
+ * (n_out_dev, one int32).  Asynchronous on the session stream. */
+RPGC_API int rpgc_forward_device(int32_t session, const int32_t* ids_dev, int64_t n);
+RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
+                                  int32_t* out_ids_dev, int32_t* n_out_dev);
+RPGC_API int rpgc_session_sync(int32_t session);
+
+/* ------------------------------------------------ kernel entry points */
+/* DequantizeRow (src/quant.h:65) over rows*cols elements, bit-exact. */
+RPGC_API int rpgc_dequantize_rows(uint32_t type, const void* w, int64_t rows, int64_t cols,
+                                  float* out, void* stream);
+/* One fused-dequant matrix-vector product: y[r] = dot(x, W[r])
+ * (QuantMatrix::MatVec, src/model.cc:23-30; DotRowQuant, src/matmul.h:35). */
+RPGC_API int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t cols,
+                         const float* x, float* y, void* stream);
+/* OUT[t*rows + r] = dot(X[t], W[r]) (QuantMatrix::MatMulBatch,
+ * src/model.cc:39-69; MatMulBlocked, src/matmul.h:55).  n == 1 takes the
+ * decode kernel, n > 1 the prefill kernel. */
+RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols,
+                         const float* X, int64_t n, float* OUT, void* stream);
+/* SampleToken / ArgMax on device logits (src/sampler.cc:96-112,
+ * src/kernels.h:42-52); *token_dev receives the id. */
+RPGC_API int rpgc_sample(const float* logits, int64_t n, float temperature, int32_t top_k,
+                         float top_p, float u, int32_t* token_dev, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* RPGC_H */

@@ -1,0 +1,1054 @@
+// engine.cu -- host orchestration of the token loop and the rpgc C ABI.
+//
+// Mirrors the reference's token loop (src/qwen3.cc:119-355) and session
+// model (src/engine.cc:383-448, src/kv_cache.h:35-82) with the compute on a
+// B200: weights uploaded once as raw ggml blocks, one stream and one device
+// KV cache per session, prefill through the batched kernels, and a decode
+// loop that runs as one captured CUDA graph per step with its state (position,
+// sampling options, stop status) in device memory.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/rpgc.h"
+#include "gguf_host.h"
+#include "kernels.h"
+
+namespace rpgc {
+namespace {
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+thread_local std::string g_last_error;
+
+[[noreturn]] void fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  throw Error(code, buf);
+}
+
+#define CK(expr)                                                                      \
+  do {                                                                                \
+    const cudaError_t e_ = (expr);                                                    \
+    if (e_ != cudaSuccess)                                                            \
+      fail(e_ == cudaErrorMemoryAllocation ? RPGC_E_OOM : RPGC_E_CUDA, "%s: %s (%s:%d)", \
+           #expr, cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+  } while (0)
+
+struct DevMatrix {
+  uint32_t type = 0;
+  int64_t rows = 0, cols = 0, row_bytes = 0;
+  const uint8_t* w = nullptr;
+};
+
+struct DevLayer {
+  const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  DevMatrix q, k, v, o, gate, up, down;
+};
+
+struct Model {
+  int device = 0;
+  rpgc_model_config c{};
+  uint8_t* blob = nullptr;
+  int64_t weight_bytes = 0;
+  DevMatrix embd, lm_head;
+  const float* out_norm = nullptr;
+  std::vector<DevLayer> layers;
+  float* rope = nullptr;
+  int64_t n_rope = 0;
+  std::vector<int32_t> sessions;
+  ~Model() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (blob) cudaFree(blob);
+    if (rope) cudaFree(rope);
+    cudaSetDevice(prev);
+  }
+};
+
+constexpr int kMaxSplits = 32;
+
+struct Session {
+  int32_t model_id = 0;
+  Model* m = nullptr;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int64_t max_seq = 0, len = 0, cap = 0;
+  bool has_logits = false;
+  float *kc = nullptr, *vc = nullptr;
+  float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+  float *gate = nullptr, *up = nullptr, *logits = nullptr, *partial = nullptr;
+  int32_t *ids = nullptr, *counters = nullptr, *gen_out = nullptr, *n_out = nullptr;
+  DecodeState* st = nullptr;
+  DecodeState* st_host = nullptr;  // pinned
+  cudaGraphExec_t step_graph = nullptr;
+  std::vector<void*> allocs;
+  std::mutex mu;
+
+  template <typename T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, count * sizeof(T)));
+    allocs.push_back(p);
+    return static_cast<T*>(p);
+  }
+  ~Session() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    if (step_graph) cudaGraphExecDestroy(step_graph);
+    for (void* p : allocs) cudaFree(p);
+    if (st_host) cudaFreeHost(st_host);
+    if (stream) cudaStreamDestroy(stream);
+    cudaSetDevice(prev);
+  }
+  size_t layer_cache_floats() const {
+    return (size_t)m->c.n_kv_heads * max_seq * m->c.head_dim;
+  }
+};
+
+std::mutex g_mu;
+std::unordered_map<int32_t, std::unique_ptr<Model>> g_models;
+std::unordered_map<int32_t, std::unique_ptr<Session>> g_sessions;
+int32_t g_next_model = 1, g_next_session = 1;
+
+Model* model_locked(int32_t h) {
+  auto it = g_models.find(h);
+  if (it == g_models.end()) fail(RPGC_E_STATE, "invalid model handle %d", h);
+  return it->second.get();
+}
+Session* session_locked(int32_t h) {
+  auto it = g_sessions.find(h);
+  if (it == g_sessions.end()) fail(RPGC_E_STATE, "invalid session handle %d", h);
+  return it->second.get();
+}
+Session* require_session(int32_t h) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return session_locked(h);
+}
+
+struct DeviceGuard {
+  int prev = 0;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+int64_t row_bytes_of(uint32_t type, int64_t cols) {
+  int64_t be, bb;
+  if (!ggml_block(type, &be, &bb) || cols % be) return -1;
+  return cols / be * bb;
+}
+
+bool kernel_type(uint32_t t) { return t == RPGC_F32 || t == RPGC_Q8_0 || t == RPGC_Q4_K || t == RPGC_Q6_K; }
+
+// ------------------------------------------------------------------ upload
+struct TensorRef {
+  const rpgc_tensor* t = nullptr;
+  size_t offset = 0;
+};
+
+int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tensors, int n) {
+  const rpgc_model_config& c = cfg;
+  if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
+      c.head_dim <= 0 || c.intermediate <= 0 || c.vocab <= 0)
+    fail(RPGC_E_ARG, "incomplete model config: layers=%d hidden=%d heads=%d kv=%d head_dim=%d ffn=%d "
+         "vocab=%d", c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate,
+         c.vocab);
+  if (c.n_heads % c.n_kv_heads) fail(RPGC_E_ARG, "heads %d not a multiple of kv heads %d", c.n_heads, c.n_kv_heads);
+  if (c.head_dim != 128) fail(RPGC_E_ARG, "head_dim %d unsupported (kernels take 128)", c.head_dim);
+  if (c.n_heads / c.n_kv_heads > 8) fail(RPGC_E_ARG, "GQA group above 8 unsupported");
+  if (c.hidden % 256 || c.intermediate % 32) fail(RPGC_E_ARG, "hidden/intermediate not block aligned");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) fail(RPGC_E_ARG, "device %d out of range (%d devices)", device, ndev);
+
+  std::unordered_map<std::string, const rpgc_tensor*> byname;
+  for (int i = 0; i < n; ++i) {
+    if (!tensors[i].name) fail(RPGC_E_ARG, "tensor %d has no name", i);
+    byname[tensors[i].name] = &tensors[i];
+  }
+  auto find = [&](const std::string& nm) -> const rpgc_tensor* {
+    auto it = byname.find(nm);
+    return it == byname.end() ? nullptr : it->second;
+  };
+  auto require = [&](const std::string& nm) -> const rpgc_tensor* {
+    const rpgc_tensor* t = find(nm);
+    if (!t) fail(RPGC_E_ARG, "tensor %s missing", nm.c_str());
+    return t;
+  };
+  auto check_matrix = [&](const rpgc_tensor* t, int64_t rows, int64_t cols) {
+    if (t->n_dims != 2 || t->dims[1] != rows || t->dims[0] != cols)
+      fail(RPGC_E_ARG, "tensor %s shape mismatch: want [%lld,%lld] (rows x cols)", t->name,
+           (long long)rows, (long long)cols);
+    if (!kernel_type(t->type)) fail(RPGC_E_ARG, "tensor %s type %u has no kernel", t->name, t->type);
+    const int64_t rb = row_bytes_of(t->type, cols);
+    if (rb < 0 || t->n_bytes < rb * rows) fail(RPGC_E_ARG, "tensor %s too short", t->name);
+  };
+  auto check_norm = [&](const rpgc_tensor* t, int64_t len) {
+    if (t->n_dims != 1 || t->dims[0] != len) fail(RPGC_E_ARG, "norm %s length mismatch", t->name);
+    if (t->type != RPGC_F32) fail(RPGC_E_ARG, "norm %s must be F32", t->name);
+  };
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
+                kvd = (int64_t)c.n_kv_heads * c.head_dim;
+
+  auto model = std::make_unique<Model>();
+  model->device = device;
+  model->c = c;
+  std::vector<const rpgc_tensor*> order;
+  const rpgc_tensor* emb = require("token_embd.weight");
+  check_matrix(emb, c.vocab, H);
+  order.push_back(emb);
+  const rpgc_tensor* out = find("output.weight");
+  if (out) {
+    check_matrix(out, c.vocab, H);
+    order.push_back(out);
+  }
+  const rpgc_tensor* onorm = require("output_norm.weight");
+  check_norm(onorm, H);
+  order.push_back(onorm);
+  struct LT {
+    const rpgc_tensor *an, *fn, *qn, *kn, *q, *k, *v, *o, *g, *u, *d;
+  };
+  std::vector<LT> lts(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    LT& t = lts[l];
+    t.an = require(p + "attn_norm.weight");
+    t.fn = require(p + "ffn_norm.weight");
+    t.qn = require(p + "attn_q_norm.weight");
+    t.kn = require(p + "attn_k_norm.weight");
+    t.q = require(p + "attn_q.weight");
+    t.k = require(p + "attn_k.weight");
+    t.v = require(p + "attn_v.weight");
+    t.o = require(p + "attn_output.weight");
+    t.g = require(p + "ffn_gate.weight");
+    t.u = require(p + "ffn_up.weight");
+    t.d = require(p + "ffn_down.weight");
+    check_norm(t.an, H);
+    check_norm(t.fn, H);
+    check_norm(t.qn, c.head_dim);
+    check_norm(t.kn, c.head_dim);
+    check_matrix(t.q, qd, H);
+    check_matrix(t.k, kvd, H);
+    check_matrix(t.v, kvd, H);
+    check_matrix(t.o, H, qd);
+    check_matrix(t.g, F, H);
+    check_matrix(t.u, F, H);
+    check_matrix(t.d, H, F);
+    for (const rpgc_tensor* x : {t.an, t.fn, t.qn, t.kn, t.q, t.k, t.v, t.o, t.g, t.u, t.d})
+      order.push_back(x);
+  }
+  std::unordered_map<const rpgc_tensor*, size_t> off;
+  size_t total = 0;
+  for (const rpgc_tensor* t : order) {
+    off[t] = total;
+    total += ((size_t)t->n_bytes + 255) & ~size_t(255);
+  }
+  DeviceGuard dg(device);
+  CK(cudaMalloc(&model->blob, total));
+  for (const rpgc_tensor* t : order) {
+    if (!t->data) fail(RPGC_E_ARG, "tensor %s has no data", t->name);
+    CK(cudaMemcpy(model->blob + off[t], t->data, (size_t)t->n_bytes, cudaMemcpyHostToDevice));
+  }
+  model->weight_bytes = 0;
+  for (const rpgc_tensor* t : order) model->weight_bytes += t->n_bytes;
+  auto mat = [&](const rpgc_tensor* t) {
+    DevMatrix d;
+    d.type = t->type;
+    d.rows = t->dims[1];
+    d.cols = t->dims[0];
+    d.row_bytes = row_bytes_of(t->type, d.cols);
+    d.w = model->blob + off[t];
+    return d;
+  };
+  auto vec = [&](const rpgc_tensor* t) { return reinterpret_cast<const float*>(model->blob + off[t]); };
+  model->embd = mat(emb);
+  model->lm_head = out ? mat(out) : model->embd;
+  model->out_norm = vec(onorm);
+  model->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    DevLayer& d = model->layers[l];
+    const LT& t = lts[l];
+    d.attn_norm = vec(t.an);
+    d.ffn_norm = vec(t.fn);
+    d.q_norm = vec(t.qn);
+    d.k_norm = vec(t.kn);
+    d.q = mat(t.q);
+    d.k = mat(t.k);
+    d.v = mat(t.v);
+    d.o = mat(t.o);
+    d.gate = mat(t.g);
+    d.up = mat(t.u);
+    d.down = mat(t.d);
+  }
+  // RoPE table: angles in double, rounded to float (src/model.cc:122-145).
+  const int32_t half = c.head_dim / 2;
+  int64_t np = c.max_pos > c.context_length ? c.context_length : c.max_pos;
+  if (np <= 0) np = 1;
+  model->n_rope = np;
+  std::vector<float> rope((size_t)np * c.head_dim);
+  std::vector<double> inv(half);
+  for (int i = 0; i < half; ++i)
+    inv[i] = 1.0 / std::pow((double)c.rope_theta, (double)(2 * i) / (double)c.head_dim);
+  for (int64_t p = 0; p < np; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double ang = (double)p * inv[i];
+      rope[p * c.head_dim + i] = (float)std::cos(ang);
+      rope[p * c.head_dim + half + i] = (float)std::sin(ang);
+    }
+  CK(cudaMalloc(&model->rope, rope.size() * sizeof(float)));
+  CK(cudaMemcpy(model->rope, rope.data(), rope.size() * sizeof(float), cudaMemcpyHostToDevice));
+
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_next_model <= 0) fail(RPGC_E_STATE, "model handles exhausted");
+  const int32_t h = g_next_model++;
+  g_models.emplace(h, std::move(model));
+  return h;
+}
+
+// ------------------------------------------------------------ sessions
+int32_t session_create(int32_t model, int32_t max_seq) {
+  Model* m;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    m = model_locked(model);
+  }
+  if (max_seq <= 0 || max_seq > m->n_rope)
+    fail(RPGC_E_ARG, "max_seq=%d must be in (0, %lld]", max_seq, (long long)m->n_rope);
+  auto s = std::make_unique<Session>();
+  s->model_id = model;
+  s->m = m;
+  s->device = m->device;
+  s->max_seq = max_seq;
+  const rpgc_model_config& c = m->c;
+  DeviceGuard dg(m->device);
+  CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  const size_t cache = (size_t)c.n_layers * s->layer_cache_floats();
+  s->kc = s->alloc<float>(cache);
+  s->vc = s->alloc<float>(cache);
+  CK(cudaMemsetAsync(s->kc, 0, cache * sizeof(float), s->stream));
+  CK(cudaMemsetAsync(s->vc, 0, cache * sizeof(float), s->stream));
+  s->cap = std::min<int64_t>(512, max_seq);
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
+                kvd = (int64_t)c.n_kv_heads * c.head_dim;
+  s->x = s->alloc<float>(s->cap * H);
+  s->h = s->alloc<float>(s->cap * H);
+  s->q = s->alloc<float>(s->cap * qd);
+  s->k = s->alloc<float>(s->cap * kvd);
+  s->v = s->alloc<float>(s->cap * kvd);
+  s->attn = s->alloc<float>(s->cap * qd);
+  s->gate = s->alloc<float>(s->cap * F);
+  s->up = s->alloc<float>(s->cap * F);
+  s->logits = s->alloc<float>(c.vocab);
+  s->ids = s->alloc<int32_t>(s->cap);
+  s->gen_out = s->alloc<int32_t>(max_seq + 1);
+  s->n_out = s->alloc<int32_t>(1);
+  s->partial = s->alloc<float>(attn_decode_partial_floats(c.n_kv_heads, c.n_heads, c.head_dim, kMaxSplits));
+  s->counters = s->alloc<int32_t>(c.n_kv_heads);
+  CK(cudaMemsetAsync(s->counters, 0, c.n_kv_heads * sizeof(int32_t), s->stream));
+  s->st = s->alloc<DecodeState>(1);
+  CK(cudaMallocHost(&s->st_host, sizeof(DecodeState)));
+  std::memset(s->st_host, 0, sizeof(DecodeState));
+  CK(cudaMemsetAsync(s->st, 0, sizeof(DecodeState), s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_next_session <= 0) fail(RPGC_E_STATE, "session handles exhausted");
+  const int32_t h = g_next_session++;
+  m->sessions.push_back(h);
+  g_sessions.emplace(h, std::move(s));
+  return h;
+}
+
+// ------------------------------------------------------------- forward
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(e == cudaErrorInvalidValue ? RPGC_E_ARG : RPGC_E_CUDA, "%s: %s", what,
+                             cudaGetErrorString(e));
+}
+
+GemvSeg seg_of(const DevMatrix& d, float* out, int32_t mode) {
+  GemvSeg s;
+  s.w = d.w;
+  s.out = out;
+  s.rows = d.rows;
+  s.row_bytes = d.row_bytes;
+  s.type = d.type;
+  s.mode = mode;
+  return s;
+}
+
+// One decode step for the token in st->token (or ids[0]) at st->pos; all
+// kernels honour st->active.  Produces s->logits.
+void launch_step(Session* s, bool token_from_state) {
+  const Model* m = s->m;
+  const rpgc_model_config& c = m->c;
+  cudaStream_t cs = s->stream;
+  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, c.hidden,
+                     token_from_state ? nullptr : s->ids, 1, s->x,
+                     token_from_state ? s->st : nullptr, cs),
+        "embed");
+  const size_t lc = s->layer_cache_floats();
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m->layers[l];
+    GemvArgs g{};
+    g.seg[0] = seg_of(L.q, s->q, kStore);
+    g.seg[1] = seg_of(L.k, s->k, kStore);
+    g.seg[2] = seg_of(L.v, s->v, kStore);
+    g.nseg = 3;
+    g.K = c.hidden;
+    g.x = s->x;
+    g.norm_w = L.attn_norm;
+    g.eps = c.rms_eps;
+    g.active = &s->st->active;
+    g.err = &s->st->error;
+    check(gemv_launch(g, cs, false), "gemv qkv");
+    QkvArgs qa{};
+    qa.q = s->q;
+    qa.k = s->k;
+    qa.v = s->v;
+    qa.q_norm = L.q_norm;
+    qa.k_norm = L.k_norm;
+    qa.rope = m->rope;
+    qa.kc = s->kc + l * lc;
+    qa.vc = s->vc + l * lc;
+    qa.max_seq = s->max_seq;
+    qa.n_heads = c.n_heads;
+    qa.n_kv = c.n_kv_heads;
+    qa.hd = c.head_dim;
+    qa.eps = c.rms_eps;
+    qa.n = 1;
+    qa.state = s->st;
+    check(qkv_rope_launch(qa, cs), "qkv rope");
+    AttnArgs aa{};
+    aa.q = s->q;
+    aa.kc = s->kc + l * lc;
+    aa.vc = s->vc + l * lc;
+    aa.out = s->attn;
+    aa.max_seq = s->max_seq;
+    aa.n_heads = c.n_heads;
+    aa.n_kv = c.n_kv_heads;
+    aa.hd = c.head_dim;
+    aa.n = 1;
+    aa.state = s->st;
+    aa.partial = s->partial;
+    aa.counters = s->counters;
+    aa.max_splits = kMaxSplits;
+    check(attn_decode_launch(aa, cs), "attn decode");
+    GemvArgs go{};
+    go.seg[0] = seg_of(L.o, s->x, kAdd);
+    go.nseg = 1;
+    go.K = c.n_heads * c.head_dim;
+    go.x = s->attn;
+    go.active = &s->st->active;
+    go.err = &s->st->error;
+    check(gemv_launch(go, cs, false), "gemv o");
+    GemvArgs gf{};
+    gf.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
+    gf.seg[1] = seg_of(L.up, s->gate, kStore);
+    gf.nseg = 2;
+    gf.K = c.hidden;
+    gf.x = s->x;
+    gf.norm_w = L.ffn_norm;
+    gf.eps = c.rms_eps;
+    gf.active = &s->st->active;
+    gf.err = &s->st->error;
+    check(gemv_launch(gf, cs, false), "gemv gate/up");
+    GemvArgs gd{};
+    gd.seg[0] = seg_of(L.down, s->x, kAdd);
+    gd.nseg = 1;
+    gd.K = c.intermediate;
+    gd.x = s->gate;
+    gd.active = &s->st->active;
+    gd.err = &s->st->error;
+    check(gemv_launch(gd, cs, false), "gemv down");
+  }
+  GemvArgs gl{};
+  gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+  gl.nseg = 1;
+  gl.K = c.hidden;
+  gl.x = s->x;
+  gl.norm_w = m->out_norm;
+  gl.eps = c.rms_eps;
+  gl.active = &s->st->active;
+  gl.err = &s->st->error;
+  check(gemv_launch(gl, cs, false), "gemv lm_head");
+}
+
+// Prefill of nc tokens (ids already in s->ids) at positions [pos0, pos0+nc).
+void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
+  const Model* m = s->m;
+  const rpgc_model_config& c = m->c;
+  cudaStream_t cs = s->stream;
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
+                kvd = (int64_t)c.n_kv_heads * c.head_dim;
+  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, c.hidden, s->ids, nc, s->x,
+                     nullptr, cs),
+        "embed");
+  const size_t lc = s->layer_cache_floats();
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m->layers[l];
+    check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
+    check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, cs), "gemm q");
+    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, cs), "gemm k");
+    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, cs), "gemm v");
+    QkvArgs qa{};
+    qa.q = s->q;
+    qa.k = s->k;
+    qa.v = s->v;
+    qa.q_norm = L.q_norm;
+    qa.k_norm = L.k_norm;
+    qa.rope = m->rope;
+    qa.kc = s->kc + l * lc;
+    qa.vc = s->vc + l * lc;
+    qa.max_seq = s->max_seq;
+    qa.n_heads = c.n_heads;
+    qa.n_kv = c.n_kv_heads;
+    qa.hd = c.head_dim;
+    qa.eps = c.rms_eps;
+    qa.pos0 = pos0;
+    qa.n = nc;
+    check(qkv_rope_launch(qa, cs), "qkv rope");
+    AttnArgs aa{};
+    aa.q = s->q;
+    aa.kc = s->kc + l * lc;
+    aa.vc = s->vc + l * lc;
+    aa.out = s->attn;
+    aa.max_seq = s->max_seq;
+    aa.n_heads = c.n_heads;
+    aa.n_kv = c.n_kv_heads;
+    aa.hd = c.head_dim;
+    aa.pos0 = pos0;
+    aa.n = nc;
+    check(attn_prefill_launch(aa, cs), "attn prefill");
+    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, true, cs), "gemm o");
+    check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
+    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, cs), "gemm gate");
+    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, cs), "gemm up");
+    check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
+    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, true, cs), "gemm down");
+  }
+}
+
+void set_state_for_forward(Session* s) {
+  DecodeState h;
+  std::memset(&h, 0, sizeof(h));
+  h.pos = (int32_t)s->len;
+  h.active = 1;
+  check(state_set_launch(s->st, h, s->stream), "state");
+}
+
+// Shared body of rpgc_forward / rpgc_forward_device.
+void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, float* last,
+             float* all) {
+  const Model* m = s->m;
+  const rpgc_model_config& c = m->c;
+  if (n <= 0) fail(RPGC_E_ARG, "empty prompt");
+  if (s->len + n > m->n_rope)
+    fail(RPGC_E_ARG, "position %lld exceeds the RoPE table (%lld positions)",
+         (long long)(s->len + n), (long long)m->n_rope);
+  if (s->len + n > s->max_seq)
+    fail(RPGC_E_CONTEXT_FULL, "position %lld exceeds the KV cache capacity %lld",
+         (long long)(s->len + n), (long long)s->max_seq);
+  if (!ids_on_device)
+    for (int64_t t = 0; t < n; ++t)
+      if (ids[t] < 0 || ids[t] >= c.vocab)
+        fail(RPGC_E_ARG, "token %lld id %d out of range (vocab %d)", (long long)t, ids[t], c.vocab);
+  DeviceGuard dg(s->device);
+  s->has_logits = false;
+  float* all_dev = nullptr;
+  if (all) CK(cudaMalloc(&all_dev, (size_t)s->cap * c.vocab * sizeof(float)));
+  try {
+    for (int64_t t0 = 0; t0 < n; t0 += s->cap) {
+      const int64_t nc = std::min<int64_t>(s->cap, n - t0);
+      CK(cudaMemcpyAsync(s->ids, ids + t0, nc * sizeof(int32_t),
+                         ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                         s->stream));
+      if (nc == 1 && !all) {
+        set_state_for_forward(s);
+        launch_step(s, false);
+      } else {
+        launch_prefill(s, nc, s->len);
+        if (all) {
+          check(rmsnorm_rows_launch(s->x, m->out_norm, nc, c.hidden, c.rms_eps, s->h, s->stream),
+                "rmsnorm");
+          check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, c.hidden,
+                            m->lm_head.row_bytes, s->h, nc, all_dev, c.vocab, false, s->stream),
+                "gemm lm_head");
+          CK(cudaMemcpyAsync(all + t0 * c.vocab, all_dev, (size_t)nc * c.vocab * sizeof(float),
+                             cudaMemcpyDeviceToHost, s->stream));
+        }
+        if (t0 + nc == n) {  // last row -> pending logits
+          GemvArgs gl{};
+          gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+          gl.nseg = 1;
+          gl.K = c.hidden;
+          gl.x = s->x + (nc - 1) * c.hidden;
+          gl.norm_w = m->out_norm;
+          gl.eps = c.rms_eps;
+          check(gemv_launch(gl, s->stream, false), "gemv lm_head");
+        }
+      }
+      s->len += nc;
+    }
+    if (last)
+      CK(cudaMemcpyAsync(last, s->logits, c.vocab * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (last || all || !ids_on_device) CK(cudaStreamSynchronize(s->stream));
+  } catch (...) {
+    if (all_dev) cudaFree(all_dev);
+    throw;
+  }
+  if (all_dev) cudaFree(all_dev);
+  s->has_logits = true;
+}
+
+void capture_step_graph(Session* s) {
+  if (s->step_graph) return;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    SampleArgs sa{};
+    sa.logits = s->logits;
+    sa.n = s->m->c.vocab;
+    sa.state = s->st;
+    sa.out_ids = s->gen_out;
+    sa.n_out = s->n_out;
+    check(sample_launch(sa, s->stream), "sample");
+    launch_step(s, true);
+    check(advance_launch(s->st, s->stream), "advance");
+  } catch (...) {
+    cudaStreamEndCapture(s->stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  CK(cudaStreamEndCapture(s->stream, &g));
+  const cudaError_t e = cudaGraphInstantiate(&s->step_graph, g, 0);
+  cudaGraphDestroy(g);
+  CK(e);
+}
+
+// Shared body of rpgc_generate / rpgc_generate_device.  Returns the number of
+// steps launched.
+int64_t generate(Session* s, const rpgc_gen_opts& o, bool sync_host) {
+  const rpgc_model_config& c = s->m->c;
+  if (!s->has_logits) fail(RPGC_E_STATE, "no pending logits: call rpgc_forward first");
+  if (o.max_tokens <= 0) fail(RPGC_E_ARG, "max_tokens must be positive, got %d", o.max_tokens);
+  if (o.n_stop < 0 || o.n_stop > RPGC_MAX_STOP) fail(RPGC_E_ARG, "at most %d stop ids", RPGC_MAX_STOP);
+  if (o.n_stop > 0 && !o.stop_ids) fail(RPGC_E_ARG, "stop_ids is NULL");
+  const int64_t room = s->max_seq - s->len;
+  if (room <= 0)
+    fail(RPGC_E_CONTEXT_FULL, "context full (%lld positions)", (long long)s->max_seq);
+  const int64_t steps = std::min<int64_t>(o.max_tokens, room);
+  DeviceGuard dg(s->device);
+  DecodeState h;
+  std::memset(&h, 0, sizeof(h));
+  h.pos = (int32_t)s->len;
+  h.active = 1;
+  h.max_tokens = o.max_tokens;
+  h.n_stop = o.n_stop;
+  for (int i = 0; i < o.n_stop; ++i) h.stop_ids[i] = o.stop_ids[i];
+  h.temperature = o.temperature;
+  h.top_k = o.top_k;
+  h.top_p = o.top_p;
+  h.seed = o.seed;
+  check(state_set_launch(s->st, h, s->stream), "state");
+  capture_step_graph(s);
+  const int64_t batch = 8;
+  for (int64_t i = 0; i < steps; i += batch) {
+    const int64_t nb = std::min(batch, steps - i);
+    for (int64_t j = 0; j < nb; ++j) CK(cudaGraphLaunch(s->step_graph, s->stream));
+    if (sync_host && o.n_stop > 0 && i + nb < steps) {
+      int32_t done = 0;
+      CK(cudaMemcpyAsync(&s->st_host->done, &s->st->done, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                         s->stream));
+      CK(cudaStreamSynchronize(s->stream));
+      done = s->st_host->done;
+      if (done) break;
+    }
+  }
+  (void)c;
+  return steps;
+}
+
+int finish_generate(Session* s, const rpgc_gen_opts& o, int64_t steps, int32_t* out,
+                    int32_t* n_out) {
+  CK(cudaMemcpyAsync(s->st_host, s->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  const DecodeState h = *s->st_host;
+  if (h.error) fail(RPGC_E_TIMEOUT, "a device wait gave up during generation (flags %d)", h.error);
+  if (h.n_gen < 0 || h.n_gen > steps) fail(RPGC_E_CUDA, "inconsistent decode state");
+  if (h.n_gen > 0) CK(cudaMemcpy(out, s->gen_out, h.n_gen * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  *n_out = h.n_gen;
+  s->len += h.n_gen;
+  s->has_logits = true;
+  if (!h.done && steps < o.max_tokens)
+    fail(RPGC_E_CONTEXT_FULL, "context full after %d generated tokens (max_seq %lld)", h.n_gen,
+         (long long)s->max_seq);
+  return RPGC_OK;
+}
+
+template <typename F>
+int guard(F&& f) {
+  try {
+    g_last_error.clear();
+    return f();
+  } catch (const Error& e) {
+    g_last_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return RPGC_E_CUDA;
+  } catch (...) {
+    g_last_error = "unknown exception";
+    return RPGC_E_CUDA;
+  }
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+}  // namespace rpgc
+
+using namespace rpgc;
+
+extern "C" {
+
+const char* rpgc_version(void) { return "0.1.0-b200"; }
+const char* rpgc_last_error(void) { return g_last_error.c_str(); }
+
+int rpgc_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int32_t rpgc_model_upload(int device, const rpgc_model_config* cfg, const rpgc_tensor* tensors,
+                          int32_t n_tensors) {
+  return guard([&] {
+    if (!cfg || !tensors || n_tensors <= 0) fail(RPGC_E_ARG, "null config or tensor table");
+    return upload(device, *cfg, tensors, n_tensors);
+  });
+}
+
+int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos) {
+  return guard([&] {
+    if (!path || !*path) fail(RPGC_E_ARG, "empty path");
+    GgufReader r;
+    try {
+      r.Open(path);
+    } catch (const std::exception& e) {
+      fail(RPGC_E_IO, "%s", e.what());
+    }
+    const std::string arch = r.Str("general.architecture", "");
+    if (arch != "qwen3") fail(RPGC_E_ARG, "architecture is '%s'; only qwen3 is implemented", arch.c_str());
+    rpgc_model_config c{};
+    const std::string a = arch + ".";
+    c.n_layers = (int32_t)r.Int(a + "block_count", 0);
+    c.hidden = (int32_t)r.Int(a + "embedding_length", 0);
+    c.n_heads = (int32_t)r.Int(a + "attention.head_count", 0);
+    c.n_kv_heads = (int32_t)r.Int(a + "attention.head_count_kv", c.n_heads);
+    c.intermediate = (int32_t)r.Int(a + "feed_forward_length", 0);
+    c.context_length = (int32_t)r.Int(a + "context_length", 4096);
+    if (c.context_length <= 0) c.context_length = 4096;
+    const int64_t key_len = r.Int(a + "attention.key_length", 0);
+    c.head_dim = key_len > 0 ? (int32_t)key_len : (c.n_heads > 0 ? c.hidden / c.n_heads : 0);
+    if (r.Int(a + "attention.value_length", c.head_dim) != c.head_dim)
+      fail(RPGC_E_ARG, "value_length differs from key_length");
+    c.rope_theta = (float)r.Float(a + "rope.freq_base", 10000.0);
+    c.rms_eps = (float)r.Float(a + "attention.layer_norm_rms_epsilon", 1e-6);
+    const size_t vocab = r.ArrayLen("tokenizer.ggml.tokens");
+    c.vocab = (int32_t)vocab;
+    c.max_pos = max_pos > 0 ? max_pos : 4096;
+    std::vector<rpgc_tensor> tab;
+    std::vector<std::string> names;
+    names.reserve(r.tensors().size());
+    for (const auto& t : r.tensors()) names.push_back(t.name);
+    size_t i = 0;
+    for (const auto& t : r.tensors()) {
+      rpgc_tensor x{};
+      x.name = names[i++].c_str();
+      x.type = t.type;
+      x.n_dims = (int32_t)t.dims.size();
+      for (size_t d = 0; d < t.dims.size(); ++d) x.dims[d] = t.dims[d];
+      x.data = r.TensorData(t);
+      x.n_bytes = t.n_bytes;
+      tab.push_back(x);
+    }
+    if (vocab == 0) {  // fall back to the embedding's rows when no token list
+      for (const auto& x : tab)
+        if (std::string(x.name) == "token_embd.weight" && x.n_dims == 2) c.vocab = (int32_t)x.dims[1];
+    }
+    return upload(device, c, tab.data(), (int32_t)tab.size());
+  });
+}
+
+int rpgc_model_get_config(int32_t model, rpgc_model_config* out) {
+  return guard([&] {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!out) fail(RPGC_E_ARG, "null output");
+    Model* m = model_locked(model);
+    *out = m->c;
+    out->max_pos = (int32_t)m->n_rope;
+    return RPGC_OK;
+  });
+}
+
+int64_t rpgc_model_weight_bytes(int32_t model) {
+  int64_t v = 0;
+  const int rc = guard([&] {
+    std::lock_guard<std::mutex> lk(g_mu);
+    v = model_locked(model)->weight_bytes;
+    return RPGC_OK;
+  });
+  return rc == RPGC_OK ? v : rc;
+}
+
+int rpgc_model_free(int32_t model) {
+  return guard([&] {
+    std::unique_ptr<Model> m;
+    std::vector<std::unique_ptr<Session>> dead;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_models.find(model);
+      if (it == g_models.end()) return RPGC_OK;  // invalid handle: no-op
+      for (int32_t s : it->second->sessions) {
+        auto si = g_sessions.find(s);
+        if (si != g_sessions.end()) {
+          dead.push_back(std::move(si->second));
+          g_sessions.erase(si);
+        }
+      }
+      m = std::move(it->second);
+      g_models.erase(it);
+    }
+    dead.clear();
+    m.reset();
+    return RPGC_OK;
+  });
+}
+
+int32_t rpgc_session_create(int32_t model, int32_t max_seq) {
+  return guard([&] { return session_create(model, max_seq); });
+}
+
+int rpgc_session_destroy(int32_t session) {
+  return guard([&] {
+    std::unique_ptr<Session> s;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_sessions.find(session);
+      if (it == g_sessions.end()) return RPGC_OK;
+      auto mi = g_models.find(it->second->model_id);
+      if (mi != g_models.end()) {
+        auto& v = mi->second->sessions;
+        for (size_t i = 0; i < v.size(); ++i)
+          if (v[i] == session) {
+            v.erase(v.begin() + i);
+            break;
+          }
+      }
+      s = std::move(it->second);
+      g_sessions.erase(it);
+    }
+    std::lock_guard<std::mutex> lk2(s->mu);
+    return RPGC_OK;
+  });
+}
+
+int64_t rpgc_session_len(int32_t session) {
+  int64_t v = 0;
+  const int rc = guard([&] {
+    v = require_session(session)->len;
+    return RPGC_OK;
+  });
+  return rc == RPGC_OK ? v : rc;
+}
+
+int rpgc_session_set_len(int32_t session, int64_t len) {
+  return guard([&] {
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    if (len < 0 || len > s->max_seq)
+      fail(RPGC_E_ARG, "length %lld out of range (capacity %lld)", (long long)len, (long long)s->max_seq);
+    s->len = len;
+    s->has_logits = false;
+    return RPGC_OK;
+  });
+}
+
+void* rpgc_session_stream(int32_t session) {
+  void* p = nullptr;
+  guard([&] {
+    p = require_session(session)->stream;
+    return RPGC_OK;
+  });
+  return p;
+}
+
+int rpgc_session_read_kv(int32_t session, float* k, float* v) {
+  return guard([&] {
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    DeviceGuard dg(s->device);
+    const size_t bytes = (size_t)s->m->c.n_layers * s->layer_cache_floats() * sizeof(float);
+    if (k) CK(cudaMemcpyAsync(k, s->kc, bytes, cudaMemcpyDeviceToHost, s->stream));
+    if (v) CK(cudaMemcpyAsync(v, s->vc, bytes, cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    return RPGC_OK;
+  });
+}
+
+int rpgc_forward(int32_t session, const int32_t* ids, int64_t n, float* last_logits,
+                 float* all_logits) {
+  return guard([&] {
+    if (!ids) fail(RPGC_E_ARG, "null ids");
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    forward(s, ids, false, n, last_logits, all_logits);
+    return RPGC_OK;
+  });
+}
+
+int rpgc_forward_device(int32_t session, const int32_t* ids_dev, int64_t n) {
+  return guard([&] {
+    if (!ids_dev) fail(RPGC_E_ARG, "null ids");
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    forward(s, ids_dev, true, n, nullptr, nullptr);
+    return RPGC_OK;
+  });
+}
+
+int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids, int32_t* n_out) {
+  return guard([&] {
+    if (!opts || !out_ids || !n_out) fail(RPGC_E_ARG, "null argument");
+    *n_out = 0;
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    const int64_t steps = generate(s, *opts, true);
+    return finish_generate(s, *opts, steps, out_ids, n_out);
+  });
+}
+
+int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids_dev,
+                         int32_t* n_out_dev) {
+  return guard([&] {
+    if (!opts || !out_ids_dev || !n_out_dev) fail(RPGC_E_ARG, "null argument");
+    if (opts->n_stop != 0)
+      fail(RPGC_E_ARG, "device-resident generation runs a fixed number of steps: no stop ids");
+    Session* s = require_session(session);
+    std::lock_guard<std::mutex> lk(s->mu);
+    const int64_t steps = generate(s, *opts, false);
+    if (steps < opts->max_tokens)
+      fail(RPGC_E_CONTEXT_FULL, "max_tokens %d exceeds the remaining context", opts->max_tokens);
+    DeviceGuard dg(s->device);
+    CK(cudaMemcpyAsync(out_ids_dev, s->gen_out, steps * sizeof(int32_t), cudaMemcpyDeviceToDevice,
+                       s->stream));
+    CK(cudaMemcpyAsync(n_out_dev, s->n_out, sizeof(int32_t), cudaMemcpyDeviceToDevice, s->stream));
+    s->len += steps;
+    s->has_logits = true;
+    return RPGC_OK;
+  });
+}
+
+int rpgc_session_sync(int32_t session) {
+  return guard([&] {
+    Session* s = require_session(session);
+    DeviceGuard dg(s->device);
+    CK(cudaStreamSynchronize(s->stream));
+    CK(cudaMemcpy(s->st_host, s->st, sizeof(DecodeState), cudaMemcpyDeviceToHost));
+    if (s->st_host->error) fail(RPGC_E_TIMEOUT, "a device wait gave up (flags %d)", s->st_host->error);
+    return RPGC_OK;
+  });
+}
+
+int rpgc_dequantize_rows(uint32_t type, const void* w, int64_t rows, int64_t cols, float* out,
+                         void* stream) {
+  return guard([&] {
+    const int64_t rb = row_bytes_of(type, cols);
+    if (!w || !out || rows <= 0 || rb < 0 || (type != RPGC_F16 && !kernel_type(type)))
+      fail(RPGC_E_ARG, "bad dequantize arguments (type %u, %lld x %lld)", type, (long long)rows,
+           (long long)cols);
+    check(dequant_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, out, as_stream(stream)),
+          "dequant");
+    return RPGC_OK;
+  });
+}
+
+int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t cols, const float* x, float* y,
+                void* stream) {
+  return guard([&] {
+    const int64_t rb = row_bytes_of(type, cols);
+    if (!w || !x || !y || rows <= 0 || rb < 0 || !kernel_type(type) || cols % 32)
+      fail(RPGC_E_ARG, "bad matvec arguments (type %u, %lld x %lld)", type, (long long)rows,
+           (long long)cols);
+    if (reinterpret_cast<uintptr_t>(w) & 15) fail(RPGC_E_ARG, "weights must be 16-byte aligned");
+    GemvArgs g{};
+    g.seg[0].w = static_cast<const uint8_t*>(w);
+    g.seg[0].out = y;
+    g.seg[0].rows = rows;
+    g.seg[0].row_bytes = rb;
+    g.seg[0].type = type;
+    g.seg[0].mode = kStore;
+    g.nseg = 1;
+    g.K = (int32_t)cols;
+    g.x = x;
+    check(gemv_launch(g, as_stream(stream), false), "gemv");
+    return RPGC_OK;
+  });
+}
+
+int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols, const float* X, int64_t n,
+                float* OUT, void* stream) {
+  if (n == 1) return rpgc_matvec(type, w, rows, cols, X, OUT, stream);
+  return guard([&] {
+    const int64_t rb = row_bytes_of(type, cols);
+    if (!w || !X || !OUT || rows <= 0 || n <= 0 || rb < 0 || !kernel_type(type) || cols % 32)
+      fail(RPGC_E_ARG, "bad matmul arguments");
+    check(gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT, rows, false,
+                      as_stream(stream)),
+          "gemm");
+    return RPGC_OK;
+  });
+}
+
+int rpgc_sample(const float* logits, int64_t n, float temperature, int32_t top_k, float top_p,
+                float u, int32_t* token_dev, void* stream) {
+  return guard([&] {
+    if (!logits || !token_dev || n <= 0) fail(RPGC_E_ARG, "bad sample arguments");
+    SampleArgs a{};
+    a.logits = logits;
+    a.n = n;
+    a.temperature = temperature;
+    a.top_k = top_k;
+    a.top_p = top_p;
+    a.u = u;
+    a.token_out = token_dev;
+    check(sample_launch(a, as_stream(stream)), "sample");
+    return RPGC_OK;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,486 @@
+// k_sample.cu -- greedy / sampled token choice on the device (one block).
+//
+// Reference: ArgMax (src/kernels.h:42-52), CounterUniform
+// (src/sampler.cc:16-34), FilterToProbs + SampleToken (src/sampler.cc:36-112):
+//   temperature -> top-k (keep >= k-th largest, 1 < k < n) -> softmax (double
+//   sum) -> top-p (ascending cumulative sum, zero while cum <= 1-p, keep the
+//   largest) -> renormalise -> first index whose cumulative sum exceeds u.
+//
+// Device formulation.  The k-th largest value is a 4-pass radix select over
+// order-preserving float keys.  The top-p cut is a 4-pass radix search over
+// the probability bits whose bucket masses are exact 2^-62 fixed-point sums,
+// which locates the first element (ascending value, ties by index) whose
+// running sum exceeds 1-p without sorting.  The inverse CDF uses the same
+// exact fixed-point prefix sums in index order.  Softmax/renormalisation sums
+// are double, reduced in a fixed order (deterministic).  When top-k is active
+// its survivors are compacted (index order kept) and the later passes run on
+// them only.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rpgc {
+namespace {
+
+constexpr int NT = 1024;
+constexpr int kCap = 4096;  // compacted survivors held in shared memory
+constexpr double kFix = 4611686018427387904.0;  // 2^62
+
+struct Smem {
+  uint32_t cnt[32][256];
+  unsigned long long msum[32][256];
+  int cidx[kCap];
+  float cval[kCap];
+  double dred[NT];
+  unsigned long long ured[NT];
+  int ired[NT];
+  float fred[32];
+  int ibest[32];
+  unsigned long long bcast_u[4];
+  double bcast_d[2];
+  int bcast_i[8];
+  float bcast_f[4];
+};
+
+__device__ __forceinline__ uint32_t fkey(float f) {  // order-preserving
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float unfkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+__device__ uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+__device__ float counter_uniform(uint64_t seed, uint64_t counter) {
+  const uint32_t bits = (uint32_t)(splitmix64(seed + 0x9E3779B97F4A7C15ull * counter) >> 40);
+  return (float)bits * (1.0f / 16777216.0f);
+}
+
+// ---- block reductions (1024 threads) ------------------------------------
+__device__ double block_sum_d(Smem& S, double v) {  // fixed pairing order
+  S.dred[threadIdx.x] = v;
+  __syncthreads();
+  for (int st = NT / 2; st > 0; st >>= 1) {
+    if (threadIdx.x < st) S.dred[threadIdx.x] += S.dred[threadIdx.x + st];
+    __syncthreads();
+  }
+  const double r = S.dred[0];
+  __syncthreads();
+  return r;
+}
+__device__ float block_max_f(Smem& S, float v) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) S.fred[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float w = S.fred[threadIdx.x];
+    w = warp_max(w);
+    if (threadIdx.x == 0) S.bcast_f[0] = w;
+  }
+  __syncthreads();
+  const float r = S.bcast_f[0];
+  __syncthreads();
+  return r;
+}
+// (value, index): larger value wins, ties -> smaller index.  NaN never wins.
+__device__ int block_argmax(Smem& S, float v, int i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    S.fred[threadIdx.x >> 5] = v;
+    S.ibest[threadIdx.x >> 5] = i;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    v = S.fred[threadIdx.x];
+    i = S.ibest[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (ov > v || (ov == v && oi < i)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    if (threadIdx.x == 0) S.bcast_i[0] = i;
+  }
+  __syncthreads();
+  const int r = S.bcast_i[0];
+  __syncthreads();
+  return r;
+}
+// exclusive prefix over threads (integers are exact, order irrelevant)
+template <typename T>
+__device__ T block_excl_scan(T* buf, T v, T* total) {
+  buf[threadIdx.x] = v;
+  __syncthreads();
+  for (int off = 1; off < NT; off <<= 1) {
+    T add = threadIdx.x >= off ? buf[threadIdx.x - off] : T(0);
+    __syncthreads();
+    buf[threadIdx.x] += add;
+    __syncthreads();
+  }
+  const T incl = buf[threadIdx.x];
+  *total = buf[NT - 1];
+  __syncthreads();
+  return incl - v;
+}
+
+__device__ void clear_hist(Smem& S, bool sums) {
+  for (int i = threadIdx.x; i < 32 * 256; i += NT) {
+    (&S.cnt[0][0])[i] = 0;
+    if (sums) (&S.msum[0][0])[i] = 0;
+  }
+  __syncthreads();
+}
+
+// Candidate view: element j of [0, m).
+struct View {
+  const float* logits;
+  float invT;
+  bool scaled;
+  bool compact;
+  const int* idx;
+  const float* val;
+  float kth;     // top-k floor (-inf when off)
+  float mx;      // softmax max
+  float inv;     // softmax 1/sum
+  int m;
+};
+__device__ __forceinline__ float v_s(const View& v, int j) {
+  float s = v.compact ? v.val[j] : (v.scaled ? v.logits[j] * v.invT : v.logits[j]);
+  return s < v.kth ? -INFINITY : s;
+}
+__device__ __forceinline__ int v_i(const View& v, int j) { return v.compact ? v.idx[j] : j; }
+__device__ __forceinline__ float v_p(const View& v, int j) {  // softmax output (float)
+  return expf(v_s(v, j) - v.mx) * v.inv;
+}
+
+__device__ int sample_probs(Smem& S, const float* logits, int n, float T, int top_k, float top_p,
+                            float u) {
+  const int tid = threadIdx.x;
+  View V;
+  V.logits = logits;
+  V.scaled = (T != 1.0f);
+  V.invT = 1.0f / T;
+  V.compact = false;
+  V.idx = S.cidx;
+  V.val = S.cval;
+  V.kth = -INFINITY;
+  V.m = n;
+  // ---------------- top-k: k-th largest value by radix select
+  if (top_k > 1 && top_k < n) {
+    uint32_t prefix = 0, pmask = 0;
+    int krem = top_k;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      clear_hist(S, false);
+      const int w = tid >> 5;
+      for (int j = tid; j < n; j += NT) {
+        const uint32_t k = fkey(v_s(V, j));
+        if ((k & pmask) == prefix) atomicAdd(&S.cnt[w][(k >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid < 256) {
+        uint32_t c = 0;
+        for (int ww = 0; ww < 32; ++ww) c += S.cnt[ww][tid];
+        S.cnt[0][tid] = c;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int above = 0, b = 255;
+        for (; b > 0; --b) {
+          const int c = (int)S.cnt[0][b];
+          if (above + c >= krem) break;
+          above += c;
+        }
+        S.bcast_i[1] = b;
+        S.bcast_i[2] = krem - above;
+      }
+      __syncthreads();
+      prefix |= (uint32_t)S.bcast_i[1] << shift;
+      pmask |= 255u << shift;
+      krem = S.bcast_i[2];
+      __syncthreads();
+    }
+    V.kth = unfkey(prefix);
+    // compact survivors in index order when they fit
+    const int C = (n + NT - 1) / NT, j0 = tid * C, j1 = min(n, j0 + C);
+    int mine = 0;
+    for (int j = j0; j < j1; ++j) mine += (v_s(V, j) != -INFINITY);
+    int total;
+    const int base = block_excl_scan<int>(S.ired, mine, &total);
+    if (total <= kCap) {
+      int o = base;
+      for (int j = j0; j < j1; ++j) {
+        const float s = v_s(V, j);
+        if (s != -INFINITY) {
+          S.cidx[o] = j;
+          S.cval[o] = s;
+          ++o;
+        }
+      }
+      __syncthreads();
+      V.compact = true;
+      V.m = total;
+      V.kth = -INFINITY;  // survivors only
+    }
+  }
+  const int m = V.m;
+  const int C = (m + NT - 1) / NT, j0 = tid * C, j1 = min(m, j0 + C);
+  // ---------------- softmax
+  float lmax = -INFINITY;
+  for (int j = j0; j < j1; ++j) lmax = fmaxf(lmax, v_s(V, j));
+  V.mx = block_max_f(S, lmax);
+  V.inv = 1.0f;
+  double le = 0.0;
+  for (int j = j0; j < j1; ++j) le += (double)expf(v_s(V, j) - V.mx);
+  V.inv = (float)(1.0 / block_sum_d(S, le));
+  // ---------------- top-p: first ascending element whose running mass > 1-p
+  const bool do_p = top_p > 0.0f && top_p < 1.0f;
+  uint32_t vkey = 0;      // crossing value (probability bits)
+  long long n_zero_ties = 0;
+  bool all_zero = false;
+  if (do_p) {
+    const double thr = 1.0 - (double)top_p;
+    const unsigned long long thr_fp = (unsigned long long)(thr * kFix);
+    unsigned long long below = 0;  // mass of elements with key < prefix range
+    uint32_t prefix = 0, pmask = 0;
+    bool crossed = true;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      clear_hist(S, true);
+      const int w = tid >> 5;
+      for (int j = j0; j < j1; ++j) {
+        const float p = v_p(V, j);
+        const uint32_t k = __float_as_uint(p);
+        if ((k & pmask) == prefix) {
+          const uint32_t b = (k >> shift) & 255u;
+          atomicAdd(&S.cnt[w][b], 1u);
+          atomicAdd(&S.msum[w][b], (unsigned long long)((double)p * kFix));
+        }
+      }
+      __syncthreads();
+      if (tid < 256) {
+        uint32_t c = 0;
+        unsigned long long s = 0;
+        for (int ww = 0; ww < 32; ++ww) {
+          c += S.cnt[ww][tid];
+          s += S.msum[ww][tid];
+        }
+        S.cnt[0][tid] = c;
+        S.msum[0][tid] = s;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long cum = below;
+        int b = 0;
+        for (; b < 256; ++b) {
+          if (cum + S.msum[0][b] > thr_fp) break;
+          cum += S.msum[0][b];
+        }
+        S.bcast_i[1] = b;
+        S.bcast_u[0] = cum;
+        S.bcast_i[3] = (b < 256) ? (int)S.cnt[0][b] : 0;
+      }
+      __syncthreads();
+      const int b = S.bcast_i[1];
+      if (b == 256) {  // never exceeds: every element is zeroed
+        crossed = false;
+        __syncthreads();
+        break;
+      }
+      prefix |= (uint32_t)b << shift;
+      pmask |= 255u << shift;
+      below = S.bcast_u[0];
+      __syncthreads();
+    }
+    if (crossed) {
+      vkey = prefix;
+      const unsigned long long vfp = (unsigned long long)((double)__uint_as_float(vkey) * kFix);
+      // ties: the j-th (index order) equal element has running mass below+(j+1)*v
+      n_zero_ties = (vfp > 0 && thr_fp >= below) ? (long long)((thr_fp - below) / vfp) : 0;
+    } else {
+      all_zero = true;
+    }
+  }
+  // tie ranks of the crossing value, per thread chunk
+  int my_ties = 0;
+  if (do_p && !all_zero)
+    for (int j = j0; j < j1; ++j) my_ties += (__float_as_uint(v_p(V, j)) == vkey);
+  int tot_ties;
+  const int tie_base = block_excl_scan<int>(S.ired, my_ties, &tot_ties);
+  // last index of the maximum (the largest element in ascending order)
+  int keep_last = -1;
+  if (do_p && all_zero) {
+    // largest value, ties -> largest index: argmax over (value, -index)
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int j = j0; j < j1; ++j) {
+      const float p = v_p(V, j);
+      if (p > bv || (p == bv && v_i(V, j) > bi)) {
+        bv = p;
+        bi = v_i(V, j);
+      }
+    }
+    const int neg = block_argmax(S, bv, bi >= 0 ? -bi : 0x7fffffff);
+    keep_last = -neg;
+  }
+  // final probability of element j (after top-p and before renormalisation)
+  auto q_raw = [&](int j, int tie_rank) -> float {
+    const float p = v_p(V, j);
+    if (!do_p) return p;
+    if (all_zero) return v_i(V, j) == keep_last ? 1.0f : 0.0f;
+    const uint32_t k = __float_as_uint(p);
+    if (k < vkey) return 0.0f;
+    if (k == vkey && tie_rank < n_zero_ties) return 0.0f;
+    return p;
+  };
+  float inv2 = 1.0f;
+  if (do_p) {
+    double ls = 0.0;
+    int r = tie_base;
+    for (int j = j0; j < j1; ++j) {
+      const bool tie = !all_zero && __float_as_uint(v_p(V, j)) == vkey;
+      ls += (double)q_raw(j, r);
+      r += tie;
+    }
+    const double tot = block_sum_d(S, ls);
+    if (tot > 0.0) inv2 = (float)(1.0 / tot);
+  }
+  // ---------------- inverse CDF in index order (exact fixed-point prefix)
+  unsigned long long mine = 0;
+  {
+    int r = tie_base;
+    for (int j = j0; j < j1; ++j) {
+      const bool tie = do_p && !all_zero && __float_as_uint(v_p(V, j)) == vkey;
+      const float q = do_p ? q_raw(j, r) * inv2 : q_raw(j, r);
+      mine += (unsigned long long)((double)q * kFix);
+      r += tie;
+    }
+  }
+  unsigned long long totm;
+  const unsigned long long before = block_excl_scan<unsigned long long>(S.ured, mine, &totm);
+  const unsigned long long ufp = (unsigned long long)((double)u * kFix);
+  if (tid == 0) S.bcast_i[4] = 0x7fffffff;
+  __syncthreads();
+  if (before <= ufp && ufp < before + mine) {  // the crossing lies in this chunk
+    unsigned long long cum = before;
+    int r = tie_base;
+    for (int j = j0; j < j1; ++j) {
+      const bool tie = do_p && !all_zero && __float_as_uint(v_p(V, j)) == vkey;
+      const float q = do_p ? q_raw(j, r) * inv2 : q_raw(j, r);
+      cum += (unsigned long long)((double)q * kFix);
+      r += tie;
+      if (cum > ufp) {
+        S.bcast_i[4] = v_i(V, j);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  int tok = S.bcast_i[4];
+  __syncthreads();
+  if (tok == 0x7fffffff) {  // u beyond the total mass: most probable token
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    int r = tie_base;
+    for (int j = j0; j < j1; ++j) {
+      const bool tie = do_p && !all_zero && __float_as_uint(v_p(V, j)) == vkey;
+      const float q = do_p ? q_raw(j, r) * inv2 : q_raw(j, r);
+      r += tie;
+      if (q > bv || (q == bv && v_i(V, j) < bi)) {
+        bv = q;
+        bi = v_i(V, j);
+      }
+    }
+    tok = block_argmax(S, bv, bi);
+  }
+  return tok;
+}
+
+__global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
+  extern __shared__ __align__(16) uint8_t raw[];
+  Smem& S = *reinterpret_cast<Smem*>(raw);
+  grid_dep_wait();
+  DecodeState* st = a.state;
+  float T = a.temperature, top_p = a.top_p, u = a.u;
+  int top_k = a.top_k;
+  if (st) {
+    const int done = st->done;
+    __syncthreads();
+    if (done) {
+      if (threadIdx.x == 0) st->active = 0;
+      return;
+    }
+    T = st->temperature;
+    top_k = st->top_k;
+    top_p = st->top_p;
+    u = counter_uniform(st->seed, (uint64_t)st->pos);
+  }
+  const int n = (int)a.n;
+  int tok;
+  if (!(T > 0.0f)) {  // greedy: first index of the maximum
+    const int C = (n + NT - 1) / NT, j0 = threadIdx.x * C, j1 = min(n, j0 + C);
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = j0; j < j1; ++j) {
+      const float v = a.logits[j];
+      if (v > bv) {
+        bv = v;
+        bi = j;
+      }
+    }
+    tok = block_argmax(S, bv, bi);
+    if (tok == 0x7fffffff) tok = 0;
+  } else {
+    tok = sample_probs(S, a.logits, n, T, top_k, top_p, u);
+  }
+  if (threadIdx.x == 0) {
+    if (st) {
+      st->token = tok;
+      a.out_ids[st->n_gen] = tok;
+      st->n_gen += 1;
+      st->active = 1;
+      bool stop = false;
+      for (int i = 0; i < st->n_stop; ++i) stop |= (st->stop_ids[i] == tok);
+      if (stop || st->n_gen >= st->max_tokens) st->done = 1;
+      if (a.n_out) *a.n_out = st->n_gen;
+    } else {
+      *a.token_out = tok;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(Smem));
+    if (e != cudaSuccess) return e;
+    configured = dev;
+  }
+  if (a.n <= 0 || a.n > 0x7ffffff0) return cudaErrorInvalidValue;
+  sample_kernel<<<1, NT, sizeof(Smem), s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace rpgc

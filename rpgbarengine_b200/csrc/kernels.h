@@ -1,0 +1,133 @@
+// kernels.h -- host-side launch interface of the sm_100a kernels (internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rpgc {
+
+// Decode-loop state living in device memory, so that one captured CUDA graph
+// serves every step (the position and the stop status are read in-kernel).
+struct DecodeState {
+  int32_t pos;        // KV length = position of the token being forwarded
+  int32_t active;     // 0: this step does nothing (generation finished)
+  int32_t done;       // set once a stop id / max_tokens was reached
+  int32_t n_gen;      // tokens produced so far
+  int32_t max_tokens;
+  int32_t n_stop;
+  int32_t top_k;
+  int32_t token;      // token being forwarded this step
+  float temperature;
+  float top_p;
+  uint64_t seed;
+  int32_t stop_ids[16];
+  int32_t error;      // kernel error flags (bounded waits)
+  int32_t pad;
+};
+
+// ------------------------------------------------------------------ GEMV
+enum GemvMode : int32_t { kStore = 0, kAdd = 1, kSwiGLU = 2 };
+
+struct GemvSeg {
+  const uint8_t* w;  // raw row-major blocks
+  float* out;        // rows outputs
+  int64_t rows;
+  int64_t row_bytes;
+  uint32_t type;
+  int32_t mode;      // kSwiGLU: this seg is the gate, seg+1 the up projection
+};
+
+struct GemvArgs {
+  GemvSeg seg[4];
+  int32_t nseg;
+  int32_t K;              // shared input length
+  const float* x;         // input [K]
+  const float* norm_w;    // optional RMSNorm gain applied to x first
+  float eps;
+  const int32_t* active;  // optional: skip when *active == 0
+  int32_t* err;           // optional error flags
+};
+
+// Launch y = W x over up to 4 segments sharing x (decode, batch 1).
+cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
+size_t gemv_smem_bytes(int K, bool need_f32);
+
+// ---------------------------------------------------------- prefill GEMM
+// OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
+cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K,
+                        int64_t row_bytes, const float* X, int64_t n, float* out, int64_t ldo,
+                        bool accumulate, cudaStream_t s);
+
+// -------------------------------------------------------------- others
+cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,
+                           int64_t row_bytes, float* out, cudaStream_t s);
+// x[t] = dequant(embd row ids[t]); ids on device.  state (optional): take the
+// single id from state->token and skip when inactive.
+cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int32_t hidden,
+                         const int32_t* ids, int64_t n, float* x, const DecodeState* state,
+                         cudaStream_t s);
+cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
+                                float* out, cudaStream_t s);
+cudaError_t swiglu_launch(float* gate, const float* up, int64_t count, cudaStream_t s);
+
+// Per token t (position pos0+t, or state->pos when state != null): RMSNorm
+// each q and k head with its gain, RoPE both, write k and v into the cache.
+struct QkvArgs {
+  float* q;            // [n][n_heads*hd] in place
+  const float* k;      // [n][n_kv*hd]
+  const float* v;      // [n][n_kv*hd]
+  const float* q_norm;
+  const float* k_norm;
+  const float* rope;   // [positions][hd/2 cos | hd/2 sin]
+  float* kc;           // cache of this layer: [n_kv][max_seq][hd]
+  float* vc;
+  int64_t max_seq;
+  int32_t n_heads, n_kv, hd;
+  float eps;
+  int64_t pos0;
+  int64_t n;
+  const DecodeState* state;
+};
+cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s);
+
+struct AttnArgs {
+  const float* q;      // [n][n_heads*hd]
+  const float* kc;     // layer cache [n_kv][max_seq][hd]
+  const float* vc;
+  float* out;          // [n][n_heads*hd]
+  int64_t max_seq;
+  int32_t n_heads, n_kv, hd;
+  int64_t pos0, n;     // prefill
+  const DecodeState* state;  // decode: pos from state, n = 1
+  float* partial;      // decode split-K scratch
+  int32_t* counters;   // decode: one per kv head, zero between launches
+  int32_t max_splits;
+};
+cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s);
+cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s);
+size_t attn_decode_partial_floats(int n_kv, int n_heads, int hd, int max_splits);
+
+// Sampler / argmax.  When state != null: decode-loop step (reads options,
+// u = CounterUniform(seed, pos), writes state->token, appends to out_ids,
+// updates done/active).  Otherwise samples with the explicit options into
+// *token_out.
+struct SampleArgs {
+  const float* logits;
+  int64_t n;
+  float temperature;
+  int32_t top_k;
+  float top_p;
+  float u;
+  int32_t* token_out;
+  DecodeState* state;
+  int32_t* out_ids;
+  int32_t* n_out;
+};
+cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s);
+// state->pos += 1 when active (end of a decode step).
+cudaError_t advance_launch(DecodeState* st, cudaStream_t s);
+// *st = v, ordered on the stream (the value travels as a kernel parameter, so
+// the host may reuse its copy immediately).
+cudaError_t state_set_launch(DecodeState* st, const DecodeState& v, cudaStream_t s);
+
+}  // namespace rpgc

@@ -1,0 +1,73 @@
+"""C-ABI surface of librpgc.so, checked without a GPU (no compute calls)."""
+import os
+import re
+import tempfile
+
+import numpy as np
+import pytest
+
+import rpgbarengine_b200 as rb
+from rpgbarengine_b200 import synth
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions(path):
+    src = open(path).read()
+    return sorted(set(re.findall(r"RPGC_API\s+[\w\s\*]+?\b(rpgc_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_header_symbol():
+    names = header_functions(os.path.join(ROOT, "include", "rpgc.h"))
+    assert len(names) >= 20
+    lib = rb.lib()
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_only_abi_symbols_are_exported():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", rb.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    funcs = [l.split()[-1] for l in out.splitlines() if " T " in l]
+    extra = [f for f in funcs if not f.startswith("rpgc_")]
+    assert not extra, extra[:10]
+
+
+def test_version_and_errors_without_gpu():
+    assert rb.version()
+    if rb.device_count() > 0:
+        pytest.skip("a GPU is present; the no-device paths are not reachable")
+    with pytest.raises(rb.RpgcError) as e:
+        rb.Model.load_gguf("/nonexistent/model.gguf")
+    assert e.value.code == rb.E_IO
+    # invalid handles are state errors, destroy/free of unknown handles are no-ops
+    assert rb.lib().rpgc_session_len(12345) == rb.E_STATE
+    assert rb.lib().rpgc_session_destroy(12345) == rb.OK
+    assert rb.lib().rpgc_model_free(12345) == rb.OK
+
+
+def test_gguf_parse_reaches_device_check():
+    if rb.device_count() > 0:
+        pytest.skip("a GPU is present")
+    d = tempfile.mkdtemp()
+    p = os.path.join(d, "tiny.gguf")
+    synth.write_model(p, synth.TINY_MIX, 1)
+    with pytest.raises(rb.RpgcError) as e:
+        rb.Model.load_gguf(p)
+    # the file parsed and the tensor table validated; only the device is missing
+    assert "device" in str(e.value).lower()
+
+
+def test_gguf_python_roundtrip():
+    d = tempfile.mkdtemp()
+    p = os.path.join(d, "t.gguf")
+    tens = synth.write_model(p, synth.TINY_Q8, 3)
+    f = rb.gguf.read(p)
+    assert f.meta["general.architecture"] == "qwen3"
+    assert f.meta["qwen3.block_count"] == synth.TINY_Q8.n_layers
+    assert len(f.meta["tokenizer.ggml.tokens"]) == synth.TINY_Q8.vocab
+    for a in tens:
+        b = f.tensor(a.name)
+        assert b.ggml_type == a.ggml_type and tuple(b.dims) == tuple(a.dims)
+        assert np.array_equal(np.asarray(b.data), a.data)

@@ -1,0 +1,159 @@
+"""Whole token loop on the GPU vs the oracle: logits, KV cache, greedy and
+sampled generation, prefix reuse, errors."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+import rpgbarengine_b200 as rb  # noqa: E402
+from rpgbarengine_b200 import synth  # noqa: E402
+from tests.gpu_util import LOGIT_REL_L2, compare_tokens, rel_l2  # noqa: E402
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_gpu():
+    if rb.device_count() == 0:
+        pytest.fail("GPU test collected without a CUDA device")
+
+
+MODELS = {}
+
+
+def pair(orc, shape, seed=5, max_pos=1024):
+    key = (shape.name, seed, max_pos)
+    if key not in MODELS:
+        tens = synth.build_tensors(shape, seed)
+        MODELS[key] = (rb.Model.upload(shape, tens, 0, max_pos), orc.model(shape, tens, max_pos), tens)
+    return MODELS[key][:2]
+
+
+@pytest.mark.parametrize("shape", [synth.TINY_MIX, synth.TINY_Q8, synth.TINY_UNTIED])
+def test_forward_logits_and_kv(orc, shape):
+    gm, om = pair(orc, shape)
+    ids = synth.prompt_ids(21, 40, shape.vocab)
+    s = gm.session(128)
+    got = s.forward_full(ids, all_rows=True)
+    okv = om.kv(128)
+    want = om.forward(ids, okv, all_rows=True)
+    for t in range(len(ids)):
+        assert rel_l2(got[t], want[t]) <= LOGIT_REL_L2, t
+    assert rel_l2(got, want) <= 1e-4  # far inside the gate
+    assert s.len == len(ids)
+    k, v = s.read_kv()
+    ok, ov = okv.arrays()
+    n = len(ids)
+    assert rel_l2(k[:, :, :n], ok[:, :, :n]) <= 1e-5
+    assert rel_l2(v[:, :, :n], ov[:, :, :n]) <= 1e-5
+    assert np.all(k[:, :, n:] == 0)
+
+
+def test_single_token_steps_match_prefill(orc):
+    # decode-path kernels (one token at a time) vs the oracle's cached forward
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    ids = synth.prompt_ids(3, 12, shape.vocab)
+    s = gm.session(64)
+    okv = om.kv(64)
+    for t in range(len(ids)):
+        got = s.forward_full(ids[t:t + 1])
+        want = om.forward(ids[t:t + 1], okv)[0]
+        assert rel_l2(got, want) <= LOGIT_REL_L2
+        assert rel_l2(got, want) <= 1e-5
+
+
+@pytest.mark.parametrize("T,k,p,seed", [(0.0, 0, 1.0, 0), (0.7, 20, 0.8, 99), (1.0, 0, 0.95, 7),
+                                        (1.2, 5, 1.0, 3)])
+@pytest.mark.parametrize("shape", [synth.TINY_MIX, synth.TINY_Q8])
+def test_generate_matches_oracle(orc, shape, T, k, p, seed):
+    gm, om = pair(orc, shape)
+    ids = synth.prompt_ids(8, 17, shape.vocab)
+    s = gm.session(96)
+    s.forward_full(ids)
+    got = s.generate(24, temperature=T, top_k=k, top_p=p, seed=seed)
+    okv = om.kv(96)
+    lg = om.forward(ids, okv)
+    want, wl = om.generate(okv, lg[-1], 24, temperature=T, top_k=k, top_p=p, seed=seed,
+                           want_logits=True)
+    if T > 0:  # sampling consumes u = CounterUniform(seed, pos): sequences must agree
+        assert list(got) == list(want)
+    else:
+        compare_tokens(got, want, wl)
+    assert s.len == len(ids) + len(got)
+
+
+def test_stop_token_is_forwarded(orc):
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    ids = synth.prompt_ids(9, 10, shape.vocab)
+    s = gm.session(96)
+    s.forward_full(ids)
+    free = s.generate(12)
+    stop = int(free[3])
+    n = list(free).index(stop) + 1
+    s2 = gm.session(96)
+    s2.forward_full(ids)
+    toks = s2.generate(12, stop_ids=[stop])
+    assert list(toks) == list(free[:n])
+    assert s2.len == len(ids) + n
+
+
+def test_prefix_reuse_warm_equals_cold(orc):
+    shape = synth.TINY_MIX
+    gm, _ = pair(orc, shape)
+    ids = synth.prompt_ids(4, 30, shape.vocab)
+    cold = gm.session(64)
+    lc = cold.forward_full(ids)
+    warm = gm.session(64)
+    warm.forward_full(ids[:19])
+    warm.forward_full(np.array([1, 2, 3, 4], np.int32))
+    warm.set_len(19)  # src/engine.cc:425-431
+    lw = warm.forward_full(ids[19:])
+    assert np.array_equal(lc.view(np.uint32), lw.view(np.uint32))
+    assert np.array_equal(cold.generate(8), warm.generate(8))
+
+
+def test_errors(orc):
+    shape = synth.TINY_MIX
+    gm, _ = pair(orc, shape)
+    s = gm.session(20)
+    with pytest.raises(rb.RpgcError):
+        s.generate(4)  # no forward yet
+    with pytest.raises(rb.RpgcError):
+        s.forward_full(np.array([shape.vocab], np.int32))
+    s.forward_full(synth.prompt_ids(1, 18, shape.vocab))
+    with pytest.raises(rb.ContextFull):
+        s.generate(8)  # 18 + 8 > 20: the reference throws once the cache is full
+    with pytest.raises(rb.ContextFull):
+        gm.session(20).forward_full(synth.prompt_ids(1, 21, shape.vocab))
+
+
+def test_gguf_load_matches_upload(orc, tmp_path):
+    shape = synth.TINY_UNTIED
+    p = str(tmp_path / "m.gguf")
+    tens = synth.write_model(p, shape, 31)
+    a = rb.Model.load_gguf(p, 0, 512)
+    b = rb.Model.upload(shape, tens, 0, 512)
+    ids = synth.prompt_ids(2, 9, shape.vocab)
+    la = a.session(32).forward_full(ids)
+    lb = b.session(32).forward_full(ids)
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    assert a.weight_bytes == b.weight_bytes
+
+
+@pytest.mark.slow
+def test_config0_full_size(orc):
+    """Qwen3-1.7B shape, Q8_0, 32-token prompt + 32 greedy."""
+    shape = synth.QWEN3_1_7B_Q8_0
+    orc.set_threads(os.cpu_count() or 8)
+    gm, om = pair(orc, shape, seed=0, max_pos=4096)
+    ids = synth.prompt_ids(0, 32)
+    s = gm.session(128)
+    got_l = s.forward_full(ids)
+    okv = om.kv(128)
+    want_l = om.forward(ids, okv)[0]
+    assert rel_l2(got_l, want_l) <= LOGIT_REL_L2
+    got = s.generate(32)
+    want, wl = om.generate(okv, want_l, 32, want_logits=True)
+    compare_tokens(got, want, wl)
