@@ -155,6 +155,16 @@ RPGC_API int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t col
  * decode kernel, n > 1 the prefill kernel. */
 RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols,
                          const float* X, int64_t n, float* OUT, void* stream);
+/* AttentionFromCache for one query token (src/qwen3.cc:79-117, seq = 1):
+ * q holds n_heads*head_dim floats (already QK-normed and rotated), the caches
+ * are one layer in the KvCache layout [n_kv_heads][max_seq][head_dim]
+ * (src/kv_cache.cc:29-33); keys [0, pos] are read; out receives
+ * n_heads*head_dim floats.  Split-K over the positions: the partial results
+ * live in scratch memory that this call allocates and frees on `stream`
+ * (stream-ordered).  head_dim must be 128 and n_heads/n_kv_heads <= 8. */
+RPGC_API int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_cache,
+                                   int64_t max_seq, int32_t n_heads, int32_t n_kv_heads,
+                                   int32_t head_dim, int64_t pos, float* out, void* stream);
 /* SampleToken / ArgMax on device logits (src/sampler.cc:96-112,
  * src/kernels.h:42-52); *token_dev receives the id. */
 RPGC_API int rpgc_sample(const float* logits, int64_t n, float temperature, int32_t top_k,

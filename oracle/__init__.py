@@ -91,6 +91,8 @@ class Oracle:
         L.orc_forward.argtypes = [C.c_void_p, C.c_void_p, _i32p, C.c_int64, _f32p, C.c_int]
         L.orc_generate.argtypes = [C.c_void_p, C.c_void_p, _f32p, C.POINTER(OrcGenOpts), _i32p,
                                    C.POINTER(C.c_int32), C.c_void_p]
+        L.orc_attention_one.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int32, C.c_int32,
+                                        C.c_int32, C.c_int64, _f32p]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_max_threads.restype = C.c_int
 
@@ -153,6 +155,16 @@ class Oracle:
     def sample_token(self, logits, temperature, top_k, top_p, u) -> int:
         x = _f32(logits)
         return int(self.lib.orc_sample_token(x, x.size, temperature, top_k, top_p, u))
+
+    def attention_one(self, q, kc, vc, pos: int, n_heads: int, n_kv: int) -> np.ndarray:
+        """One query token over one layer's cache [n_kv, max_seq, hd]."""
+        q, kc, vc = _f32(q).reshape(-1), _f32(kc), _f32(vc)
+        hd = q.size // n_heads
+        out = np.empty(q.size, np.float32)
+        if self.lib.orc_attention_one(q, kc.reshape(-1), vc.reshape(-1), kc.shape[-2], n_heads,
+                                      n_kv, hd, pos, out) != 0:
+            raise ValueError("bad attention arguments")
+        return out
 
     def set_threads(self, n: int):
         self.lib.orc_set_threads(n)

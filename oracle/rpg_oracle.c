@@ -708,6 +708,33 @@ static void attention(const orc_config* c, const float* q, int64_t seq, int64_t 
   }
 }
 
+/* src/qwen3.cc:79-117 for one query token at position pos over one layer's
+ * cache [nkv][max_seq][hd]: scores = dot(q, K[s]) * (1/sqrt(hd)) for s <= pos,
+ * softmax (double sum), out = sum_s p_s V[s] accumulated in float. */
+int orc_attention_one(const float* q, const float* kc, const float* vc, int64_t max_seq,
+                      int32_t nh, int32_t nkv, int32_t hd, int64_t pos, float* out) {
+  if (nh <= 0 || nkv <= 0 || nh % nkv || pos < 0 || pos >= max_seq) return -1;
+  const int32_t group = nh / nkv;
+  const float scale = 1.0f / sqrtf((float)hd);
+  float* scores = (float*)malloc((size_t)(pos + 1) * sizeof(float));
+  if (!scores) return -1;
+  for (int32_t h = 0; h < nh; ++h) {
+    const float* kb = kc + (int64_t)(h / group) * max_seq * hd;
+    const float* vb = vc + (int64_t)(h / group) * max_seq * hd;
+    const float* qh = q + (int64_t)h * hd;
+    for (int64_t s = 0; s <= pos; ++s) scores[s] = dot4(qh, kb + s * hd, hd) * scale;
+    softmax_inplace(scores, pos + 1);
+    float* oh = out + (int64_t)h * hd;
+    for (int32_t d = 0; d < hd; ++d) oh[d] = 0.0f;
+    for (int64_t s = 0; s <= pos; ++s) {
+      const float p = scores[s];
+      for (int32_t d = 0; d < hd; ++d) oh[d] += p * vb[s * hd + d];
+    }
+  }
+  free(scores);
+  return 0;
+}
+
 /* src/qwen3.cc:119-206 */
 static void forward_layer(const orc_model* m, const orc_layer* w, int32_t layer, int64_t pos0,
                           scratch_t* s, int64_t seq, orc_kv* kv) {

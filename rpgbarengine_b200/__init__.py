@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
         "rpgc_matvec": ([u32, vp, i64, i64, vp, vp, vp], C.c_int),
         "rpgc_matmul": ([u32, vp, i64, i64, vp, i64, vp, vp], C.c_int),
         "rpgc_sample": ([vp, i64, f32, i32, f32, f32, vp, vp], C.c_int),
+        "rpgc_attention_decode": ([vp, vp, vp, i64, i32, i32, i32, i64, vp, vp], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -300,6 +301,19 @@ def sample_token(logits, temperature: float, top_k: int, top_p: float, u: float,
     _check(lib().rpgc_sample(_ptr(logits), logits.numel(), temperature, top_k, top_p, u, _ptr(tok),
                              _stream(stream)))
     return int(tok.item())
+
+
+def attention_decode(q, k_cache, v_cache, pos: int, n_heads: int, n_kv_heads: int,
+                     out=None, stream=None):
+    """Attention of one query token over cache positions [0, pos]
+    (AttentionFromCache, src/qwen3.cc:79-117).  q: [n_heads*128] float32;
+    caches: [n_kv_heads, max_seq, 128] float32, all on the device."""
+    import torch
+    out = out if out is not None else torch.empty_like(q)
+    max_seq = k_cache.shape[-2]
+    _check(lib().rpgc_attention_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), max_seq, n_heads,
+                                       n_kv_heads, 128, pos, _ptr(out), _stream(stream)))
+    return out
 
 
 row_bytes = _gguf.row_bytes

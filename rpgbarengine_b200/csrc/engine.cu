@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <climits>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -726,6 +727,7 @@ int guard(F&& f) {
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 }  // namespace
+
 }  // namespace rpgc
 
 using namespace rpgc;
@@ -1030,6 +1032,49 @@ int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols, const 
     check(gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT, rows, false,
                       as_stream(stream)),
           "gemm");
+    return RPGC_OK;
+  });
+}
+
+int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_cache,
+                          int64_t max_seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                          int64_t pos, float* out, void* stream) {
+  return guard([&] {
+    if (!q || !k_cache || !v_cache || !out || n_heads <= 0 || n_kv_heads <= 0 || max_seq <= 0)
+      fail(RPGC_E_ARG, "bad attention arguments");
+    if (head_dim != 128 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
+      fail(RPGC_E_ARG, "attention takes head_dim 128 and a GQA group of at most 8");
+    if (pos < 0 || pos >= max_seq || pos > INT32_MAX - 1) fail(RPGC_E_ARG, "pos out of range");
+    cudaStream_t cs = as_stream(stream);
+    const size_t pf = attn_decode_partial_floats(n_kv_heads, n_heads, head_dim, kMaxSplits);
+    float* partial = nullptr;
+    int32_t* counters = nullptr;
+    CK(cudaMallocAsync(reinterpret_cast<void**>(&partial), pf * sizeof(float), cs));
+    const cudaError_t ec = cudaMallocAsync(reinterpret_cast<void**>(&counters),
+                                           n_kv_heads * sizeof(int32_t), cs);
+    if (ec != cudaSuccess) {
+      cudaFreeAsync(partial, cs);
+      CK(ec);
+    }
+    AttnArgs a{};
+    a.q = q;
+    a.kc = k_cache;
+    a.vc = v_cache;
+    a.out = out;
+    a.max_seq = max_seq;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv_heads;
+    a.hd = head_dim;
+    a.pos0 = pos;
+    a.n = 1;
+    a.partial = partial;
+    a.counters = counters;
+    a.max_splits = kMaxSplits;
+    cudaError_t e = cudaMemsetAsync(counters, 0, n_kv_heads * sizeof(int32_t), cs);
+    if (e == cudaSuccess) e = attn_decode_launch(a, cs);
+    cudaFreeAsync(counters, cs);
+    cudaFreeAsync(partial, cs);
+    check(e, "attention decode");
     return RPGC_OK;
   });
 }

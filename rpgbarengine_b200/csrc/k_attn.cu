@@ -61,13 +61,13 @@ constexpr int kMaxGroup = 8;
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   grid_dep_wait();
   const DecodeState* st = a.state;
-  if (!st->active) return;
+  if (st && !st->active) return;
   __shared__ __align__(16) float sm[4][kMaxGroup][132];  // rows padded to 16 B
   __shared__ int s_last;
   const int kh = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.n_heads / a.n_kv, hd = a.hd;
-  const int L = st->pos + 1;
+  const int L = (st ? st->pos : (int)a.pos0) + 1;  // keys [0, pos]
   const int chunk = (L + S - 1) / S;
   const int c0 = split * chunk, c1 = min(L, c0 + chunk);
   const float scale = 1.0f / sqrtf((float)hd);
@@ -297,7 +297,7 @@ size_t attn_decode_partial_floats(int n_kv, int n_heads, int hd, int max_splits)
 }
 
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
-  if (a.hd != 128 || a.n_heads % a.n_kv || a.n_heads / a.n_kv > kMaxGroup || !a.state)
+  if (a.hd != 128 || a.n_heads % a.n_kv || a.n_heads / a.n_kv > kMaxGroup || a.max_splits < 1)
     return cudaErrorInvalidValue;
   dim3 grid((unsigned)a.n_kv, (unsigned)a.max_splits);
   attn_decode_kernel<<<grid, 128, 0, s>>>(a);

@@ -126,3 +126,17 @@ def test_sampler_known_answers():
     assert [s([4, 2, 0], t, 0, 1.0, 0.95) for t in (0.5, 1.0, 2.0)] == [0, 1, 2]
     assert s([1, 9, 3], 0.0, 0, 1.0, 0.123) == 1
     assert s([3, 9, 9, 1], 0.0, 0, 1.0, 0.5) == 1  # ties -> lowest index
+
+
+@pytest.mark.parametrize("n_heads,n_kv,max_seq,pos", [(32, 8, 1152, 0), (32, 8, 1152, 767),
+                                                      (16, 8, 96, 95), (4, 2, 40, 17)])
+def test_attention_decode_matches_oracle(orc, n_heads, n_kv, max_seq, pos):
+    rng = np.random.default_rng(pos + n_heads)
+    q = rng.standard_normal(n_heads * 128).astype(np.float32)
+    kc = rng.standard_normal((n_kv, max_seq, 128)).astype(np.float32)
+    vc = rng.standard_normal((n_kv, max_seq, 128)).astype(np.float32)
+    want = orc.attention_one(q, kc, vc, pos, n_heads, n_kv)
+    got = rb.attention_decode(torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(),
+                              torch.from_numpy(vc).cuda(), pos, n_heads, n_kv).cpu().numpy()
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err
