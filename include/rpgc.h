@@ -165,6 +165,23 @@ RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t col
 RPGC_API int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_cache,
                                    int64_t max_seq, int32_t n_heads, int32_t n_kv_heads,
                                    int32_t head_dim, int64_t pos, float* out, void* stream);
+/* Allocation-free variant of rpgc_attention_decode.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory when they call
+ * (a host whose GPU heap belongs to another runtime, or a latency-critical
+ * path that must not enter the allocator): the split-K scratch is a fixed
+ * 2.03 MiB array inside the library, resident on every GPU that loads it
+ * until the process exits.  Limits: head_dim 128, at most 16 kv heads and 8
+ * query heads per kv head; larger shapes return RPGC_E_ARG.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress), so make
+ * that first call outside any stream capture.  Every call shares the array and
+ * clears its counters first; calls whose kernels overlap on the GPU race on
+ * it and must be serialised by the caller.  Same arguments and results as
+ * rpgc_attention_decode. */
+RPGC_API int rpgc_attention_decode_noalloc(const float* q, const float* k_cache,
+                                           const float* v_cache, int64_t max_seq,
+                                           int32_t n_heads, int32_t n_kv_heads,
+                                           int32_t head_dim, int64_t pos, float* out,
+                                           void* stream);
 /* SampleToken / ArgMax on device logits (src/sampler.cc:96-112,
  * src/kernels.h:42-52); *token_dev receives the id. */
 RPGC_API int rpgc_sample(const float* logits, int64_t n, float temperature, int32_t top_k,

@@ -728,6 +728,9 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 }  // namespace
 
+// Lets other translation units of the library report through rpgc_last_error().
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 }  // namespace rpgc
 
 using namespace rpgc;
