@@ -85,6 +85,7 @@ struct Model {
 };
 
 constexpr int kMaxSplits = 32;
+constexpr int kGemvMaxSplitTiles = 512;
 
 struct Session {
   int32_t model_id = 0;
@@ -97,6 +98,9 @@ struct Session {
   float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
   float *gate = nullptr, *up = nullptr, *logits = nullptr, *partial = nullptr;
   int32_t *ids = nullptr, *counters = nullptr, *gen_out = nullptr, *n_out = nullptr;
+  float* gemv_partial = nullptr;  // split-K scratch of the decode GEMVs
+  int32_t* gemv_counters = nullptr;
+  size_t gemv_partial_n = 0;
   DecodeState* st = nullptr;
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
@@ -368,6 +372,10 @@ int32_t session_create(int32_t model, int32_t max_seq) {
   s->partial = s->alloc<float>(attn_decode_partial_floats(c.n_kv_heads, c.n_heads, c.head_dim, kMaxSplits));
   s->counters = s->alloc<int32_t>(c.n_kv_heads);
   CK(cudaMemsetAsync(s->counters, 0, c.n_kv_heads * sizeof(int32_t), s->stream));
+  s->gemv_partial_n = gemv_partial_floats(kGemvMaxSplitTiles);
+  s->gemv_partial = s->alloc<float>(s->gemv_partial_n);
+  s->gemv_counters = s->alloc<int32_t>(kGemvMaxSplitTiles);
+  CK(cudaMemsetAsync(s->gemv_counters, 0, kGemvMaxSplitTiles * sizeof(int32_t), s->stream));
   s->st = s->alloc<DecodeState>(1);
   CK(cudaMallocHost(&s->st_host, sizeof(DecodeState)));
   std::memset(s->st_host, 0, sizeof(DecodeState));
@@ -398,52 +406,53 @@ GemvSeg seg_of(const DevMatrix& d, float* out, int32_t mode) {
   return s;
 }
 
-// One decode step for the token in st->token (or ids[0]) at st->pos; all
-// kernels honour st->active.  Produces s->logits.
-void launch_step(Session* s, bool token_from_state) {
+// Common GEMV arguments of a decode step (active flag, error flags, split-K
+// scratch of the session).
+GemvArgs step_gemv(Session* s, const float* x, int32_t K, const float* norm_w) {
+  GemvArgs g{};
+  g.K = K;
+  g.x = x;
+  g.norm_w = norm_w;
+  g.eps = s->m->c.rms_eps;
+  g.active = &s->st->active;
+  g.err = &s->st->error;
+  g.partial = s->gemv_partial;
+  g.counters = s->gemv_counters;
+  g.partial_floats = s->gemv_partial_n;
+  g.n_counters = kGemvMaxSplitTiles;
+  return g;
+}
+
+// Transformer layers + lm_head of one decode step for the token whose
+// embedding is already in s->x, at position st->pos.  Every kernel honours
+// st->active and is launched as a programmatic dependent of the previous one,
+// so each GEMV's weight streaming starts while its predecessor finishes.
+void launch_layers_step(Session* s) {
   const Model* m = s->m;
   const rpgc_model_config& c = m->c;
   cudaStream_t cs = s->stream;
-  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, c.hidden,
-                     token_from_state ? nullptr : s->ids, 1, s->x,
-                     token_from_state ? s->st : nullptr, cs),
-        "embed");
   const size_t lc = s->layer_cache_floats();
+  const int32_t qd = c.n_heads * c.head_dim;
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
-    GemvArgs g{};
+    GemvArgs g = step_gemv(s, s->x, c.hidden, L.attn_norm);
     g.seg[0] = seg_of(L.q, s->q, kStore);
     g.seg[1] = seg_of(L.k, s->k, kStore);
     g.seg[2] = seg_of(L.v, s->v, kStore);
     g.nseg = 3;
-    g.K = c.hidden;
-    g.x = s->x;
-    g.norm_w = L.attn_norm;
-    g.eps = c.rms_eps;
-    g.active = &s->st->active;
-    g.err = &s->st->error;
-    check(gemv_launch(g, cs, false), "gemv qkv");
-    QkvArgs qa{};
-    qa.q = s->q;
-    qa.k = s->k;
-    qa.v = s->v;
-    qa.q_norm = L.q_norm;
-    qa.k_norm = L.k_norm;
-    qa.rope = m->rope;
-    qa.kc = s->kc + l * lc;
-    qa.vc = s->vc + l * lc;
-    qa.max_seq = s->max_seq;
-    qa.n_heads = c.n_heads;
-    qa.n_kv = c.n_kv_heads;
-    qa.hd = c.head_dim;
-    qa.eps = c.rms_eps;
-    qa.n = 1;
-    qa.state = s->st;
-    check(qkv_rope_launch(qa, cs), "qkv rope");
+    check(gemv_launch(g, cs, true), "gemv qkv");
     AttnArgs aa{};
     aa.q = s->q;
     aa.kc = s->kc + l * lc;
     aa.vc = s->vc + l * lc;
+    aa.kc_w = s->kc + l * lc;
+    aa.vc_w = s->vc + l * lc;
+    aa.k_new = s->k;
+    aa.v_new = s->v;
+    aa.q_norm = L.q_norm;
+    aa.k_norm = L.k_norm;
+    aa.rope = m->rope;
+    aa.eps = c.rms_eps;
     aa.out = s->attn;
     aa.max_seq = s->max_seq;
     aa.n_heads = c.n_heads;
@@ -454,45 +463,35 @@ void launch_step(Session* s, bool token_from_state) {
     aa.partial = s->partial;
     aa.counters = s->counters;
     aa.max_splits = kMaxSplits;
+    aa.pdl = true;
     check(attn_decode_launch(aa, cs), "attn decode");
-    GemvArgs go{};
+    GemvArgs go = step_gemv(s, s->attn, qd, nullptr);
     go.seg[0] = seg_of(L.o, s->x, kAdd);
     go.nseg = 1;
-    go.K = c.n_heads * c.head_dim;
-    go.x = s->attn;
-    go.active = &s->st->active;
-    go.err = &s->st->error;
-    check(gemv_launch(go, cs, false), "gemv o");
-    GemvArgs gf{};
+    check(gemv_launch(go, cs, true), "gemv o");
+    GemvArgs gf = step_gemv(s, s->x, c.hidden, L.ffn_norm);
     gf.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
     gf.seg[1] = seg_of(L.up, s->gate, kStore);
     gf.nseg = 2;
-    gf.K = c.hidden;
-    gf.x = s->x;
-    gf.norm_w = L.ffn_norm;
-    gf.eps = c.rms_eps;
-    gf.active = &s->st->active;
-    gf.err = &s->st->error;
-    check(gemv_launch(gf, cs, false), "gemv gate/up");
-    GemvArgs gd{};
+    check(gemv_launch(gf, cs, true), "gemv gate/up");
+    GemvArgs gd = step_gemv(s, s->gate, c.intermediate, nullptr);
     gd.seg[0] = seg_of(L.down, s->x, kAdd);
     gd.nseg = 1;
-    gd.K = c.intermediate;
-    gd.x = s->gate;
-    gd.active = &s->st->active;
-    gd.err = &s->st->error;
-    check(gemv_launch(gd, cs, false), "gemv down");
+    check(gemv_launch(gd, cs, true), "gemv down");
   }
-  GemvArgs gl{};
+  GemvArgs gl = step_gemv(s, s->x, c.hidden, m->out_norm);
   gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
   gl.nseg = 1;
-  gl.K = c.hidden;
-  gl.x = s->x;
-  gl.norm_w = m->out_norm;
-  gl.eps = c.rms_eps;
-  gl.active = &s->st->active;
-  gl.err = &s->st->error;
-  check(gemv_launch(gl, cs, false), "gemv lm_head");
+  check(gemv_launch(gl, cs, true), "gemv lm_head");
+}
+
+// One decode step for ids[0] at st->pos (the host set the state).
+void launch_step(Session* s) {
+  const Model* m = s->m;
+  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, m->c.hidden, s->ids, 1, s->x,
+                     nullptr, s->stream),
+        "embed");
+  launch_layers_step(s);
 }
 
 // Prefill of nc tokens (ids already in s->ids) at positions [pos0, pos0+nc).
@@ -586,7 +585,7 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
                          s->stream));
       if (nc == 1 && !all) {
         set_state_for_forward(s);
-        launch_step(s, false);
+        launch_step(s);
       } else {
         launch_prefill(s, nc, s->len);
         if (all) {
@@ -627,15 +626,21 @@ void capture_step_graph(Session* s) {
   cudaGraph_t g = nullptr;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
   try {
+    const Model* m = s->m;
     SampleArgs sa{};
     sa.logits = s->logits;
-    sa.n = s->m->c.vocab;
+    sa.n = m->c.vocab;
     sa.state = s->st;
     sa.out_ids = s->gen_out;
     sa.n_out = s->n_out;
+    sa.embd = m->embd.w;
+    sa.embd_row_bytes = m->embd.row_bytes;
+    sa.embd_type = m->embd.type;
+    sa.hidden = m->c.hidden;
+    sa.x = s->x;
+    sa.pdl = true;
     check(sample_launch(sa, s->stream), "sample");
-    launch_step(s, true);
-    check(advance_launch(s->st, s->stream), "advance");
+    launch_layers_step(s);
   } catch (...) {
     cudaStreamEndCapture(s->stream, &g);
     if (g) cudaGraphDestroy(g);
@@ -663,6 +668,7 @@ int64_t generate(Session* s, const rpgc_gen_opts& o, bool sync_host) {
   DecodeState h;
   std::memset(&h, 0, sizeof(h));
   h.pos = (int32_t)s->len;
+  h.start_pos = (int32_t)s->len;
   h.active = 1;
   h.max_tokens = o.max_tokens;
   h.n_stop = o.n_stop;

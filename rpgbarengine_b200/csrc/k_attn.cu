@@ -57,48 +57,111 @@ __global__ void qkv_rope_kernel(const QkvArgs a) {
 // ---------------------------------------------------------------- decode
 // grid (n_kv, splits), 128 threads.  hd == 128 (4 dims per lane), group <= 8.
 constexpr int kMaxGroup = 8;
+constexpr int kPre = 4;  // positions per warp whose K/V are loaded up front
+
+// QK-norm + RoPE of one 128-wide head held as a float4 per lane (dims
+// 4*lane..4*lane+3): RMSNorm with a double sum of squares, then the half-split
+// rotation with the reference's separate roundings.  `mine` is this lane's
+// float4; the partner dims (i +- 64) come from lane^16.
+__device__ __forceinline__ float4 norm_rope_head(float4 v, const float* w, const float* cs,
+                                                 float eps, int lane) {
+  double ss = (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  ss = warp_sum(ss);
+  const float scale = (float)(1.0 / sqrt(ss / 128.0 + (double)eps));
+  const float4 g = *reinterpret_cast<const float4*>(w + 4 * lane);
+  float y[4] = {v.x * scale * g.x, v.y * scale * g.y, v.z * scale * g.z, v.w * scale * g.w};
+  float o[4];
+  const bool lo = lane < 16;  // dims < 64
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[k], 16);
+    const int i = (4 * lane + k) & 63;
+    const float c = cs[i], sn = cs[64 + i];
+    o[k] = lo ? __fsub_rn(__fmul_rn(y[k], c), __fmul_rn(partner, sn))
+              : __fadd_rn(__fmul_rn(y[k], c), __fmul_rn(partner, sn));
+  }
+  return make_float4(o[0], o[1], o[2], o[3]);
+}
 
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   grid_dep_wait();
   const DecodeState* st = a.state;
   if (st && !st->active) return;
   __shared__ __align__(16) float sm[4][kMaxGroup][132];  // rows padded to 16 B
+  __shared__ __align__(16) float4 knew_s[32], vnew_s[32];
+  __shared__ float fsc[kMaxGroup][32];
   __shared__ int s_last;
   const int kh = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.n_heads / a.n_kv, hd = a.hd;
-  const int L = (st ? st->pos : (int)a.pos0) + 1;  // keys [0, pos]
+  const int pos = st ? st->pos : (int)a.pos0;
+  const int L = pos + 1;  // keys [0, pos]
   const int chunk = (L + S - 1) / S;
   const int c0 = split * chunk, c1 = min(L, c0 + chunk);
   const float scale = 1.0f / sqrtf((float)hd);
   const float* kb = a.kc + (int64_t)kh * a.max_seq * hd;
   const float* vb = a.vc + (int64_t)kh * a.max_seq * hd;
+  const bool fused = a.q_norm != nullptr;
+  const bool has_new = fused && c0 <= pos && pos < c1;  // this split owns the new token
+  const float* cs = fused ? a.rope + (int64_t)pos * hd : nullptr;
 
   float4 qv[kMaxGroup], ov[kMaxGroup];
   float m[kMaxGroup], l[kMaxGroup];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
-    if (g < G) qv[g] = *reinterpret_cast<const float4*>(a.q + (kh * G + g) * hd + 4 * lane);
+    if (g < G) {
+      qv[g] = *reinterpret_cast<const float4*>(a.q + (kh * G + g) * hd + 4 * lane);
+      if (fused) qv[g] = norm_rope_head(qv[g], a.q_norm, cs, a.eps, lane);
+    }
     ov[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     m[g] = kNegBig;
     l[g] = 0.0f;
   }
-  for (int p = c0 + warp; p < c1; p += 4) {
-    const float4 kv = *reinterpret_cast<const float4*>(kb + (int64_t)p * hd + 4 * lane);
-    const float4 vv = *reinterpret_cast<const float4*>(vb + (int64_t)p * hd + 4 * lane);
+  if (has_new && warp == 0) {
+    // the new token's k/v: normalise + rotate k, write both into the cache
+    float4 k4 = *reinterpret_cast<const float4*>(a.k_new + kh * hd + 4 * lane);
+    k4 = norm_rope_head(k4, a.k_norm, cs, a.eps, lane);
+    const float4 v4 = *reinterpret_cast<const float4*>(a.v_new + kh * hd + 4 * lane);
+    const int64_t off = ((int64_t)kh * a.max_seq + pos) * hd + 4 * lane;
+    *reinterpret_cast<float4*>(a.kc_w + off) = k4;
+    *reinterpret_cast<float4*>(a.vc_w + off) = v4;
+    knew_s[lane] = k4;
+    vnew_s[lane] = v4;
+  }
+  __syncthreads();
+  // positions of this warp: c0 + warp + 4*i; K/V of up to kPre loaded at once
+  for (int p0 = c0 + warp; p0 < c1; p0 += 4 * kPre) {
+    float4 kr[kPre], vr[kPre];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g >= G) break;
-      float s = qv[g].x * kv.x + qv[g].y * kv.y + qv[g].z * kv.z + qv[g].w * kv.w;
-      s = warp_sum(s) * scale;
-      const float mn = fmaxf(m[g], s);
-      const float corr = expf(m[g] - mn), pe = expf(s - mn);
-      l[g] = l[g] * corr + pe;
-      ov[g].x = ov[g].x * corr + pe * vv.x;
-      ov[g].y = ov[g].y * corr + pe * vv.y;
-      ov[g].z = ov[g].z * corr + pe * vv.z;
-      ov[g].w = ov[g].w * corr + pe * vv.w;
-      m[g] = mn;
+    for (int i = 0; i < kPre; ++i) {
+      const int p = p0 + 4 * i;
+      if (p < c1) {
+        if (has_new && p == pos) {
+          kr[i] = knew_s[lane];
+          vr[i] = vnew_s[lane];
+        } else {
+          kr[i] = *reinterpret_cast<const float4*>(kb + (int64_t)p * hd + 4 * lane);
+          vr[i] = *reinterpret_cast<const float4*>(vb + (int64_t)p * hd + 4 * lane);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+      if (p0 + 4 * i >= c1) break;
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) {
+        if (g >= G) break;
+        float s = qv[g].x * kr[i].x + qv[g].y * kr[i].y + qv[g].z * kr[i].z + qv[g].w * kr[i].w;
+        s = warp_sum(s) * scale;
+        const float mn = fmaxf(m[g], s);
+        const float corr = expf(m[g] - mn), pe = expf(s - mn);
+        l[g] = l[g] * corr + pe;
+        ov[g].x = ov[g].x * corr + pe * vr[i].x;
+        ov[g].y = ov[g].y * corr + pe * vr[i].y;
+        ov[g].z = ov[g].z * corr + pe * vr[i].z;
+        ov[g].w = ov[g].w * corr + pe * vr[i].w;
+        m[g] = mn;
+      }
     }
   }
   // merge the 4 warps of this split
@@ -135,20 +198,22 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // last split of this kv head: combine all splits
+  // last split of this kv head: combine all splits (S <= 32: one lane per split)
   const float* pk = a.partial + (int64_t)kh * S * G * 130;
+  for (int g = warp; g < G; g += 4) {
+    const float ms = lane < S ? __ldcg(pk + (lane * G + g) * 130 + 128) : kNegBig;
+    const float ls = lane < S ? __ldcg(pk + (lane * G + g) * 130 + 129) : 0.0f;
+    const float M = warp_max(ms);
+    const float f = lane < S ? expf(ms - M) : 0.0f;
+    const float Lsum = warp_sum(ls * f);
+    fsc[g][lane] = f / Lsum;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * 128; idx += 128) {
     const int g = idx >> 7, d = idx & 127;
-    float M = kNegBig;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(pk + (s * G + g) * 130 + 128));
-    float O = 0.0f, Lsum = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      const float* pp = pk + (s * G + g) * 130;
-      const float f = expf(__ldcg(pp + 128) - M);
-      O += __ldcg(pp + d) * f;
-      Lsum += __ldcg(pp + 129) * f;
-    }
-    a.out[(kh * G + g) * hd + d] = O / Lsum;
+    float O = 0.0f;
+    for (int s = 0; s < S; ++s) O += __ldcg(pk + (s * G + g) * 130 + d) * fsc[g][s];
+    a.out[(kh * G + g) * hd + d] = O;
   }
   if (threadIdx.x == 0) a.counters[kh] = 0;
 }
@@ -297,11 +362,21 @@ size_t attn_decode_partial_floats(int n_kv, int n_heads, int hd, int max_splits)
 }
 
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
-  if (a.hd != 128 || a.n_heads % a.n_kv || a.n_heads / a.n_kv > kMaxGroup || a.max_splits < 1)
+  if (a.hd != 128 || a.n_heads % a.n_kv || a.n_heads / a.n_kv > kMaxGroup || a.max_splits < 1 ||
+      a.max_splits > 32)
     return cudaErrorInvalidValue;
-  dim3 grid((unsigned)a.n_kv, (unsigned)a.max_splits);
-  attn_decode_kernel<<<grid, 128, 0, s>>>(a);
-  return cudaGetLastError();
+  if (a.q_norm && (!a.k_norm || !a.rope || !a.k_new || !a.v_new || !a.kc_w || !a.vc_w))
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)a.max_splits);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
 }
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {

@@ -218,21 +218,42 @@ __device__ int sample_probs(Smem& S, const float* logits, int n, float T, int to
       __syncthreads();
     }
     V.kth = unfkey(prefix);
-    // compact survivors in index order when they fit
-    const int C = (n + NT - 1) / NT, j0 = tid * C, j1 = min(n, j0 + C);
+    // compact survivors in index order when they fit: warp w owns a
+    // contiguous index range, read 32 consecutive logits per round
+    // (coalesced); ballots give each survivor its slot.
+    const int w = tid >> 5, lane = tid & 31;
+    const int R = ((n + 32 * 32 - 1) / (32 * 32)) * 32;  // range length per warp
+    const int w0 = w * R, w1 = min(n, w0 + R);
     int mine = 0;
-    for (int j = j0; j < j1; ++j) mine += (v_s(V, j) != -INFINITY);
-    int total;
-    const int base = block_excl_scan<int>(S.ired, mine, &total);
+    for (int j = w0 + lane; j - lane < w1; j += 32) {
+      const bool keep = j < w1 && v_s(V, j) != -INFINITY;
+      mine += __popc(__ballot_sync(0xffffffffu, keep));
+    }
+    if (lane == 0) S.ired[w] = mine;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int ww = 0; ww < 32; ++ww) {
+        const int c = S.ired[ww];
+        S.ired[ww] = acc;
+        acc += c;
+      }
+      S.bcast_i[3] = acc;
+    }
+    __syncthreads();
+    const int total = S.bcast_i[3];
     if (total <= kCap) {
-      int o = base;
-      for (int j = j0; j < j1; ++j) {
-        const float s = v_s(V, j);
-        if (s != -INFINITY) {
-          S.cidx[o] = j;
-          S.cval[o] = s;
-          ++o;
+      int o = S.ired[w];
+      for (int j = w0 + lane; j - lane < w1; j += 32) {
+        const float sv = j < w1 ? v_s(V, j) : -INFINITY;
+        const bool keep = sv != -INFINITY;
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+          const int at = o + __popc(bal & ((1u << lane) - 1u));
+          S.cidx[at] = j;
+          S.cval[at] = sv;
         }
+        o += __popc(bal);
       }
       __syncthreads();
       V.compact = true;
@@ -420,6 +441,7 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
   DecodeState* st = a.state;
   float T = a.temperature, top_p = a.top_p, u = a.u;
   int top_k = a.top_k;
+  int pos = 0;
   if (st) {
     const int done = st->done;
     __syncthreads();
@@ -430,17 +452,17 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
     T = st->temperature;
     top_k = st->top_k;
     top_p = st->top_p;
-    u = counter_uniform(st->seed, (uint64_t)st->pos);
+    pos = st->start_pos + st->n_gen;  // where the picked token will be written
+    u = counter_uniform(st->seed, (uint64_t)pos);
   }
   const int n = (int)a.n;
   int tok;
-  if (!(T > 0.0f)) {  // greedy: first index of the maximum
-    const int C = (n + NT - 1) / NT, j0 = threadIdx.x * C, j1 = min(n, j0 + C);
+  if (!(T > 0.0f)) {  // greedy: first index of the maximum (coalesced sweep)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int j = j0; j < j1; ++j) {
+    for (int j = threadIdx.x; j < n; j += NT) {
       const float v = a.logits[j];
-      if (v > bv) {
+      if (v > bv) {  // a thread's indices increase, so strict > keeps the first
         bv = v;
         bi = j;
       }
@@ -450,8 +472,13 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
   } else {
     tok = sample_probs(S, a.logits, n, T, top_k, top_p, u);
   }
+  if (st && a.x) {  // the decode step continues with this token's embedding row
+    const uint8_t* row = a.embd + (int64_t)tok * a.embd_row_bytes;
+    for (int e = threadIdx.x; e < a.hidden; e += NT) a.x[e] = deq_elem(a.embd_type, row, e);
+  }
   if (threadIdx.x == 0) {
     if (st) {
+      st->pos = pos;
       st->token = tok;
       a.out_ids[st->n_gen] = tok;
       st->n_gen += 1;
@@ -479,8 +506,17 @@ cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
     configured = dev;
   }
   if (a.n <= 0 || a.n > 0x7ffffff0) return cudaErrorInvalidValue;
-  sample_kernel<<<1, NT, sizeof(Smem), s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, sample_kernel, a);
 }
 
 }  // namespace rpgc

@@ -10,6 +10,7 @@ namespace rpgc {
 // serves every step (the position and the stop status are read in-kernel).
 struct DecodeState {
   int32_t pos;        // KV length = position of the token being forwarded
+  int32_t start_pos;  // KV length when generation started
   int32_t active;     // 0: this step does nothing (generation finished)
   int32_t done;       // set once a stop id / max_tokens was reached
   int32_t n_gen;      // tokens produced so far
@@ -22,7 +23,6 @@ struct DecodeState {
   uint64_t seed;
   int32_t stop_ids[16];
   int32_t error;      // kernel error flags (bounded waits)
-  int32_t pad;
 };
 
 // ------------------------------------------------------------------ GEMV
@@ -46,11 +46,16 @@ struct GemvArgs {
   float eps;
   const int32_t* active;  // optional: skip when *active == 0
   int32_t* err;           // optional error flags
+  float* partial;         // optional split-K scratch (null: no split)
+  int32_t* counters;      // split-K tile counters, zero between launches
+  size_t partial_floats;
+  int64_t n_counters;
 };
 
 // Launch y = W x over up to 4 segments sharing x (decode, batch 1).
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
 size_t gemv_smem_bytes(int K, bool need_f32);
+size_t gemv_partial_floats(int64_t max_tiles);
 
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
@@ -91,7 +96,7 @@ struct QkvArgs {
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s);
 
 struct AttnArgs {
-  const float* q;      // [n][n_heads*hd]
+  const float* q;      // [n][n_heads*hd] (decode with q_norm: raw projections)
   const float* kc;     // layer cache [n_kv][max_seq][hd]
   const float* vc;
   float* out;          // [n][n_heads*hd]
@@ -102,6 +107,17 @@ struct AttnArgs {
   float* partial;      // decode split-K scratch
   int32_t* counters;   // decode: one per kv head, zero between launches
   int32_t max_splits;
+  // decode only, optional: fuse QK-norm + RoPE + K/V cache write of the new
+  // token (q/k/v raw projections, k_new/v_new the token's k and v rows)
+  const float* q_norm;
+  const float* k_norm;
+  const float* rope;
+  const float* k_new;
+  const float* v_new;
+  float* kc_w;         // writable views of the caches
+  float* vc_w;
+  float eps;
+  bool pdl;
 };
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s);
@@ -122,6 +138,13 @@ struct SampleArgs {
   DecodeState* state;
   int32_t* out_ids;
   int32_t* n_out;
+  // decode loop: also gather the picked token's embedding row into x
+  const uint8_t* embd;
+  int64_t embd_row_bytes;
+  uint32_t embd_type;
+  int32_t hidden;
+  float* x;
+  bool pdl;
 };
 cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s);
 // state->pos += 1 when active (end of a decode step).

@@ -60,7 +60,7 @@ def test_single_token_steps_match_prefill(orc):
         got = s.forward_full(ids[t:t + 1])
         want = om.forward(ids[t:t + 1], okv)[0]
         assert rel_l2(got, want) <= LOGIT_REL_L2
-        assert rel_l2(got, want) <= 1e-5
+        assert rel_l2(got, want) <= 1e-4
 
 
 @pytest.mark.parametrize("T,k,p,seed", [(0.0, 0, 1.0, 0), (0.7, 20, 0.8, 99), (1.0, 0, 0.95, 7),
