@@ -147,7 +147,9 @@ RPGC_API int rpgc_session_sync(int32_t session);
 RPGC_API int rpgc_dequantize_rows(uint32_t type, const void* w, int64_t rows, int64_t cols,
                                   float* out, void* stream);
 /* One fused-dequant matrix-vector product: y[r] = dot(x, W[r])
- * (QuantMatrix::MatVec, src/model.cc:23-30; DotRowQuant, src/matmul.h:35). */
+ * (QuantMatrix::MatVec, src/model.cc:23-30; DotRowQuant, src/matmul.h:35).
+ * w must be 16-byte aligned and readable up to the next 16-byte boundary
+ * past its last byte; cols must be a multiple of 64. */
 RPGC_API int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t cols,
                          const float* x, float* y, void* stream);
 /* OUT[t*rows + r] = dot(X[t], W[r]) (QuantMatrix::MatMulBatch,

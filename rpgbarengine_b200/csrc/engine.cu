@@ -85,7 +85,6 @@ struct Model {
 };
 
 constexpr int kMaxSplits = 32;
-constexpr int kGemvMaxSplitTiles = 512;
 
 struct Session {
   int32_t model_id = 0;
@@ -98,9 +97,6 @@ struct Session {
   float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
   float *gate = nullptr, *up = nullptr, *logits = nullptr, *partial = nullptr;
   int32_t *ids = nullptr, *counters = nullptr, *gen_out = nullptr, *n_out = nullptr;
-  float* gemv_partial = nullptr;  // split-K scratch of the decode GEMVs
-  int32_t* gemv_counters = nullptr;
-  size_t gemv_partial_n = 0;
   DecodeState* st = nullptr;
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
@@ -372,10 +368,6 @@ int32_t session_create(int32_t model, int32_t max_seq) {
   s->partial = s->alloc<float>(attn_decode_partial_floats(c.n_kv_heads, c.n_heads, c.head_dim, kMaxSplits));
   s->counters = s->alloc<int32_t>(c.n_kv_heads);
   CK(cudaMemsetAsync(s->counters, 0, c.n_kv_heads * sizeof(int32_t), s->stream));
-  s->gemv_partial_n = gemv_partial_floats(kGemvMaxSplitTiles);
-  s->gemv_partial = s->alloc<float>(s->gemv_partial_n);
-  s->gemv_counters = s->alloc<int32_t>(kGemvMaxSplitTiles);
-  CK(cudaMemsetAsync(s->gemv_counters, 0, kGemvMaxSplitTiles * sizeof(int32_t), s->stream));
   s->st = s->alloc<DecodeState>(1);
   CK(cudaMallocHost(&s->st_host, sizeof(DecodeState)));
   std::memset(s->st_host, 0, sizeof(DecodeState));
@@ -406,8 +398,8 @@ GemvSeg seg_of(const DevMatrix& d, float* out, int32_t mode) {
   return s;
 }
 
-// Common GEMV arguments of a decode step (active flag, error flags, split-K
-// scratch of the session).
+// Common GEMV arguments of a decode step (the session's active flag and
+// error flags).
 GemvArgs step_gemv(Session* s, const float* x, int32_t K, const float* norm_w) {
   GemvArgs g{};
   g.K = K;
@@ -416,10 +408,6 @@ GemvArgs step_gemv(Session* s, const float* x, int32_t K, const float* norm_w) {
   g.eps = s->m->c.rms_eps;
   g.active = &s->st->active;
   g.err = &s->st->error;
-  g.partial = s->gemv_partial;
-  g.counters = s->gemv_counters;
-  g.partial_floats = s->gemv_partial_n;
-  g.n_counters = kGemvMaxSplitTiles;
   return g;
 }
 

@@ -3,34 +3,39 @@
 // Replaces the reference's fused dequant dot-row (src/matmul_avx2.cc:95-289,
 // dispatched per row by QuantMatrix::MatVec/MatMulBatch, src/model.cc:23-69).
 //
-// Data path.  Weights stay in their ggml block layout in HBM.  One CTA per SM
-// (<= 112 KB of shared memory, so the next kernel's CTA fits beside it).  A
-// producer warp streams row segments into a 4-stage shared-memory ring with
-// bulk async copies (cp.async.bulk + mbarrier, evict-first L2 policy).  It
-// does not wait for the previous kernel: weights do not depend on it, and with
-// programmatic dependent launch the copies overlap the previous kernel's
-// tail.  Consumer warps own one weight row per lane and split each row's
-// blocks between warps, so activation reads are warp-uniform broadcasts.
-// Weight reads are bank-conflict free: Q4_K slots are 16-byte aligned with an
-// odd 16-byte pitch (128-bit loads); Q6_K rows whose length is 4 or 12 mod 16
-// are assigned to lanes so that the 32 lanes of a warp start in 32 distinct
-// banks (32-bit loads).
+// Work split.  A row of K elements is cut into U = K/64 units of 64
+// consecutive elements (a Q4_K group, a quarter of a Q6_K block, two Q8_0
+// blocks).  Consumer thread t of a CTA owns unit u = t % U for the whole
+// launch and is row slot s = t / U; S = floor(320 / U) slots work on S rows
+// at a time, two rows per step so that one read of the activation serves two
+// weight rows (a 128-bit shared load costs 3-4.5 SM cycles whatever its
+// pattern, so activation reads, not weight reads, bound the inner loop).
+// Each thread's partial sum of (row, unit) goes to shared memory; rows are
+// summed over their U units in a fixed order once a chunk of stages is
+// complete, so results are deterministic.
 //
-// Work items are (32-row tile, K range) pairs.  Matrices with few tiles are
-// split along K across CTAs; the CTA that completes a tile last (atomic
-// counter) adds the partial sums in a fixed order, so results are
-// deterministic.
+// Data path.  Every CTA owns a contiguous, balanced range of rows of each
+// segment (no split along K).  Rows are contiguous in HBM, so one stage of
+// the ring is ONE bulk async copy of m whole rows (16-24 KB: copies of that
+// size stream at ~6 TB/s, 500-byte ones at ~2 TB/s).  A dedicated producer
+// warp issues them with an evict-first L2 policy (issuing a bulk copy blocks
+// the issuing thread for a time proportional to its size, so no consumer
+// does it).  The first stages are issued before griddepcontrol.wait:
+// weights do not depend on the previous kernel, so with programmatic
+// dependent launch they stream in during its tail.  A CTA uses at most 112
+// KB of shared memory and 2 x 352 x 88 registers fit an SM, so the next
+// kernel's CTA can sit beside it.
 //
-// Arithmetic.  The fp32 activation is turned, once per CTA, into a 24-bit
-// fixed-point copy per group of 32 elements (power-of-two scale 2^(e-23),
-// |A| < 2^23) held as three byte limbs A = 65536*A2 + 256*A1 + A0.  A block
-// dot product is then 3 dp4a per 4 weights with exact int32 partial sums, and
-// the ggml scales are applied per sub-block in fp32:
-//   Q4_K  sum = s_g * (d*sc * S - dmin*m * sum(A))
-//   Q6_K  sum = s_g * (d*sc) * (S - 32 * sum(A))       (q stored as 0..63)
-//   Q8_0  sum = s_g * d * S
+// Arithmetic.  Activation groups of 32 get a power-of-two scale 2^(e-149)
+// and a 24-bit integer copy held as three byte limbs A = 65536*A2 + 256*A1 +
+// A0.  A block dot product is 3 dp4a per 4 weights with exact int32 partial
+// sums, then the ggml scales are applied per sub-block in fp32:
+//   Q4_K  s_g * (d*sc * S - dmin*m * sum(A))
+//   Q6_K  s_g * d*sc * (S - 32 * sum(A))          (q stored as 0..63)
+//   Q8_0  s_g * d * S
 // The fixed-point rounding is 2^-24 of the group maximum, far inside the
 // per-row gate max|d| / sum|a*w| <= 1e-5.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -39,533 +44,624 @@
 namespace rpgc {
 namespace {
 
-constexpr int kNW = 8;             // consumer warps
-constexpr int kThreads = (kNW + 1) * 32;
-constexpr int kRPT = 32;           // rows per tile (one per lane)
-constexpr int kMaxStages = 4;
-constexpr int kSmemLimit = 112 * 1024;  // leaves room for the next kernel's CTA
-constexpr int kStageMax = 20 * 1024;
-constexpr int kMaxKParts = 8;
+constexpr int kCWarps = 10;                  // consumer warps
+constexpr int kConsumers = kCWarps * 32;     // consumer threads
+constexpr int kThreads = kConsumers + 32;    // + one producer warp
+constexpr int kMaxStages = 6;
+constexpr int kSmemLimit = 112 * 1024;       // leaves room for the next kernel's CTA
+constexpr int kStageTarget = 24 * 1024;
+constexpr int kRedBudget = 16 * 1024;        // partial sums of one reduction chunk
+constexpr int kMaxWordsPerThread = 10;       // K <= 4 * 320 * 10
 
-struct ActView {
-  const uint32_t* l2;  // signed high limb words (4 elements each)
-  const uint32_t* l1;
-  const uint32_t* l0;
-  const float* gs;     // per 32-group scale 2^(e-23)
-  const int* sa32;     // per 32-group sum of A
-  const int* sa16;     // per 16-group sum of A
-  const float* xf;     // fp32 copy (F32 weights only)
-};
-
-struct SegInfo {
-  int64_t item_begin;  // first global work item of this segment
-  int64_t tile_begin;  // first global tile (counter index)
-  int32_t tiles;       // 0 for the up half of a SwiGLU pair
-  int32_t ks;          // K parts per tile
-  int32_t be, bb;      // block elements / bytes
-  int32_t nb;          // blocks per row
-  int32_t cb;          // blocks per chunk
-  int32_t nch;         // chunks per row
-  int32_t slot;        // bytes per row slot in a stage
-  int32_t perm;        // 1: permuted lane->row map (rows 4 or 12 mod 16 bytes)
+struct LSeg {      // logical segment: one matrix, or a SwiGLU (gate, up) pair
+  int64_t rows;
+  int32_t first;   // index into GemvArgs::seg
+  int32_t pair;    // 1: seg[first] is the gate, seg[first + 1] the up matrix
+  int32_t m;       // rows per stage (multiple of S)
+  int32_t cs;      // stages per reduction chunk
 };
 
 struct Plan {
-  SegInfo si[4];
-  int64_t n_items;
+  LSeg ls[4];
+  int32_t nls;
+  int32_t U, S;          // units per row, row slots
+  int32_t stages;        // ring depth
+  int32_t stage_bytes;   // bytes per ring slot
+  int32_t half_bytes;    // offset of the up matrix inside a slot
+  int32_t red_floats;    // floats of the partial-sum buffer
   int32_t need_f32;
-  int32_t split;       // some segment is split along K
-  int32_t stages;      // ring depth (<= kMaxStages)
 };
+
+// ---------------------------------------------------------------- activation
+// Fixed-point activation in shared memory, laid out so that the consumer
+// threads of a warp (consecutive units) read consecutive 16-byte words:
+// limb[(L * 4 + i) * U + u] holds words 4i..4i+3 of limb L (0: A2, 1: A1,
+// 2: A0) of unit u, word j covering elements 4j..4j+3 of the unit.
+struct ActS {
+  const uint4* limb;
+  const float* g;    // [2][U] group scales 2^(e-149) (0 for a flushed group)
+  const float* gm;   // [2][U] Q4_K: g * sum(A) of each 32-element group
+  const float* g6;   // [4][U] Q6_K: 32 * g * sum(A) of each 16-element sub-block
+  const float* xf;   // [K] fp32 copy (F32 weights only)
+  int U;
+};
+
+// Activation words 8h..8h+7 of the three limbs of unit u.
+__device__ __forceinline__ void act_half(const ActS& A, int u, int h, uint32_t* a2, uint32_t* a1,
+                                         uint32_t* a0) {
+#pragma unroll
+  for (int L = 0; L < 3; ++L) {
+    const uint4 x = A.limb[(L * 4 + 2 * h) * A.U + u];
+    const uint4 y = A.limb[(L * 4 + 2 * h + 1) * A.U + u];
+    uint32_t* d = L == 0 ? a2 : (L == 1 ? a1 : a0);
+    d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+    d[4] = y.x; d[5] = y.y; d[6] = y.z; d[7] = y.w;
+  }
+}
 
 __device__ __forceinline__ float comb(int s2, int s1, int s0) {
-  return (float)s2 * 65536.0f + (float)s1 * 256.0f + (float)s0;
+  return (float)(s2 * 256 + s1) * 256.0f + (float)s0;
 }
 
-// ---- per-unit dot products (one unit = one lane's row piece) -------------
-
-// Byte k (0..11) of the Q4_K scale field held in three registers.
-__device__ __forceinline__ uint32_t sbyte(uint32_t w0, uint32_t w1, uint32_t w2, int k) {
-  const uint32_t w = k < 4 ? w0 : (k < 8 ? w1 : w2);
-  return (w >> (8 * (k & 3))) & 0xFFu;
+// fp16 in the low half of w -> fp32 (exact conversion).
+__device__ __forceinline__ float half_lo(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
 }
-// get_scale_min_k4 on register-held scale bytes.
-__device__ __forceinline__ void scale_min_regs(int j, uint32_t w0, uint32_t w1, uint32_t w2,
-                                               uint32_t* sc, uint32_t* m) {
-  if (j < 4) {
-    *sc = sbyte(w0, w1, w2, j) & 63u;
-    *m = sbyte(w0, w1, w2, j + 4) & 63u;
-  } else {
-    *sc = (sbyte(w0, w1, w2, j + 4) & 0x0Fu) | ((sbyte(w0, w1, w2, j - 4) >> 6) << 4);
-    *m = (sbyte(w0, w1, w2, j + 4) >> 4) | ((sbyte(w0, w1, w2, j) >> 6) << 4);
+
+// N words starting at a 2-byte-aligned shared address, shifted right by
+// `extra` more bits (0 or 4): N + 1 aligned loads and N funnel shifts.
+template <int N>
+__device__ __forceinline__ void ldw(const uint8_t* p, uint32_t extra, uint32_t* out) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 3) * 8 + extra;
+  uint32_t prev = w[0];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t nx = w[j + 1];
+    out[j] = __funnelshift_r(prev, nx, sh);
+    prev = nx;
   }
 }
 
-// Q4_K: unit = 64-element group g of a 256-element block (144 B, 16-aligned).
-__device__ __forceinline__ float unit_q4k(const uint8_t* blk, int g, int e0, const ActView& a) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-  const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
-  const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
-  const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  uint32_t sc0, m0, sc1, m1;  // the 12 scale bytes are hdr.y, hdr.z, hdr.w
-  scale_min_regs(2 * g, hdr.y, hdr.z, hdr.w, &sc0, &m0);
-  scale_min_regs(2 * g + 1, hdr.y, hdr.z, hdr.w, &sc1, &m1);
-  const int wb = e0 >> 2;
-  const uint4* L2 = reinterpret_cast<const uint4*>(a.l2 + wb);
-  const uint4* L1 = reinterpret_cast<const uint4*>(a.l1 + wb);
-  const uint4* L0 = reinterpret_cast<const uint4*>(a.l0 + wb);
-  int lo2 = 0, lo1 = 0, lo0 = 0, hi2 = 0, hi1 = 0, hi0 = 0;
+// ------------------------------------------------------------ unit products
+// Each computes one unit of R rows (R = 2: p0 and p1 share the activation reads).
+
+// Q4_K: unit = group g (64 elements) of a 144-byte block (16-byte aligned).
+// Low nibbles of qs[32g..32g+32) are elements 0..31, high nibbles 32..63; the
+// high nibbles are used in place (16x) and the 1/16 is folded into the scale.
+template <int R>
+__device__ __forceinline__ void q4k_pair(const uint8_t* b0, const uint8_t* b1, int u, const ActS& A,
+                                         float* y) {
+  const int g = u & 3;
+  const uint8_t* bp[2] = {b0, b1};
+  uint4 hdr[2];
+  uint32_t q[2][8];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint4 x2 = L2[h], x1 = L1[h], x0 = L0[h];
-    const uint4 y2 = L2[2 + h], y1 = L1[2 + h], y0 = L0[2 + h];
-    const uint32_t a2[4] = {x2.x, x2.y, x2.z, x2.w}, a1[4] = {x1.x, x1.y, x1.z, x1.w},
-                   a0[4] = {x0.x, x0.y, x0.z, x0.w};
-    const uint32_t b2[4] = {y2.x, y2.y, y2.z, y2.w}, b1[4] = {y1.x, y1.y, y1.z, y1.w},
-                   b0[4] = {y0.x, y0.y, y0.z, y0.w};
+  for (int r = 0; r < R; ++r) {
+    hdr[r] = *reinterpret_cast<const uint4*>(bp[r]);
+    const uint4 qa = *reinterpret_cast<const uint4*>(bp[r] + 16 + 32 * g);
+    const uint4 qb = *reinterpret_cast<const uint4*>(bp[r] + 32 + 32 * g);
+    q[r][0] = qa.x; q[r][1] = qa.y; q[r][2] = qa.z; q[r][3] = qa.w;
+    q[r][4] = qb.x; q[r][5] = qb.y; q[r][6] = qb.z; q[r][7] = qb.w;
+  }
+  float c[2][2];  // [row][sub-block] combined integer sums
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t w = qw[4 * h + j];
-      const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-      lo2 = dp4a_us(lo, a2[j], lo2);
-      lo1 = dp4a_uu(lo, a1[j], lo1);
-      lo0 = dp4a_uu(lo, a0[j], lo0);
-      hi2 = dp4a_us(hi, b2[j], hi2);
-      hi1 = dp4a_uu(hi, b1[j], hi1);
-      hi0 = dp4a_uu(hi, b0[j], hi0);
+  for (int h = 0; h < 2; ++h) {  // h = 0: low nibbles (elements 0..31), 1: high nibbles
+    uint32_t a2[8], a1[8], a0[8];
+    act_half(A, u, h, a2, a1, a0);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      int s2 = 0, s1 = 0, s0 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t w = q[r][j] & (h ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
+        s2 = dp4a_us(w, a2[j], s2);
+        s1 = dp4a_uu(w, a1[j], s1);
+        s0 = dp4a_uu(w, a0[j], s0);
+      }
+      c[r][h] = comb(s2, s1, s0);
     }
   }
-  const float d = f16_bits_to_f32(hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(hdr.x >> 16);
-  const int grp = e0 >> 5;
-  const float t0 = (d * (float)sc0) * comb(lo2, lo1, lo0) - (dmin * (float)m0) * (float)a.sa32[grp];
-  const float t1 =
-      (d * (float)sc1) * comb(hi2, hi1, hi0) - (dmin * (float)m1) * (float)a.sa32[grp + 1];
-  return a.gs[grp] * t0 + a.gs[grp + 1] * t1;
+  const float g0 = A.g[u], g1 = A.g[A.U + u] * 0.0625f;
+  const float m0 = A.gm[u], m1 = A.gm[A.U + u];
+  const uint32_t selP = (g & 1) ? 0x7632u : 0x5410u, selQ = (g & 1) ? 0x3232u : 0x1010u;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    // 6-bit (scale, min) of sub-blocks 2g and 2g+1 (ggml get_scale_min_k4) as
+    // bytes [sc0, sc1, m0, m1]; the 12-byte scale field is hdr.y, hdr.z, hdr.w.
+    // g < 2: bytes (2g, 2g+1) and (2g+4, 2g+5), low 6 bits.  g >= 2: low/high
+    // nibbles of bytes 2g+4, 2g+5 with the top 2 bits of bytes 2g-4, 2g-3
+    // (scales) and 2g, 2g+1 (mins).
+    const uint32_t P = __byte_perm(hdr[r].y, hdr[r].z, selP);
+    const uint32_t Q = __byte_perm(hdr[r].w, hdr[r].w, selQ);
+    const uint32_t hiform = (Q & 0x00000F0Fu) | ((Q >> 4) & 0x0F0F0000u) | ((P >> 2) & 0x30303030u);
+    const uint32_t SM = g >= 2 ? hiform : (P & 0x3F3F3F3Fu);
+    const float d = half_lo(hdr[r].x), dmin = half_lo(hdr[r].x >> 16);
+    y[r] = (d * (float)(SM & 0xFFu)) * (g0 * c[r][0]) - (dmin * (float)((SM >> 16) & 0xFFu)) * m0 +
+           (d * (float)((SM >> 8) & 0xFFu)) * (g1 * c[r][1]) - (dmin * (float)(SM >> 24)) * m1;
+  }
 }
 
-// Q6_K: unit = one quarter of a 256-element block: half h, l-range
-// [16*jb, 16*jb + 16), all four 32-element quadrants -> 64 elements in four
-// 16-element sub-blocks (210-byte blocks, 2-byte aligned).
-__device__ __forceinline__ float unit_q6k(const uint8_t* blk, int u, int e0, const ActView& a) {
-  const int h = u >> 1, jb = u & 1;
-  uint32_t qa[4], qb[4], qh[4], scw[2];
-  lds_words<4>(blk + 64 * h + 16 * jb, qa);       // ql[l]      (quadrants 0, 2)
-  lds_words<4>(blk + 64 * h + 32 + 16 * jb, qb);  // ql[l + 32] (quadrants 1, 3)
-  lds_words<4>(blk + 128 + 32 * h + 16 * jb, qh);
-  lds_words<2>(blk + 192 + 8 * h, scw);
-  const float d = f16_bits_to_f32(lds_u32(blk + 208) & 0xFFFFu);
-  const int wb = e0 >> 2;  // word of element 128*h of this block
-  float acc = 0.0f;
+// Q6_K: unit v (0..3) of a 210-byte block (2-byte aligned) = elements
+// [64v, 64v+64) = quadrants 2*odd and 2*odd+1 of half h = v >> 1, odd = v & 1:
+// nibble 4*odd of ql[64h .. 64h+64), bit pairs 4*odd + (0, 2) of
+// qh[32h .. 32h+32), int8 scales [4v, 4v+4), fp16 d at byte 208.
+template <int R>
+__device__ __forceinline__ void q6k_pair(const uint8_t* b0, const uint8_t* b1, int u, const ActS& A,
+                                         float* y) {
+  const int v = u & 3, h = v >> 1;
+  const uint32_t ext = (uint32_t)(v & 1) * 4;
+  const uint8_t* bp[2] = {b0, b1};
+  uint32_t qh[2][8], sw[2], d2[2];
 #pragma unroll
-  for (int qd = 0; qd < 4; ++qd) {
-    const int aw = wb + 8 * qd + 4 * jb;
-    const uint4 A2 = *reinterpret_cast<const uint4*>(a.l2 + aw);
-    const uint4 A1 = *reinterpret_cast<const uint4*>(a.l1 + aw);
-    const uint4 A0 = *reinterpret_cast<const uint4*>(a.l0 + aw);
-    const uint32_t a2[4] = {A2.x, A2.y, A2.z, A2.w}, a1[4] = {A1.x, A1.y, A1.z, A1.w},
-                   a0[4] = {A0.x, A0.y, A0.z, A0.w};
-    int s2 = 0, s1 = 0, s0 = 0;
+  for (int r = 0; r < R; ++r) {
+    ldw<8>(bp[r] + 128 + 32 * h, ext, qh[r]);
+    ldw<1>(bp[r] + 192 + 4 * v, 0, &sw[r]);
+    ldw<1>(bp[r] + 208, 0, &d2[r]);
+  }
+  float acc[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const uint32_t A = qa[jj], B = qb[jj], H = qh[jj];
-      uint32_t q;
-      if (qd == 0) q = (A & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-      else if (qd == 1) q = (B & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-      else if (qd == 2) q = ((A >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-      else q = ((B >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-      s2 = dp4a_us(q, a2[jj], s2);
-      s1 = dp4a_uu(q, a1[jj], s1);
-      s0 = dp4a_uu(q, a0[jj], s0);
+  for (int part = 0; part < 2; ++part) {  // elements [32*part, 32*part + 32)
+    uint32_t a2[8], a1[8], a0[8];
+    act_half(A, u, part, a2, a1, a0);
+    const float gp = A.g[part * A.U + u];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      uint32_t ql[8];
+      ldw<8>(bp[r] + 64 * h + 32 * part, ext, ql);
+      const float d = half_lo(d2[r]);
+#pragma unroll
+      for (int sb = 0; sb < 2; ++sb) {  // 16-element sub-block 2*part + sb
+        int s2 = 0, s1 = 0, s0 = 0;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = 4 * sb + jj;
+          const uint32_t hb =
+              part == 0 ? ((qh[r][j] << 4) & 0x30303030u) : ((qh[r][j] << 2) & 0x30303030u);
+          const uint32_t q = (ql[j] & 0x0F0F0F0Fu) | hb;
+          s2 = dp4a_us(q, a2[j], s2);
+          s1 = dp4a_uu(q, a1[j], s1);
+          s0 = dp4a_uu(q, a0[j], s0);
+        }
+        const int k = 2 * part + sb;
+        const float sc = (float)(int)(int8_t)((sw[r] >> (8 * k)) & 0xFFu);
+        acc[r] += (d * sc) * (gp * comb(s2, s1, s0) - A.g6[k * A.U + u]);
+      }
     }
-    const int sbi = jb + 2 * qd;  // scale index inside this half
-    const int sc = (int)(int8_t)((scw[sbi >> 2] >> (8 * (sbi & 3))) & 0xFFu);
-    const int e = e0 + 32 * qd + 16 * jb;
-    acc += a.gs[e >> 5] * (d * (float)sc) * (comb(s2, s1, s0) - 32.0f * (float)a.sa16[e >> 4]);
   }
-  return acc;
+  y[0] = acc[0];
+  if (R == 2) y[1] = acc[1];
 }
 
-// Q8_0: unit = one 32-element block (34 B, 2-byte aligned).
-__device__ __forceinline__ float unit_q8_0(const uint8_t* blk, int e0, const ActView& a) {
-  uint32_t w[9];
-  lds_words<9>(blk, w);
-  const float d = f16_bits_to_f32(w[0] & 0xFFFFu);
-  const int wb = e0 >> 2;
-  int s2 = 0, s1 = 0, s0 = 0;
+// Q8_0: unit = two 34-byte blocks (4-byte aligned): 17 words.
+template <int R>
+__device__ __forceinline__ void q8_0_pair(const uint8_t* b0, const uint8_t* b1, int u, const ActS& A,
+                                          float* y) {
+  const uint32_t* wp[2] = {reinterpret_cast<const uint32_t*>(b0), reinterpret_cast<const uint32_t*>(b1)};
+  float acc[2] = {0.0f, 0.0f};
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t q = __funnelshift_r(w[j], w[j + 1], 16);
-    s2 = dp4a_ss(q, a.l2[wb + j], s2);
-    s1 = dp4a_su(q, a.l1[wb + j], s1);
-    s0 = dp4a_su(q, a.l0[wb + j], s0);
-  }
-  return a.gs[e0 >> 5] * d * comb(s2, s1, s0);
-}
-
-// F32: unit = 32 elements, plain fp32 dot.
-__device__ __forceinline__ float unit_f32(const uint8_t* p, int e0, const ActView& a) {
-  const float4* w = reinterpret_cast<const float4*>(p);
-  const float4* x = reinterpret_cast<const float4*>(a.xf + e0);
-  float s = 0.0f;
+  for (int blk = 0; blk < 2; ++blk) {  // block 0: bytes 2..33, block 1: bytes 36..67
+    uint32_t a2[8], a1[8], a0[8];
+    act_half(A, u, blk, a2, a1, a0);
+    const float gb = A.g[blk * A.U + u];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 u = w[j], v = x[j];
-    s += u.x * v.x + u.y * v.y + u.z * v.z + u.w * v.w;
+    for (int r = 0; r < R; ++r) {
+      uint32_t w[9];
+#pragma unroll
+      for (int j = 0; j < 9; ++j) w[j] = wp[r][8 * blk + j];
+      int s2 = 0, s1 = 0, s0 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t q = blk == 0 ? __funnelshift_r(w[j], w[j + 1], 16) : w[j + 1];
+        s2 = dp4a_ss(q, a2[j], s2);
+        s1 = dp4a_su(q, a1[j], s1);
+        s0 = dp4a_su(q, a0[j], s0);
+      }
+      const float d = blk == 0 ? half_lo(w[0]) : half_lo(w[0] >> 16);
+      acc[r] += d * (gb * comb(s2, s1, s0));
+    }
   }
-  return s;
+  y[0] = acc[0];
+  if (R == 2) y[1] = acc[1];
 }
 
-__device__ __forceinline__ int units_per_block(uint32_t type) {
-  return (type == kQ4_K || type == kQ6_K) ? 4 : 1;
+// F32: unit = 64 floats, plain fp32 dot with the fp32 activation copy.
+template <int R>
+__device__ __forceinline__ void f32_pair(const uint8_t* b0, const uint8_t* b1, int u, const ActS& A,
+                                         float* y) {
+  const float4* w0 = reinterpret_cast<const float4*>(b0);
+  const float4* w1 = reinterpret_cast<const float4*>(b1);
+  const float4* x = reinterpret_cast<const float4*>(A.xf + 64 * u);
+  float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const float4 v = x[j], p = w0[j], q = w1[j];
+    s0 += p.x * v.x + p.y * v.y + p.z * v.z + p.w * v.w;
+    if (R == 2) s1 += q.x * v.x + q.y * v.y + q.z * v.z + q.w * v.w;
+  }
+  y[0] = s0;
+  if (R == 2) y[1] = s1;
 }
 
-// Row of lane `lane` in a tile: identity, or the permutation that puts the 32
-// lanes of a warp in 32 distinct banks when rows are 4 or 12 mod 16 bytes
-// (lanes l, l+8, l+16, l+24 then hold rows whose data start at different
-// 4-byte offsets inside their 16-byte-aligned slots).
-__device__ __forceinline__ int lane_row(int lane, int perm) {
-  return perm ? 4 * (lane & 7) + (lane >> 3) : lane;
-}
-
-struct Item {
-  int seg;        // segment (the gate for a SwiGLU pair)
-  int64_t tile;   // tile index inside the segment
-  int kp;         // K part
-};
-
-__device__ __forceinline__ Item locate(const GemvArgs& A, const Plan& P, int64_t t) {
-  int k = 0;  // last segment owning items that starts at or before t
-  for (int i = 1; i < A.nseg; ++i)
-    if (P.si[i].tiles > 0 && t >= P.si[i].item_begin) k = i;
-  const int64_t r = t - P.si[k].item_begin;
-  Item it;
-  it.seg = k;
-  it.tile = r / P.si[k].ks;
-  it.kp = (int)(r - it.tile * P.si[k].ks);
-  return it;
-}
-
-// Chunk range [c0, c1) of K part kp.
-__device__ __forceinline__ void kpart_chunks(const SegInfo& I, int kp, int* c0, int* c1) {
-  const int per = (I.nch + I.ks - 1) / I.ks;
-  *c0 = min(I.nch, kp * per);
-  *c1 = min(I.nch, *c0 + per);
+// Unit u of R (1 or 2) rows.
+template <int R>
+__device__ __forceinline__ void unit_rows(uint32_t type, const uint8_t* p0, const uint8_t* p1, int u,
+                                          const ActS& A, float* y) {
+  if (type == kQ4_K) q4k_pair<R>(p0 + 144 * (u >> 2), p1 + 144 * (u >> 2), u, A, y);
+  else if (type == kQ6_K) q6k_pair<R>(p0 + 210 * (u >> 2), p1 + 210 * (u >> 2), u, A, y);
+  else if (type == kQ8_0) q8_0_pair<R>(p0 + 68 * u, p1 + 68 * u, u, A, y);
+  else f32_pair<R>(p0 + 256 * u, p1 + 256 * u, u, A, y);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs A, const Plan P) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int K = A.K;
-  const bool need_f32 = P.need_f32 != 0;
-  // ---- shared-memory carve-up (must match gemv_smem_bytes)
-  uint8_t* p = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(p);
-  uint64_t* empty = full + kMaxStages;
-  const int kStages = P.stages;
-  p += 128;
-  float* red = reinterpret_cast<float*>(p);  // [2][kNW][32]
-  p += 2 * kNW * 32 * 4;
-  float* pair_buf = reinterpret_cast<float*>(p);  // [32] gate of a SwiGLU pair
-  p += 32 * 4;
-  double* dred = reinterpret_cast<double*>(p);  // [kNW]
-  p += 16 * 8;
-  int* flag = reinterpret_cast<int*>(p);
-  p += 128;
-  uint32_t* l2 = reinterpret_cast<uint32_t*>(p);
-  p += K;
-  uint32_t* l1 = reinterpret_cast<uint32_t*>(p);
-  p += K;
-  uint32_t* l0 = reinterpret_cast<uint32_t*>(p);
-  p += K;
-  float* gs = reinterpret_cast<float*>(p);
-  p += (K / 32) * 4;
-  int* sa32 = reinterpret_cast<int*>(p);
-  p += (K / 32) * 4;
-  int* sa16 = reinterpret_cast<int*>(p);
-  p += (K / 16) * 4;
-  float* xf = reinterpret_cast<float*>(p);
-  if (need_f32) p += (size_t)K * 4;
-  p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 127) & ~uintptr_t(127));
-  uint8_t* stage_base = p;
+__device__ __forceinline__ float row_sum(const float* p, int U) {
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  int q = 0;
+  for (; q + 4 <= U; q += 4) {
+    a0 += p[q];
+    a1 += p[q + 1];
+    a2 += p[q + 2];
+    a3 += p[q + 3];
+  }
+  for (; q < U; ++q) a0 += p[q];
+  return (a0 + a1) + (a2 + a3);
+}
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+// ------------------------------------------------------------ stage map
+// The stages of this CTA: for each logical segment its row range [lo, hi)
+// and first stage index; stage `it` covers rows [r, r + n) of one segment.
+struct StageMap {
+  int64_t lo[4], hi[4];
+  int32_t first[5];  // first[nls] = total stages
+};
+
+__device__ __forceinline__ void build_map(const Plan& P, StageMap* M) {
+  int32_t acc = 0;
+  for (int i = 0; i < P.nls; ++i) {
+    const uint32_t rows = (uint32_t)P.ls[i].rows;  // rows * grid < 2^32 (host check)
+    M->lo[i] = rows * blockIdx.x / gridDim.x;
+    M->hi[i] = rows * (blockIdx.x + 1) / gridDim.x;
+    M->first[i] = acc;
+    acc += (int32_t)((M->hi[i] - M->lo[i] + P.ls[i].m - 1) / P.ls[i].m);
+  }
+  M->first[P.nls] = acc;
+}
+
+__device__ __forceinline__ int stage_ls(const Plan& P, const StageMap* M, int it) {
+  int i = 0;
+  while (i + 1 < P.nls && it >= M->first[i + 1]) ++i;
+  return i;
+}
+
+__device__ __forceinline__ void stage_rows(const Plan& P, const StageMap* M, int ls, int it, int64_t* r,
+                                           int* n) {
+  const int m = P.ls[ls].m;
+  *r = M->lo[ls] + (int64_t)(it - M->first[ls]) * m;
+  const int64_t left = M->hi[ls] - *r;
+  *n = (int)(left < m ? left : m);
+}
+
+// One stage = rows [r, r + n) of the matrix (and of the up matrix of a pair),
+// copied whole from the 16-byte boundary at or below the first byte to the
+// one at or above the last.
+__device__ __forceinline__ void issue_stage(const GemvArgs& A, const Plan& P, const StageMap* M, int it,
+                                            uint8_t* dst, uint64_t* bar, uint64_t pol) {
+  const int ls = stage_ls(P, M, it);
+  int64_t r;
+  int n;
+  stage_rows(P, M, ls, it, &r, &n);
+  const LSeg& L = P.ls[ls];
+  const GemvSeg& G0 = A.seg[L.first];
+  const uintptr_t s0 = reinterpret_cast<uintptr_t>(G0.w) + (uintptr_t)r * G0.row_bytes;
+  const uintptr_t b0 = s0 & ~uintptr_t(15);
+  const uint32_t n0 = (uint32_t)(((s0 + (uintptr_t)n * G0.row_bytes + 15) & ~uintptr_t(15)) - b0);
+  uintptr_t b1 = 0;
+  uint32_t n1 = 0;
+  if (L.pair) {
+    const GemvSeg& G1 = A.seg[L.first + 1];
+    const uintptr_t s1 = reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * G1.row_bytes;
+    b1 = s1 & ~uintptr_t(15);
+    n1 = (uint32_t)(((s1 + (uintptr_t)n * G1.row_bytes + 15) & ~uintptr_t(15)) - b1);
+  }
+  mbar_arrive_expect_tx(bar, n0 + n1);
+  bulk_g2s(dst, reinterpret_cast<const void*>(b0), n0, bar, pol);
+  if (L.pair) bulk_g2s(dst + P.half_bytes, reinterpret_cast<const void*>(b1), n1, bar, pol);
+}
+
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumers) : "memory");
+}
+
+// Activation prologue of the consumer threads: thread t handles the
+// 4-element words w = t + 320 i (i < NWT); the 8 lanes of a 32-element group
+// are 8 consecutive lanes of one warp.  The RMSNorm gains are read before the
+// grid-dependency wait (they do not depend on the previous kernel), x and all
+// its words at once after it.  Returns false when the step is inactive.
+template <int NWT>
+__device__ __forceinline__ bool prologue(const GemvArgs& A, const Plan& P, int tid, int lane, int warp,
+                                         double* dred, uint4* limb, float* ucon, float* xf) {
+  const int K = A.K, NW = K / 4, U = P.U;
+  const float4* x4 = reinterpret_cast<const float4*>(A.x);
+  const float4* n4 = reinterpret_cast<const float4*>(A.norm_w);
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 nv[NWT];
+  if (A.norm_w) {
+#pragma unroll
+    for (int i = 0; i < NWT; ++i) {
+      const int w = i * kConsumers + tid;
+      nv[i] = w < NW ? __ldg(n4 + w) : zero;
+    }
+  }
+  grid_dep_wait();  // x (and *active) are written by the previous kernel
+  if (A.active && __ldcg(A.active) == 0) return false;
+  float4 xv[NWT];
+#pragma unroll
+  for (int i = 0; i < NWT; ++i) {
+    const int w = i * kConsumers + tid;
+    xv[i] = w < NW ? __ldcg(x4 + w) : zero;
+  }
+  if (A.norm_w) {  // RMSNorm scale of x (sum of squares in double)
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < NWT; ++i) {
+      const float4 v = xv[i];
+      ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) dred[warp] = ss;
+    consumer_sync();
+    double tot = 0.0;
+    for (int w = 0; w < kCWarps; ++w) tot += dred[w];
+    const float nscale = (float)(1.0 / sqrt(tot / (double)K + (double)A.eps));
+#pragma unroll
+    for (int i = 0; i < NWT; ++i) {
+      xv[i].x = xv[i].x * nscale * nv[i].x;
+      xv[i].y = xv[i].y * nscale * nv[i].y;
+      xv[i].z = xv[i].z * nscale * nv[i].z;
+      xv[i].w = xv[i].w * nscale * nv[i].w;
+    }
+  }
+  uint32_t* limbw = reinterpret_cast<uint32_t*>(limb);
+#pragma unroll
+  for (int i = 0; i < NWT; ++i) {
+    if (i * kConsumers >= NW) break;  // warp-uniform
+    const int w = i * kConsumers + tid;
+    const bool in = w < NW;
+    const float4 v = xv[i];
+    if (in && P.need_f32) reinterpret_cast<float4*>(xf)[w] = v;
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const uint32_t eb = (__float_as_uint(amax) >> 23) & 0xFFu;  // biased exponent
+    const bool live = eb >= 30 && eb < 255;  // tinier groups contribute nothing
+    // amax < 2^(eb-126): scaling by 2^(149-eb) keeps |q| < 2^23
+    const float up = live ? __uint_as_float((276u - eb) << 23) : 0.0f;
+    const float gsc = live ? __uint_as_float((eb - 22u) << 23) : 0.0f;  // 2^(eb-149)
+    const int q0 = max(-8388607, min(8388607, __float2int_rn(v.x * up)));
+    const int q1 = max(-8388607, min(8388607, __float2int_rn(v.y * up)));
+    const int q2 = max(-8388607, min(8388607, __float2int_rn(v.z * up)));
+    const int q3 = max(-8388607, min(8388607, __float2int_rn(v.w * up)));
+    int s16 = q0 + q1 + q2 + q3;
+    s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
+    s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);
+    if (in) {
+      const uint32_t a = (uint32_t)q0, b = (uint32_t)q1, c = (uint32_t)q2, d = (uint32_t)q3;
+      const int u = w >> 4, k = w & 15;  // unit, word in unit
+      const int base = ((k >> 2) * U + u) * 4 + (k & 3);
+      limbw[base] = __byte_perm(__byte_perm(a, b, 0x0062u), __byte_perm(c, d, 0x0062u), 0x5410u);
+      limbw[base + 16 * U] =
+          __byte_perm(__byte_perm(a, b, 0x0051u), __byte_perm(c, d, 0x0051u), 0x5410u);
+      limbw[base + 32 * U] =
+          __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+      const int grp = k >> 3;
+      if ((k & 3) == 0) ucon[(4 + (k >> 2)) * U + u] = 32.0f * gsc * (float)s16;
+      if ((k & 7) == 0) {
+        ucon[grp * U + u] = gsc;
+        ucon[(2 + grp) * U + u] = gsc * (float)s32;
+      }
+    }
+  }
+  consumer_sync();  // limbs, per-unit constants (and the fp32 copy) are visible
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A,
+                                                           const __grid_constant__ Plan P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int K = A.K, U = P.U, S = P.S, NS = P.stages;
+  const int Ur = U | 1;  // row stride of the partial sums
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // ---- shared-memory carve-up (must match fixed_bytes())
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);              // [kMaxStages]
+  uint64_t* empty = full + kMaxStages;                             // [kMaxStages]
+  StageMap* map = reinterpret_cast<StageMap*>(smem + 128);         // 84 bytes
+  double* dred = reinterpret_cast<double*>(smem + 256);            // [16]
+  float* ucon = reinterpret_cast<float*>(smem + 384);              // g[2U], gm[2U], g6[4U]
+  uint4* limb = reinterpret_cast<uint4*>(smem + 384 + ((32 * U + 127) & ~127));  // [12][U]
+  float* red = reinterpret_cast<float*>(limb + 12 * U);            // [red_floats]
+  float* xf = red + P.red_floats;                                  // [K] (F32 weights only)
+  const uintptr_t sp = reinterpret_cast<uintptr_t>(xf + (P.need_f32 ? K : 0));
+  uint8_t* stages = reinterpret_cast<uint8_t*>((sp + 127) & ~uintptr_t(127));
+
+  if (tid == kConsumers) {  // producer lane: stage map, barriers, first stages
+    build_map(P, map);
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kNW);
+      mbar_init(&empty[i], kCWarps);
     }
     fence_barrier_init();
-    grid_dep_launch();  // the next kernel may start its own weight prefetch
-  }
-  __syncthreads();
-
-  if (warp == kNW) {
-    // ============================== producer warp
     const uint64_t pol = policy_evict_first();
-    uint32_t it = 0;
-    for (int64_t t = blockIdx.x; t < P.n_items; t += gridDim.x) {
-      const Item I0 = locate(A, P, t);
-      const int passes = (A.seg[I0.seg].mode == kSwiGLU) ? 2 : 1;
-      const SegInfo& I = P.si[I0.seg];  // chunking is identical within a pair
-      const int64_t row0 = I0.tile * kRPT;
-      const int r = lane_row(lane, I.perm);
-      int c0, c1;
-      kpart_chunks(I, I0.kp, &c0, &c1);
-      for (int ps = 0; ps < passes; ++ps) {
-        const GemvSeg& G = A.seg[I0.seg + ps];
-        for (int c = c0; c < c1; ++c, ++it) {
-          const int st = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
-          if (it >= kStages) mbar_wait(&empty[st], ph ^ 1u, A.err);
-          const int b0 = c * I.cb;
-          const int nbk = min(I.cb, I.nb - b0);
-          uint32_t bytes = 0;
-          const uint8_t* src = nullptr;
-          uint8_t* dst = nullptr;
-          if (row0 + r < G.rows) {
-            const uintptr_t s0 = reinterpret_cast<uintptr_t>(G.w) +
-                                 (uintptr_t)(row0 + r) * G.row_bytes + (uintptr_t)b0 * I.bb;
-            const uintptr_t a0 = s0 & ~uintptr_t(15);
-            const uintptr_t a1 = (s0 + (uintptr_t)nbk * I.bb + 15) & ~uintptr_t(15);
-            bytes = (uint32_t)(a1 - a0);
-            src = reinterpret_cast<const uint8_t*>(a0);
-            dst = stage_base + (size_t)st * kStageMax + (size_t)lane * I.slot;
-          }
-          const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
-          if (lane == 0) mbar_arrive_expect_tx(&full[st], total);
-          __syncwarp();
-          if (bytes) bulk_g2s(dst, src, bytes, &full[st], pol);
-        }
-      }
+    const int n0 = map->first[P.nls];
+    for (int i = 0; i < NS && i < n0; ++i)
+      issue_stage(A, P, map, i, stages + (size_t)i * P.stage_bytes, &full[i], pol);
+  }
+  grid_dep_launch();  // the next kernel may start its own weight prefetch
+  __syncthreads();
+  const int n_stages = map->first[P.nls];
+  if (n_stages == 0) return;  // no rows for this CTA
+
+  if (warp == kCWarps) {
+    // ============================================================ producer
+    if (lane != 0) return;
+    grid_dep_wait();  // *active is written by the previous kernel
+    if (A.active && __ldcg(A.active) == 0) {  // drain the copies in flight, then leave
+      for (int i = 0; i < NS && i < n_stages; ++i) mbar_wait(&full[i], 0, A.err);
+      return;
+    }
+    const uint64_t pol = policy_evict_first();
+    for (int it = NS; it < n_stages; ++it) {
+      const int slot = it % NS;
+      mbar_wait(&empty[slot], (uint32_t)(it / NS - 1) & 1u, A.err);
+      issue_stage(A, P, map, it, stages + (size_t)slot * P.stage_bytes, &full[slot], pol);
     }
     return;
   }
 
-  // ================================ consumer warps
-  grid_dep_wait();
-  const bool active = !A.active || *A.active != 0;
-  const int ctid = threadIdx.x;  // 0 .. kNW*32-1
-  float nscale = 1.0f;
-  if (active) {
-    // ---- optional RMSNorm scale of x (sum of squares in double)
-    if (A.norm_w) {
-      double ss = 0.0;
-      for (int i = ctid; i < K; i += kNW * 32) {
-        const float v = A.x[i];
-        ss += (double)v * v;
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) dred[warp] = ss;
-      asm volatile("bar.sync 1, %0;" ::"r"(kNW * 32));
-      double tot = 0.0;
-      for (int w = 0; w < kNW; ++w) tot += dred[w];
-      nscale = (float)(1.0 / sqrt(tot / (double)K + (double)A.eps));
-    }
-    // ---- fixed-point activation limbs, one warp per 32-element group
-    for (int g = warp; g < K / 32; g += kNW) {
-      float h = A.x[g * 32 + lane];
-      if (A.norm_w) h = h * nscale * A.norm_w[g * 32 + lane];
-      if (need_f32) xf[g * 32 + lane] = h;
-      const float amax = warp_max(fabsf(h));
-      const uint32_t eb = (__float_as_uint(amax) >> 23) & 0xFFu;  // biased exponent
-      int q = 0;
-      float scale = 0.0f;
-      if (eb >= 30 && eb < 255) {  // amax >= 2^-97 (tinier groups contribute nothing)
-        // amax < 2^(eb-126): scaling by 2^(149-eb) keeps |q| < 2^23
-        q = __float2int_rn(h * __uint_as_float((uint32_t)(276 - eb) << 23));
-        q = max(-8388607, min(8388607, q));
-        scale = __uint_as_float((eb - 22) << 23);  // 2^(eb-149)
-      }
-      const int sh = 8 * (lane & 3);
-      uint32_t w0 = ((uint32_t)q & 0xFFu) << sh;
-      uint32_t w1 = (((uint32_t)q >> 8) & 0xFFu) << sh;
-      uint32_t w2 = (((uint32_t)(q >> 16)) & 0xFFu) << sh;
-#pragma unroll
-      for (int o = 1; o <= 2; o <<= 1) {
-        w0 |= __shfl_xor_sync(0xffffffffu, w0, o);
-        w1 |= __shfl_xor_sync(0xffffffffu, w1, o);
-        w2 |= __shfl_xor_sync(0xffffffffu, w2, o);
-      }
-      if ((lane & 3) == 0) {
-        l0[g * 8 + (lane >> 2)] = w0;
-        l1[g * 8 + (lane >> 2)] = w1;
-        l2[g * 8 + (lane >> 2)] = w2;
-      }
-      int s16 = q;
-#pragma unroll
-      for (int o = 1; o <= 8; o <<= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-      const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
-      if (lane == 0) {
-        gs[g] = scale;
-        sa32[g] = s32;
-        sa16[2 * g] = s16;
-      } else if (lane == 16) {
-        sa16[2 * g + 1] = s16;
-      }
-    }
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(kNW * 32));
+  // ============================================================== consumers
+  const int NW = K / 4;
+  const bool live = NW <= 4 * kConsumers
+                        ? prologue<4>(A, P, tid, lane, warp, dred, limb, ucon, xf)
+                        : prologue<kMaxWordsPerThread>(A, P, tid, lane, warp, dred, limb, ucon, xf);
+  if (!live) return;
 
-  const ActView av{l2, l1, l0, gs, sa32, sa16, xf};
-  uint32_t it = 0;
-  int rb = 0;
-  for (int64_t t = blockIdx.x; t < P.n_items; t += gridDim.x) {
-    const Item I0 = locate(A, P, t);
-    const SegInfo& I = P.si[I0.seg];
-    const int passes = (A.seg[I0.seg].mode == kSwiGLU) ? 2 : 1;
-    const int64_t row0 = I0.tile * kRPT;
-    const int r = lane_row(lane, I.perm);
-    int c0, c1;
-    kpart_chunks(I, I0.kp, &c0, &c1);
-    for (int ps = 0; ps < passes; ++ps) {
-      const GemvSeg& G = A.seg[I0.seg + ps];
-      const bool have = active && (row0 + r < G.rows);
-      const int upb = units_per_block(G.type);
-      float acc = 0.0f;
-      for (int c = c0; c < c1; ++c, ++it) {
-        const int st = it % kStages;
-        const uint32_t ph = (it / kStages) & 1u;
-        mbar_wait(&full[st], ph, A.err);
-        const int b0 = c * I.cb;
-        const int nbk = min(I.cb, I.nb - b0);
-        if (have) {
-          const uintptr_t s0 = reinterpret_cast<uintptr_t>(G.w) +
-                               (uintptr_t)(row0 + r) * G.row_bytes + (uintptr_t)b0 * I.bb;
-          const uint8_t* rowp =
-              stage_base + (size_t)st * kStageMax + (size_t)lane * I.slot + (s0 & 15);
-          const int nu = nbk * upb;
-          for (int u = warp; u < nu; u += kNW) {
-            const int bi = u / upb, sub = u - bi * upb;
-            const uint8_t* blk = rowp + (size_t)bi * I.bb;
-            const int eb = (b0 + bi) * I.be;  // element index of the block
-            if (G.type == kQ4_K) acc += unit_q4k(blk, sub, eb + 64 * sub, av);
-            else if (G.type == kQ6_K) acc += unit_q6k(blk, sub, eb + 128 * (sub >> 1), av);
-            else if (G.type == kQ8_0) acc += unit_q8_0(blk, eb, av);
-            else acc += unit_f32(blk, eb, av);
-          }
+  ActS act;
+  act.limb = limb;
+  act.g = ucon;
+  act.gm = ucon + 2 * U;
+  act.g6 = ucon + 4 * U;
+  act.xf = xf;
+  act.U = U;
+  const int u = tid % U, s = tid / U;
+  const bool busy = s < S;
+
+  // ---- main loop over the ring
+  int chunk_it0 = 0;      // first stage of the current reduction chunk
+  int64_t chunk_r0 = 0;   // its first row
+  for (int it = 0; it < n_stages; ++it) {
+    const int slot = it % NS;
+    const int ls = stage_ls(P, map, it);
+    const LSeg& L = P.ls[ls];
+    int64_t r;
+    int n;
+    stage_rows(P, map, ls, it, &r, &n);
+    if (it == chunk_it0) chunk_r0 = r;
+    const GemvSeg& G = A.seg[L.first];
+    const int64_t rb = G.row_bytes;
+    const uint8_t* sb = stages + (size_t)slot * P.stage_bytes;
+    const uint8_t* base0 = sb + ((reinterpret_cast<uintptr_t>(G.w) + (uintptr_t)r * rb) & 15);
+    const int jr0 = (int)(r - chunk_r0);  // row of this stage inside the chunk
+    const int ck_rows = L.cs * L.m;       // row capacity of a chunk
+    mbar_wait(&full[slot], (uint32_t)(it / NS) & 1u, A.err);
+    if (busy) {
+      float y[2];
+      if (L.pair) {  // gate and up rows j share the activation
+        const GemvSeg& G1 = A.seg[L.first + 1];
+        const uint8_t* base1 =
+            sb + P.half_bytes + ((reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * rb) & 15);
+        for (int j = s; j < n; j += S) {
+          unit_rows<2>(G.type, base0 + (size_t)j * rb, base1 + (size_t)j * rb, u, act, y);
+          red[(jr0 + j) * Ur + u] = y[0];
+          red[(ck_rows + jr0 + j) * Ur + u] = y[1];
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-      }
-      if (!active) continue;
-      // ---- cross-warp reduction in fixed order
-      float* rbuf = red + rb * kNW * 32;
-      rbuf[warp * 32 + lane] = acc;
-      asm volatile("bar.sync 1, %0;" ::"r"(kNW * 32));
-      rb ^= 1;
-      if (warp != 0) continue;
-      float y = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kNW; ++w) y += rbuf[w * 32 + lane];
-      const int64_t row = row0 + r;
-      if (I.ks == 1) {  // whole K in this CTA: epilogue now
-        if (row < G.rows) {
-          if (G.mode == kSwiGLU) pair_buf[lane] = y;
-          else if (ps == 1) G.out[row] = silu_mul(pair_buf[lane], y);
-          else if (G.mode == kAdd) G.out[row] += y;
-          else G.out[row] = y;
+      } else {  // rows j and j + S together
+        int j = s;
+        for (; j + S < n; j += 2 * S) {
+          unit_rows<2>(G.type, base0 + (size_t)j * rb, base0 + (size_t)(j + S) * rb, u, act, y);
+          red[(jr0 + j) * Ur + u] = y[0];
+          red[(jr0 + j + S) * Ur + u] = y[1];
         }
-      } else {  // partial: park it; the CTA finishing the tile last combines
-        A.partial[((I.item_begin + I0.tile * I.ks + I0.kp) * 2 + ps) * kRPT + lane] = y;
-      }
-    }
-    if (!active || I.ks == 1 || warp != 0) continue;
-    // ---- split tile: the CTA that completes it last sums the parts in order
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) {
-      int* cnt = A.counters + (I.tile_begin + I0.tile);
-      const int last = (atomicAdd(cnt, 1) == I.ks - 1);
-      if (last) *cnt = 0;  // ready for the next launch
-      flag[0] = last;
-    }
-    __syncwarp();
-    if (flag[0]) {
-      __threadfence();
-      float y[2] = {0.0f, 0.0f};
-      const float* base = A.partial + (I.item_begin + I0.tile * I.ks) * 2 * kRPT;
-      for (int ps = 0; ps < passes; ++ps)
-        for (int kp = 0; kp < I.ks; ++kp) y[ps] += __ldcg(base + (kp * 2 + ps) * kRPT + lane);
-      const int64_t row = row0 + r;
-      const GemvSeg& G = A.seg[I0.seg];
-      if (row < G.rows) {
-        if (passes == 2) A.seg[I0.seg + 1].out[row] = silu_mul(y[0], y[1]);
-        else if (G.mode == kAdd) G.out[row] += y[0];
-        else G.out[row] = y[0];
+        if (j < n) {  // an odd row out
+          unit_rows<1>(G.type, base0 + (size_t)j * rb, base0 + (size_t)j * rb, u, act, y);
+          red[(jr0 + j) * Ur + u] = y[0];
+        }
       }
     }
     __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);  // the slot may be refilled
+    const bool seg_end = it + 1 == map->first[ls + 1];
+    if (!seg_end && it + 1 - chunk_it0 < L.cs) continue;
+    // ---- chunk complete: one thread per row sums its U partials (row stride
+    // Ur is odd: conflict-free), four interleaved accumulators added in a
+    // fixed order
+    consumer_sync();
+    const int rows = (int)(r + n - chunk_r0);
+    for (int j = tid; j < rows; j += kConsumers) {
+      const float y0 = row_sum(red + j * Ur, U);
+      const float y1 = L.pair ? row_sum(red + (ck_rows + j) * Ur, U) : 0.0f;
+      const int64_t row = chunk_r0 + j;
+      if (L.pair) A.seg[L.first + 1].out[row] = silu_mul(y0, y1);
+      else if (G.mode == kAdd) G.out[row] += y0;
+      else G.out[row] = y0;
+    }
+    consumer_sync();  // the partial-sum buffer may be reused
+    chunk_it0 = it + 1;
   }
 }
 
 // Work decomposition shared by the launcher and the kernel.
-bool make_plan(const GemvArgs& a, Plan* P, int sms) {
-  int64_t tiles_total = 0;
+bool make_plan(const GemvArgs& a, Plan* P) {
+  if (a.nseg < 1 || a.nseg > 4 || a.K <= 0 || a.K % 64 != 0) return false;
+  if (a.K > 4 * kConsumers * kMaxWordsPerThread) return false;
+  if (a.norm_w && a.K > 4 * kConsumers * 4) return false;  // gains preloaded in registers
+  const int U = a.K / 64;
+  if (U > kConsumers) return false;
+  P->U = U;
+  P->S = kConsumers / U;
+  P->need_f32 = 0;
+  P->nls = 0;
+  int stage_bytes = 0, half_bytes = 0, red = 0;
   for (int i = 0; i < a.nseg; ++i) {
     const GemvSeg& G = a.seg[i];
-    SegInfo& I = P->si[i];
+    int be, bb;
     switch (G.type) {
-      case kQ4_K: I.be = 256; I.bb = 144; break;
-      case kQ6_K: I.be = 256; I.bb = 210; break;
-      case kQ8_0: I.be = 32; I.bb = 34; break;
-      case kF32: I.be = 32; I.bb = 128; break;
+      case kQ4_K: be = 256; bb = 144; break;
+      case kQ6_K: be = 256; bb = 210; break;
+      case kQ8_0: be = 32; bb = 34; break;
+      case kF32: be = 32; bb = 128; P->need_f32 = 1; break;
       default: return false;
     }
-    if (a.K % I.be != 0 || a.K % 32 != 0) return false;
-    I.nb = a.K / I.be;
-    if ((int64_t)I.nb * I.bb != G.row_bytes) return false;
-    const int max_cb = (kStageMax / kRPT - 64) / I.bb;
-    if (max_cb < 1) return false;
-    I.nch = (I.nb + max_cb - 1) / max_cb;
-    I.cb = (I.nb + I.nch - 1) / I.nch;
-    int slot = ((I.cb * I.bb + 32) + 15) & ~15;
-    if (((slot >> 4) & 1) == 0) slot += 16;  // odd 16-byte pitch: conflict-free 128-bit loads
-    if (slot * kRPT > kStageMax) return false;
-    I.slot = slot;
-    const int rm = (int)(G.row_bytes & 15);
-    I.perm = (G.type == kQ6_K && (rm == 4 || rm == 12)) ? 1 : 0;
-    const bool up_of_pair = (i > 0 && a.seg[i - 1].mode == kSwiGLU);
+    if (a.K % be != 0 || (int64_t)(a.K / be) * bb != G.row_bytes) return false;
+    if (reinterpret_cast<uintptr_t>(G.w) & 15) return false;  // bulk copies need 16 B
+    if (G.rows <= 0 || G.rows > (int64_t)(0xFFFFFFFFu / 1024)) return false;
+    const bool up_of_pair = i > 0 && a.seg[i - 1].mode == kSwiGLU;
     if (up_of_pair) {
       if (G.rows != a.seg[i - 1].rows || G.type != a.seg[i - 1].type) return false;
-      I.tiles = 0;
-    } else {
-      I.tiles = (int32_t)((G.rows + kRPT - 1) / kRPT);
-      tiles_total += I.tiles;
-    }
-  }
-  if (a.nseg > 0 && a.seg[a.nseg - 1].mode == kSwiGLU) return false;
-  // split along K until there are about two work items per SM
-  int ks = 1;
-  while (tiles_total * ks < 2 * (int64_t)sms && ks < kMaxKParts) ks *= 2;
-  int64_t items = 0, tiles = 0;
-  P->split = 0;
-  for (int i = 0; i < a.nseg; ++i) {
-    SegInfo& I = P->si[i];
-    if (I.tiles == 0) {  // up half of a pair mirrors the gate
-      I.ks = P->si[i - 1].ks;
-      I.item_begin = P->si[i - 1].item_begin;
-      I.tile_begin = P->si[i - 1].tile_begin;
       continue;
     }
-    I.ks = ks < I.nch ? ks : I.nch;
-    if (a.partial == nullptr || a.counters == nullptr) I.ks = 1;
-    if (I.ks > 1) P->split = 1;
-    I.item_begin = items;
-    I.tile_begin = tiles;
-    items += (int64_t)I.tiles * I.ks;
-    tiles += I.tiles;
+    LSeg& L = P->ls[P->nls++];
+    L.rows = G.rows;
+    L.first = i;
+    L.pair = G.mode == kSwiGLU ? 1 : 0;
+    const int64_t per_round = (int64_t)P->S * G.row_bytes * (L.pair + 1);
+    int64_t rounds = kStageTarget / per_round;
+    if (rounds < 1) rounds = 1;
+    L.m = (int32_t)(rounds * P->S);
+    const int64_t slot = ((int64_t)L.m * G.row_bytes + 32 + 127) & ~int64_t(127);
+    if (slot > kSmemLimit / 2) return false;
+    if (L.pair) half_bytes = half_bytes > (int)slot ? half_bytes : (int)slot;
+    const int need = (int)slot * (L.pair + 1);
+    stage_bytes = stage_bytes > need ? stage_bytes : need;
+    const int per_stage = L.m * (U | 1) * (L.pair + 1);  // partial sums of one stage
+    int cs = kRedBudget / (4 * per_stage);
+    if (cs < 1) cs = 1;
+    L.cs = cs;
+    red = red > cs * per_stage ? red : cs * per_stage;
   }
-  P->n_items = items;
-  if (P->split) {
-    if ((size_t)items * 2 * kRPT > a.partial_floats || tiles > a.n_counters) return false;
-  }
-  P->need_f32 = 0;
-  for (int i = 0; i < a.nseg; ++i) {
-    if (a.seg[i].type == kF32) P->need_f32 = 1;
-    if (reinterpret_cast<uintptr_t>(a.seg[i].w) & 15) return false;  // bulk copies need 16 B
-  }
+  if (a.seg[a.nseg - 1].mode == kSwiGLU) return false;
+  P->stage_bytes = stage_bytes;
+  P->half_bytes = half_bytes;
+  P->red_floats = red;
   return true;
+}
+
+size_t fixed_bytes(const Plan& P, int K) {
+  const size_t b = 384 + (((size_t)32 * P.U + 127) & ~size_t(127)) + (size_t)12 * 16 * P.U +
+                   (size_t)P.red_floats * 4 + (P.need_f32 ? (size_t)K * 4 : 0);
+  return (b + 127) & ~size_t(127);
 }
 
 int sm_count() {
@@ -577,43 +673,25 @@ int sm_count() {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    sms[dev] = n > 0 ? n : 148;
+    sms[dev] = n > 0 && n <= 1024 ? n : 148;
   }
   return sms[dev];
 }
 
 }  // namespace
 
-size_t gemv_act_bytes(int K, bool need_f32) {
-  size_t b = 128 + 2 * kNW * 32 * 4 + 32 * 4 + 16 * 8 + 128;
-  b += 3 * (size_t)K + (K / 32) * 8 + (K / 16) * 4;
-  if (need_f32) b += (size_t)K * 4;
-  return (b + 127) & ~size_t(127);
-}
-
-int gemv_stages(int K, bool need_f32) {
-  const size_t act = gemv_act_bytes(K, need_f32);
-  if (act >= (size_t)kSmemLimit) return 0;
-  const int n = (int)((kSmemLimit - act) / kStageMax);
-  return n < kMaxStages ? n : kMaxStages;
-}
-
-size_t gemv_smem_bytes(int K, bool need_f32) {
-  return gemv_act_bytes(K, need_f32) + (size_t)gemv_stages(K, need_f32) * kStageMax;
-}
-
-size_t gemv_partial_floats(int64_t max_tiles) {
-  return (size_t)max_tiles * kMaxKParts * 2 * kRPT;
-}
-
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl) {
   const int sms = sm_count();
   Plan P;
-  if (a.nseg < 1 || a.nseg > 4 || !make_plan(a, &P, sms)) return cudaErrorInvalidValue;
-  P.stages = gemv_stages(a.K, P.need_f32 != 0);
-  if (P.stages < 2) return cudaErrorInvalidValue;
-  const size_t smem = gemv_smem_bytes(a.K, P.need_f32 != 0);
-  const int grid = (int)(P.n_items < (int64_t)sms ? P.n_items : (int64_t)sms);
+  if (!make_plan(a, &P)) return cudaErrorInvalidValue;
+  const size_t fixed = fixed_bytes(P, a.K);
+  if (fixed + 2 * (size_t)P.stage_bytes > (size_t)kSmemLimit) return cudaErrorInvalidValue;
+  const int ns = (int)((kSmemLimit - fixed) / P.stage_bytes);
+  P.stages = ns < kMaxStages ? ns : kMaxStages;
+  const size_t smem = fixed + (size_t)P.stages * P.stage_bytes;
+  int64_t max_rows = 0;
+  for (int i = 0; i < P.nls; ++i) max_rows = P.ls[i].rows > max_rows ? P.ls[i].rows : max_rows;
+  const int grid = (int)(max_rows < (int64_t)sms ? max_rows : (int64_t)sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -40,22 +40,18 @@ struct GemvSeg {
 struct GemvArgs {
   GemvSeg seg[4];
   int32_t nseg;
-  int32_t K;              // shared input length
+  int32_t K;              // shared input length (multiple of 64)
   const float* x;         // input [K]
   const float* norm_w;    // optional RMSNorm gain applied to x first
   float eps;
   const int32_t* active;  // optional: skip when *active == 0
   int32_t* err;           // optional error flags
-  float* partial;         // optional split-K scratch (null: no split)
-  int32_t* counters;      // split-K tile counters, zero between launches
-  size_t partial_floats;
-  int64_t n_counters;
 };
 
-// Launch y = W x over up to 4 segments sharing x (decode, batch 1).
+// Launch y = W x over up to 4 segments sharing x (decode, batch 1).  Weight
+// bytes up to the next 16-byte boundary past each segment's last row are
+// read (and ignored).
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
-size_t gemv_smem_bytes(int K, bool need_f32);
-size_t gemv_partial_floats(int64_t max_tiles);
 
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
