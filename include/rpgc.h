@@ -160,24 +160,19 @@ RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t col
 /* AttentionFromCache for one query token (src/qwen3.cc:79-117, seq = 1):
  * q holds n_heads*head_dim floats (already QK-normed and rotated), the caches
  * are one layer in the KvCache layout [n_kv_heads][max_seq][head_dim]
- * (src/kv_cache.cc:29-33); keys [0, pos] are read; out receives
- * n_heads*head_dim floats.  Split-K over the positions: the partial results
- * live in scratch memory that this call allocates and frees on `stream`
- * (stream-ordered).  head_dim must be 128 and n_heads/n_kv_heads <= 8. */
+ * (src/kv_cache.cc:29-33), 16-byte aligned; keys [0, pos] are read; out
+ * receives n_heads*head_dim floats.  The positions are split over one
+ * thread-block cluster per kv head that merges its splits on chip: no scratch
+ * memory.  head_dim must be 128 and n_heads/n_kv_heads 1, 2, 4 or 8. */
 RPGC_API int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_cache,
                                    int64_t max_seq, int32_t n_heads, int32_t n_kv_heads,
                                    int32_t head_dim, int64_t pos, float* out, void* stream);
 /* Allocation-free variant of rpgc_attention_decode.  No counterpart in the
  * reference.  For callers that cannot allocate device memory when they call
  * (a host whose GPU heap belongs to another runtime, or a latency-critical
- * path that must not enter the allocator): the split-K scratch is a fixed
- * 2.03 MiB array inside the library, resident on every GPU that loads it
- * until the process exits.  Limits: head_dim 128, at most 16 kv heads and 8
- * query heads per kv head; larger shapes return RPGC_E_ARG.  The first call on
- * a device looks up the array's device address (cudaGetSymbolAddress), so make
- * that first call outside any stream capture.  Every call shares the array and
- * clears its counters first; calls whose kernels overlap on the GPU race on
- * it and must be serialised by the caller.  Same arguments and results as
+ * path that must not enter the allocator): its contract is that a call
+ * allocates nothing and keeps no state between calls, so calls on different
+ * streams may overlap.  Same arguments, limits and results as
  * rpgc_attention_decode. */
 RPGC_API int rpgc_attention_decode_noalloc(const float* q, const float* k_cache,
                                            const float* v_cache, int64_t max_seq,

@@ -84,7 +84,6 @@ struct Model {
   }
 };
 
-constexpr int kMaxSplits = 32;
 
 struct Session {
   int32_t model_id = 0;
@@ -95,8 +94,8 @@ struct Session {
   bool has_logits = false;
   float *kc = nullptr, *vc = nullptr;
   float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
-  float *gate = nullptr, *up = nullptr, *logits = nullptr, *partial = nullptr;
-  int32_t *ids = nullptr, *counters = nullptr, *gen_out = nullptr, *n_out = nullptr;
+  float *gate = nullptr, *up = nullptr, *logits = nullptr;
+  int32_t *ids = nullptr, *gen_out = nullptr, *n_out = nullptr;
   DecodeState* st = nullptr;
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
@@ -178,7 +177,11 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
          c.vocab);
   if (c.n_heads % c.n_kv_heads) fail(RPGC_E_ARG, "heads %d not a multiple of kv heads %d", c.n_heads, c.n_kv_heads);
   if (c.head_dim != 128) fail(RPGC_E_ARG, "head_dim %d unsupported (kernels take 128)", c.head_dim);
-  if (c.n_heads / c.n_kv_heads > 8) fail(RPGC_E_ARG, "GQA group above 8 unsupported");
+  {
+    const int g = c.n_heads / c.n_kv_heads;
+    if (!(g == 1 || g == 2 || g == 4 || g == 8))
+      fail(RPGC_E_ARG, "GQA group %d unsupported (1, 2, 4 or 8)", g);
+  }
   if (c.hidden % 256 || c.intermediate % 32) fail(RPGC_E_ARG, "hidden/intermediate not block aligned");
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
@@ -365,9 +368,6 @@ int32_t session_create(int32_t model, int32_t max_seq) {
   s->ids = s->alloc<int32_t>(s->cap);
   s->gen_out = s->alloc<int32_t>(max_seq + 1);
   s->n_out = s->alloc<int32_t>(1);
-  s->partial = s->alloc<float>(attn_decode_partial_floats(c.n_kv_heads, c.n_heads, c.head_dim, kMaxSplits));
-  s->counters = s->alloc<int32_t>(c.n_kv_heads);
-  CK(cudaMemsetAsync(s->counters, 0, c.n_kv_heads * sizeof(int32_t), s->stream));
   s->st = s->alloc<DecodeState>(1);
   CK(cudaMallocHost(&s->st_host, sizeof(DecodeState)));
   std::memset(s->st_host, 0, sizeof(DecodeState));
@@ -448,9 +448,7 @@ void launch_layers_step(Session* s) {
     aa.hd = c.head_dim;
     aa.n = 1;
     aa.state = s->st;
-    aa.partial = s->partial;
-    aa.counters = s->counters;
-    aa.max_splits = kMaxSplits;
+    aa.err = &s->st->error;
     aa.pdl = true;
     check(attn_decode_launch(aa, cs), "attn decode");
     GemvArgs go = step_gemv(s, s->attn, qd, nullptr);
@@ -1039,20 +1037,13 @@ int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_c
   return guard([&] {
     if (!q || !k_cache || !v_cache || !out || n_heads <= 0 || n_kv_heads <= 0 || max_seq <= 0)
       fail(RPGC_E_ARG, "bad attention arguments");
-    if (head_dim != 128 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
-      fail(RPGC_E_ARG, "attention takes head_dim 128 and a GQA group of at most 8");
+    const int32_t grp = n_heads % n_kv_heads ? 0 : n_heads / n_kv_heads;
+    if (head_dim != 128 || !(grp == 1 || grp == 2 || grp == 4 || grp == 8))
+      fail(RPGC_E_ARG, "attention takes head_dim 128 and a GQA group of 1, 2, 4 or 8");
     if (pos < 0 || pos >= max_seq || pos > INT32_MAX - 1) fail(RPGC_E_ARG, "pos out of range");
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
+      fail(RPGC_E_ARG, "caches must be 16-byte aligned");
     cudaStream_t cs = as_stream(stream);
-    const size_t pf = attn_decode_partial_floats(n_kv_heads, n_heads, head_dim, kMaxSplits);
-    float* partial = nullptr;
-    int32_t* counters = nullptr;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&partial), pf * sizeof(float), cs));
-    const cudaError_t ec = cudaMallocAsync(reinterpret_cast<void**>(&counters),
-                                           n_kv_heads * sizeof(int32_t), cs);
-    if (ec != cudaSuccess) {
-      cudaFreeAsync(partial, cs);
-      CK(ec);
-    }
     AttnArgs a{};
     a.q = q;
     a.kc = k_cache;
@@ -1064,14 +1055,7 @@ int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_c
     a.hd = head_dim;
     a.pos0 = pos;
     a.n = 1;
-    a.partial = partial;
-    a.counters = counters;
-    a.max_splits = kMaxSplits;
-    cudaError_t e = cudaMemsetAsync(counters, 0, n_kv_heads * sizeof(int32_t), cs);
-    if (e == cudaSuccess) e = attn_decode_launch(a, cs);
-    cudaFreeAsync(counters, cs);
-    cudaFreeAsync(partial, cs);
-    check(e, "attention decode");
+    check(attn_decode_launch(a, cs), "attention decode");
     return RPGC_OK;
   });
 }

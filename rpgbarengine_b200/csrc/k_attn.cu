@@ -5,6 +5,7 @@
 // (src/kernels.h:108-120), cache layout ((l*nkv + h)*max_seq + pos)*hd
 // (src/kv_cache.cc:29-33), AttentionFromCache with a softmax over [0, pos]
 // (src/qwen3.cc:79-117).
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -13,6 +14,7 @@
 namespace rpgc {
 namespace {
 
+namespace cg = cooperative_groups;
 constexpr float kNegBig = -3.0e38f;
 
 // One block per (token, head); hd threads.  q heads first, then kv heads.
@@ -55,14 +57,24 @@ __global__ void qkv_rope_kernel(const QkvArgs a) {
 }
 
 // ---------------------------------------------------------------- decode
-// grid (n_kv, splits), 128 threads.  hd == 128 (4 dims per lane), group <= 8.
+// One thread-block cluster per kv head, S = 8 or 16 CTAs (splits of the
+// positions [0, pos]), 8 warps each; hd == 128 (4 dims per lane), group G =
+// n_heads / n_kv in {1, 2, 4, 8}.  Each CTA streams its K and V rows into
+// shared memory with two bulk copies per tile of up to 64 positions.  A warp
+// step scores PB = 32 / G positions against the G query heads at once: the
+// 32 partial dot products of a lane are folded across the warp by a
+// transpose-reduction (31 shuffles leave lane l with score l), so no score
+// needs its own warp-wide sum.  Warps keep an online softmax; the CTA merges
+// its warps in shared memory and cluster rank 0 merges the S CTAs through
+// distributed shared memory, in a fixed order (deterministic).
 constexpr int kMaxGroup = 8;
-constexpr int kPre = 4;  // positions per warp whose K/V are loaded up front
+constexpr int kAWarps = 8;
+constexpr int kTileP = 64;  // positions per K/V tile
 
 // QK-norm + RoPE of one 128-wide head held as a float4 per lane (dims
 // 4*lane..4*lane+3): RMSNorm with a double sum of squares, then the half-split
-// rotation with the reference's separate roundings.  `mine` is this lane's
-// float4; the partner dims (i +- 64) come from lane^16.
+// rotation with the reference's separate roundings.  The partner dims
+// (i +- 64) come from lane^16.
 __device__ __forceinline__ float4 norm_rope_head(float4 v, const float* w, const float* cs,
                                                  float eps, int lane) {
   double ss = (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
@@ -83,139 +95,190 @@ __device__ __forceinline__ float4 norm_rope_head(float4 v, const float* w, const
   return make_float4(o[0], o[1], o[2], o[3]);
 }
 
-__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+
+// 32 values per lane -> lane l holds the warp-wide sum of value l.
+__device__ __forceinline__ float transpose_reduce(float* v, int lane) {
+#pragma unroll
+  for (int n = 16; n >= 1; n >>= 1) {
+    const bool up = (lane & n) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = up ? v[i] : v[i + n];
+      const float keep = up ? v[i + n] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, n);
+    }
+  }
+  return v[0];
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const AttnArgs a) {
+  constexpr int PB = 32 / G;  // positions per warp step
+  extern __shared__ __align__(128) float kv_tile[];  // K [kTileP][128], then V
+  float* Ks = kv_tile;
+  float* Vs = kv_tile + kTileP * 128;
+  __shared__ __align__(16) float qs[G][128];
+  __shared__ __align__(16) float wo[kAWarps][G][128];
+  __shared__ float wm[kAWarps][G], wl[kAWarps][G];
+  __shared__ __align__(16) float cpart[G][132];  // merged o[128], m, l of this CTA
+  __shared__ __align__(8) uint64_t bar;
+
   grid_dep_wait();
   const DecodeState* st = a.state;
-  if (st && !st->active) return;
-  __shared__ __align__(16) float sm[4][kMaxGroup][132];  // rows padded to 16 B
-  __shared__ __align__(16) float4 knew_s[32], vnew_s[32];
-  __shared__ float fsc[kMaxGroup][32];
-  __shared__ int s_last;
-  const int kh = blockIdx.x, split = blockIdx.y, S = gridDim.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = a.n_heads / a.n_kv, hd = a.hd;
+  if (st && !st->active) return;  // the whole cluster leaves together
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)gridDim.y, split = (int)blockIdx.y, kh = (int)blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pos = st ? st->pos : (int)a.pos0;
   const int L = pos + 1;  // keys [0, pos]
   const int chunk = (L + S - 1) / S;
-  const int c0 = split * chunk, c1 = min(L, c0 + chunk);
-  const float scale = 1.0f / sqrtf((float)hd);
-  const float* kb = a.kc + (int64_t)kh * a.max_seq * hd;
-  const float* vb = a.vc + (int64_t)kh * a.max_seq * hd;
+  const int c0 = min(L, split * chunk), c1 = min(L, c0 + chunk);
+  const float scale = 1.0f / sqrtf(128.0f);
   const bool fused = a.q_norm != nullptr;
-  const bool has_new = fused && c0 <= pos && pos < c1;  // this split owns the new token
-  const float* cs = fused ? a.rope + (int64_t)pos * hd : nullptr;
+  const bool owner = fused && c0 <= pos && pos < c1;  // this split holds the new token
+  const float* cs = fused ? a.rope + (int64_t)pos * 128 : nullptr;
+  const float* kb = a.kc + (int64_t)kh * a.max_seq * 128;
+  const float* vb = a.vc + (int64_t)kh * a.max_seq * 128;
 
-  float4 qv[kMaxGroup], ov[kMaxGroup];
-  float m[kMaxGroup], l[kMaxGroup];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g < G) {
-      qv[g] = *reinterpret_cast<const float4*>(a.q + (kh * G + g) * hd + 4 * lane);
-      if (fused) qv[g] = norm_rope_head(qv[g], a.q_norm, cs, a.eps, lane);
-    }
-    ov[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    m[g] = kNegBig;
-    l[g] = 0.0f;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
   }
-  if (has_new && warp == 0) {
+  // query heads of this kv head (normalised and rotated when fused)
+  for (int g = warp; g < G; g += kAWarps) {
+    float4 v = *reinterpret_cast<const float4*>(a.q + (kh * G + g) * 128 + 4 * lane);
+    if (fused) v = norm_rope_head(v, a.q_norm, cs, a.eps, lane);
+    *reinterpret_cast<float4*>(&qs[g][4 * lane]) = v;
+  }
+  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  if (owner && warp == kAWarps - 1) {
     // the new token's k/v: normalise + rotate k, write both into the cache
-    float4 k4 = *reinterpret_cast<const float4*>(a.k_new + kh * hd + 4 * lane);
-    k4 = norm_rope_head(k4, a.k_norm, cs, a.eps, lane);
-    const float4 v4 = *reinterpret_cast<const float4*>(a.v_new + kh * hd + 4 * lane);
-    const int64_t off = ((int64_t)kh * a.max_seq + pos) * hd + 4 * lane;
-    *reinterpret_cast<float4*>(a.kc_w + off) = k4;
-    *reinterpret_cast<float4*>(a.vc_w + off) = v4;
-    knew_s[lane] = k4;
-    vnew_s[lane] = v4;
+    knew = *reinterpret_cast<const float4*>(a.k_new + kh * 128 + 4 * lane);
+    knew = norm_rope_head(knew, a.k_norm, cs, a.eps, lane);
+    vnew = *reinterpret_cast<const float4*>(a.v_new + kh * 128 + 4 * lane);
+    const int64_t off = ((int64_t)kh * a.max_seq + pos) * 128 + 4 * lane;
+    *reinterpret_cast<float4*>(a.kc_w + off) = knew;
+    *reinterpret_cast<float4*>(a.vc_w + off) = vnew;
   }
   __syncthreads();
-  // positions of this warp: c0 + warp + 4*i; K/V of up to kPre loaded at once
-  for (int p0 = c0 + warp; p0 < c1; p0 += 4 * kPre) {
-    float4 kr[kPre], vr[kPre];
+
+  float4 q[G], o[G];
 #pragma unroll
-    for (int i = 0; i < kPre; ++i) {
-      const int p = p0 + 4 * i;
-      if (p < c1) {
-        if (has_new && p == pos) {
-          kr[i] = knew_s[lane];
-          vr[i] = vnew_s[lane];
-        } else {
-          kr[i] = *reinterpret_cast<const float4*>(kb + (int64_t)p * hd + 4 * lane);
-          vr[i] = *reinterpret_cast<const float4*>(vb + (int64_t)p * hd + 4 * lane);
+  for (int g = 0; g < G; ++g) {
+    q[g] = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
+    o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mh = kNegBig, lh = 0.0f;  // running max / sum of this lane's head lane / PB
+  const int gl = lane / PB, jl = lane % PB;
+  uint32_t phase = 0;
+  for (int t0 = c0; t0 < c1; t0 += kTileP) {
+    const int tn = min(kTileP, c1 - t0);
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)tn * 512u;
+      const uint64_t pol = policy_evict_first();
+      mbar_arrive_expect_tx(&bar, 2 * bytes);
+      bulk_g2s(Ks, kb + (int64_t)t0 * 128, bytes, &bar, pol);
+      bulk_g2s(Vs, vb + (int64_t)t0 * 128, bytes, &bar, pol);
+    }
+    mbar_wait(&bar, phase, a.err);
+    phase ^= 1u;
+    if (owner && warp == kAWarps - 1 && pos >= t0 && pos < t0 + tn) {
+      reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = knew;
+      reinterpret_cast<float4*>(Vs + (pos - t0) * 128)[lane] = vnew;
+    }
+    __syncthreads();
+    for (int pb = warp * PB; pb < tn; pb += kAWarps * PB) {
+      float val[32];
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        const float4 k = pb + j < tn ? reinterpret_cast<const float4*>(Ks + (pb + j) * 128)[lane]
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < G; ++g) val[g * PB + j] = dot4(q[g], k);
+      }
+      const bool valid = pb + jl < tn;
+      const float tr = transpose_reduce(val, lane);  // every lane takes part
+      const float sc = valid ? tr * scale : kNegBig;
+      float mx = sc;
+#pragma unroll
+      for (int n = PB / 2; n >= 1; n >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, n));
+      const float mn = fmaxf(mh, mx);
+      const float corr = expf(mh - mn);
+      const float pe = valid ? expf(sc - mn) : 0.0f;
+      float ps = pe;
+#pragma unroll
+      for (int n = PB / 2; n >= 1; n >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, n);
+      lh = lh * corr + ps;
+      mh = mn;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float cg_ = __shfl_sync(0xffffffffu, corr, g * PB);
+        o[g].x *= cg_;
+        o[g].y *= cg_;
+        o[g].z *= cg_;
+        o[g].w *= cg_;
+      }
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        if (pb + j >= tn) break;  // warp-uniform
+        const float4 v = reinterpret_cast<const float4*>(Vs + (pb + j) * 128)[lane];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float p = __shfl_sync(0xffffffffu, pe, g * PB + j);
+          o[g].x += p * v.x;
+          o[g].y += p * v.y;
+          o[g].z += p * v.z;
+          o[g].w += p * v.w;
         }
       }
     }
-#pragma unroll
-    for (int i = 0; i < kPre; ++i) {
-      if (p0 + 4 * i >= c1) break;
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        if (g >= G) break;
-        float s = qv[g].x * kr[i].x + qv[g].y * kr[i].y + qv[g].z * kr[i].z + qv[g].w * kr[i].w;
-        s = warp_sum(s) * scale;
-        const float mn = fmaxf(m[g], s);
-        const float corr = expf(m[g] - mn), pe = expf(s - mn);
-        l[g] = l[g] * corr + pe;
-        ov[g].x = ov[g].x * corr + pe * vr[i].x;
-        ov[g].y = ov[g].y * corr + pe * vr[i].y;
-        ov[g].z = ov[g].z * corr + pe * vr[i].z;
-        ov[g].w = ov[g].w * corr + pe * vr[i].w;
-        m[g] = mn;
-      }
-    }
+    __syncthreads();  // the tile buffers may be refilled
   }
-  // merge the 4 warps of this split
+  // ---- merge the warps of this CTA
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g >= G) break;
-    *reinterpret_cast<float4*>(&sm[warp][g][4 * lane]) = ov[g];
-    if (lane == 0) {
-      sm[warp][g][128] = m[g];
-      sm[warp][g][129] = l[g];
-    }
+  for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(&wo[warp][g][4 * lane]) = o[g];
+  if (jl == 0) {
+    wm[warp][gl] = mh;
+    wl[warp][gl] = lh;
   }
   __syncthreads();
-  float* part = a.partial + ((int64_t)kh * S + split) * G * 130;
-  for (int idx = threadIdx.x; idx < G * 128; idx += 128) {
+  for (int idx = tid; idx < G * 128; idx += kAWarps * 32) {
     const int g = idx >> 7, d = idx & 127;
     float M = kNegBig;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w][g][128]);
-    float O = 0.0f, Lsum = 0.0f;
-    for (int w = 0; w < 4; ++w) {
-      const float f = expf(sm[w][g][128] - M);
-      O += sm[w][g][d] * f;
-      Lsum += sm[w][g][129] * f;
+    for (int w = 0; w < kAWarps; ++w) M = fmaxf(M, wm[w][g]);
+    float O = 0.0f, Ls = 0.0f;
+    for (int w = 0; w < kAWarps; ++w) {
+      const float f = expf(wm[w][g] - M);
+      O += wo[w][g][d] * f;
+      Ls += wl[w][g] * f;
     }
-    part[g * 130 + d] = O;
+    cpart[g][d] = O;
     if (d == 0) {
-      part[g * 130 + 128] = M;
-      part[g * 130 + 129] = Lsum;
+      cpart[g][128] = M;
+      cpart[g][129] = Ls;
     }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&a.counters[kh], 1) == S - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // last split of this kv head: combine all splits (S <= 32: one lane per split)
-  const float* pk = a.partial + (int64_t)kh * S * G * 130;
-  for (int g = warp; g < G; g += 4) {
-    const float ms = lane < S ? __ldcg(pk + (lane * G + g) * 130 + 128) : kNegBig;
-    const float ls = lane < S ? __ldcg(pk + (lane * G + g) * 130 + 129) : 0.0f;
-    const float M = warp_max(ms);
-    const float f = lane < S ? expf(ms - M) : 0.0f;
-    const float Lsum = warp_sum(ls * f);
-    fsc[g][lane] = f / Lsum;
+  // ---- merge the CTAs of the cluster on rank 0 (distributed shared memory)
+  cluster.sync();
+  if (cluster.block_rank() == 0) {
+    for (int idx = tid; idx < G * 128; idx += kAWarps * 32) {
+      const int g = idx >> 7, d = idx & 127;
+      float M = kNegBig;
+      for (int r = 0; r < S; ++r) M = fmaxf(M, cluster.map_shared_rank(&cpart[g][128], r)[0]);
+      float O = 0.0f, Ls = 0.0f;
+      for (int r = 0; r < S; ++r) {
+        const float* rp = cluster.map_shared_rank(&cpart[g][0], r);
+        const float f = expf(rp[128] - M);
+        O += rp[d] * f;
+        Ls += rp[129] * f;
+      }
+      a.out[(kh * G + g) * 128 + d] = O / Ls;
+    }
   }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < G * 128; idx += 128) {
-    const int g = idx >> 7, d = idx & 127;
-    float O = 0.0f;
-    for (int s = 0; s < S; ++s) O += __ldcg(pk + (s * G + g) * 130 + d) * fsc[g][s];
-    a.out[(kh * G + g) * hd + d] = O;
-  }
-  if (threadIdx.x == 0) a.counters[kh] = 0;
+  cluster.sync();  // keep every CTA's shared memory alive until rank 0 is done
 }
 
 // --------------------------------------------------------------- prefill
@@ -357,26 +420,79 @@ cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-size_t attn_decode_partial_floats(int n_kv, int n_heads, int hd, int max_splits) {
-  return (size_t)n_kv * max_splits * (n_heads / n_kv) * 130 + (size_t)0 * hd;
+namespace {
+
+// Cluster size per device: 16 splits where a 16-CTA cluster of the kernel
+// can be scheduled, else the portable 8.
+template <int G>
+int cluster_size() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 8;
+  if (!cached[dev]) {
+    const int smem = 2 * kTileP * 128 * (int)sizeof(float);
+    cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int sz = 8;
+    if (cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 16);
+      cfg.blockDim = dim3(kAWarps * 32);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 1;
+      at[0].val.clusterDim.y = 16;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<G>, &cfg) == cudaSuccess && n >= 1)
+        sz = 16;
+    }
+    cudaGetLastError();  // a refused probe leaves no error behind
+    cached[dev] = sz;
+  }
+  return cached[dev];
 }
 
+template <int G>
+cudaError_t launch_decode(const AttnArgs& a, cudaStream_t s) {
+  const int S = cluster_size<G>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)S);
+  cfg.blockDim = dim3(kAWarps * 32);
+  cfg.dynamicSmemBytes = 2 * kTileP * 128 * sizeof(float);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)S;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<G>, a);
+}
+
+}  // namespace
+
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
-  if (a.hd != 128 || a.n_heads % a.n_kv || a.n_heads / a.n_kv > kMaxGroup || a.max_splits < 1 ||
-      a.max_splits > 32)
+  const int G = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
+  if (a.hd != 128 || a.n_kv <= 0 || a.n_heads % a.n_kv) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15)
     return cudaErrorInvalidValue;
   if (a.q_norm && (!a.k_norm || !a.rope || !a.k_new || !a.v_new || !a.kc_w || !a.vc_w))
     return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)a.max_splits);
-  cfg.blockDim = dim3(128);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = a.pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+  switch (G) {
+    case 1: return launch_decode<1>(a, s);
+    case 2: return launch_decode<2>(a, s);
+    case 4: return launch_decode<4>(a, s);
+    case 8: return launch_decode<8>(a, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {

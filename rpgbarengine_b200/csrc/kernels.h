@@ -100,9 +100,7 @@ struct AttnArgs {
   int32_t n_heads, n_kv, hd;
   int64_t pos0, n;     // prefill
   const DecodeState* state;  // decode: pos from state, n = 1
-  float* partial;      // decode split-K scratch
-  int32_t* counters;   // decode: one per kv head, zero between launches
-  int32_t max_splits;
+  int32_t* err;        // decode: optional error flags (bounded waits)
   // decode only, optional: fuse QK-norm + RoPE + K/V cache write of the new
   // token (q/k/v raw projections, k_new/v_new the token's k and v rows)
   const float* q_norm;
@@ -115,9 +113,11 @@ struct AttnArgs {
   float eps;
   bool pdl;
 };
+// Decode attention needs no scratch: the splits of a kv head form one
+// thread-block cluster and merge in distributed shared memory.  Group sizes
+// n_heads / n_kv of 1, 2, 4 or 8; head_dim 128; caches 16-byte aligned.
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s);
-size_t attn_decode_partial_floats(int n_kv, int n_heads, int hd, int max_splits);
 
 // Sampler / argmax.  When state != null: decode-loop step (reads options,
 // u = CounterUniform(seed, pos), writes state->token, appends to out_ids,

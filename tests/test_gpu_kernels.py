@@ -129,7 +129,9 @@ def test_sampler_known_answers():
 
 
 @pytest.mark.parametrize("n_heads,n_kv,max_seq,pos", [(32, 8, 1152, 0), (32, 8, 1152, 767),
-                                                      (16, 8, 96, 95), (4, 2, 40, 17)])
+                                                      (16, 8, 96, 95), (4, 2, 40, 17),
+                                                      (8, 8, 4200, 4100), (64, 8, 200, 150),
+                                                      (32, 8, 8192, 8191)])
 def test_attention_decode_matches_oracle(orc, n_heads, n_kv, max_seq, pos):
     rng = np.random.default_rng(pos + n_heads)
     q = rng.standard_normal(n_heads * 128).astype(np.float32)

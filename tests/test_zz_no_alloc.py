@@ -2,11 +2,11 @@
 
 Callers that cannot allocate device memory (a host whose GPU heap belongs to
 another runtime, or a latency-critical path that must stay out of the
-allocator) use rpgc_attention_decode_noalloc, whose split-K scratch is a fixed
-array inside the library.  It must give the same result as
-rpgc_attention_decode, which allocates its scratch per call -- including on a
-second call in a row, which finds the previous call's leftovers in the shared
-array.  This file is collected last on purpose.
+allocator) use rpgc_attention_decode_noalloc, which guarantees that a call
+allocates nothing and keeps no state between calls (its position splits merge
+inside a thread-block cluster).  It must give the same result as
+rpgc_attention_decode on consecutive calls of different shapes.  This file is
+collected last on purpose.
 """
 import ctypes as C
 
@@ -58,13 +58,13 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert _rel(got, want) <= TOL
 
 
-def test_noalloc_rejects_shapes_beyond_its_scratch():
+def test_noalloc_rejects_unsupported_groups():
     if rb.device_count() == 0:
         pytest.fail("GPU test collected without a CUDA device")
     fn = _noalloc()
-    q, kc, vc = _case(3, 32, 32, 16)
+    q, kc, vc = _case(3, 24, 8, 16)  # 3 query heads per kv head
     out = torch.empty_like(q)
-    rc = fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), 16, 32, 32, 128, 3, out.data_ptr(),
+    rc = fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), 16, 24, 8, 128, 3, out.data_ptr(),
             torch.cuda.current_stream().cuda_stream)
     assert rc == rb.E_ARG
-    assert b"scratch" in rb.lib().rpgc_last_error()
+    assert b"group" in rb.lib().rpgc_last_error()
