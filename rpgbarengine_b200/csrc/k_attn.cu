@@ -433,6 +433,8 @@ int cluster_size() {
   if (!cached[dev]) {
     const int smem = 2 * kTileP * 128 * (int)sizeof(float);
     cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
     int sz = 8;
     if (cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed,
                              1) == cudaSuccess) {

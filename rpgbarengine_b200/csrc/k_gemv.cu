@@ -50,8 +50,7 @@ constexpr int kThreads = kConsumers + 32;    // + one producer warp
 constexpr int kMaxStages = 6;
 constexpr int kSmemLimit = 112 * 1024;       // leaves room for the next kernel's CTA
 constexpr int kStageTarget = 24 * 1024;
-constexpr int kRedBudget = 16 * 1024;        // partial sums of one reduction chunk
-constexpr int kMaxWordsPerThread = 10;       // K <= 4 * 320 * 10
+constexpr int kRedBudget = 8 * 1024;         // partial sums of one reduction chunk (x2 buffers)
 
 struct LSeg {      // logical segment: one matrix, or a SwiGLU (gate, up) pair
   int64_t rows;
@@ -284,88 +283,100 @@ __device__ __forceinline__ void f32_pair(const uint8_t* b0, const uint8_t* b1, i
   if (R == 2) y[1] = s1;
 }
 
+// Type-mask bits: the block types a kernel instantiation handles.
+constexpr uint32_t kMQ4K = 1, kMQ6K = 2, kMQ80 = 4, kMF32 = 8, kMAll = 15;
+
+__host__ __device__ constexpr uint32_t type_bit(uint32_t type) {
+  return type == kQ4_K ? kMQ4K : type == kQ6_K ? kMQ6K : type == kQ8_0 ? kMQ80 : type == kF32 ? kMF32 : 0;
+}
+
 // Unit u of R (1 or 2) rows.
-template <int R>
+template <int R, uint32_t TM>
 __device__ __forceinline__ void unit_rows(uint32_t type, const uint8_t* p0, const uint8_t* p1, int u,
                                           const ActS& A, float* y) {
-  if (type == kQ4_K) q4k_pair<R>(p0 + 144 * (u >> 2), p1 + 144 * (u >> 2), u, A, y);
-  else if (type == kQ6_K) q6k_pair<R>(p0 + 210 * (u >> 2), p1 + 210 * (u >> 2), u, A, y);
-  else if (type == kQ8_0) q8_0_pair<R>(p0 + 68 * u, p1 + 68 * u, u, A, y);
-  else f32_pair<R>(p0 + 256 * u, p1 + 256 * u, u, A, y);
+  if ((TM & kMQ4K) && type == kQ4_K) q4k_pair<R>(p0 + 144 * (u >> 2), p1 + 144 * (u >> 2), u, A, y);
+  else if ((TM & kMQ6K) && type == kQ6_K) q6k_pair<R>(p0 + 210 * (u >> 2), p1 + 210 * (u >> 2), u, A, y);
+  else if ((TM & kMQ80) && type == kQ8_0) q8_0_pair<R>(p0 + 68 * u, p1 + 68 * u, u, A, y);
+  else if (TM & kMF32) f32_pair<R>(p0 + 256 * u, p1 + 256 * u, u, A, y);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
-__device__ __forceinline__ float row_sum(const float* p, int U) {
-  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-  int q = 0;
-  for (; q + 4 <= U; q += 4) {
-    a0 += p[q];
-    a1 += p[q + 1];
-    a2 += p[q + 2];
-    a3 += p[q + 3];
-  }
-  for (; q < U; ++q) a0 += p[q];
-  return (a0 + a1) + (a2 + a3);
+// ------------------------------------------------------------ stages
+// The CTA's rows of logical segment i are [lo_i, hi_i) (balanced split of
+// rows_i over the grid); they are streamed in stages of at most m_i rows.
+__device__ __forceinline__ void cta_rows(const Plan& P, int ls, int64_t* lo, int64_t* hi) {
+  const uint32_t rows = (uint32_t)P.ls[ls].rows;  // rows * grid < 2^32 (host check)
+  *lo = rows * blockIdx.x / gridDim.x;
+  *hi = rows * (blockIdx.x + 1) / gridDim.x;
 }
 
-// ------------------------------------------------------------ stage map
-// The stages of this CTA: for each logical segment its row range [lo, hi)
-// and first stage index; stage `it` covers rows [r, r + n) of one segment.
-struct StageMap {
-  int64_t lo[4], hi[4];
-  int32_t first[5];  // first[nls] = total stages
+__device__ __forceinline__ int count_stages(const Plan& P) {
+  int n = 0;
+  for (int i = 0; i < P.nls; ++i) {
+    int64_t lo, hi;
+    cta_rows(P, i, &lo, &hi);
+    n += (int)((hi - lo + P.ls[i].m - 1) / P.ls[i].m);
+  }
+  return n;
+}
+
+// What the consumers need to know about a ring slot's current stage; written
+// by the producer before it arms the slot's barrier.
+struct StageDesc {
+  int64_t r;      // first row
+  int32_t n;      // rows
+  int32_t ls;     // logical segment
+  int32_t last;   // 1: last stage of its logical segment
+  uint32_t off0;  // byte offset of row r inside the slot
+  uint32_t off1;  // same for the up matrix of a pair
+  int32_t pad;
 };
 
-__device__ __forceinline__ void build_map(const Plan& P, StageMap* M) {
-  int32_t acc = 0;
-  for (int i = 0; i < P.nls; ++i) {
-    const uint32_t rows = (uint32_t)P.ls[i].rows;  // rows * grid < 2^32 (host check)
-    M->lo[i] = rows * blockIdx.x / gridDim.x;
-    M->hi[i] = rows * (blockIdx.x + 1) / gridDim.x;
-    M->first[i] = acc;
-    acc += (int32_t)((M->hi[i] - M->lo[i] + P.ls[i].m - 1) / P.ls[i].m);
+// Producer-side walk over the stages (logical segment, row range).
+struct Cursor {
+  int ls;
+  int64_t r, hi;
+};
+
+__device__ __forceinline__ void cursor_seek(const Plan& P, Cursor* c) {
+  while (c->ls < P.nls && c->r >= c->hi) {
+    if (++c->ls < P.nls) cta_rows(P, c->ls, &c->r, &c->hi);
   }
-  M->first[P.nls] = acc;
 }
 
-__device__ __forceinline__ int stage_ls(const Plan& P, const StageMap* M, int it) {
-  int i = 0;
-  while (i + 1 < P.nls && it >= M->first[i + 1]) ++i;
-  return i;
-}
-
-__device__ __forceinline__ void stage_rows(const Plan& P, const StageMap* M, int ls, int it, int64_t* r,
-                                           int* n) {
-  const int m = P.ls[ls].m;
-  *r = M->lo[ls] + (int64_t)(it - M->first[ls]) * m;
-  const int64_t left = M->hi[ls] - *r;
-  *n = (int)(left < m ? left : m);
-}
-
-// One stage = rows [r, r + n) of the matrix (and of the up matrix of a pair),
-// copied whole from the 16-byte boundary at or below the first byte to the
-// one at or above the last.
-__device__ __forceinline__ void issue_stage(const GemvArgs& A, const Plan& P, const StageMap* M, int it,
-                                            uint8_t* dst, uint64_t* bar, uint64_t pol) {
-  const int ls = stage_ls(P, M, it);
-  int64_t r;
-  int n;
-  stage_rows(P, M, ls, it, &r, &n);
-  const LSeg& L = P.ls[ls];
+// Issue the next stage into `slot`: descriptor, barrier arming, one bulk copy
+// of the rows (two for a pair), each from the 16-byte boundary at or below
+// the first byte to the one at or above the last.
+__device__ __forceinline__ void issue_next(const GemvArgs& A, const Plan& P, Cursor* c, uint8_t* dst,
+                                           StageDesc* desc, uint64_t* bar, uint64_t pol) {
+  const LSeg& L = P.ls[c->ls];
+  const int64_t r = c->r;
+  const int n = (int)(c->hi - r < L.m ? c->hi - r : L.m);
   const GemvSeg& G0 = A.seg[L.first];
   const uintptr_t s0 = reinterpret_cast<uintptr_t>(G0.w) + (uintptr_t)r * G0.row_bytes;
   const uintptr_t b0 = s0 & ~uintptr_t(15);
   const uint32_t n0 = (uint32_t)(((s0 + (uintptr_t)n * G0.row_bytes + 15) & ~uintptr_t(15)) - b0);
-  uintptr_t b1 = 0;
+  uintptr_t b1 = 0, s1 = 0;
   uint32_t n1 = 0;
   if (L.pair) {
     const GemvSeg& G1 = A.seg[L.first + 1];
-    const uintptr_t s1 = reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * G1.row_bytes;
+    s1 = reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * G1.row_bytes;
     b1 = s1 & ~uintptr_t(15);
     n1 = (uint32_t)(((s1 + (uintptr_t)n * G1.row_bytes + 15) & ~uintptr_t(15)) - b1);
   }
-  mbar_arrive_expect_tx(bar, n0 + n1);
+  StageDesc d;
+  d.r = r;
+  d.n = n;
+  d.ls = c->ls;
+  c->r += n;
+  d.last = c->r >= c->hi;
+  d.off0 = (uint32_t)(s0 - b0);
+  d.off1 = (uint32_t)P.half_bytes + (uint32_t)(s1 - b1);
+  d.pad = 0;
+  *desc = d;
+  cursor_seek(P, c);
+  mbar_arrive_expect_tx(bar, n0 + n1);  // release: the descriptor is visible to the waiters
   bulk_g2s(dst, reinterpret_cast<const void*>(b0), n0, bar, pol);
   if (L.pair) bulk_g2s(dst + P.half_bytes, reinterpret_cast<const void*>(b1), n1, bar, pol);
 }
@@ -374,101 +385,135 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumers) : "memory");
 }
 
+// Fixed-point limbs of NB consecutive-in-thread words (4 activation values
+// each; word w of the thread is element block w = base + 320 * i).  Group
+// maxima and sums come from the 8 lanes of a 32-element group (8
+// consecutive lanes).  Straight-line: every word's shuffle chain is issued
+// before any store, so the chains of different words overlap.
+template <int NB>
+__device__ __forceinline__ void quant_words(const float4 (&v)[NB], int w0, int NW, int U,
+                                            uint32_t* limbw, float* ucon) {
+  float gsc[NB], up[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    float a = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+    up[i] = a;
+  }
+#pragma unroll
+  for (int n = 1; n <= 4; n <<= 1) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) up[i] = fmaxf(up[i], __shfl_xor_sync(0xffffffffu, up[i], n));
+  }
+  uint32_t l2[NB], l1[NB], l0[NB];
+  int s16[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    const uint32_t eb = (__float_as_uint(up[i]) >> 23) & 0xFFu;  // biased exponent of the group max
+    const bool live = eb >= 30 && eb < 255;  // tinier groups contribute nothing
+    // amax < 2^(eb-126): scaling by 2^(149-eb) keeps |q| < 2^23
+    const float sc = live ? __uint_as_float((276u - eb) << 23) : 0.0f;
+    gsc[i] = live ? __uint_as_float((eb - 22u) << 23) : 0.0f;  // 2^(eb-149)
+    const int q0 = max(-8388607, min(8388607, __float2int_rn(v[i].x * sc)));
+    const int q1 = max(-8388607, min(8388607, __float2int_rn(v[i].y * sc)));
+    const int q2 = max(-8388607, min(8388607, __float2int_rn(v[i].z * sc)));
+    const int q3 = max(-8388607, min(8388607, __float2int_rn(v[i].w * sc)));
+    s16[i] = (q0 + q1) + (q2 + q3);
+    const uint32_t a = (uint32_t)q0, b = (uint32_t)q1, c = (uint32_t)q2, d = (uint32_t)q3;
+    l2[i] = __byte_perm(__byte_perm(a, b, 0x0062u), __byte_perm(c, d, 0x0062u), 0x5410u);
+    l1[i] = __byte_perm(__byte_perm(a, b, 0x0051u), __byte_perm(c, d, 0x0051u), 0x5410u);
+    l0[i] = __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+  }
+  int s32[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) s16[i] += __shfl_xor_sync(0xffffffffu, s16[i], 1);
+#pragma unroll
+  for (int i = 0; i < NB; ++i) s16[i] += __shfl_xor_sync(0xffffffffu, s16[i], 2);
+#pragma unroll
+  for (int i = 0; i < NB; ++i) s32[i] = s16[i] + __shfl_xor_sync(0xffffffffu, s16[i], 4);
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    const int w = w0 + i * kConsumers;
+    const int u = w >> 4, k = w & 15;  // unit, word in unit
+    const int base = ((k >> 2) * U + u) * 4 + (k & 3);
+    const bool in = w < NW;
+    if (in) {
+      limbw[base] = l2[i];
+      limbw[base + 16 * U] = l1[i];
+      limbw[base + 32 * U] = l0[i];
+    }
+    if (in && (k & 3) == 0) ucon[(4 + (k >> 2)) * U + u] = 32.0f * gsc[i] * (float)s16[i];
+    if (in && (k & 7) == 0) {
+      ucon[(k >> 3) * U + u] = gsc[i];
+      ucon[(2 + (k >> 3)) * U + u] = gsc[i] * (float)s32[i];
+    }
+  }
+}
+
 // Activation prologue of the consumer threads: thread t handles the
-// 4-element words w = t + 320 i (i < NWT); the 8 lanes of a 32-element group
-// are 8 consecutive lanes of one warp.  The RMSNorm gains are read before the
-// grid-dependency wait (they do not depend on the previous kernel), x and all
-// its words at once after it.  Returns false when the step is inactive.
-template <int NWT>
+// 4-element words w = t + 320 i (coalesced loads); the 8 lanes of a
+// 32-element group are 8 consecutive lanes of one warp.  The RMSNorm gains
+// are read before the grid-dependency wait (they do not depend on the
+// previous kernel), x after it.  Returns false when the step is inactive.
 __device__ __forceinline__ bool prologue(const GemvArgs& A, const Plan& P, int tid, int lane, int warp,
                                          double* dred, uint4* limb, float* ucon, float* xf) {
+  constexpr int NB = 4;  // words per batch
   const int K = A.K, NW = K / 4, U = P.U;
   const float4* x4 = reinterpret_cast<const float4*>(A.x);
   const float4* n4 = reinterpret_cast<const float4*>(A.norm_w);
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 nv[NWT];
-  if (A.norm_w) {
+  const bool norm = A.norm_w != nullptr;  // then NW <= 4 * 320 (host check): one batch
+  float4 nv[NB];
+  if (norm) {
 #pragma unroll
-    for (int i = 0; i < NWT; ++i) {
-      const int w = i * kConsumers + tid;
+    for (int i = 0; i < NB; ++i) {
+      const int w = tid + i * kConsumers;
       nv[i] = w < NW ? __ldg(n4 + w) : zero;
     }
   }
   grid_dep_wait();  // x (and *active) are written by the previous kernel
   if (A.active && __ldcg(A.active) == 0) return false;
-  float4 xv[NWT];
-#pragma unroll
-  for (int i = 0; i < NWT; ++i) {
-    const int w = i * kConsumers + tid;
-    xv[i] = w < NW ? __ldcg(x4 + w) : zero;
-  }
-  if (A.norm_w) {  // RMSNorm scale of x (sum of squares in double)
-    double ss = 0.0;
-#pragma unroll
-    for (int i = 0; i < NWT; ++i) {
-      const float4 v = xv[i];
-      ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) dred[warp] = ss;
-    consumer_sync();
-    double tot = 0.0;
-    for (int w = 0; w < kCWarps; ++w) tot += dred[w];
-    const float nscale = (float)(1.0 / sqrt(tot / (double)K + (double)A.eps));
-#pragma unroll
-    for (int i = 0; i < NWT; ++i) {
-      xv[i].x = xv[i].x * nscale * nv[i].x;
-      xv[i].y = xv[i].y * nscale * nv[i].y;
-      xv[i].z = xv[i].z * nscale * nv[i].z;
-      xv[i].w = xv[i].w * nscale * nv[i].w;
-    }
-  }
   uint32_t* limbw = reinterpret_cast<uint32_t*>(limb);
+  for (int b = 0; b < NW; b += NB * kConsumers) {  // uniform trip count
+    float4 v[NB];
 #pragma unroll
-  for (int i = 0; i < NWT; ++i) {
-    if (i * kConsumers >= NW) break;  // warp-uniform
-    const int w = i * kConsumers + tid;
-    const bool in = w < NW;
-    const float4 v = xv[i];
-    if (in && P.need_f32) reinterpret_cast<float4*>(xf)[w] = v;
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const uint32_t eb = (__float_as_uint(amax) >> 23) & 0xFFu;  // biased exponent
-    const bool live = eb >= 30 && eb < 255;  // tinier groups contribute nothing
-    // amax < 2^(eb-126): scaling by 2^(149-eb) keeps |q| < 2^23
-    const float up = live ? __uint_as_float((276u - eb) << 23) : 0.0f;
-    const float gsc = live ? __uint_as_float((eb - 22u) << 23) : 0.0f;  // 2^(eb-149)
-    const int q0 = max(-8388607, min(8388607, __float2int_rn(v.x * up)));
-    const int q1 = max(-8388607, min(8388607, __float2int_rn(v.y * up)));
-    const int q2 = max(-8388607, min(8388607, __float2int_rn(v.z * up)));
-    const int q3 = max(-8388607, min(8388607, __float2int_rn(v.w * up)));
-    int s16 = q0 + q1 + q2 + q3;
-    s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
-    s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
-    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);
-    if (in) {
-      const uint32_t a = (uint32_t)q0, b = (uint32_t)q1, c = (uint32_t)q2, d = (uint32_t)q3;
-      const int u = w >> 4, k = w & 15;  // unit, word in unit
-      const int base = ((k >> 2) * U + u) * 4 + (k & 3);
-      limbw[base] = __byte_perm(__byte_perm(a, b, 0x0062u), __byte_perm(c, d, 0x0062u), 0x5410u);
-      limbw[base + 16 * U] =
-          __byte_perm(__byte_perm(a, b, 0x0051u), __byte_perm(c, d, 0x0051u), 0x5410u);
-      limbw[base + 32 * U] =
-          __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
-      const int grp = k >> 3;
-      if ((k & 3) == 0) ucon[(4 + (k >> 2)) * U + u] = 32.0f * gsc * (float)s16;
-      if ((k & 7) == 0) {
-        ucon[grp * U + u] = gsc;
-        ucon[(2 + grp) * U + u] = gsc * (float)s32;
+    for (int i = 0; i < NB; ++i) {
+      const int w = b + tid + i * kConsumers;
+      v[i] = w < NW ? __ldcg(x4 + w) : zero;
+    }
+    if (norm) {  // RMSNorm scale of x (sum of squares in double)
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < NB; ++i)
+        ss += (double)v[i].x * v[i].x + (double)v[i].y * v[i].y + (double)v[i].z * v[i].z +
+              (double)v[i].w * v[i].w;
+      ss = warp_sum(ss);
+      if (lane == 0) dred[warp] = ss;
+      consumer_sync();
+      double tot = 0.0;
+      for (int w = 0; w < kCWarps; ++w) tot += dred[w];
+      const float nscale = (float)(1.0 / sqrt(tot / (double)K + (double)A.eps));
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        v[i].x = v[i].x * nscale * nv[i].x;
+        v[i].y = v[i].y * nscale * nv[i].y;
+        v[i].z = v[i].z * nscale * nv[i].z;
+        v[i].w = v[i].w * nscale * nv[i].w;
       }
     }
+    if (P.need_f32) {
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const int w = b + tid + i * kConsumers;
+        if (w < NW) reinterpret_cast<float4*>(xf)[w] = v[i];
+      }
+    }
+    quant_words<NB>(v, b + tid, NW, U, limbw, ucon);
   }
   consumer_sync();  // limbs, per-unit constants (and the fp32 copy) are visible
   return true;
 }
 
+template <uint32_t TM>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A,
                                                            const __grid_constant__ Plan P) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -478,31 +523,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   // ---- shared-memory carve-up (must match fixed_bytes())
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);              // [kMaxStages]
   uint64_t* empty = full + kMaxStages;                             // [kMaxStages]
-  StageMap* map = reinterpret_cast<StageMap*>(smem + 128);         // 84 bytes
-  double* dred = reinterpret_cast<double*>(smem + 256);            // [16]
+  StageDesc* desc = reinterpret_cast<StageDesc*>(smem + 128);      // [kMaxStages]
+  double* dred = reinterpret_cast<double*>(smem + 128 + 32 * kMaxStages);  // [16]
   float* ucon = reinterpret_cast<float*>(smem + 384);              // g[2U], gm[2U], g6[4U]
   uint4* limb = reinterpret_cast<uint4*>(smem + 384 + ((32 * U + 127) & ~127));  // [12][U]
-  float* red = reinterpret_cast<float*>(limb + 12 * U);            // [red_floats]
-  float* xf = red + P.red_floats;                                  // [K] (F32 weights only)
+  float* red = reinterpret_cast<float*>(limb + 12 * U);            // [2][red_floats]
+  float* xf = red + 2 * P.red_floats;                              // [K] (F32 weights only)
   const uintptr_t sp = reinterpret_cast<uintptr_t>(xf + (P.need_f32 ? K : 0));
   uint8_t* stages = reinterpret_cast<uint8_t*>((sp + 127) & ~uintptr_t(127));
 
-  if (tid == kConsumers) {  // producer lane: stage map, barriers, first stages
-    build_map(P, map);
+  const int n_stages = count_stages(P);
+  if (n_stages == 0) {  // no rows for this CTA
+    grid_dep_launch();
+    return;
+  }
+  Cursor cur;
+  if (tid == kConsumers) {  // producer lane: barriers, first stages
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCWarps);
     }
     fence_barrier_init();
     const uint64_t pol = policy_evict_first();
-    const int n0 = map->first[P.nls];
-    for (int i = 0; i < NS && i < n0; ++i)
-      issue_stage(A, P, map, i, stages + (size_t)i * P.stage_bytes, &full[i], pol);
+    cur.ls = 0;
+    cta_rows(P, 0, &cur.r, &cur.hi);
+    cursor_seek(P, &cur);
+    for (int i = 0; i < NS && i < n_stages; ++i)
+      issue_next(A, P, &cur, stages + (size_t)i * P.stage_bytes, &desc[i], &full[i], pol);
   }
   grid_dep_launch();  // the next kernel may start its own weight prefetch
   __syncthreads();
-  const int n_stages = map->first[P.nls];
-  if (n_stages == 0) return;  // no rows for this CTA
 
   if (warp == kCWarps) {
     // ============================================================ producer
@@ -516,17 +566,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     for (int it = NS; it < n_stages; ++it) {
       const int slot = it % NS;
       mbar_wait(&empty[slot], (uint32_t)(it / NS - 1) & 1u, A.err);
-      issue_stage(A, P, map, it, stages + (size_t)slot * P.stage_bytes, &full[slot], pol);
+      issue_next(A, P, &cur, stages + (size_t)slot * P.stage_bytes, &desc[slot], &full[slot], pol);
     }
     return;
   }
 
   // ============================================================== consumers
-  const int NW = K / 4;
-  const bool live = NW <= 4 * kConsumers
-                        ? prologue<4>(A, P, tid, lane, warp, dred, limb, ucon, xf)
-                        : prologue<kMaxWordsPerThread>(A, P, tid, lane, warp, dred, limb, ucon, xf);
-  if (!live) return;
+  if (!prologue(A, P, tid, lane, warp, dred, limb, ucon, xf)) return;
 
   ActS act;
   act.limb = limb;
@@ -541,72 +587,81 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   // ---- main loop over the ring
   int chunk_it0 = 0;      // first stage of the current reduction chunk
   int64_t chunk_r0 = 0;   // its first row
+  int cbuf = 0;           // partial-sum buffer of the chunk
   for (int it = 0; it < n_stages; ++it) {
     const int slot = it % NS;
-    const int ls = stage_ls(P, map, it);
-    const LSeg& L = P.ls[ls];
-    int64_t r;
-    int n;
-    stage_rows(P, map, ls, it, &r, &n);
-    if (it == chunk_it0) chunk_r0 = r;
-    const GemvSeg& G = A.seg[L.first];
-    const int64_t rb = G.row_bytes;
-    const uint8_t* sb = stages + (size_t)slot * P.stage_bytes;
-    const uint8_t* base0 = sb + ((reinterpret_cast<uintptr_t>(G.w) + (uintptr_t)r * rb) & 15);
-    const int jr0 = (int)(r - chunk_r0);  // row of this stage inside the chunk
-    const int ck_rows = L.cs * L.m;       // row capacity of a chunk
     mbar_wait(&full[slot], (uint32_t)(it / NS) & 1u, A.err);
+    const StageDesc d = desc[slot];
+    const LSeg& L = P.ls[d.ls];
+    const GemvSeg& G = A.seg[L.first];
+    const int rb = (int)G.row_bytes;
+    const uint32_t type = G.type;
+    if (it == chunk_it0) chunk_r0 = d.r;
+    const int jr0 = (it - chunk_it0) * L.m;  // row of this stage inside the chunk
+    const int ck_rows = L.cs * L.m;          // row capacity of a chunk
+    float* rbuf = red + cbuf * P.red_floats;
+    const uint8_t* sb = stages + (size_t)slot * P.stage_bytes;
     if (busy) {
       float y[2];
+      const uint8_t* base0 = sb + d.off0;
       if (L.pair) {  // gate and up rows j share the activation
-        const GemvSeg& G1 = A.seg[L.first + 1];
-        const uint8_t* base1 =
-            sb + P.half_bytes + ((reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * rb) & 15);
-        for (int j = s; j < n; j += S) {
-          unit_rows<2>(G.type, base0 + (size_t)j * rb, base1 + (size_t)j * rb, u, act, y);
-          red[(jr0 + j) * Ur + u] = y[0];
-          red[(ck_rows + jr0 + j) * Ur + u] = y[1];
+        const uint8_t* base1 = sb + d.off1;
+        for (int j = s; j < d.n; j += S) {
+          unit_rows<2, TM>(type, base0 + j * rb, base1 + j * rb, u, act, y);
+          rbuf[(jr0 + j) * Ur + u] = y[0];
+          rbuf[(ck_rows + jr0 + j) * Ur + u] = y[1];
         }
       } else {  // rows j and j + S together
         int j = s;
-        for (; j + S < n; j += 2 * S) {
-          unit_rows<2>(G.type, base0 + (size_t)j * rb, base0 + (size_t)(j + S) * rb, u, act, y);
-          red[(jr0 + j) * Ur + u] = y[0];
-          red[(jr0 + j + S) * Ur + u] = y[1];
+        for (; j + S < d.n; j += 2 * S) {
+          unit_rows<2, TM>(type, base0 + j * rb, base0 + (j + S) * rb, u, act, y);
+          rbuf[(jr0 + j) * Ur + u] = y[0];
+          rbuf[(jr0 + j + S) * Ur + u] = y[1];
         }
-        if (j < n) {  // an odd row out
-          unit_rows<1>(G.type, base0 + (size_t)j * rb, base0 + (size_t)j * rb, u, act, y);
-          red[(jr0 + j) * Ur + u] = y[0];
+        if (j < d.n) {  // an odd row out
+          unit_rows<1, TM>(type, base0 + j * rb, base0 + j * rb, u, act, y);
+          rbuf[(jr0 + j) * Ur + u] = y[0];
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);  // the slot may be refilled
-    const bool seg_end = it + 1 == map->first[ls + 1];
-    if (!seg_end && it + 1 - chunk_it0 < L.cs) continue;
-    // ---- chunk complete: one thread per row sums its U partials (row stride
-    // Ur is odd: conflict-free), four interleaved accumulators added in a
-    // fixed order
+    if (!d.last && it + 1 - chunk_it0 < L.cs) continue;
+    // ---- chunk complete: every row total is summed by 4 threads (units
+    // u = q mod 4) whose results are added by two shuffles; for a pair the
+    // gate and up totals of a row sit in 8 consecutive lanes.  Fixed order,
+    // so deterministic.  The other buffer takes the next chunk, and this one
+    // is not written again before the next chunk's barrier.
     consumer_sync();
-    const int rows = (int)(r + n - chunk_r0);
-    for (int j = tid; j < rows; j += kConsumers) {
-      const float y0 = row_sum(red + j * Ur, U);
-      const float y1 = L.pair ? row_sum(red + (ck_rows + j) * Ur, U) : 0.0f;
-      const int64_t row = chunk_r0 + j;
-      if (L.pair) A.seg[L.first + 1].out[row] = silu_mul(y0, y1);
-      else if (G.mode == kAdd) G.out[row] += y0;
-      else G.out[row] = y0;
+    const int rows = jr0 + d.n;
+    const int nsum = rows * (L.pair + 1);
+    for (int b0 = 0; b0 < 4 * nsum; b0 += kConsumers) {  // warp-uniform trip count
+      const int idx = b0 + tid, q = idx & 3, sid = idx >> 2;
+      const int j = L.pair ? sid >> 1 : sid, h = L.pair ? sid & 1 : 0;
+      float t = 0.0f;
+      if (sid < nsum) {
+        const float* p = rbuf + (h * ck_rows + j) * Ur;
+        for (int v = q; v < U; v += 4) t += p[v];
+      }
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      const float other = __shfl_xor_sync(0xffffffffu, t, 4);  // up total for a pair's gate lane
+      if (sid < nsum && q == 0 && h == 0) {
+        const int64_t row = chunk_r0 + j;
+        if (L.pair) A.seg[L.first + 1].out[row] = silu_mul(t, other);
+        else if (G.mode == kAdd) G.out[row] += t;
+        else G.out[row] = t;
+      }
     }
-    consumer_sync();  // the partial-sum buffer may be reused
     chunk_it0 = it + 1;
+    cbuf ^= 1;
   }
 }
 
 // Work decomposition shared by the launcher and the kernel.
 bool make_plan(const GemvArgs& a, Plan* P) {
   if (a.nseg < 1 || a.nseg > 4 || a.K <= 0 || a.K % 64 != 0) return false;
-  if (a.K > 4 * kConsumers * kMaxWordsPerThread) return false;
-  if (a.norm_w && a.K > 4 * kConsumers * 4) return false;  // gains preloaded in registers
+  if (a.norm_w && a.K > 16 * kConsumers) return false;  // gains preloaded: one batch of words
   const int U = a.K / 64;
   if (U > kConsumers) return false;
   P->U = U;
@@ -660,28 +715,46 @@ bool make_plan(const GemvArgs& a, Plan* P) {
 
 size_t fixed_bytes(const Plan& P, int K) {
   const size_t b = 384 + (((size_t)32 * P.U + 127) & ~size_t(127)) + (size_t)12 * 16 * P.U +
-                   (size_t)P.red_floats * 4 + (P.need_f32 ? (size_t)K * 4 : 0);
+                   (size_t)2 * P.red_floats * 4 + (P.need_f32 ? (size_t)K * 4 : 0);
   return (b + 127) & ~size_t(127);
 }
 
-int sm_count() {
+// Kernel instantiations by type mix.
+template <uint32_t TM>
+void configure(int dev) {
+  static bool done[64] = {false};
+  if (dev < 0 || dev >= 64 || done[dev]) return;
+  cudaFuncSetAttribute(gemv_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  // the largest shared-memory carveout, so that two CTAs (this kernel's and
+  // the next kernel's) fit on an SM at once
+  cudaFuncSetAttribute(gemv_kernel<TM>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
+  done[dev] = true;
+}
+
+int sm_count(int dev) {
   static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
   if (!sms[dev]) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     sms[dev] = n > 0 && n <= 1024 ? n : 148;
   }
   return sms[dev];
 }
 
+template <uint32_t TM>
+cudaError_t launch_tm(const GemvArgs& a, const Plan& P, cudaLaunchConfig_t* cfg, int dev) {
+  configure<TM>(dev);
+  return cudaLaunchKernelEx(cfg, gemv_kernel<TM>, a, P);
+}
+
 }  // namespace
 
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl) {
-  const int sms = sm_count();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = sm_count(dev);
   Plan P;
   if (!make_plan(a, &P)) return cudaErrorInvalidValue;
   const size_t fixed = fixed_bytes(P, a.K);
@@ -690,7 +763,9 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl) {
   P.stages = ns < kMaxStages ? ns : kMaxStages;
   const size_t smem = fixed + (size_t)P.stages * P.stage_bytes;
   int64_t max_rows = 0;
+  uint32_t mask = 0;
   for (int i = 0; i < P.nls; ++i) max_rows = P.ls[i].rows > max_rows ? P.ls[i].rows : max_rows;
+  for (int i = 0; i < a.nseg; ++i) mask |= type_bit(a.seg[i].type);
   const int grid = (int)(max_rows < (int64_t)sms ? max_rows : (int64_t)sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -702,7 +777,12 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel, a, P);
+  // One instantiation serves every launch of a model's decode step (the
+  // K-quant mix, or Q8_0): consecutive kernels then run the same code, which
+  // stays in the instruction caches.
+  if ((mask & ~(kMQ4K | kMQ6K)) == 0) return launch_tm<kMQ4K | kMQ6K>(a, P, &cfg, dev);
+  if (mask == kMQ80) return launch_tm<kMQ80>(a, P, &cfg, dev);
+  return launch_tm<kMAll>(a, P, &cfg, dev);
 }
 
 }  // namespace rpgc
