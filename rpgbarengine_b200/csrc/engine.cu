@@ -96,6 +96,8 @@ struct Session {
   float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
   float *gate = nullptr, *up = nullptr, *logits = nullptr;
   int32_t *ids = nullptr, *gen_out = nullptr, *n_out = nullptr;
+  void* gscratch = nullptr;  // prefill GEMM: split activations
+  size_t gscratch_bytes = 0;
   DecodeState* st = nullptr;
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
@@ -365,6 +367,12 @@ int32_t session_create(int32_t model, int32_t max_seq) {
   s->gate = s->alloc<float>(s->cap * F);
   s->up = s->alloc<float>(s->cap * F);
   s->logits = s->alloc<float>(c.vocab);
+  {
+    int64_t kmax = H > qd ? H : qd;
+    kmax = kmax > F ? kmax : F;
+    s->gscratch_bytes = gemm_scratch_bytes(s->cap, kmax);
+    s->gscratch = s->alloc<uint8_t>(s->gscratch_bytes);
+  }
   s->ids = s->alloc<int32_t>(s->cap);
   s->gen_out = s->alloc<int32_t>(max_seq + 1);
   s->n_out = s->alloc<int32_t>(1);
@@ -494,9 +502,9 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
     check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
-    check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, cs), "gemm q");
-    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, cs), "gemm k");
-    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, cs), "gemm v");
+    check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, s->gscratch, s->gscratch_bytes, cs), "gemm q");
+    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs), "gemm k");
+    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs), "gemm v");
     QkvArgs qa{};
     qa.q = s->q;
     qa.k = s->k;
@@ -526,12 +534,12 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
     aa.pos0 = pos0;
     aa.n = nc;
     check(attn_prefill_launch(aa, cs), "attn prefill");
-    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, true, cs), "gemm o");
+    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, true, s->gscratch, s->gscratch_bytes, cs), "gemm o");
     check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
-    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, cs), "gemm gate");
-    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, cs), "gemm up");
+    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm gate");
+    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm up");
     check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
-    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, true, cs), "gemm down");
+    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, true, s->gscratch, s->gscratch_bytes, cs), "gemm down");
   }
 }
 
@@ -578,7 +586,8 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
           check(rmsnorm_rows_launch(s->x, m->out_norm, nc, c.hidden, c.rms_eps, s->h, s->stream),
                 "rmsnorm");
           check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, c.hidden,
-                            m->lm_head.row_bytes, s->h, nc, all_dev, c.vocab, false, s->stream),
+                            m->lm_head.row_bytes, s->h, nc, all_dev, c.vocab, false, s->gscratch,
+                            s->gscratch_bytes, s->stream),
                 "gemm lm_head");
           CK(cudaMemcpyAsync(all + t0 * c.vocab, all_dev, (size_t)nc * c.vocab * sizeof(float),
                              cudaMemcpyDeviceToHost, s->stream));
@@ -1024,9 +1033,14 @@ int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols, const 
     const int64_t rb = row_bytes_of(type, cols);
     if (!w || !X || !OUT || rows <= 0 || n <= 0 || rb < 0 || !kernel_type(type) || cols % 32)
       fail(RPGC_E_ARG, "bad matmul arguments");
-    check(gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT, rows, false,
-                      as_stream(stream)),
-          "gemm");
+    cudaStream_t cs = as_stream(stream);
+    const size_t sb = gemm_scratch_bytes(n, cols);
+    void* scratch = nullptr;
+    CK(cudaMallocAsync(&scratch, sb, cs));
+    const cudaError_t e = gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT,
+                                      rows, false, scratch, sb, cs);
+    cudaFreeAsync(scratch, cs);
+    check(e, "gemm");
     return RPGC_OK;
   });
 }

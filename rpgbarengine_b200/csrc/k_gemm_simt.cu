@@ -1,4 +1,6 @@
-// k_gemm_simt.cu -- prefill matmul over raw ggml blocks on CUDA cores.
+// k_gemm_simt.cu -- prefill matmul over raw ggml blocks on CUDA cores (for
+// shapes the tensor-core path does not take: K not a multiple of 64, or no
+// scratch), and the dispatch between the two.
 //
 // Replaces the reference's 8-token blocked kernel (MatMulBlocked,
 // src/matmul_avx2.cc:482-507): one dequantised weight tile in shared memory
@@ -87,9 +89,14 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(uint32_t type, const uin
 
 }  // namespace
 
+size_t gemm_scratch_bytes(int64_t n, int64_t K) { return gemm_tc_scratch_bytes(n, K); }
+
 cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K,
                         int64_t row_bytes, const float* X, int64_t n, float* out, int64_t ldo,
-                        bool accumulate, cudaStream_t s) {
+                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (scratch && scratch_bytes >= gemm_tc_scratch_bytes(n, K) && gemm_tc_supported(type, K))
+    return gemm_tc_launch(type, w, rows, K, row_bytes, X, n, out, ldo, accumulate, scratch,
+                          scratch_bytes, s);
   if (K % BK != 0 || (reinterpret_cast<uintptr_t>(X) & 15)) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
   gemm_simt_kernel<<<grid, 256, 0, s>>>(type, w, rows, K, row_bytes, X, n, out, ldo,

@@ -1,0 +1,475 @@
+// k_gemm_tc.cu -- prefill matmul over raw ggml blocks on the 5th-generation
+// tensor cores (tcgen05, sm_100a).
+//
+// Replaces the reference's blocked multi-token kernel (MatMulBlocked,
+// src/matmul_avx2.cc:482-507, called by QuantMatrix::MatMulBatch,
+// src/model.cc:32-69): OUT[t][r] (+)= dot(X[t], W[r]).
+//
+// Precision.  The tensor cores multiply fp16 operands into fp32.  Each
+// weight is dequantised bit-exactly (the reference's fp32 value) and split
+// into fp16 hi + lo (W = Wh + Wl to 2^-22); each token row of X is scaled by
+// a power of two and split the same way (X s = Xh + Xl).  Three products
+// Xh Wh + Xh Wl + Xl Wh accumulate over the whole K in TMEM; the dropped
+// Xl Wl term and the fp16 roundings leave ~2^-21 of sum|a w|, inside the
+// per-row gate 1e-5.  The epilogue divides by the token's scale.
+//
+// Data path (one CTA per 256 tokens x 128 weight rows):
+//   warp 0      TMA of the Xh / Xl tiles (SWIZZLE_128B, 64 K x 256 tokens)
+//   warp 1      TMEM allocation and the MMA issue (one thread): per 64-K
+//               stage 2 token blocks x 4 k16 steps x 3 products, M=128
+//               N=128 K=16 each, then tcgen05.commit frees the stage
+//   warps 2-9   dequantise the stage's weight tile into Wh / Wl (same
+//               swizzled K-major layout), then read the two 128x128 fp32
+//               accumulators back from TMEM and write OUT
+// Two 96 KB stages; all waits are bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rpgc {
+namespace {
+
+constexpr int TMt = 256;  // tokens per CTA
+constexpr int TNt = 128;  // weight rows per CTA
+constexpr int TKt = 64;   // K per stage (one 128-byte swizzle row of fp16)
+constexpr int kStg = 2;
+constexpr int kDeqWarps = 8;
+constexpr int kGThreads = (2 + kDeqWarps) * 32;
+constexpr uint32_t kTmemCols = 256;  // two 128 x 128 fp32 accumulators
+constexpr int kABytes = TMt * TKt * 2;   // one of Xh / Xl per stage
+constexpr int kWBytes = TNt * TKt * 2;   // one of Wh / Wl per stage
+constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
+constexpr int kGemmSmem = kStg * kStageBytes + 1024 + 1024;  // + barriers, + alignment slack
+
+struct GemmArgs {
+  const uint8_t* w;
+  int64_t rows, K, row_bytes;
+  int64_t n;              // tokens
+  float* out;
+  int64_t ldo;
+  const float* inv_scale; // per token
+  int32_t* err;
+  uint32_t type;
+  int32_t accumulate;
+};
+
+// ------------------------------------------------------------ tcgen05 glue
+// Shared-memory matrix descriptor, K-major with 128-byte swizzle: start
+// address, stride between 8-row groups 1024 B, descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc(const void* p) {
+  const uint64_t a = smem_u32(p);
+  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// Instruction descriptor: fp16 x fp16 -> fp32, both K-major, M = 128, N = 128.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(TNt >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ------------------------------------------------------------ dequant
+// Aligned little-endian words covering an arbitrary 2-byte-aligned global
+// range, realigned by funnel shifts: N words starting at p.
+template <int N>
+__device__ __forceinline__ void ldg_words(const uint8_t* p, uint32_t* out) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 3) * 8;
+  uint32_t prev = __ldg(w);
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t nx = __ldg(w + j + 1);
+    out[j] = __funnelshift_r(prev, nx, sh);
+    prev = nx;
+  }
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w0, uint32_t w1, uint32_t w2, int k) {
+  const uint32_t w = k < 4 ? w0 : (k < 8 ? w1 : w2);
+  return (w >> (8 * (k & 3))) & 0xFFu;
+}
+
+// The 32 weights [k0, k0 + 32) of one row (k0 a multiple of 32), bit-exact
+// with the reference's DequantizeRow (src/quant.cc:207-217, 327-354,
+// 396-429): the same fp32 operations in the same order, no contraction.
+__device__ __forceinline__ void deq32(uint32_t type, const uint8_t* row, int64_t k0, float* w) {
+  if (type == kQ4_K) {
+    const uint8_t* blk = row + (k0 >> 8) * 144;
+    const int i0 = (int)(k0 & 255), g = i0 >> 6, half = (i0 >> 5) & 1, j = 2 * g + half;
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * g));
+    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * g));
+    uint32_t sc, m;
+    if (j < 4) {
+      sc = byte_of(hdr.y, hdr.z, hdr.w, j) & 63u;
+      m = byte_of(hdr.y, hdr.z, hdr.w, j + 4) & 63u;
+    } else {
+      sc = (byte_of(hdr.y, hdr.z, hdr.w, j + 4) & 0x0Fu) | ((byte_of(hdr.y, hdr.z, hdr.w, j - 4) >> 6) << 4);
+      m = (byte_of(hdr.y, hdr.z, hdr.w, j + 4) >> 4) | ((byte_of(hdr.y, hdr.z, hdr.w, j) >> 6) << 4);
+    }
+    const float d = f16_bits_to_f32(hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(hdr.x >> 16);
+    const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)m);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t b = (q[l >> 2] >> (8 * (l & 3) + 4 * half)) & 15u;
+      w[l] = __fsub_rn(__fmul_rn(ds, (float)b), dm);
+    }
+  } else if (type == kQ6_K) {
+    const uint8_t* blk = row + (k0 >> 8) * 210;
+    const int i0 = (int)(k0 & 255), h = i0 >> 7, qd = (i0 & 127) >> 5;
+    uint32_t ql[8], qh[8], sw[1], dw[1];
+    ldg_words<8>(blk + 64 * h + 32 * (qd & 1), ql);
+    ldg_words<8>(blk + 128 + 32 * h, qh);
+    ldg_words<1>(blk + 192 + 8 * h + 2 * qd, sw);
+    ldg_words<1>(blk + 208, dw);
+    const float d = f16_bits_to_f32(dw[0] & 0xFFFFu);
+    const float dsc0 = __fmul_rn(d, (float)(int)(int8_t)(sw[0] & 0xFFu));
+    const float dsc1 = __fmul_rn(d, (float)(int)(int8_t)((sw[0] >> 8) & 0xFFu));
+    const int nsh = qd >= 2 ? 4 : 0;
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t nib = (ql[l >> 2] >> (8 * (l & 3) + nsh)) & 15u;
+      const uint32_t hb = (qh[l >> 2] >> (8 * (l & 3) + 2 * qd)) & 3u;
+      const int q = (int)(nib | (hb << 4)) - 32;
+      w[l] = __fmul_rn(l < 16 ? dsc0 : dsc1, (float)q);
+    }
+  } else if (type == kQ8_0) {
+    const uint8_t* blk = row + (k0 >> 5) * 34;
+    uint32_t v[9];
+    ldg_words<9>(blk, v);
+    const float d = f16_bits_to_f32(v[0] & 0xFFFFu);
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {  // byte 2 + l of the block
+      const int b = (int)(int8_t)((v[(l + 2) >> 2] >> (8 * ((l + 2) & 3))) & 0xFFu);
+      w[l] = __fmul_rn((float)b, d);
+    }
+  } else {  // F32
+    const float4* p = reinterpret_cast<const float4*>(row + k0 * 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldg(p + i);
+      w[4 * i] = v.x;
+      w[4 * i + 1] = v.y;
+      w[4 * i + 2] = v.z;
+      w[4 * i + 3] = v.w;
+    }
+  }
+}
+
+// fp16 hi/lo split of 8 values packed for a 16-byte store.
+__device__ __forceinline__ void split8(const float* v, uint4* hi, uint4* lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half a = __float2half_rn(v[2 * i]), b = __float2half_rn(v[2 * i + 1]);
+    const __half c = __float2half_rn(v[2 * i] - __half2float(a));
+    const __half d = __float2half_rn(v[2 * i + 1] - __half2float(b));
+    h[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+    l[i] = (uint32_t)__half_as_ushort(c) | ((uint32_t)__half_as_ushort(d) << 16);
+  }
+  *hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Byte offset of 16-byte chunk c of row r in a K-major tile with 128-byte
+// rows and the 128-byte swizzle (chunk index XOR row mod 8).
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_h,
+                                                               const __grid_constant__ CUtensorMap tm_l,
+                                                               const GemmArgs g) {
+  extern __shared__ uint8_t gsm_raw[];
+  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStg * kStageBytes);
+  uint64_t* full_a = bars;              // [kStg] TMA bytes of the X tiles
+  uint64_t* full_w = bars + kStg;       // [kStg] the dequant warps
+  uint64_t* empty = bars + 2 * kStg;    // [kStg] MMAs of the stage done
+  uint64_t* acc_full = bars + 3 * kStg; // all MMAs done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kStg + 1);
+  auto Ah = [&](int s) { return gsm + s * kStageBytes; };
+  auto Al = [&](int s) { return gsm + s * kStageBytes + kABytes; };
+  auto Wh = [&](int s) { return gsm + s * kStageBytes + 2 * kABytes; };
+  auto Wl = [&](int s) { return gsm + s * kStageBytes + 2 * kABytes + kWBytes; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * TNt;  // first weight row
+  const int t0 = (int)blockIdx.y * TMt;          // first token
+  const int nk = (int)(g.K / TKt);
+
+  if (tid == 0) {
+    for (int s = 0; s < kStg; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_w[s], kDeqWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (X tiles)
+    if (lane == 0) {
+      for (int c = 0; c < nk; ++c) {
+        const int s = c % kStg;
+        if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
+        mbar_arrive_expect_tx(&full_a[s], 2 * kABytes);
+        tma_load_2d(Ah(s), &tm_h, c * TKt, t0, &full_a[s]);
+        tma_load_2d(Al(s), &tm_l, c * TKt, t0, &full_a[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issue
+    if (lane == 0) {
+      for (int c = 0; c < nk; ++c) {
+        const int s = c % kStg;
+        const uint32_t ph = (uint32_t)(c / kStg) & 1u;
+        mbar_wait(&full_a[s], ph, g.err);
+        mbar_wait(&full_w[s], ph, g.err);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TKt / 16; ++kk) {
+          const uint64_t bh = sdesc(Wh(s) + kk * 32), bl = sdesc(Wl(s) + kk * 32);
+#pragma unroll
+          for (int mb = 0; mb < 2; ++mb) {
+            const uint64_t ah = sdesc(Ah(s) + mb * (128 * 128) + kk * 32);
+            const uint64_t al = sdesc(Al(s) + mb * (128 * 128) + kk * 32);
+            const uint32_t d = tmem + (uint32_t)(mb * 128);
+            mma_f16(d, ah, bh, (c > 0 || kk > 0) ? 1u : 0u);
+            mma_f16(d, ah, bl, 1u);
+            mma_f16(d, al, bh, 1u);
+          }
+        }
+        mma_commit(&empty[s]);  // the stage may be refilled once these MMAs are done
+      }
+      mma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------ weight dequant
+    const int dt = tid - 64;                 // 0..255
+    const int r = dt >> 1, half = dt & 1;    // tile row, 32-element half of the stage's 64
+    const int64_t gr = n0 + r;
+    const uint8_t* row = g.w + gr * g.row_bytes;
+    for (int c = 0; c < nk; ++c) {
+      const int s = c % kStg;
+      if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
+      float w[32];
+      if (gr < g.rows) {
+        deq32(g.type, row, (int64_t)c * TKt + 32 * half, w);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = 0.0f;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 hi, lo;
+        split8(w + 8 * q, &hi, &lo);
+        const uint32_t off = swz(r, 4 * half + q);
+        *reinterpret_cast<uint4*>(Wh(s) + off) = hi;
+        *reinterpret_cast<uint4*>(Wl(s) + off) = lo;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_w[s]);
+    }
+    // ------------------------------------------------ epilogue
+    mbar_wait(acc_full, 0, g.err);
+    tc_fence_after();
+    const int ew = warp - 2, mb = ew >> 2, quarter = warp & 3;
+    const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
+    const int64_t t = t0 + tl;
+    const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < TNt / 32; ++j) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mb * 128 + 32 * j), v);
+      if (t < g.n) {
+        float* o = g.out + t * g.ldo + n0 + 32 * j;
+        const int64_t lim = g.rows - (n0 + 32 * j);  // columns left in the matrix
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < lim) {
+            const float y = v[i] * inv;
+            o[i] = g.accumulate ? o[i] + y : y;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// Per token: power-of-two scale s (max |x| s in [2^14, 2^15)), Xh = fp16(x s),
+// Xl = fp16(x s - Xh), 1/s.
+__global__ void __launch_bounds__(256) act_split_kernel(const float* __restrict__ X, int64_t K,
+                                                        __half* __restrict__ xh, __half* __restrict__ xl,
+                                                        float* __restrict__ inv_scale) {
+  __shared__ float red[8];
+  const int64_t t = blockIdx.x;
+  const float* x = X + t * K;
+  float m = 0.0f;
+  for (int64_t k = threadIdx.x; k < K; k += 256) m = fmaxf(m, fabsf(x[k]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mx = 0.0f;
+  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);  // biased exponent of the max
+  // scale 2^(141 - e): max |x| s in [2^14, 2^15); clamped to stay finite
+  int se = 141 - e;
+  se = se > 100 ? 100 : (se < -100 ? -100 : se);
+  const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
+  for (int64_t k = threadIdx.x; k < K; k += 256) {
+    const float v = x[k] * s;
+    const __half h = __float2half_rn(v);
+    xh[t * K + k] = h;
+    xl[t * K + k] = __float2half_rn(v - __half2float(h));
+  }
+  if (threadIdx.x == 0) inv_scale[t] = 1.0f / s;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_x_map(CUtensorMap* m, const __half* base, int64_t n, int64_t K) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)n};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)TKt, (cuuint32_t)TMt};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t gemm_tc_scratch_bytes(int64_t n, int64_t K) {
+  return (size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 256;
+}
+
+bool gemm_tc_supported(uint32_t type, int64_t K) {
+  return K % TKt == 0 && K <= (int64_t)1 << 30 &&
+         (type == kQ4_K || type == kQ6_K || type == kQ8_0 || type == kF32);
+}
+
+cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
+                           const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
+                           void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (!gemm_tc_supported(type, K) || n <= 0 || rows <= 0 ||
+      scratch_bytes < gemm_tc_scratch_bytes(n, K) || (reinterpret_cast<uintptr_t>(scratch) & 255))
+    return cudaErrorInvalidValue;
+  if (type == kF32 && (row_bytes & 15)) return cudaErrorInvalidValue;
+  __half* xh = static_cast<__half*>(scratch);
+  __half* xl = xh + n * K;
+  float* inv = reinterpret_cast<float*>(xl + n * K);
+  act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  CUtensorMap mh, ml;
+  if (!make_x_map(&mh, xh, n, K) || !make_x_map(&ml, xl, n, K)) return cudaErrorInvalidValue;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  GemmArgs g;
+  g.w = w;
+  g.rows = rows;
+  g.K = K;
+  g.row_bytes = row_bytes;
+  g.n = n;
+  g.out = out;
+  g.ldo = ldo;
+  g.inv_scale = inv;
+  g.err = nullptr;
+  g.type = type;
+  g.accumulate = accumulate ? 1 : 0;
+  dim3 grid((unsigned)((rows + TNt - 1) / TNt), (unsigned)((n + TMt - 1) / TMt));
+  gemm_tc_kernel<<<grid, kGThreads, kGemmSmem, s>>>(mh, ml, g);
+  return cudaGetLastError();
+}
+
+}  // namespace rpgc

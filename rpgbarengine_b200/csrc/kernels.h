@@ -55,9 +55,19 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
+// Prefill matmul OUT[t][r] (+)= dot(X[t], W[r]).  With scratch of at least
+// gemm_scratch_bytes(n, K) bytes (256-byte aligned) and K a multiple of 64 it
+// runs on the tensor cores (tcgen05); otherwise on CUDA cores.
 cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K,
                         int64_t row_bytes, const float* X, int64_t n, float* out, int64_t ldo,
-                        bool accumulate, cudaStream_t s);
+                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s);
+size_t gemm_scratch_bytes(int64_t n, int64_t K);
+// tensor-core path (k_gemm_tc.cu)
+size_t gemm_tc_scratch_bytes(int64_t n, int64_t K);
+bool gemm_tc_supported(uint32_t type, int64_t K);
+cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
+                           const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
+                           void* scratch, size_t scratch_bytes, cudaStream_t s);
 
 // -------------------------------------------------------------- others
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,
