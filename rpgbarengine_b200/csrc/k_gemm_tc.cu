@@ -51,8 +51,9 @@ struct GemmArgs {
   const uint8_t* w;
   int64_t rows, K, row_bytes;
   int64_t n;              // tokens
-  float* out;
+  float* out;             // ks == 1: OUT; else the partial sums [ks][n][rows]
   int64_t ldo;
+  int32_t ks;             // K partitions (gridDim.z)
   const float* inv_scale; // per token
   int32_t* err;
   uint32_t type;
@@ -140,84 +141,110 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w0, uint32_t w1, uint32_t w
   return (w >> (8 * (k & 3))) & 0xFFu;
 }
 
-// The 32 weights [k0, k0 + 32) of one row (k0 a multiple of 32), bit-exact
-// with the reference's DequantizeRow (src/quant.cc:207-217, 327-354,
-// 396-429): the same fp32 operations in the same order, no contraction.
-__device__ __forceinline__ void deq32(uint32_t type, const uint8_t* row, int64_t k0, float* w) {
+// Raw bytes of 32 weights [k0, k0 + 32) of one row (k0 a multiple of 32),
+// fetched one stage ahead of their use so that the global-memory latency
+// hides behind the previous stage's dequantisation.
+constexpr int kRaw = 20;  // words
+__device__ __forceinline__ void fetch32(uint32_t type, const uint8_t* row, int64_t k0, uint32_t* r) {
   if (type == kQ4_K) {
     const uint8_t* blk = row + (k0 >> 8) * 144;
-    const int i0 = (int)(k0 & 255), g = i0 >> 6, half = (i0 >> 5) & 1, j = 2 * g + half;
+    const int g = (int)(k0 & 255) >> 6;
     const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
     const uint4 qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * g));
     const uint4 qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * g));
-    uint32_t sc, m;
-    if (j < 4) {
-      sc = byte_of(hdr.y, hdr.z, hdr.w, j) & 63u;
-      m = byte_of(hdr.y, hdr.z, hdr.w, j + 4) & 63u;
-    } else {
-      sc = (byte_of(hdr.y, hdr.z, hdr.w, j + 4) & 0x0Fu) | ((byte_of(hdr.y, hdr.z, hdr.w, j - 4) >> 6) << 4);
-      m = (byte_of(hdr.y, hdr.z, hdr.w, j + 4) >> 4) | ((byte_of(hdr.y, hdr.z, hdr.w, j) >> 6) << 4);
-    }
-    const float d = f16_bits_to_f32(hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(hdr.x >> 16);
-    const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)m);
-    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-    for (int l = 0; l < 32; ++l) {
-      const uint32_t b = (q[l >> 2] >> (8 * (l & 3) + 4 * half)) & 15u;
-      w[l] = __fsub_rn(__fmul_rn(ds, (float)b), dm);
-    }
+    r[0] = hdr.x; r[1] = hdr.y; r[2] = hdr.z; r[3] = hdr.w;
+    r[4] = qa.x; r[5] = qa.y; r[6] = qa.z; r[7] = qa.w;
+    r[8] = qb.x; r[9] = qb.y; r[10] = qb.z; r[11] = qb.w;
   } else if (type == kQ6_K) {
     const uint8_t* blk = row + (k0 >> 8) * 210;
     const int i0 = (int)(k0 & 255), h = i0 >> 7, qd = (i0 & 127) >> 5;
-    uint32_t ql[8], qh[8], sw[1], dw[1];
-    ldg_words<8>(blk + 64 * h + 32 * (qd & 1), ql);
-    ldg_words<8>(blk + 128 + 32 * h, qh);
-    ldg_words<1>(blk + 192 + 8 * h + 2 * qd, sw);
-    ldg_words<1>(blk + 208, dw);
-    const float d = f16_bits_to_f32(dw[0] & 0xFFFFu);
-    const float dsc0 = __fmul_rn(d, (float)(int)(int8_t)(sw[0] & 0xFFu));
-    const float dsc1 = __fmul_rn(d, (float)(int)(int8_t)((sw[0] >> 8) & 0xFFu));
+    ldg_words<8>(blk + 64 * h + 32 * (qd & 1), r);
+    ldg_words<8>(blk + 128 + 32 * h, r + 8);
+    ldg_words<1>(blk + 192 + 8 * h + 2 * qd, r + 16);
+    ldg_words<1>(blk + 208, r + 17);
+  } else if (type == kQ8_0) {
+    ldg_words<9>(row + (k0 >> 5) * 34, r);
+  }
+}
+
+// Small non-negative integer -> float without the conversion unit: the
+// float with bits 0x4B000000 | q is 2^23 + q.
+__device__ __forceinline__ float small_int_f(uint32_t q) {
+  return __uint_as_float(0x4B000000u | q) - 8388608.0f;
+}
+
+// kWScale * the 32 weights from their raw bytes: the reference's
+// DequantizeRow values (src/quant.cc:207-217, 327-354, 396-429), computed
+// with the same fp32 operations in the same order (no contraction) on scales
+// premultiplied by the power of two kWScale, which commutes with every
+// rounding.  The factor keeps the fp16 lo halves of the split out of the
+// subnormal range.  F32 rows are read here.
+constexpr float kWScale = 256.0f;
+__device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, const uint8_t* row,
+                                          int64_t k0, float* w) {
+  if (type == kQ4_K) {
+    const int i0 = (int)(k0 & 255), g = i0 >> 6, half = (i0 >> 5) & 1, j = 2 * g + half;
+    uint32_t sc, m;
+    if (j < 4) {
+      sc = byte_of(r[1], r[2], r[3], j) & 63u;
+      m = byte_of(r[1], r[2], r[3], j + 4) & 63u;
+    } else {
+      sc = (byte_of(r[1], r[2], r[3], j + 4) & 0x0Fu) | ((byte_of(r[1], r[2], r[3], j - 4) >> 6) << 4);
+      m = (byte_of(r[1], r[2], r[3], j + 4) >> 4) | ((byte_of(r[1], r[2], r[3], j) >> 6) << 4);
+    }
+    const float d = f16_bits_to_f32(r[0] & 0xFFFFu), dmin = f16_bits_to_f32(r[0] >> 16);
+    const float ds = __fmul_rn(d, (float)sc) * kWScale, dm = __fmul_rn(dmin, (float)m) * kWScale;
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t b = (r[4 + (l >> 2)] >> (8 * (l & 3) + 4 * half)) & 15u;
+      w[l] = __fsub_rn(__fmul_rn(ds, small_int_f(b)), dm);
+    }
+  } else if (type == kQ6_K) {
+    const int qd = ((int)(k0 & 255) & 127) >> 5;
+    const float d = f16_bits_to_f32(r[17] & 0xFFFFu);
+    const float dsc0 = __fmul_rn(d, (float)(int)(int8_t)(r[16] & 0xFFu)) * kWScale;
+    const float dsc1 = __fmul_rn(d, (float)(int)(int8_t)((r[16] >> 8) & 0xFFu)) * kWScale;
     const int nsh = qd >= 2 ? 4 : 0;
 #pragma unroll
     for (int l = 0; l < 32; ++l) {
-      const uint32_t nib = (ql[l >> 2] >> (8 * (l & 3) + nsh)) & 15u;
-      const uint32_t hb = (qh[l >> 2] >> (8 * (l & 3) + 2 * qd)) & 3u;
-      const int q = (int)(nib | (hb << 4)) - 32;
-      w[l] = __fmul_rn(l < 16 ? dsc0 : dsc1, (float)q);
+      const uint32_t nib = (r[l >> 2] >> (8 * (l & 3) + nsh)) & 15u;
+      const uint32_t hb = (r[8 + (l >> 2)] >> (8 * (l & 3) + 2 * qd)) & 3u;
+      const float q = small_int_f(nib | (hb << 4)) - 32.0f;  // exact
+      w[l] = __fmul_rn(l < 16 ? dsc0 : dsc1, q);
     }
   } else if (type == kQ8_0) {
-    const uint8_t* blk = row + (k0 >> 5) * 34;
-    uint32_t v[9];
-    ldg_words<9>(blk, v);
-    const float d = f16_bits_to_f32(v[0] & 0xFFFFu);
+    const float d = f16_bits_to_f32(r[0] & 0xFFFFu) * kWScale;
 #pragma unroll
-    for (int l = 0; l < 32; ++l) {  // byte 2 + l of the block
-      const int b = (int)(int8_t)((v[(l + 2) >> 2] >> (8 * ((l + 2) & 3))) & 0xFFu);
-      w[l] = __fmul_rn((float)b, d);
+    for (int l = 0; l < 32; ++l) {  // byte 2 + l of the block, signed
+      const uint32_t b = (r[(l + 2) >> 2] >> (8 * ((l + 2) & 3))) & 0xFFu;
+      w[l] = __fmul_rn(small_int_f(b ^ 0x80u) - 128.0f, d);
     }
   } else {  // F32
     const float4* p = reinterpret_cast<const float4*>(row + k0 * 4);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float4 v = __ldg(p + i);
-      w[4 * i] = v.x;
-      w[4 * i + 1] = v.y;
-      w[4 * i + 2] = v.z;
-      w[4 * i + 3] = v.w;
+      w[4 * i] = v.x * kWScale;
+      w[4 * i + 1] = v.y * kWScale;
+      w[4 * i + 2] = v.z * kWScale;
+      w[4 * i + 3] = v.w * kWScale;
     }
   }
 }
 
 // fp16 hi/lo split of 8 values packed for a 16-byte store.
+// hi = v rounded to 11 significant bits by integer arithmetic (exactly an
+// fp16 value in range), lo = v - hi exactly, then both packed to fp16.
 __device__ __forceinline__ void split8(const float* v, uint4* hi, uint4* lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __half a = __float2half_rn(v[2 * i]), b = __float2half_rn(v[2 * i + 1]);
-    const __half c = __float2half_rn(v[2 * i] - __half2float(a));
-    const __half d = __float2half_rn(v[2 * i + 1] - __half2float(b));
-    h[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-    l[i] = (uint32_t)__half_as_ushort(c) | ((uint32_t)__half_as_ushort(d) << 16);
+    const float a = __uint_as_float((__float_as_uint(v[2 * i]) + 0x1000u) & 0xFFFFE000u);
+    const float b = __uint_as_float((__float_as_uint(v[2 * i + 1]) + 0x1000u) & 0xFFFFE000u);
+    const __half2 ph = __floats2half2_rn(a, b);
+    const __half2 pl = __floats2half2_rn(v[2 * i] - a, v[2 * i + 1] - b);
+    h[i] = *reinterpret_cast<const uint32_t*>(&ph);
+    l[i] = *reinterpret_cast<const uint32_t*>(&pl);
   }
   *hi = make_uint4(h[0], h[1], h[2], h[3]);
   *lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -246,7 +273,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n0 = (int64_t)blockIdx.x * TNt;  // first weight row
   const int t0 = (int)blockIdx.y * TMt;          // first token
-  const int nk = (int)(g.K / TKt);
+  const int nk_all = (int)(g.K / TKt);
+  const int kc0 = (int)((int64_t)nk_all * blockIdx.z / g.ks);  // this CTA's stages
+  const int nk = (int)((int64_t)nk_all * (blockIdx.z + 1) / g.ks) - kc0;
 
   if (tid == 0) {
     for (int s = 0; s < kStg; ++s) {
@@ -276,8 +305,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
         const int s = c % kStg;
         if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
         mbar_arrive_expect_tx(&full_a[s], 2 * kABytes);
-        tma_load_2d(Ah(s), &tm_h, c * TKt, t0, &full_a[s]);
-        tma_load_2d(Al(s), &tm_l, c * TKt, t0, &full_a[s]);
+        tma_load_2d(Ah(s), &tm_h, (kc0 + c) * TKt, t0, &full_a[s]);
+        tma_load_2d(Al(s), &tm_l, (kc0 + c) * TKt, t0, &full_a[s]);
       }
     }
   } else if (warp == 1) {
@@ -312,16 +341,26 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
     const int r = dt >> 1, half = dt & 1;    // tile row, 32-element half of the stage's 64
     const int64_t gr = n0 + r;
     const uint8_t* row = g.w + gr * g.row_bytes;
+    // Raw bytes run two stages ahead: the loads for stage c + 2 are issued
+    // after stage c is published (the proxy fence would otherwise wait for
+    // them), and consumed after stage c + 1 has been processed.
+    const bool live = gr < g.rows;
+    uint32_t raw0[kRaw], raw1[kRaw];
+    if (live) {
+      fetch32(g.type, row, (int64_t)kc0 * TKt + 32 * half, raw0);
+      if (nk > 1) fetch32(g.type, row, (int64_t)(kc0 + 1) * TKt + 32 * half, raw1);
+    }
     for (int c = 0; c < nk; ++c) {
       const int s = c % kStg;
-      if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
+      const int64_t k0 = (int64_t)(kc0 + c) * TKt + 32 * half;
       float w[32];
-      if (gr < g.rows) {
-        deq32(g.type, row, (int64_t)c * TKt + 32 * half, w);
+      if (live) {
+        convert32(g.type, raw0, row, k0, w);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) w[i] = 0.0f;
       }
+      if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 hi, lo;
@@ -333,6 +372,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMA
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_w[s]);
+#pragma unroll
+      for (int i = 0; i < kRaw; ++i) raw0[i] = raw1[i];
+      if (live && c + 2 < nk) fetch32(g.type, row, k0 + 2 * TKt, raw1);
     }
     // ------------------------------------------------ epilogue
     mbar_wait(acc_full, 0, g.err);
@@ -341,18 +383,20 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
     const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
     const int64_t t = t0 + tl;
     const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
+    const bool part = g.ks > 1;
+    float* obase = part ? g.out + ((int64_t)blockIdx.z * g.n + t) * g.rows : g.out + t * g.ldo;
 #pragma unroll 1
     for (int j = 0; j < TNt / 32; ++j) {
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mb * 128 + 32 * j), v);
       if (t < g.n) {
-        float* o = g.out + t * g.ldo + n0 + 32 * j;
+        float* o = obase + n0 + 32 * j;
         const int64_t lim = g.rows - (n0 + 32 * j);  // columns left in the matrix
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if (i < lim) {
             const float y = v[i] * inv;
-            o[i] = g.accumulate ? o[i] + y : y;
+            o[i] = (g.accumulate && !part) ? o[i] + y : y;
           }
         }
       }
@@ -393,7 +437,20 @@ __global__ void __launch_bounds__(256) act_split_kernel(const float* __restrict_
     xh[t * K + k] = h;
     xl[t * K + k] = __float2half_rn(v - __half2float(h));
   }
-  if (threadIdx.x == 0) inv_scale[t] = 1.0f / s;
+  if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);  // undoes both scalings
+}
+
+// OUT[t][r] (+)= sum over the K partitions of the partial sums, in order.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int ks,
+                                                            int64_t n, int64_t rows, float* out,
+                                                            int64_t ldo, int accumulate) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n * rows) return;
+  const int64_t t = i / rows, r = i - t * rows;
+  float y = 0.0f;
+  for (int p = 0; p < ks; ++p) y += part[(int64_t)p * n * rows + i];
+  float* o = out + t * ldo + r;
+  *o = accumulate ? *o + y : y;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -423,8 +480,12 @@ bool make_x_map(CUtensorMap* m, const __half* base, int64_t n, int64_t K) {
 
 }  // namespace
 
+// Split-K partial sums are bounded by n x kMaxPartRows floats.
+constexpr int64_t kMaxPartRows = 9216;
+
 size_t gemm_tc_scratch_bytes(int64_t n, int64_t K) {
-  return (size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 256;
+  return (((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255) +
+         (size_t)n * kMaxPartRows * sizeof(float) + 256;
 }
 
 bool gemm_tc_supported(uint32_t type, int64_t K) {
@@ -442,6 +503,9 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   __half* xh = static_cast<__half*>(scratch);
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
+  float* part = reinterpret_cast<float*>(
+      static_cast<uint8_t*>(scratch) +
+      (((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255));
   act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -467,8 +531,29 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   g.err = nullptr;
   g.type = type;
   g.accumulate = accumulate ? 1 : 0;
-  dim3 grid((unsigned)((rows + TNt - 1) / TNt), (unsigned)((n + TMt - 1) / TMt));
+  // Split K when the tiles alone leave SMs idle: enough partitions to fill
+  // the GPU once, at least 8 stages each, partial sums within the scratch.
+  static int sms[64] = {0};
+  if (dev >= 0 && dev < 64 && !sms[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = v > 0 ? v : 148;
+  }
+  const int nsm = (dev >= 0 && dev < 64) ? sms[dev] : 148;
+  const int64_t tiles = ((rows + TNt - 1) / TNt) * ((n + TMt - 1) / TMt);
+  int64_t ks = tiles >= nsm ? 1 : nsm / tiles;
+  const int64_t nk = K / TKt;
+  if (ks > nk / 8) ks = nk / 8 > 0 ? nk / 8 : 1;
+  while (ks > 1 && ks * rows > kMaxPartRows) --ks;
+  g.ks = (int32_t)ks;
+  g.out = ks > 1 ? part : out;
+  dim3 grid((unsigned)((rows + TNt - 1) / TNt), (unsigned)((n + TMt - 1) / TMt), (unsigned)ks);
   gemm_tc_kernel<<<grid, kGThreads, kGemmSmem, s>>>(mh, ml, g);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || ks == 1) return e;
+  const int64_t total = n * rows;
+  splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(part, (int)ks, n, rows, out, ldo,
+                                                                       accumulate ? 1 : 0);
   return cudaGetLastError();
 }
 
