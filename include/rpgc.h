@@ -86,6 +86,10 @@ typedef struct rpgc_gen_opts {
 
 /* ------------------------------------------------------------- library */
 RPGC_API const char* rpgc_version(void);
+/* Kernels the library has enqueued on any device since it was loaded (a
+ * decode-step graph replay counts each kernel in it).  Instrumentation for
+ * benchmarks; no counterpart in the reference. */
+RPGC_API int64_t rpgc_kernel_launches(void);
 /* Thread-local; valid until the next call on this thread; do not free
  * (src/common.cc:11, 54-56). */
 RPGC_API const char* rpgc_last_error(void);

@@ -74,6 +74,7 @@ def lib() -> C.CDLL:
     vp, i32, i64, u32, f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint32, C.c_float
     sig = {
         "rpgc_version": ([], C.c_char_p),
+        "rpgc_kernel_launches": ([], C.c_int64),
         "rpgc_last_error": ([], C.c_char_p),
         "rpgc_device_count": ([], C.c_int),
         "rpgc_model_upload": ([C.c_int, C.POINTER(ModelConfig), C.POINTER(Tensor), i32], i32),
@@ -269,6 +270,11 @@ def _stream(stream) -> int:
         import torch
         return int(torch.cuda.current_stream().cuda_stream)
     return int(stream)
+
+
+def kernel_launches() -> int:
+    """Kernels the library has enqueued so far (graph replays count their kernels)."""
+    return int(lib().rpgc_kernel_launches())
 
 
 def dequantize_rows(ggml_type: int, w, rows: int, cols: int, out=None, stream=None):

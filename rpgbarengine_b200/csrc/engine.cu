@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <climits>
 #include <cstring>
 #include <memory>
@@ -101,6 +102,7 @@ struct Session {
   DecodeState* st = nullptr;
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
+  int64_t graph_kernels = 0;  // kernels in step_graph
   std::vector<void*> allocs;
   std::mutex mu;
 
@@ -616,10 +618,17 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
   s->has_logits = true;
 }
 
+// Kernel launches enqueued by this thread while it captures a graph are
+// counted into the graph, not as launches.
+thread_local int64_t* t_capture_count = nullptr;
+std::atomic<int64_t> g_launches{0};
+
 void capture_step_graph(Session* s) {
   if (s->step_graph) return;
   cudaGraph_t g = nullptr;
+  int64_t nk = 0;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  t_capture_count = &nk;
   try {
     const Model* m = s->m;
     SampleArgs sa{};
@@ -637,14 +646,17 @@ void capture_step_graph(Session* s) {
     check(sample_launch(sa, s->stream), "sample");
     launch_layers_step(s);
   } catch (...) {
+    t_capture_count = nullptr;
     cudaStreamEndCapture(s->stream, &g);
     if (g) cudaGraphDestroy(g);
     throw;
   }
+  t_capture_count = nullptr;
   CK(cudaStreamEndCapture(s->stream, &g));
   const cudaError_t e = cudaGraphInstantiate(&s->step_graph, g, 0);
   cudaGraphDestroy(g);
   CK(e);
+  s->graph_kernels = nk;
 }
 
 // Shared body of rpgc_generate / rpgc_generate_device.  Returns the number of
@@ -677,7 +689,10 @@ int64_t generate(Session* s, const rpgc_gen_opts& o, bool sync_host) {
   const int64_t batch = 8;
   for (int64_t i = 0; i < steps; i += batch) {
     const int64_t nb = std::min(batch, steps - i);
-    for (int64_t j = 0; j < nb; ++j) CK(cudaGraphLaunch(s->step_graph, s->stream));
+    for (int64_t j = 0; j < nb; ++j) {
+      CK(cudaGraphLaunch(s->step_graph, s->stream));
+      count_launches(s->graph_kernels);
+    }
     if (sync_host && o.n_stop > 0 && i + nb < steps) {
       int32_t done = 0;
       CK(cudaMemcpyAsync(&s->st_host->done, &s->st->done, sizeof(int32_t), cudaMemcpyDeviceToHost,
@@ -732,6 +747,12 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 // Lets other translation units of the library report through rpgc_last_error().
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
+void count_launches(int64_t k) {
+  if (t_capture_count) *t_capture_count += k;
+  else g_launches.fetch_add(k, std::memory_order_relaxed);
+}
+int64_t launches_enqueued() { return g_launches.load(std::memory_order_relaxed); }
+
 }  // namespace rpgc
 
 using namespace rpgc;
@@ -739,6 +760,8 @@ using namespace rpgc;
 extern "C" {
 
 const char* rpgc_version(void) { return "0.1.0-b200"; }
+
+int64_t rpgc_kernel_launches(void) { return launches_enqueued(); }
 const char* rpgc_last_error(void) { return g_last_error.c_str(); }
 
 int rpgc_device_count(void) {

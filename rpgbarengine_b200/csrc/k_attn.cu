@@ -417,7 +417,9 @@ cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s) {
   if (a.hd > 256 || (a.hd & 31) || a.n <= 0) return cudaErrorInvalidValue;
   dim3 grid((unsigned)a.n, (unsigned)(a.n_heads + a.n_kv));
   qkv_rope_kernel<<<grid, a.hd, 0, s>>>(a);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 namespace {
@@ -476,7 +478,9 @@ cudaError_t launch_decode(const AttnArgs& a, cudaStream_t s) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<G>, a);
+  const cudaError_t e_ = cudaLaunchKernelEx(&cfg, attn_decode_kernel<G>, a);
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 }  // namespace
@@ -511,7 +515,9 @@ cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
   }
   dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + QT - 1) / QT));
   attn_prefill_kernel<<<grid, 256, smem, s>>>(a);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 }  // namespace rpgc

@@ -101,7 +101,9 @@ cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K
   dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
   gemm_simt_kernel<<<grid, 256, 0, s>>>(type, w, rows, K, row_bytes, X, n, out, ldo,
                                         accumulate ? 1 : 0);
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
+  return e;
 }
 
 }  // namespace rpgc

@@ -509,6 +509,7 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  count_launches(1);
   CUtensorMap mh, ml;
   if (!make_x_map(&mh, xh, n, K) || !make_x_map(&ml, xl, n, K)) return cudaErrorInvalidValue;
   static int configured[64] = {0};
@@ -550,11 +551,14 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   dim3 grid((unsigned)((rows + TNt - 1) / TNt), (unsigned)((n + TMt - 1) / TMt), (unsigned)ks);
   gemm_tc_kernel<<<grid, kGThreads, kGemmSmem, s>>>(mh, ml, g);
   e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
   if (e != cudaSuccess || ks == 1) return e;
   const int64_t total = n * rows;
   splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(part, (int)ks, n, rows, out, ldo,
                                                                        accumulate ? 1 : 0);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
+  return e;
 }
 
 }  // namespace rpgc

@@ -746,7 +746,9 @@ int sm_count(int dev) {
 template <uint32_t TM>
 cudaError_t launch_tm(const GemvArgs& a, const Plan& P, cudaLaunchConfig_t* cfg, int dev) {
   configure<TM>(dev);
-  return cudaLaunchKernelEx(cfg, gemv_kernel<TM>, a, P);
+  const cudaError_t e_ = cudaLaunchKernelEx(cfg, gemv_kernel<TM>, a, P);
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 }  // namespace

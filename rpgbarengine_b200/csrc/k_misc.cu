@@ -82,7 +82,9 @@ cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   const int64_t nb_ = (total + 255) / 256;
   const int blocks = (int)(nb_ < 148 * 16 ? nb_ : 148 * 16);
   dequant_kernel<<<blocks, 256, 0, s>>>(type, w, rows, cols, row_bytes, out);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int32_t hidden,
@@ -90,30 +92,40 @@ cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, 
                          cudaStream_t s) {
   dim3 grid((hidden + 255) / 256, (unsigned)n);
   embed_kernel<<<grid, 256, 0, s>>>(type, embd, row_bytes, hidden, ids, x, st);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
                                 float* out, cudaStream_t s) {
   rmsnorm_rows_kernel<<<(unsigned)n, 256, 0, s>>>(x, w, dim, eps, out);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 cudaError_t swiglu_launch(float* gate, const float* up, int64_t count, cudaStream_t s) {
   const int64_t nb_ = (count + 255) / 256;
   const int blocks = (int)(nb_ < 148 * 16 ? nb_ : 148 * 16);
   swiglu_kernel<<<blocks, 256, 0, s>>>(gate, up, count);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 cudaError_t state_set_launch(DecodeState* st, const DecodeState& v, cudaStream_t s) {
   state_set_kernel<<<1, 1, 0, s>>>(st, v);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 cudaError_t advance_launch(DecodeState* st, cudaStream_t s) {
   advance_kernel<<<1, 1, 0, s>>>(st);
-  return cudaGetLastError();
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 }  // namespace rpgc

@@ -516,7 +516,9 @@ cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, sample_kernel, a);
+  const cudaError_t e_ = cudaLaunchKernelEx(&cfg, sample_kernel, a);
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
 }
 
 }  // namespace rpgc

@@ -48,6 +48,11 @@ struct GemvArgs {
   int32_t* err;           // optional error flags
 };
 
+// Library-wide count of kernels enqueued (instrumentation for benchmarks):
+// every launch function adds the kernels it enqueued.
+void count_launches(int64_t k);
+int64_t launches_enqueued();
+
 // Launch y = W x over up to 4 segments sharing x (decode, batch 1).  Weight
 // bytes up to the next 16-byte boundary past each segment's last row are
 // read (and ignored).
