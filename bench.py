@@ -123,10 +123,11 @@ def gemv_roofline(torch, dev, hbm, src, launches=48, reps=5):
         g.replay()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(reps):
-        g.replay()
-    e1.record(s)
+    with torch.cuda.stream(s):  # replays go to the current stream
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
     torch.cuda.synchronize(dev)
     us = e0.elapsed_time(e1) * 1e3 / (reps * launches)
     algo = np.mean([rows * gguf.row_bytes(ty, cols) for (ty, rows, cols, *_), _ in plan])
@@ -153,6 +154,7 @@ def run_gpu(args):
     import torch
 
     import rpgbarengine_b200 as rb
+    from rpgbarengine_b200 import dist as rdist
     from rpgbarengine_b200 import synth
 
     rank = int(os.environ.get("RANK", "0"))
@@ -177,7 +179,9 @@ def run_gpu(args):
     max_seq = PROMPT + DECODE + 8
     sess = model.session(max_seq)
     stream = torch.cuda.ExternalStream(sess.stream_ptr, device=dev)
-    ids_host = synth.prompt_ids(SEED_PROMPT + rank, PROMPT)
+    # one session per rank: global session index = rank
+    (session,) = rdist.shard_sessions(world, rank, world)
+    ids_host = synth.prompt_ids(rdist.session_seed(SEED_PROMPT, session), PROMPT)
     ids_dev = torch.from_numpy(ids_host).to(f"cuda:{dev}")
     out_dev = torch.zeros(DECODE + 8, dtype=torch.int32, device=f"cuda:{dev}")
     n_dev = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
@@ -241,15 +245,8 @@ def run_gpu(args):
     hbm, _, src = peaks()
     kernel_roof = gemv_roofline(torch, dev, hbm, src)
 
-    def gmax(v):
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{dev}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    total_ms, pre_ms, dec_ms, e2e_s = gmax(total_ms), gmax(pre_ms), gmax(dec_ms), gmax(e2e_s)
-    greedy_ms, sampled_ms = gmax(greedy_ms), gmax(sampled_ms)
+    total_ms, pre_ms, dec_ms, e2e_s, greedy_ms, sampled_ms = rdist.max_over_ranks(
+        [total_ms, pre_ms, dec_ms, e2e_s, greedy_ms, sampled_ms], dist, f"cuda:{dev}")
     if dist:
         dist.destroy_process_group()
     if rank != 0:
