@@ -14,6 +14,7 @@
 #include <atomic>
 #include <climits>
 #include <cstring>
+#include <initializer_list>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
@@ -187,6 +188,10 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
       fail(RPGC_E_ARG, "GQA group %d unsupported (1, 2, 4 or 8)", g);
   }
   if (c.hidden % 256 || c.intermediate % 32) fail(RPGC_E_ARG, "hidden/intermediate not block aligned");
+  if (!gemv_supported(c.hidden, true) || !gemv_supported(c.intermediate, false) ||
+      !gemv_supported((int64_t)c.n_heads * c.head_dim, false))
+    fail(RPGC_E_ARG, "decode kernels need hidden, intermediate and heads*head_dim to be multiples of "
+                     "128 within the decode kernel's limits");
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) fail(RPGC_E_ARG, "device %d out of range (%d devices)", device, ndev);
@@ -408,6 +413,21 @@ GemvSeg seg_of(const DevMatrix& d, float* out, int32_t mode) {
   return s;
 }
 
+// Bytes of the next launch's rows each CTA prefetches into L2 per matrix.
+constexpr int32_t kPrefetchBytes = 64 * 1024;
+
+// L2 prefetch of the matrices of the next matrix-vector launch of the step.
+void prefetch_of(GemvArgs* g, std::initializer_list<const DevMatrix*> next) {
+  g->npf = 0;
+  for (const DevMatrix* d : next) {
+    GemvPrefetch& f = g->pf[g->npf++];
+    f.w = d->w;
+    f.rows = d->rows;
+    f.row_bytes = d->row_bytes;
+  }
+  g->pf_bytes = kPrefetchBytes;
+}
+
 // Common GEMV arguments of a decode step (the session's active flag and
 // error flags).
 GemvArgs step_gemv(Session* s, const float* x, int32_t K, const float* norm_w) {
@@ -438,6 +458,7 @@ void launch_layers_step(Session* s) {
     g.seg[1] = seg_of(L.k, s->k, kStore);
     g.seg[2] = seg_of(L.v, s->v, kStore);
     g.nseg = 3;
+    prefetch_of(&g, {&L.o});
     check(gemv_launch(g, cs, true), "gemv qkv");
     AttnArgs aa{};
     aa.q = s->q;
@@ -464,20 +485,29 @@ void launch_layers_step(Session* s) {
     GemvArgs go = step_gemv(s, s->attn, qd, nullptr);
     go.seg[0] = seg_of(L.o, s->x, kAdd);
     go.nseg = 1;
+    prefetch_of(&go, {&L.gate, &L.up});
     check(gemv_launch(go, cs, true), "gemv o");
     GemvArgs gf = step_gemv(s, s->x, c.hidden, L.ffn_norm);
     gf.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
     gf.seg[1] = seg_of(L.up, s->gate, kStore);
     gf.nseg = 2;
+    prefetch_of(&gf, {&L.down});
     check(gemv_launch(gf, cs, true), "gemv gate/up");
     GemvArgs gd = step_gemv(s, s->gate, c.intermediate, nullptr);
     gd.seg[0] = seg_of(L.down, s->x, kAdd);
     gd.nseg = 1;
+    if (l + 1 < c.n_layers) {
+      const DevLayer& N = m->layers[l + 1];
+      prefetch_of(&gd, {&N.q, &N.k, &N.v});
+    } else {
+      prefetch_of(&gd, {&m->lm_head});
+    }
     check(gemv_launch(gd, cs, true), "gemv down");
   }
   GemvArgs gl = step_gemv(s, s->x, c.hidden, m->out_norm);
   gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
   gl.nseg = 1;
+  prefetch_of(&gl, {&m->layers[0].q, &m->layers[0].k, &m->layers[0].v});  // the next step
   check(gemv_launch(gl, cs, true), "gemv lm_head");
 }
 
@@ -1034,6 +1064,12 @@ int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t cols, const 
       fail(RPGC_E_ARG, "bad matvec arguments (type %u, %lld x %lld)", type, (long long)rows,
            (long long)cols);
     if (reinterpret_cast<uintptr_t>(w) & 15) fail(RPGC_E_ARG, "weights must be 16-byte aligned");
+    if (!gemv_supported(cols, false)) {  // input length outside the decode kernel: CUDA-core GEMM
+      check(gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, x, 1, y, rows, false,
+                        nullptr, 0, as_stream(stream)),
+            "matvec");
+      return RPGC_OK;
+    }
     GemvArgs g{};
     g.seg[0].w = static_cast<const uint8_t*>(w);
     g.seg[0].out = y;

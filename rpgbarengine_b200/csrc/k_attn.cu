@@ -126,12 +126,15 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   __shared__ __align__(16) float cpart[G][132];  // merged o[128], m, l of this CTA
   __shared__ __align__(8) uint64_t bar;
 
-  grid_dep_wait();
   const DecodeState* st = a.state;
-  if (st && !st->active) return;  // the whole cluster leaves together
   cg::cluster_group cluster = cg::this_cluster();
   const int S = (int)gridDim.y, split = (int)blockIdx.y, kh = (int)blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The position (decode state) was written before the previous kernel
+  // started, and cache rows below it by earlier steps: every kernel of the
+  // decode step signals its dependents only after its own grid-dependency
+  // wait, so the kernel two launches back has completed.  The first K/V tile
+  // is therefore copied before this kernel's wait.
   const int pos = st ? st->pos : (int)a.pos0;
   const int L = pos + 1;  // keys [0, pos]
   const int chunk = (L + S - 1) / S;
@@ -146,6 +149,19 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_barrier_init();
+    if (c0 < c1) {  // first tile (the new token's row is replaced in shared memory)
+      const uint32_t bytes = (uint32_t)min(kTileP, c1 - c0) * 512u;
+      const uint64_t pol = policy_evict_first();
+      mbar_arrive_expect_tx(&bar, 2 * bytes);
+      bulk_g2s(Ks, kb + (int64_t)c0 * 128, bytes, &bar, pol);
+      bulk_g2s(Vs, vb + (int64_t)c0 * 128, bytes, &bar, pol);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  if (st && !st->active) {  // the whole cluster leaves together, copies drained
+    if (tid == 0 && c0 < c1) mbar_wait(&bar, 0, a.err);
+    return;
   }
   // query heads of this kv head (normalised and rotated when fused)
   for (int g = warp; g < G; g += kAWarps) {
@@ -176,7 +192,7 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   uint32_t phase = 0;
   for (int t0 = c0; t0 < c1; t0 += kTileP) {
     const int tn = min(kTileP, c1 - t0);
-    if (tid == 0) {
+    if (tid == 0 && t0 != c0) {
       const uint32_t bytes = (uint32_t)tn * 512u;
       const uint64_t pol = policy_evict_first();
       mbar_arrive_expect_tx(&bar, 2 * bytes);

@@ -37,9 +37,21 @@ struct GemvSeg {
   int32_t mode;      // kSwiGLU: this seg is the gate, seg+1 the up projection
 };
 
+// Rows of the next matrix-vector launch to prefetch into L2: CTA b of this
+// launch prefetches the first pf_bytes of the rows CTA b of the next launch
+// owns (the same balanced split over the grid).
+struct GemvPrefetch {
+  const uint8_t* w;
+  int64_t rows;
+  int64_t row_bytes;
+};
+
 struct GemvArgs {
   GemvSeg seg[4];
   int32_t nseg;
+  GemvPrefetch pf[4];
+  int32_t npf;
+  int32_t pf_bytes;
   int32_t K;              // shared input length (multiple of 64)
   const float* x;         // input [K]
   const float* norm_w;    // optional RMSNorm gain applied to x first
@@ -57,6 +69,9 @@ int64_t launches_enqueued();
 // bytes up to the next 16-byte boundary past each segment's last row are
 // read (and ignored).
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
+// Whether gemv_launch takes input length K (a multiple of 128; with an
+// RMSNorm gain when norm is set).
+bool gemv_supported(int64_t K, bool norm);
 
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
