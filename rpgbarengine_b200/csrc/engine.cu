@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <atomic>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <initializer_list>
 #include <memory>
@@ -104,6 +105,12 @@ struct Session {
   DecodeState* st_host = nullptr;  // pinned
   cudaGraphExec_t step_graph = nullptr;
   int64_t graph_kernels = 0;  // kernels in step_graph
+  // persistent decode step (k_step.cu); null: per-launch kernels
+  StepPlan* step_plan = nullptr;
+  bool step_planned = false;
+  float* step_part = nullptr;     // attention partials
+  uint32_t* step_ctr = nullptr;   // step counter + per-layer head counters
+  size_t step_ctr_bytes = 0;
   std::vector<void*> allocs;
   std::mutex mu;
 
@@ -120,6 +127,7 @@ struct Session {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     if (step_graph) cudaGraphExecDestroy(step_graph);
+    step_plan_free(step_plan);
     for (void* p : allocs) cudaFree(p);
     if (st_host) cudaFreeHost(st_host);
     if (stream) cudaStreamDestroy(stream);
@@ -441,11 +449,97 @@ GemvArgs step_gemv(Session* s, const float* x, int32_t K, const float* norm_w) {
   return g;
 }
 
+// Whether the persistent decode-step kernel is enabled (RPGC_STEP_KERNEL=0
+// selects the per-launch kernels, for comparison).
+bool step_kernel_enabled() {
+  const char* e = std::getenv("RPGC_STEP_KERNEL");
+  return !(e && e[0] == '0' && e[1] == 0);
+}
+
+// Plans the persistent decode step of a session once (device allocations:
+// call outside graph capture).  Leaves step_plan null when the model's block
+// types or shapes are outside the step kernel, or it is disabled.
+void ensure_step_plan(Session* s) {
+  if (s->step_planned) return;
+  s->step_planned = true;
+  if (!step_kernel_enabled()) return;
+  const Model* m = s->m;
+  const rpgc_model_config& c = m->c;
+  const size_t lc = s->layer_cache_floats();
+  const int32_t qd = c.n_heads * c.head_dim;
+  s->step_ctr_bytes = sizeof(uint32_t) * (1 + (size_t)c.n_layers * c.n_kv_heads);
+  s->step_ctr = s->alloc<uint32_t>(1 + (size_t)c.n_layers * c.n_kv_heads);
+  std::vector<StepPhaseIn> ph;
+  auto gemv_phase = [&](const float* x, int32_t K, const float* norm) {
+    StepPhaseIn p;
+    std::memset(&p, 0, sizeof(p));
+    p.kind = 0;
+    p.g.x = x;
+    p.g.K = K;
+    p.g.norm_w = norm;
+    return p;
+  };
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m->layers[l];
+    StepPhaseIn q = gemv_phase(s->x, c.hidden, L.attn_norm);
+    q.g.seg[0] = seg_of(L.q, s->q, kStore);
+    q.g.seg[1] = seg_of(L.k, s->k, kStore);
+    q.g.seg[2] = seg_of(L.v, s->v, kStore);
+    q.g.nseg = 3;
+    ph.push_back(q);
+    StepPhaseIn a;
+    std::memset(&a, 0, sizeof(a));
+    a.kind = 1;
+    a.a.q = s->q;
+    a.a.k_new = s->k;
+    a.a.v_new = s->v;
+    a.a.q_norm = L.q_norm;
+    a.a.k_norm = L.k_norm;
+    a.a.kc = s->kc + l * lc;
+    a.a.vc = s->vc + l * lc;
+    a.a.out = s->attn;
+    a.a.head_ctr = s->step_ctr + 1 + (size_t)l * c.n_kv_heads;
+    ph.push_back(a);
+    StepPhaseIn o = gemv_phase(s->attn, qd, nullptr);
+    o.g.seg[0] = seg_of(L.o, s->x, kAdd);
+    o.g.nseg = 1;
+    ph.push_back(o);
+    StepPhaseIn f = gemv_phase(s->x, c.hidden, L.ffn_norm);
+    f.g.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
+    f.g.seg[1] = seg_of(L.up, s->gate, kStore);
+    f.g.nseg = 2;
+    ph.push_back(f);
+    StepPhaseIn d = gemv_phase(s->gate, c.intermediate, nullptr);
+    d.g.seg[0] = seg_of(L.down, s->x, kAdd);
+    d.g.nseg = 1;
+    ph.push_back(d);
+  }
+  StepPhaseIn h = gemv_phase(s->x, c.hidden, m->out_norm);
+  h.g.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+  h.g.nseg = 1;
+  ph.push_back(h);
+  StepPlan* plan = nullptr;
+  if (step_plan_create(ph.data(), (int)ph.size(), c.n_heads, c.n_kv_heads, s->max_seq, s->device, &plan) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  s->step_plan = plan;
+  s->step_part = s->alloc<float>(step_part_floats(plan));
+}
+
 // Transformer layers + lm_head of one decode step for the token whose
 // embedding is already in s->x, at position st->pos.  Every kernel honours
 // st->active and is launched as a programmatic dependent of the previous one,
 // so each GEMV's weight streaming starts while its predecessor finishes.
 void launch_layers_step(Session* s) {
+  if (s->step_plan) {
+    CK(cudaMemsetAsync(s->step_ctr, 0, s->step_ctr_bytes, s->stream));
+    check(step_launch(s->step_plan, s->st, s->m->rope, s->m->c.rms_eps, s->step_part, s->step_ctr,
+                      &s->st->error, s->stream),
+          "decode step");
+    return;
+  }
   const Model* m = s->m;
   const rpgc_model_config& c = m->c;
   cudaStream_t cs = s->stream;
@@ -611,6 +705,7 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
                          s->stream));
       if (nc == 1 && !all) {
         set_state_for_forward(s);
+        ensure_step_plan(s);
         launch_step(s);
       } else {
         launch_prefill(s, nc, s->len);
@@ -655,6 +750,7 @@ std::atomic<int64_t> g_launches{0};
 
 void capture_step_graph(Session* s) {
   if (s->step_graph) return;
+  ensure_step_plan(s);
   cudaGraph_t g = nullptr;
   int64_t nk = 0;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));

@@ -8,6 +8,7 @@
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
+#include "attn_dev.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -15,7 +16,7 @@ namespace rpgc {
 namespace {
 
 namespace cg = cooperative_groups;
-constexpr float kNegBig = -3.0e38f;
+using namespace attn;
 
 // One block per (token, head); hd threads.  q heads first, then kv heads.
 __global__ void qkv_rope_kernel(const QkvArgs a) {
@@ -70,49 +71,6 @@ __global__ void qkv_rope_kernel(const QkvArgs a) {
 constexpr int kMaxGroup = 8;
 constexpr int kAWarps = 8;
 constexpr int kTileP = 64;  // positions per K/V tile
-
-// QK-norm + RoPE of one 128-wide head held as a float4 per lane (dims
-// 4*lane..4*lane+3): RMSNorm with a double sum of squares, then the half-split
-// rotation with the reference's separate roundings.  The partner dims
-// (i +- 64) come from lane^16.
-__device__ __forceinline__ float4 norm_rope_head(float4 v, const float* w, const float* cs,
-                                                 float eps, int lane) {
-  double ss = (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-  ss = warp_sum(ss);
-  const float scale = (float)(1.0 / sqrt(ss / 128.0 + (double)eps));
-  const float4 g = *reinterpret_cast<const float4*>(w + 4 * lane);
-  float y[4] = {v.x * scale * g.x, v.y * scale * g.y, v.z * scale * g.z, v.w * scale * g.w};
-  float o[4];
-  const bool lo = lane < 16;  // dims < 64
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float partner = __shfl_xor_sync(0xffffffffu, y[k], 16);
-    const int i = (4 * lane + k) & 63;
-    const float c = cs[i], sn = cs[64 + i];
-    o[k] = lo ? __fsub_rn(__fmul_rn(y[k], c), __fmul_rn(partner, sn))
-              : __fadd_rn(__fmul_rn(y[k], c), __fmul_rn(partner, sn));
-  }
-  return make_float4(o[0], o[1], o[2], o[3]);
-}
-
-__device__ __forceinline__ float dot4(float4 a, float4 b) {
-  return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
-}
-
-// 32 values per lane -> lane l holds the warp-wide sum of value l.
-__device__ __forceinline__ float transpose_reduce(float* v, int lane) {
-#pragma unroll
-  for (int n = 16; n >= 1; n >>= 1) {
-    const bool up = (lane & n) != 0;
-#pragma unroll
-    for (int i = 0; i < n; ++i) {
-      const float send = up ? v[i] : v[i + n];
-      const float keep = up ? v[i + n] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, n);
-    }
-  }
-  return v[0];
-}
 
 template <int G>
 __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const AttnArgs a) {

@@ -1,0 +1,948 @@
+// k_step.cu -- the persistent decode step: every transformer layer of one
+// decode step and the lm_head in ONE kernel, one CTA per SM (cooperative
+// launch, so all CTAs are resident together).
+//
+// Replaces, for decode, the per-token chain of the reference's ForwardStep
+// (src/qwen3.cc:119-206, 292-300): per layer RMSNorm -> q/k/v projections ->
+// QK-norm + RoPE + KV write + AttentionFromCache -> o projection + residual ->
+// RMSNorm -> gate/up + SwiGLU -> down + residual; then the output RMSNorm and
+// the lm_head (src/qwen3.cc:208-290).
+//
+// Phases.  The step is a list of phases (matrix-vector products and one
+// attention per layer), each consuming the complete output of the phase
+// before it.  A CTA finishes its share of phase p, then increments one step
+// counter (release); phase p + 1 starts when the counter reaches
+// (p + 1) x grid (acquire; a bounded wait that sets an error flag if it gives
+// up).  Every CTA waits for every phase before it signals, so the count
+// cannot run ahead of the slowest CTA.
+//
+// Weight streaming.  The producer warp of each CTA walks the whole step's
+// stage program (its rows of every matrix, then its attention tiles) and
+// keeps the shared-memory ring full; it never waits for a phase barrier, only
+// for free ring slots.  While the consumers stall at a phase boundary (barrier,
+// loading and quantising the new input vector), HBM keeps filling the ring,
+// so the boundary costs consumer time but no memory time.
+//
+// Matrix-vector phases use the building blocks of the per-launch GEMV
+// (gemv_dev.cuh: activation unit in registers, interleaved 64-element units,
+// per-format dp4a unit products, deterministic per-row reduction).
+//
+// Attention phase.  Work item (kv head kh, split s) of n_kv x splits items
+// goes to CTA kh * splits + s: positions [c0, c1) of [0, pos] (the new
+// token's row is written into the cache and patched into the shared tile by
+// the owner split), online softmax over tiles streamed by the producer, merge
+// of 8 warps in shared memory, then the split's partial (o, max, sum per query
+// head) goes to global scratch; the last split of a head to arrive (counter
+// per head) merges all splits of that head in a fixed order.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "attn_dev.cuh"
+#include "common.cuh"
+#include "gemv_dev.cuh"
+#include "kernels.h"
+
+namespace rpgc {
+namespace {
+
+using namespace gemv;
+using attn::kNegBig;
+
+constexpr int kCWarps = 15;
+constexpr int kNC = kCWarps * 32;          // consumer threads
+constexpr int kThreads = kNC + 32;         // + one producer warp
+constexpr int kMaxStages = 8;
+constexpr int kSmemMax = 227 * 1024;       // dynamic shared memory of the one CTA per SM
+constexpr int kStageTarget = 32 * 1024;
+constexpr int kRedBudget = 16 * 1024;      // partial sums of one reduction chunk (x2 buffers)
+constexpr int kAttnWarps = 8;              // warps that score positions
+constexpr uint32_t kMaxBarrierPolls = 1u << 22;
+constexpr int kRec = 132;                  // floats per attention partial record (16-byte multiple)
+constexpr int kMaxItems = 4;               // activation items per consumer thread (K <= 8 * 4 * 480)
+
+struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
+  int32_t rows;
+  int32_t first;   // index into seg
+  int32_t pair;
+  int32_t m;       // rows per stage
+  int32_t cs;      // stages per reduction chunk
+};
+
+struct PhaseDev {
+  int32_t kind;    // 0 matrix-vector, 1 attention
+  int32_t nseg, K, U, S, nls, red_floats, half_bytes;
+  int32_t deferred;  // 1: every partial of the phase fits the buffers: one reduction at the end
+  GemvSeg seg[3];
+  SLSeg ls[3];
+  const float* x;
+  const float* norm_w;
+  StepAttn a;
+};
+
+struct StepParams {
+  const PhaseDev* ph;
+  int32_t nph;
+  const DecodeState* st;
+  const float* rope;
+  float eps;
+  int32_t n_kv, splits;
+  int64_t max_seq;
+  float* part;      // [n_kv][splits][G][kRec]: o[128], max, sum, 2 pad
+  uint32_t* ctr;    // step counter
+  int32_t* err;
+  int32_t stages, stage_bytes, tile_pos, attn_half;
+  int32_t ucon_off, lim_off, red_off, ring_off;  // shared-memory carve-up
+};
+
+struct SDesc {     // one ring slot's stage, written by the producer before arming
+  int64_t r;       // first row / first position
+  int32_t n;       // rows / positions
+  int32_t ls;      // logical segment (-1: attention tile)
+  int32_t last;    // last stage of its logical segment
+  uint32_t off0;   // byte offset of row r inside the slot
+  uint32_t off1;   // same for the up matrix of a pair
+  int32_t phase;
+};
+static_assert(sizeof(SDesc) == 32, "descriptor size");
+
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"r"(kNC) : "memory"); }
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Rows [lo, hi) of a segment owned by this CTA (balanced split over the grid).
+__device__ __forceinline__ void seg_rows(int32_t rows, int32_t* lo, int32_t* hi) {
+  *lo = (int32_t)((uint32_t)rows * blockIdx.x / gridDim.x);
+  *hi = (int32_t)((uint32_t)rows * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Positions [c0, c1) of attention work item (kh, split) for keys [0, pos].
+__device__ __forceinline__ void attn_range(int pos, int splits, int split, int* c0, int* c1) {
+  const int L = pos + 1, chunk = (L + splits - 1) / splits;
+  *c0 = min(L, split * chunk);
+  *c1 = min(L, *c0 + chunk);
+}
+
+// Bounded wait until the step counter reaches target (thread 0 of the
+// consumers), then release the other consumers.
+__device__ __forceinline__ void phase_wait(const StepParams& P, uint32_t target, int tid) {
+  if (tid == 0) {
+    uint32_t i = 0;
+    while (ld_acquire(P.ctr) < target) {
+      if (++i > kMaxBarrierPolls) {
+        atomicOr(P.err, kErrTimeout);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  csync();
+}
+
+__device__ __forceinline__ void phase_signal(const StepParams& P, int tid) {
+  csync();  // every consumer's output of this phase is written
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(P.ctr, 1u);
+  }
+}
+
+// ============================================================== producer
+__device__ __forceinline__ void slot_acquire(uint64_t* empty, const RingPos& rp, int32_t* err) {
+  if (rp.wrapped) mbar_wait(&empty[rp.slot], rp.parity ^ 1u, err);
+}
+
+__device__ void producer(const StepParams& P, uint64_t* full, uint64_t* empty, SDesc* desc,
+                         uint8_t* ring, int pos) {
+  const uint64_t pol = policy_evict_first();
+  const int NS = P.stages;
+  RingPos rp;
+  for (int p = 0; p < P.nph; ++p) {
+    const PhaseDev& ph = P.ph[p];
+    if (ph.kind == 0) {
+      for (int l = 0; l < ph.nls; ++l) {
+        const SLSeg L = ph.ls[l];
+        int32_t lo, hi;
+        seg_rows(L.rows, &lo, &hi);
+        const GemvSeg& G0 = ph.seg[L.first];
+        for (int32_t r = lo; r < hi; r += L.m, rp.advance(NS)) {
+          const int n = min(L.m, hi - r);
+          const int slot = rp.slot;
+          slot_acquire(empty, rp, P.err);
+          uint8_t* dst = ring + (size_t)slot * P.stage_bytes;
+          const uintptr_t s0 = reinterpret_cast<uintptr_t>(G0.w) + (uintptr_t)r * G0.row_bytes;
+          const uintptr_t b0 = s0 & ~uintptr_t(15);
+          const uint32_t n0 = (uint32_t)(((s0 + (uintptr_t)n * G0.row_bytes + 15) & ~uintptr_t(15)) - b0);
+          uintptr_t s1 = 0, b1 = 0;
+          uint32_t n1 = 0;
+          if (L.pair) {
+            const GemvSeg& G1 = ph.seg[L.first + 1];
+            s1 = reinterpret_cast<uintptr_t>(G1.w) + (uintptr_t)r * G1.row_bytes;
+            b1 = s1 & ~uintptr_t(15);
+            n1 = (uint32_t)(((s1 + (uintptr_t)n * G1.row_bytes + 15) & ~uintptr_t(15)) - b1);
+          }
+          SDesc d;
+          d.r = r;
+          d.n = n;
+          d.ls = l;
+          d.last = r + n >= hi;
+          d.off0 = (uint32_t)(s0 - b0);
+          d.off1 = (uint32_t)ph.half_bytes + (uint32_t)(s1 - b1);
+          d.phase = p;
+          desc[slot] = d;
+          mbar_arrive_expect_tx(&full[slot], n0 + n1);
+          bulk_g2s(dst, reinterpret_cast<const void*>(b0), n0, &full[slot], pol);
+          if (L.pair) bulk_g2s(dst + ph.half_bytes, reinterpret_cast<const void*>(b1), n1, &full[slot], pol);
+        }
+      }
+    } else {
+      const int item = (int)blockIdx.x;
+      if (item >= P.n_kv * P.splits) continue;
+      const int kh = item / P.splits, split = item % P.splits;
+      int c0, c1;
+      attn_range(pos, P.splits, split, &c0, &c1);
+      const float* kb = ph.a.kc + (int64_t)kh * P.max_seq * 128;
+      const float* vb = ph.a.vc + (int64_t)kh * P.max_seq * 128;
+      for (int t0 = c0; t0 < c1; t0 += P.tile_pos, rp.advance(NS)) {
+        const int tn = min(P.tile_pos, c1 - t0);
+        const int slot = rp.slot;
+        slot_acquire(empty, rp, P.err);
+        uint8_t* dst = ring + (size_t)slot * P.stage_bytes;
+        SDesc d;
+        d.r = t0;
+        d.n = tn;
+        d.ls = -1;
+        d.last = t0 + tn >= c1;
+        d.off0 = 0;
+        d.off1 = (uint32_t)P.attn_half;
+        d.phase = p;
+        desc[slot] = d;
+        const uint32_t bytes = (uint32_t)tn * 512u;
+        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+        bulk_g2s(dst, kb + (int64_t)t0 * 128, bytes, &full[slot], pol);
+        bulk_g2s(dst + P.attn_half, vb + (int64_t)t0 * 128, bytes, &full[slot], pol);
+      }
+    }
+  }
+}
+
+// ============================================================== consumers
+// Input vector of a matrix-vector phase.  Thread t quantises items t + NC b
+// (two float4 of x each, coalesced); the RMSNorm gains are loaded before the
+// phase barrier (they are constant), x after it (written by other CTAs, so
+// read through L2), every load of the thread in flight at once.
+__device__ __forceinline__ float gemv_prologue(const StepParams& P, const PhaseDev& ph, uint32_t target,
+                                               int tid, int lane, int warp, double* dred, uint4* lim,
+                                               float* ucon) {
+  const int K = ph.K, NI = K / 8, U = ph.U;
+  const bool norm = ph.norm_w != nullptr;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 g0[kMaxItems], g1[kMaxItems];
+#pragma unroll
+  for (int b = 0; b < kMaxItems; ++b) {
+    const int i = b * kNC + tid;
+    g0[b] = g1[b] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm && i < NI) {
+      g0[b] = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + 2 * i);
+      g1[b] = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + 2 * i + 1);
+    }
+  }
+  phase_wait(P, target, tid);
+  float4 v0[kMaxItems], v1[kMaxItems];
+#pragma unroll
+  for (int b = 0; b < kMaxItems; ++b) {
+    const int i = b * kNC + tid;
+    v0[b] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
+    v1[b] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int b = 0; b < kMaxItems; ++b) {
+    if (b * kNC >= NI) break;  // uniform
+    const int i = b * kNC + tid;
+    const float4 a = v0[b], c = v1[b];
+    if (norm)
+      ss += (double)a.x * a.x + (double)a.y * a.y + (double)a.z * a.z + (double)a.w * a.w +
+            (double)c.x * c.x + (double)c.y * c.y + (double)c.z * c.z + (double)c.w * c.w;
+    const float4 x0 = make_float4(a.x * g0[b].x, a.y * g0[b].y, a.z * g0[b].z, a.w * g0[b].w);
+    const float4 x1 = make_float4(c.x * g1[b].x, c.y * g1[b].y, c.z * g1[b].z, c.w * g1[b].w);
+    quantize_item(x0, x1, i, i < NI, U, lim, ucon);
+  }
+  if (norm) {
+    ss = warp_sum(ss);
+    if (lane == 0) dred[warp] = ss;
+  }
+  csync();
+  if (!norm) return 1.0f;
+  double tot = 0.0;
+#pragma unroll 1
+  for (int w = 0; w < kCWarps; ++w) tot += dred[w];
+  return 1.0f / sqrtf((float)tot / (float)K + P.eps);
+}
+
+template <uint32_t TM>
+__device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, RingPos* rpp,
+                                           uint64_t* full, uint64_t* empty, const SDesc* desc, uint32_t ring32,
+                                           double* dred, uint4* lim, float* ucon, float* red, int tid, int lane,
+                                           int warp) {
+  const float nscale = gemv_prologue(P, ph, target, tid, lane, warp, dred, lim, ucon);
+  const int U = ph.U, S = ph.S, Ur = U | 1, NS = P.stages;
+  const int u = tid % U, s = tid / U;
+  const bool busy = s < S;
+  const UnitOff uo = unit_offsets(u);
+  ActR act;
+  if (busy) {
+#pragma unroll
+    for (int L = 0; L < 3; ++L) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = lim[(L * 4 + j) * U + u];
+        act.a[L][4 * j] = v.x;
+        act.a[L][4 * j + 1] = v.y;
+        act.a[L][4 * j + 2] = v.z;
+        act.a[L][4 * j + 3] = v.w;
+      }
+    }
+    act.g = ucon[u];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) act.ga[j] = ucon[(1 + j) * U + u];
+  }
+  RingPos rp = *rpp;
+  const uint32_t sbytes = (uint32_t)P.stage_bytes;
+  // rows j (stage-relative) of one stage into partial slots p0 (+ j * Ur)
+  // and, for the second row, p1
+  auto rows = [&](const SDesc& d, int slot, const SLSeg& L, uint32_t type, int rb, float* p0, float* p1) {
+    if (!busy) return;
+    const uint32_t sb = ring32 + (uint32_t)slot * sbytes;
+    stage_rows<TM>(type, sb + d.off0, L.pair ? sb + d.off1 : sb + d.off0, d.n, s, S, L.pair != 0, rb, u, Ur, uo,
+                   act, nullptr, p0, p1);
+  };
+  // row total of partial row pp, 4 threads per row, fixed order
+  auto row_total = [&](const float* pp, int q, bool live) {
+    float t = 0.0f;
+    if (live) {
+#pragma unroll 4
+      for (int v = q; v < U; v += 4) t += pp[v];
+    }
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    return t * nscale;
+  };
+  if (ph.deferred) {
+    int base = 0;
+#pragma unroll 1
+    for (int l = 0; l < ph.nls; ++l) {
+      const SLSeg L = ph.ls[l];
+      int32_t lo, hi;
+      seg_rows(L.rows, &lo, &hi);
+      const GemvSeg G = ph.seg[L.first];
+      const int nrows = hi - lo, nst = (nrows + L.m - 1) / L.m;
+#pragma unroll 1
+      for (int k = 0; k < nst; ++k, rp.advance(NS)) {
+        const int slot = rp.slot;
+        mbar_wait(&full[slot], rp.parity, P.err);
+        const SDesc d = desc[slot];
+        const int jr0 = (int)d.r - lo;
+        rows(d, slot, L, G.type, (int)G.row_bytes, red + base + jr0 * Ur, red + base + (nrows + jr0) * Ur);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      base += nrows * (L.pair + 1) * Ur;
+    }
+    csync();
+    // one reduction over every segment's rows
+    int total = 0;
+#pragma unroll 1
+    for (int l = 0; l < ph.nls; ++l) {
+      int32_t lo, hi;
+      seg_rows(ph.ls[l].rows, &lo, &hi);
+      total += (hi - lo) * (ph.ls[l].pair + 1);
+    }
+#pragma unroll 1
+    for (int b0 = 0; b0 < 4 * total; b0 += kNC) {
+      const int idx = b0 + tid, q = idx & 3;
+      int sid = idx >> 2, l = 0, bse = 0, lo = 0, hi = 0;
+      // segment of sum sid (at most three segments)
+#pragma unroll 1
+      for (; l < ph.nls; ++l) {
+        seg_rows(ph.ls[l].rows, &lo, &hi);
+        const int n = (hi - lo) * (ph.ls[l].pair + 1);
+        if (sid < n) break;
+        sid -= n;
+        bse += n * Ur;
+      }
+      const bool live = l < ph.nls;
+      const int ll = live ? l : 0;
+      const SLSeg& L = ph.ls[ll];
+      const int nrows = hi - lo;
+      const int j = L.pair ? sid >> 1 : sid, h = L.pair ? sid & 1 : 0;
+      const float t = row_total(red + bse + (h * nrows + j) * Ur, q, live);
+      const float other = __shfl_xor_sync(0xffffffffu, t, 4);  // up total for a pair's gate lane
+      if (live && q == 0 && h == 0) {
+        const GemvSeg& G = ph.seg[L.first];
+        const int32_t row = lo + j;
+        if (L.pair) ph.seg[L.first + 1].out[row] = silu_mul(t, other);
+        else if (G.mode == kAdd) G.out[row] += t;
+        else G.out[row] = t;
+      }
+    }
+    *rpp = rp;
+    return;
+  }
+#pragma unroll 1
+  for (int l = 0; l < ph.nls; ++l) {
+    const SLSeg L = ph.ls[l];
+    int32_t lo, hi;
+    seg_rows(L.rows, &lo, &hi);
+    const GemvSeg G = ph.seg[L.first];
+    float* up_out = L.pair ? ph.seg[L.first + 1].out : nullptr;
+    const int rb = (int)G.row_bytes, ck_rows = L.cs * L.m;
+    const int nst = (hi - lo + L.m - 1) / L.m;
+    int chunk0 = 0, cbuf = 0;
+    int32_t chunk_r0 = lo;
+#pragma unroll 1
+    for (int k = 0; k < nst; ++k, rp.advance(NS)) {
+      const int slot = rp.slot;
+      mbar_wait(&full[slot], rp.parity, P.err);
+      const SDesc d = desc[slot];
+      if (k == chunk0) chunk_r0 = (int32_t)d.r;
+      const int jr0 = (k - chunk0) * L.m;
+      float* rbuf = red + cbuf * ph.red_floats;
+      rows(d, slot, L, G.type, rb, rbuf + jr0 * Ur, rbuf + (ck_rows + jr0) * Ur);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (!d.last && k + 1 - chunk0 < L.cs) continue;
+      // chunk complete: 4 threads per row total, fixed order (deterministic)
+      csync();
+      const int rows = jr0 + d.n, nsum = rows * (L.pair + 1);
+#pragma unroll 1
+      for (int b0 = 0; b0 < 4 * nsum; b0 += kNC) {
+        const int idx = b0 + tid, q = idx & 3, sid = idx >> 2;
+        const int j = L.pair ? sid >> 1 : sid, h = L.pair ? sid & 1 : 0;
+        const float t = row_total(rbuf + (h * ck_rows + j) * Ur, q, sid < nsum);
+        const float other = __shfl_xor_sync(0xffffffffu, t, 4);
+        if (sid < nsum && q == 0 && h == 0) {
+          const int32_t row = chunk_r0 + j;
+          if (L.pair) up_out[row] = silu_mul(t, other);
+          else if (G.mode == kAdd) G.out[row] += t;
+          else G.out[row] = t;
+        }
+      }
+      chunk0 = k + 1;
+      cbuf ^= 1;
+    }
+  }
+  *rpp = rp;
+}
+
+// Attention phase of one layer for a group of G query heads per kv head.
+template <int G>
+__device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, RingPos* rpp, uint64_t* full,
+                                           uint64_t* empty, const SDesc* desc, uint8_t* ring, float* scratch,
+                                           int* flag, int pos, int tid, int lane, int warp) {
+  constexpr int PB = 32 / G;
+  const StepAttn& A = ph.a;
+  const int item = (int)blockIdx.x, NS = P.stages;
+  const bool has_item = item < P.n_kv * P.splits;
+  const int kh = has_item ? item / P.splits : 0, split = has_item ? item % P.splits : 0;
+  int c0 = 0, c1 = 0;
+  if (has_item) attn_range(pos, P.splits, split, &c0, &c1);
+  const bool owner = has_item && c0 <= pos && pos < c1;
+  const float* cs = P.rope + (int64_t)pos * 128;
+  // scratch: qs[G][128] | wo[kAttnWarps][G][128] | wm[kAttnWarps][G] | wl[kAttnWarps][G] | cpart[G][130]
+  float* qs = scratch;
+  float* wo = qs + G * 128;
+  float* wm = wo + kAttnWarps * G * 128;
+  float* wl = wm + kAttnWarps * G;
+  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  phase_wait(P, target, tid);
+  if (has_item) {
+    if (warp < G) {
+      float4 v = __ldcg(reinterpret_cast<const float4*>(A.q + (kh * G + warp) * 128) + lane);
+      v = attn::norm_rope_head(v, A.q_norm, cs, P.eps, lane);
+      reinterpret_cast<float4*>(qs + warp * 128)[lane] = v;
+    }
+    if (owner && warp == kAttnWarps) {  // the new token's k and v: into the cache
+      knew = __ldcg(reinterpret_cast<const float4*>(A.k_new + kh * 128) + lane);
+      knew = attn::norm_rope_head(knew, A.k_norm, cs, P.eps, lane);
+      vnew = __ldcg(reinterpret_cast<const float4*>(A.v_new + kh * 128) + lane);
+      const int64_t off = ((int64_t)kh * P.max_seq + pos) * 128 + 4 * lane;
+      *reinterpret_cast<float4*>(A.kc + off) = knew;
+      *reinterpret_cast<float4*>(A.vc + off) = vnew;
+    }
+  }
+  csync();
+  const float scale = 1.0f / sqrtf(128.0f);
+  float4 q[G], o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    q[g] = reinterpret_cast<const float4*>(qs + g * 128)[lane];
+    o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mh = kNegBig, lh = 0.0f;
+  const int gl = lane / PB, jl = lane % PB;
+  RingPos rp = *rpp;
+  for (int t0 = c0; t0 < c1; t0 += P.tile_pos, rp.advance(NS)) {
+    const int slot = rp.slot;
+    mbar_wait(&full[slot], rp.parity, P.err);
+    const int tn = min(P.tile_pos, c1 - t0);
+    float* Ks = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes);
+    float* Vs = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes + P.attn_half);
+    if (owner && warp == kAttnWarps && pos >= t0 && pos < t0 + tn) {
+      reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = knew;
+      reinterpret_cast<float4*>(Vs + (pos - t0) * 128)[lane] = vnew;
+    }
+    csync();
+    if (warp < kAttnWarps) {
+      for (int pb = warp * PB; pb < tn; pb += kAttnWarps * PB) {
+        float val[32];
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          const float4 k = pb + j < tn ? reinterpret_cast<const float4*>(Ks + (pb + j) * 128)[lane]
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int g = 0; g < G; ++g) val[g * PB + j] = attn::dot4(q[g], k);
+        }
+        const bool valid = pb + jl < tn;
+        const float tr = attn::transpose_reduce(val, lane);
+        const float sc = valid ? tr * scale : kNegBig;
+        float mx = sc;
+#pragma unroll
+        for (int n = PB / 2; n >= 1; n >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, n));
+        const float mn = fmaxf(mh, mx);
+        const float corr = expf(mh - mn);
+        const float pe = valid ? expf(sc - mn) : 0.0f;
+        float ps = pe;
+#pragma unroll
+        for (int n = PB / 2; n >= 1; n >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, n);
+        lh = lh * corr + ps;
+        mh = mn;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float cg_ = __shfl_sync(0xffffffffu, corr, g * PB);
+          o[g].x *= cg_;
+          o[g].y *= cg_;
+          o[g].z *= cg_;
+          o[g].w *= cg_;
+        }
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          if (pb + j >= tn) break;  // warp-uniform
+          const float4 v = reinterpret_cast<const float4*>(Vs + (pb + j) * 128)[lane];
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float pj = __shfl_sync(0xffffffffu, pe, g * PB + j);
+            o[g].x += pj * v.x;
+            o[g].y += pj * v.y;
+            o[g].z += pj * v.z;
+            o[g].w += pj * v.w;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  *rpp = rp;
+  // ---- merge the scoring warps of this CTA into the split's partial
+  if (warp < kAttnWarps) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) reinterpret_cast<float4*>(wo + (warp * G + g) * 128)[lane] = o[g];
+    if (jl == 0) {
+      wm[warp * G + gl] = mh;
+      wl[warp * G + gl] = lh;
+    }
+  }
+  csync();
+  float* mypart = P.part + ((int64_t)kh * P.splits + split) * (G * kRec);
+  if (has_item) {
+    for (int idx = tid; idx < G * 128; idx += kNC) {
+      const int g = idx >> 7, d = idx & 127;
+      float M = kNegBig;
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * G + g]);
+      float O = 0.0f, Ls = 0.0f;
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = expf(wm[w * G + g] - M);
+        O += wo[(w * G + g) * 128 + d] * f;
+        Ls += wl[w * G + g] * f;
+      }
+      mypart[g * kRec + d] = O;
+      if (d == 0) {
+        mypart[g * kRec + 128] = M;
+        mypart[g * kRec + 129] = Ls;
+      }
+    }
+  }
+  csync();
+  if (tid == 0) {
+    int last = 0;
+    if (has_item) {
+      __threadfence();
+      last = atomicAdd(A.head_ctr + kh, 1u) == (uint32_t)P.splits - 1u;
+      if (last) __threadfence();
+    }
+    *flag = last;
+  }
+  csync();
+  if (*flag) {  // every split of head kh has written its partial: merge them
+    // all partials of the head into shared memory at once (async copies
+    // through L2), then the merge from shared memory in a fixed order
+    float* hs = scratch;  // [splits][G][kRec]
+    const float* hp = P.part + (int64_t)kh * P.splits * (G * kRec);
+    const int nchunk = P.splits * G * kRec / 4;
+#pragma unroll 1
+    for (int c = tid; c < nchunk; c += kNC) cp_async16(hs + 4 * c, hp + 4 * c);
+    cp_async_wait_all();
+    csync();
+    for (int idx = tid; idx < G * 128; idx += kNC) {
+      const int g = idx >> 7, d = idx & 127;
+      float M = kNegBig;
+      for (int r = 0; r < P.splits; ++r) M = fmaxf(M, hs[(r * G + g) * kRec + 128]);
+      float O = 0.0f, Ls = 0.0f;
+      for (int r = 0; r < P.splits; ++r) {
+        const float* rp = hs + (r * G + g) * kRec;
+        const float f = expf(rp[128] - M);
+        O += rp[d] * f;
+        Ls += rp[129] * f;
+      }
+      A.out[(kh * G + g) * 128 + d] = O / Ls;
+    }
+  }
+}
+
+template <uint32_t TM, int G>
+__global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);             // [kMaxStages]
+  uint64_t* empty = full + kMaxStages;                            // [kMaxStages]
+  SDesc* desc = reinterpret_cast<SDesc*>(smem + 128);             // [kMaxStages]
+  double* dred = reinterpret_cast<double*>(smem + 384);           // [16]
+  int* flag = reinterpret_cast<int*>(smem + 512);
+  float* ucon = reinterpret_cast<float*>(smem + P.ucon_off);
+  uint4* lim = reinterpret_cast<uint4*>(smem + P.lim_off);
+  float* red = reinterpret_cast<float*>(smem + P.red_off);
+  float* scratch = reinterpret_cast<float*>(smem + P.lim_off);   // attention (aliases lim, red)
+  uint8_t* ring = smem + P.ring_off;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const DecodeState* st = P.st;
+  if (st && !st->active) return;  // every CTA leaves
+  const int pos = st ? st->pos : 0;
+  if (tid == kNC) {
+    for (int i = 0; i < P.stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kCWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid >= kNC) {
+    if (tid == kNC) producer(P, full, empty, desc, ring, pos);
+    return;
+  }
+  const uint32_t ring32 = smem_u32(ring);
+  RingPos it;
+#pragma unroll 1
+  for (int p = 0; p < P.nph; ++p) {
+    const PhaseDev& ph = P.ph[p];
+    const uint32_t target = (uint32_t)p * gridDim.x;
+    if (ph.kind == 0)
+      gemv_phase<TM>(P, ph, target, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
+    else
+      attn_phase<G>(P, ph, target, &it, full, empty, desc, ring, scratch, flag, pos, tid, lane, warp);
+    phase_signal(P, tid);
+  }
+}
+
+// ------------------------------------------------------------------ host
+constexpr uint32_t type_mask(uint32_t t) {
+  return t == kQ4_K ? kMQ4K : t == kQ6_K ? kMQ6K : t == kQ8_0 ? kMQ80 : 0;
+}
+
+struct Geometry {
+  int stage_bytes = 0, stages = 0, tile_pos = 0, attn_half = 0;
+  int ucon_off = 0, lim_off = 0, red_off = 0, ring_off = 0, smem = 0;
+};
+
+bool plan_gemv(const StepGemv& g, PhaseDev* d, int* slot_need) {
+  if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 128 != 0) return false;
+  const int U = g.K / 64;
+  if (U > kNC) return false;
+  d->kind = 0;
+  d->nseg = g.nseg;
+  d->K = g.K;
+  d->U = U;
+  d->S = kNC / U;
+  d->x = g.x;
+  d->norm_w = g.norm_w;
+  d->nls = 0;
+  int half = 0, red = 0, need = 0;
+  for (int i = 0; i < g.nseg; ++i) {
+    const GemvSeg& G = g.seg[i];
+    d->seg[i] = G;
+    int be, bb;
+    switch (G.type) {
+      case kQ4_K: be = 256; bb = 144; break;
+      case kQ6_K: be = 256; bb = 210; break;
+      case kQ8_0: be = 32; bb = 34; break;
+      default: return false;
+    }
+    if (g.K % be != 0 || (int64_t)(g.K / be) * bb != G.row_bytes) return false;
+    if (reinterpret_cast<uintptr_t>(G.w) & 15) return false;
+    if (G.rows <= 0 || G.rows > (int64_t)(0xFFFFFFFFu / 1024)) return false;
+    const bool up_of_pair = i > 0 && g.seg[i - 1].mode == kSwiGLU;
+    if (up_of_pair) {
+      if (G.rows != g.seg[i - 1].rows || G.type != g.seg[i - 1].type) return false;
+      continue;
+    }
+    SLSeg& L = d->ls[d->nls++];
+    L.rows = (int32_t)G.rows;
+    L.first = i;
+    L.pair = G.mode == kSwiGLU ? 1 : 0;
+    const int64_t per_round = (int64_t)d->S * G.row_bytes * 2;
+    int64_t rounds = kStageTarget / per_round;
+    if (rounds < 1) rounds = 1;
+    L.m = (int32_t)(rounds * d->S * (L.pair ? 1 : 2));
+    const int slot = (int)(((int64_t)L.m * G.row_bytes + 32 + 127) & ~int64_t(127));
+    if (L.pair) half = std::max(half, slot);
+    need = std::max(need, slot * (L.pair + 1));
+    const int per_stage = L.m * (U | 1) * (L.pair + 1);
+    int cs = kRedBudget / (4 * per_stage);
+    if (cs < 1) cs = 1;
+    L.cs = cs;
+    red = std::max(red, cs * per_stage);
+  }
+  if (g.seg[g.nseg - 1].mode == kSwiGLU) return false;
+  if (g.K / 8 > kMaxItems * kNC) return false;
+  d->red_floats = red;
+  d->deferred = 0;
+  d->half_bytes = half;
+  *slot_need = need;
+  return true;
+}
+
+int sms_of(int dev) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <uint32_t TM, int G>
+cudaError_t launch_g(const StepParams& p, int grid, int smem, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && configured[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<TM, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, step_kernel<TM, G>, p);
+  if (e == cudaSuccess) count_launches(1);
+  return e;
+}
+
+// Whether one CTA of the instantiation fits an SM with `smem` bytes.
+template <uint32_t TM, int G>
+bool fits_g(int smem) {
+  if (cudaFuncSetAttribute(step_kernel<TM, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel<TM, G>, kThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return n >= 1;
+}
+
+template <uint32_t TM>
+bool fits_tm(int G, int smem) {
+  switch (G) {
+    case 1: return fits_g<TM, 1>(smem);
+    case 2: return fits_g<TM, 2>(smem);
+    case 4: return fits_g<TM, 4>(smem);
+    case 8: return fits_g<TM, 8>(smem);
+    default: return false;
+  }
+}
+
+bool fits(uint32_t mask, int G, int smem) {
+  if ((mask & ~(kMQ4K | kMQ6K)) == 0) return fits_tm<kMQ4K | kMQ6K>(G, smem);
+  if (mask == kMQ80) return fits_tm<kMQ80>(G, smem);
+  return fits_tm<kMQ4K | kMQ6K | kMQ80>(G, smem);
+}
+
+template <uint32_t TM>
+cudaError_t launch_tm(const StepParams& p, int G, int grid, int smem, cudaStream_t s) {
+  switch (G) {
+    case 1: return launch_g<TM, 1>(p, grid, smem, s);
+    case 2: return launch_g<TM, 2>(p, grid, smem, s);
+    case 4: return launch_g<TM, 4>(p, grid, smem, s);
+    case 8: return launch_g<TM, 8>(p, grid, smem, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+struct StepPlan {
+  PhaseDev* dev = nullptr;  // device phase table
+  int nph = 0;
+  Geometry geo;
+  uint32_t mask = 0;
+  int grid = 0, n_kv = 0, G = 0, splits = 0;
+  int64_t max_seq = 0;
+};
+
+size_t step_part_floats(const StepPlan* p) {
+  return p ? (size_t)p->n_kv * p->splits * p->G * kRec : 0;
+}
+
+cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv, int64_t max_seq,
+                             int device, StepPlan** out) {
+  *out = nullptr;
+  if (n <= 0 || n_kv <= 0 || n_heads % n_kv) return cudaErrorInvalidValue;
+  const int G = n_heads / n_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return cudaErrorInvalidValue;
+  std::vector<PhaseDev> ph((size_t)n);
+  int need = 0, Umax = 0, redmax = 0;
+  uint32_t mask = 0;
+  for (int i = 0; i < n; ++i) {
+    std::memset(&ph[i], 0, sizeof(PhaseDev));
+    if (in[i].kind == 0) {
+      int slot = 0;
+      if (!plan_gemv(in[i].g, &ph[i], &slot)) return cudaErrorInvalidValue;
+      need = std::max(need, slot);
+      Umax = std::max(Umax, ph[i].U);
+      redmax = std::max(redmax, ph[i].red_floats);
+      for (int k = 0; k < in[i].g.nseg; ++k) mask |= type_mask(in[i].g.seg[k].type);
+    } else {
+      ph[i].kind = 1;
+      ph[i].a = in[i].a;
+    }
+  }
+  StepPlan* P = new StepPlan();
+  P->grid = sms_of(device);
+  P->n_kv = n_kv;
+  P->G = G;
+  P->splits = P->grid / n_kv;
+  P->max_seq = max_seq;
+  P->mask = mask;
+  P->nph = n;
+  if (P->splits < 1) {
+    delete P;
+    return cudaErrorInvalidValue;
+  }
+  Geometry& g = P->geo;
+  g.ucon_off = 640;
+  g.lim_off = g.ucon_off + ((20 * Umax + 127) & ~127);
+  g.red_off = g.lim_off + 192 * Umax;
+  int end = g.red_off + ((2 * redmax * 4 + 127) & ~127);
+  const int attn_scratch = (G * 128 + kAttnWarps * G * 128 + 2 * kAttnWarps * G) * 4;
+  end = std::max(end, g.lim_off + ((attn_scratch + 127) & ~127));
+  // the merge stages every split's partial of a head in the same region
+  const int per_split = G * kRec * 4;
+  P->splits = std::min(P->splits, std::max(1, (end - g.lim_off) / per_split));
+  g.ring_off = (end + 127) & ~127;
+  const int stage_bytes = std::max(need, 2 * 16 * 512);  // an attention tile holds 16 positions at least
+  g.stage_bytes = stage_bytes;
+  g.stages = std::min(kMaxStages, (kSmemMax - g.ring_off) / stage_bytes);
+  if (g.stages < 2) {
+    delete P;
+    return cudaErrorInvalidValue;
+  }
+  g.attn_half = (stage_bytes / 2) & ~15;
+  g.tile_pos = g.attn_half / 512;
+  g.smem = g.ring_off + g.stages * stage_bytes;
+  // second pass: a segment whose rows of one CTA fit one slot takes one
+  // stage; a phase whose partials fit both buffers reduces once at its end
+  for (int i = 0; i < n; ++i) {
+    PhaseDev& d = ph[i];
+    if (d.kind != 0) continue;
+    int total = 0;
+    for (int l = 0; l < d.nls; ++l)
+      total += ((d.ls[l].rows + P->grid - 1) / P->grid) * (d.ls[l].pair + 1) * (d.U | 1);
+    d.deferred = total <= 2 * d.red_floats ? 1 : 0;
+    if (!d.deferred) continue;  // chunked: the buffers are sized for the planned stages
+    for (int l = 0; l < d.nls; ++l) {
+      SLSeg& L = d.ls[l];
+      const int64_t rb = d.seg[L.first].row_bytes;
+      const int per_cta = (L.rows + P->grid - 1) / P->grid;
+      const int64_t one = ((int64_t)per_cta * rb + 32 + 127) & ~int64_t(127);
+      if (per_cta > L.m && one * (L.pair + 1) <= stage_bytes && (!L.pair || one <= d.half_bytes))
+        L.m = per_cta;
+    }
+  }
+  if (!fits(mask, G, g.smem)) {
+    delete P;
+    return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaMalloc(&P->dev, sizeof(PhaseDev) * (size_t)n);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(P->dev, ph.data(), sizeof(PhaseDev) * (size_t)n, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (P->dev) cudaFree(P->dev);
+    delete P;
+    return e;
+  }
+  *out = P;
+  return cudaSuccess;
+}
+
+void step_plan_free(StepPlan* p) {
+  if (!p) return;
+  if (p->dev) cudaFree(p->dev);
+  delete p;
+}
+
+int step_plan_splits(const StepPlan* p) { return p ? p->splits : 0; }
+int step_plan_grid(const StepPlan* p) { return p ? p->grid : 0; }
+
+cudaError_t step_launch(const StepPlan* plan, const DecodeState* st, const float* rope, float eps,
+                        float* part, uint32_t* ctr, int32_t* err, cudaStream_t s) {
+  StepParams p{};
+  p.ph = plan->dev;
+  p.nph = plan->nph;
+  p.st = st;
+  p.rope = rope;
+  p.eps = eps;
+  p.n_kv = plan->n_kv;
+  p.splits = plan->splits;
+  p.max_seq = plan->max_seq;
+  p.part = part;
+  p.ctr = ctr;
+  p.err = err;
+  p.stages = plan->geo.stages;
+  p.stage_bytes = plan->geo.stage_bytes;
+  p.tile_pos = plan->geo.tile_pos;
+  p.attn_half = plan->geo.attn_half;
+  p.ucon_off = plan->geo.ucon_off;
+  p.lim_off = plan->geo.lim_off;
+  p.red_off = plan->geo.red_off;
+  p.ring_off = plan->geo.ring_off;
+  const uint32_t m = plan->mask;
+  if ((m & ~(kMQ4K | kMQ6K)) == 0) return launch_tm<kMQ4K | kMQ6K>(p, plan->G, plan->grid, plan->geo.smem, s);
+  if (m == kMQ80) return launch_tm<kMQ80>(p, plan->G, plan->grid, plan->geo.smem, s);
+  return launch_tm<kMQ4K | kMQ6K | kMQ80>(p, plan->G, plan->grid, plan->geo.smem, s);
+}
+
+}  // namespace rpgc

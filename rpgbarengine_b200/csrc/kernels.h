@@ -73,6 +73,48 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
 // RMSNorm gain when norm is set).
 bool gemv_supported(int64_t K, bool norm);
 
+// ------------------------------------------------- persistent decode step
+// One matrix-vector phase of the step (up to three segments sharing x).
+struct StepGemv {
+  GemvSeg seg[3];
+  int32_t nseg;
+  int32_t K;
+  const float* x;
+  const float* norm_w;  // optional RMSNorm gain
+};
+// One decode-attention phase (one layer, the token at state->pos).
+struct StepAttn {
+  const float* q;       // [n_heads][128] raw projections
+  const float* k_new;   // [n_kv][128]
+  const float* v_new;
+  const float* q_norm;  // [128]
+  const float* k_norm;
+  float* kc;            // this layer's caches [n_kv][max_seq][128]
+  float* vc;
+  float* out;           // [n_heads][128]
+  uint32_t* head_ctr;   // [n_kv] split arrival counters (zero before the step)
+};
+struct StepPhaseIn {
+  int32_t kind;  // 0 matrix-vector, 1 attention
+  StepGemv g;
+  StepAttn a;
+};
+struct StepPlan;
+// Plans the step's phases for `device` (shapes, ring, shared memory) and
+// uploads the phase table; fails (cudaErrorInvalidValue) for block types or
+// shapes the step kernel does not take, so the caller keeps per-launch kernels.
+cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv, int64_t max_seq,
+                             int device, StepPlan** out);
+void step_plan_free(StepPlan* p);
+int step_plan_splits(const StepPlan* p);
+int step_plan_grid(const StepPlan* p);
+// Attention partial scratch (floats) of a plan.
+size_t step_part_floats(const StepPlan* p);
+// One decode step: every phase of the plan in one cooperative launch.  ctr
+// (1 + the attention phases' head counters) must be zero when it starts.
+cudaError_t step_launch(const StepPlan* plan, const DecodeState* st, const float* rope, float eps,
+                        float* part, uint32_t* ctr, int32_t* err, cudaStream_t s);
+
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
 // Prefill matmul OUT[t][r] (+)= dot(X[t], W[r]).  With scratch of at least
