@@ -88,58 +88,10 @@ class Clocks:
 # DRAM bytes (read + write) per launch of the roofline kernel, from one ncu
 # capture of each shape (gpu__time_duration / dram__bytes_*.sum pass of the
 # same kernel on the same matrices): gate 14.08 MB, down 20.56 MB.
-GEMV_TRAFFIC = {(12, 9728, 2560): 14_084_096, (14, 2560, 9728): 20_561_152}
-
-
-def gemv_roofline(torch, dev, hbm, src, launches=48, reps=5):
-    """The dominant decode kernel (gemv_kernel) timed alone: the config-2
-    gate (Q4_K 9728 x 2560) and down (Q6_K 2560 x 9728) matrices alternate,
-    each launch on its own weight copy (copies cycled past L2), all launches
-    captured in one CUDA graph and timed with CUDA events on that stream."""
-    import rpgbarengine_b200 as rb
-    from rpgbarengine_b200 import gguf, synth
-    rng = np.random.default_rng(7)
-    shapes = [(gguf.Q4_K, 9728, 2560), (gguf.Q6_K, 2560, 9728)]
-    mats = []
-    for ty, rows, cols in shapes:
-        one = torch.from_numpy(synth.random_blocks(rng, ty, rows, cols)).to(f"cuda:{dev}")
-        copies = int(np.ceil(160e6 / one.numel()))
-        ws = [one] + [one.clone() for _ in range(copies - 1)]
-        x = torch.randn(cols, device=f"cuda:{dev}")
-        y = torch.empty(rows, device=f"cuda:{dev}")
-        mats.append((ty, rows, cols, ws, x, y))
-    s = torch.cuda.Stream(dev)
-    plan = [(mats[i % 2], i // 2) for i in range(launches)]
-
-    def run():
-        for (ty, rows, cols, ws, x, y), j in plan:
-            rb.matvec(ty, ws[j % len(ws)], rows, cols, x, out=y, stream=s.cuda_stream)
-
-    with torch.cuda.stream(s):
-        run()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            run()
-        g.replay()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):  # replays go to the current stream
-        e0.record(s)
-        for _ in range(reps):
-            g.replay()
-        e1.record(s)
-    torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) * 1e3 / (reps * launches)
-    algo = np.mean([rows * gguf.row_bytes(ty, cols) for (ty, rows, cols, *_), _ in plan])
-    traffic = np.mean([GEMV_TRAFFIC[(ty, rows, cols)] for (ty, rows, cols, *_), _ in plan])
-    achieved = algo / (us * 1e-6) / 1e9
-    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(achieved / hbm, 4), "traffic": int(traffic), "peak_source": src,
-            "kernel": "gemv_kernel (decode GEMV), config-2 gate Q4_K 9728x2560 and down Q6_K "
-                      "2560x9728 alternating, weights cycled past L2",
-            "algorithmic_bytes_per_launch": int(algo), "launch_us": round(us, 2),
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
-                              "same shapes"}
+# DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
+# dram__bytes_write.sum, config-2 model, 512-token prompt, context 516)
+STEP_TRAFFIC = None
+STEP_TRAFFIC_CTX = 516
 
 
 def decode_bytes_per_token(shape, ctx: int) -> float:
@@ -243,7 +195,6 @@ def run_gpu(args):
     barrier()
     e2e_s = time.perf_counter() - e0
     hbm, _, src = peaks()
-    kernel_roof = gemv_roofline(torch, dev, hbm, src)
 
     total_ms, pre_ms, dec_ms, e2e_s, greedy_ms, sampled_ms = rdist.max_over_ranks(
         [total_ms, pre_ms, dec_ms, e2e_s, greedy_ms, sampled_ms], dist, f"cuda:{dev}")
@@ -291,11 +242,19 @@ def run_gpu(args):
         "prefill_tflops": round(prefill_flops / (pre_ms / args.steps / 1e3) / 1e12, 2),
         "greedy_tok_s": round(DECODE * args.steps * world / (greedy_ms / 1e3), 2),
         "sampled_tok_s": round(DECODE * args.steps * world / (sampled_ms / 1e3), 2),
-        "roofline": kernel_roof,
-        "step_roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
-                          "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                          "what": "whole decode step: weights + KV bytes per token / time per token",
-                          "bytes_per_token": int(bytes_tok), "peak_source": src},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4),
+                     "traffic": (int(STEP_TRAFFIC + (bytes_tok - decode_bytes_per_token(shape, STEP_TRAFFIC_CTX)))
+                                 if STEP_TRAFFIC else None),
+                     "peak_source": src,
+                     "kernel": "step_kernel: one launch per decode token runs all 36 layers and the "
+                               "lm_head (the graph's other launch, the single-block sampler, is "
+                               "under 1% of the step)",
+                     "algorithmic_bytes_per_launch": int(bytes_tok),
+                     "launch_us": round(per_tok_s * 1e6, 2),
+                     "timing": "CUDA events on the session stream around the decode loops",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
+                                       f"context {STEP_TRAFFIC_CTX}, KV bytes scaled to the mean context"},
         "e2e": {"value": round(e2e_tok, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * (PROMPT + 1),
                 "d2h_bytes_per_step": 4 * (2 * shape.vocab + 2 * DECODE)},

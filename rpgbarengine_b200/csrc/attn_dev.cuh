@@ -38,6 +38,26 @@ __device__ __forceinline__ float4 norm_rope_head(float4 v, const float* w, const
   return make_float4(o[0], o[1], o[2], o[3]);
 }
 
+// The same with the gains g and the lane's cosines c and sines sn (dims
+// (4 lane + k) & 63) already in registers.
+__device__ __forceinline__ float4 norm_rope_head_pre(float4 v, float4 g, float4 c, float4 sn, float eps,
+                                                     int lane) {
+  double ss = (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  ss = warp_sum(ss);
+  const float scale = (float)(1.0 / sqrt(ss / 128.0 + (double)eps));
+  const float y[4] = {v.x * scale * g.x, v.y * scale * g.y, v.z * scale * g.z, v.w * scale * g.w};
+  const float cc[4] = {c.x, c.y, c.z, c.w}, ss4[4] = {sn.x, sn.y, sn.z, sn.w};
+  float o[4];
+  const bool lo = lane < 16;  // dims < 64
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[k], 16);
+    o[k] = lo ? __fsub_rn(__fmul_rn(y[k], cc[k]), __fmul_rn(partner, ss4[k]))
+              : __fadd_rn(__fmul_rn(y[k], cc[k]), __fmul_rn(partner, ss4[k]));
+  }
+  return make_float4(o[0], o[1], o[2], o[3]);
+}
+
 __device__ __forceinline__ float dot4(float4 a, float4 b) {
   return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
 }

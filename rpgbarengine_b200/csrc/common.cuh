@@ -156,6 +156,27 @@ RPGC_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread up to `ns` nanoseconds (woken early
+// when the phase completes), so a waiting warp does not spin on the issue
+// slots other warps need.
+RPGC_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with suspension: at most kMaxSleepPolls polls of up to 2 us.
+constexpr uint32_t kMaxSleepPolls = 1u << 19;
+RPGC_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < kMaxSleepPolls; ++i)
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+  if (err) atomicOr(err, kErrTimeout);
+  return false;
+}
 // Bounded wait: returns false (and sets the error flag) if the phase never
 // completed within kMaxPolls polls.
 RPGC_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {

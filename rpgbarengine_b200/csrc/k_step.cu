@@ -63,6 +63,8 @@ constexpr int kAttnWarps = 8;              // warps that score positions
 constexpr uint32_t kMaxBarrierPolls = 1u << 22;
 constexpr int kRec = 132;                  // floats per attention partial record (16-byte multiple)
 constexpr int kMaxItems = 4;               // activation items per consumer thread (K <= 8 * 4 * 480)
+constexpr int kMaxNormItems = 2;           // ... with RMSNorm gains (the first round)
+static_assert(kMaxNormItems == 2 && kMaxItems % 2 == 0, "prologue rounds of two items");
 
 struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
   int32_t rows;
@@ -156,7 +158,7 @@ __device__ __forceinline__ void phase_signal(const StepParams& P, int tid) {
 
 // ============================================================== producer
 __device__ __forceinline__ void slot_acquire(uint64_t* empty, const RingPos& rp, int32_t* err) {
-  if (rp.wrapped) mbar_wait(&empty[rp.slot], rp.parity ^ 1u, err);
+  if (rp.wrapped) mbar_wait_sleep(&empty[rp.slot], rp.parity ^ 1u, err);
 }
 
 __device__ void producer(const StepParams& P, uint64_t* full, uint64_t* empty, SDesc* desc,
@@ -244,9 +246,9 @@ __device__ __forceinline__ float gemv_prologue(const StepParams& P, const PhaseD
   const int K = ph.K, NI = K / 8, U = ph.U;
   const bool norm = ph.norm_w != nullptr;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 g0[kMaxItems], g1[kMaxItems];
+  float4 g0[kMaxNormItems], g1[kMaxNormItems];
 #pragma unroll
-  for (int b = 0; b < kMaxItems; ++b) {
+  for (int b = 0; b < kMaxNormItems; ++b) {
     const int i = b * kNC + tid;
     g0[b] = g1[b] = make_float4(1.f, 1.f, 1.f, 1.f);
     if (norm && i < NI) {
@@ -255,25 +257,34 @@ __device__ __forceinline__ float gemv_prologue(const StepParams& P, const PhaseD
     }
   }
   phase_wait(P, target, tid);
-  float4 v0[kMaxItems], v1[kMaxItems];
-#pragma unroll
-  for (int b = 0; b < kMaxItems; ++b) {
-    const int i = b * kNC + tid;
-    v0[b] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
-    v1[b] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
-  }
   double ss = 0.0;
+  // two items per round, both rounds' loads in flight before any use
+#pragma unroll 1
+  for (int b0 = 0; b0 < kMaxItems; b0 += 2) {
+    if (b0 * kNC >= NI) break;  // uniform
+    float4 v0[2], v1[2];
 #pragma unroll
-  for (int b = 0; b < kMaxItems; ++b) {
-    if (b * kNC >= NI) break;  // uniform
-    const int i = b * kNC + tid;
-    const float4 a = v0[b], c = v1[b];
-    if (norm)
-      ss += (double)a.x * a.x + (double)a.y * a.y + (double)a.z * a.z + (double)a.w * a.w +
-            (double)c.x * c.x + (double)c.y * c.y + (double)c.z * c.z + (double)c.w * c.w;
-    const float4 x0 = make_float4(a.x * g0[b].x, a.y * g0[b].y, a.z * g0[b].z, a.w * g0[b].w);
-    const float4 x1 = make_float4(c.x * g1[b].x, c.y * g1[b].y, c.z * g1[b].z, c.w * g1[b].w);
-    quantize_item(x0, x1, i, i < NI, U, lim, ucon);
+    for (int k = 0; k < 2; ++k) {
+      const int i = (b0 + k) * kNC + tid;
+      v0[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
+      v1[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int b = b0 + k;
+      if (b * kNC >= NI) break;  // uniform
+      const int i = b * kNC + tid;
+      const float4 a = v0[k], c = v1[k];
+      if (norm)
+        ss += (double)a.x * a.x + (double)a.y * a.y + (double)a.z * a.z + (double)a.w * a.w +
+              (double)c.x * c.x + (double)c.y * c.y + (double)c.z * c.z + (double)c.w * c.w;
+      float4 x0 = a, x1 = c;
+      if (b0 == 0) {  // gains cover the first two items (host check)
+        x0 = make_float4(a.x * g0[k].x, a.y * g0[k].y, a.z * g0[k].z, a.w * g0[k].w);
+        x1 = make_float4(c.x * g1[k].x, c.y * g1[k].y, c.z * g1[k].z, c.w * g1[k].w);
+      }
+      quantize_item(x0, x1, i, i < NI, U, lim, ucon);
+    }
   }
   if (norm) {
     ss = warp_sum(ss);
@@ -347,7 +358,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
 #pragma unroll 1
       for (int k = 0; k < nst; ++k, rp.advance(NS)) {
         const int slot = rp.slot;
-        mbar_wait(&full[slot], rp.parity, P.err);
+        mbar_wait_sleep(&full[slot], rp.parity, P.err);
         const SDesc d = desc[slot];
         const int jr0 = (int)d.r - lo;
         rows(d, slot, L, G.type, (int)G.row_bytes, red + base + jr0 * Ur, red + base + (nrows + jr0) * Ur);
@@ -410,7 +421,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
 #pragma unroll 1
     for (int k = 0; k < nst; ++k, rp.advance(NS)) {
       const int slot = rp.slot;
-      mbar_wait(&full[slot], rp.parity, P.err);
+      mbar_wait_sleep(&full[slot], rp.parity, P.err);
       const SDesc d = desc[slot];
       if (k == chunk0) chunk_r0 = (int32_t)d.r;
       const int jr0 = (k - chunk0) * L.m;
@@ -462,16 +473,21 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
   float* wm = wo + kAttnWarps * G * 128;
   float* wl = wm + kAttnWarps * G;
   float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  // constants of the QK-norm and the rotation, before the phase barrier
+  const float4 rc = __ldg(reinterpret_cast<const float4*>(cs + ((4 * lane) & 63)));
+  const float4 rs = __ldg(reinterpret_cast<const float4*>(cs + 64 + ((4 * lane) & 63)));
+  const float4 gq = __ldg(reinterpret_cast<const float4*>(A.q_norm) + lane);
+  const float4 gk = __ldg(reinterpret_cast<const float4*>(A.k_norm) + lane);
   phase_wait(P, target, tid);
   if (has_item) {
     if (warp < G) {
       float4 v = __ldcg(reinterpret_cast<const float4*>(A.q + (kh * G + warp) * 128) + lane);
-      v = attn::norm_rope_head(v, A.q_norm, cs, P.eps, lane);
+      v = attn::norm_rope_head_pre(v, gq, rc, rs, P.eps, lane);
       reinterpret_cast<float4*>(qs + warp * 128)[lane] = v;
     }
     if (owner && warp == kAttnWarps) {  // the new token's k and v: into the cache
       knew = __ldcg(reinterpret_cast<const float4*>(A.k_new + kh * 128) + lane);
-      knew = attn::norm_rope_head(knew, A.k_norm, cs, P.eps, lane);
+      knew = attn::norm_rope_head_pre(knew, gk, rc, rs, P.eps, lane);
       vnew = __ldcg(reinterpret_cast<const float4*>(A.v_new + kh * 128) + lane);
       const int64_t off = ((int64_t)kh * P.max_seq + pos) * 128 + 4 * lane;
       *reinterpret_cast<float4*>(A.kc + off) = knew;
@@ -491,7 +507,7 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
   RingPos rp = *rpp;
   for (int t0 = c0; t0 < c1; t0 += P.tile_pos, rp.advance(NS)) {
     const int slot = rp.slot;
-    mbar_wait(&full[slot], rp.parity, P.err);
+    mbar_wait_sleep(&full[slot], rp.parity, P.err);
     const int tn = min(P.tile_pos, c1 - t0);
     float* Ks = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes);
     float* Vs = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes + P.attn_half);
@@ -721,6 +737,7 @@ bool plan_gemv(const StepGemv& g, PhaseDev* d, int* slot_need) {
   }
   if (g.seg[g.nseg - 1].mode == kSwiGLU) return false;
   if (g.K / 8 > kMaxItems * kNC) return false;
+  if (g.norm_w && g.K / 8 > kMaxNormItems * kNC) return false;
   d->red_floats = red;
   d->deferred = 0;
   d->half_bytes = half;

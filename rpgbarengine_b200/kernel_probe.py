@@ -8,6 +8,7 @@ mix) shapes, for timing and profiler captures of a single kernel.
   python -m rpgbarengine_b200.kernel_probe gemm-q 512    # Q4_K 4096 x 2560
   python -m rpgbarengine_b200.kernel_probe gemm-down 512 # Q6_K 2560 x 9728
   python -m rpgbarengine_b200.kernel_probe attn 767      # decode attention, 32 / 8 heads, pos 767
+  python -m rpgbarengine_b200.kernel_probe step 4        # config-2 model: 512-token prefill, 4 decode steps
 
 Weights are seeded random blocks of the benchmark's distributions; each
 launch reads its own weight copy, the copies together larger than L2.
@@ -49,6 +50,13 @@ def main(argv):
             else:
                 rb.matmul_batch(ty, w, rows, cols, X, out=out)
         work = f"{name} {rows}x{cols} n={n}"
+    elif kind == "step":  # the whole token loop: prefill launches, then persistent decode steps
+        shape = synth.QWEN3_4B_Q4KM
+        model = rb.Model.upload(shape, synth.build_tensors(shape, 1234), 0, 4096)
+        sess = model.session(800)
+        sess.forward_full(synth.prompt_ids(42, 512))
+        print("tokens", sess.generate(arg or 4))
+        return
     elif kind == "attn":
         pos = arg or 767
         max_seq = pos + 1
