@@ -104,6 +104,19 @@ RPGC_API int32_t rpgc_model_upload(int device, const rpgc_model_config* cfg,
 /* Parses a GGUF v1-v3 file (src/gguf.cc:69-160), reads the qwen3.*
  * hyper-parameters (src/model.cc:159-211) and uploads it. */
 RPGC_API int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos);
+/* Tensor parallelism (the 8B shape: column-split q/k/v/gate/up and untied
+ * output, row-split o and down, one NCCL all-reduce after each row-split
+ * matmul, the logits' vocabulary slices all-gathered).  One process (or
+ * thread) per GPU: one rank calls rpgc_tp_id (a 128-byte NCCL unique id),
+ * every rank passes the same bytes with its rank to rpgc_model_upload_tp and
+ * then makes the same session calls in the same order (each holds
+ * collectives).  The tensor table is the whole model's; each rank uploads its
+ * shard.  Needs libnccl.so.2 at run time. */
+RPGC_API int rpgc_tp_id(void* id, int64_t bytes);
+RPGC_API int32_t rpgc_model_upload_tp(int device, const rpgc_model_config* cfg,
+                                      const rpgc_tensor* tensors, int32_t n_tensors, int32_t rank,
+                                      int32_t world, const void* id);
+/* The whole model's configuration (also for a tensor-parallel shard). */
 RPGC_API int rpgc_model_get_config(int32_t model, rpgc_model_config* out);
 /* Raw weight bytes resident in HBM (src/model.h:139-143). */
 RPGC_API int64_t rpgc_model_weight_bytes(int32_t model);

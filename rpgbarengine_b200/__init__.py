@@ -78,6 +78,9 @@ def lib() -> C.CDLL:
         "rpgc_last_error": ([], C.c_char_p),
         "rpgc_device_count": ([], C.c_int),
         "rpgc_model_upload": ([C.c_int, C.POINTER(ModelConfig), C.POINTER(Tensor), i32], i32),
+        "rpgc_tp_id": ([C.c_void_p, C.c_int64], C.c_int),
+        "rpgc_model_upload_tp": ([C.c_int, C.POINTER(ModelConfig), C.POINTER(Tensor), i32, i32, i32,
+                                  C.c_void_p], i32),
         "rpgc_model_load_gguf": ([C.c_int, C.c_char_p, i32], i32),
         "rpgc_model_get_config": ([i32, C.POINTER(ModelConfig)], C.c_int),
         "rpgc_model_weight_bytes": ([i32], i64),
@@ -157,6 +160,21 @@ class Model:
                           max_pos, shape.rope_theta, shape.rms_eps)
         tab, keep = tensor_table(tensors)
         h = _check(lib().rpgc_model_upload(device, C.byref(cfg), tab, len(tensors)))
+        del keep
+        return cls(h)
+
+    @classmethod
+    def upload_tp(cls, shape, tensors, device: int, rank: int, world: int, nccl_id: bytes,
+                  max_pos: int = 4096) -> "Model":
+        """Rank `rank` of a `world`-way tensor-parallel model (rpgc_model_upload_tp):
+        every rank passes the whole tensor table and the same NCCL id."""
+        cfg = ModelConfig(shape.n_layers, shape.hidden, shape.n_heads, shape.n_kv_heads,
+                          shape.head_dim, shape.intermediate, shape.vocab, shape.context_length,
+                          max_pos, shape.rope_theta, shape.rms_eps)
+        tab, keep = tensor_table(tensors)
+        idbuf = C.create_string_buffer(bytes(nccl_id), len(nccl_id))
+        h = _check(lib().rpgc_model_upload_tp(device, C.byref(cfg), tab, len(tensors), rank, world,
+                                              C.cast(idbuf, C.c_void_p)))
         del keep
         return cls(h)
 
@@ -270,6 +288,14 @@ def _stream(stream) -> int:
         import torch
         return int(torch.cuda.current_stream().cuda_stream)
     return int(stream)
+
+
+def tp_unique_id() -> bytes:
+    """A new 128-byte NCCL unique id for rpgc_model_upload_tp (one rank makes
+    it and shares it with the others)."""
+    buf = C.create_string_buffer(128)
+    _check(lib().rpgc_tp_id(C.cast(buf, C.c_void_p), 128))
+    return buf.raw
 
 
 def kernel_launches() -> int:

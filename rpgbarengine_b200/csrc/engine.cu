@@ -14,6 +14,8 @@
 #include <atomic>
 #include <climits>
 #include <cstdlib>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <cstring>
 #include <initializer_list>
 #include <memory>
@@ -66,9 +68,42 @@ struct DevLayer {
   DevMatrix q, k, v, o, gate, up, down;
 };
 
+// ------------------------------------------------------------------ NCCL
+// Loaded at first use (libnccl.so.2; a host that already uses NCCL, such as
+// torch, has it mapped), so the library has no link-time NCCL dependency.
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_id = nullptr;
+  decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+};
+
+const NcclApi* nccl_api() {
+  static NcclApi api;
+  static bool ok = false;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_id = reinterpret_cast<decltype(api.get_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    ok = api.get_id && api.init_rank && api.destroy && api.all_reduce && api.all_gather && api.error_string;
+  });
+  return ok ? &api : nullptr;
+}
+
 struct Model {
   int device = 0;
-  rpgc_model_config c{};
+  rpgc_model_config c{};   // this rank's shapes (heads, kv heads, intermediate of its shard)
+  rpgc_model_config cg{};  // the whole model
+  int32_t tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;  // tensor parallelism (tp_world > 1)
   uint8_t* blob = nullptr;
   int64_t weight_bytes = 0;
   DevMatrix embd, lm_head;
@@ -83,6 +118,7 @@ struct Model {
     cudaSetDevice(device);
     if (blob) cudaFree(blob);
     if (rope) cudaFree(rope);
+    if (comm && nccl_api()) nccl_api()->destroy(comm);
     cudaSetDevice(prev);
   }
 };
@@ -98,6 +134,7 @@ struct Session {
   float *kc = nullptr, *vc = nullptr;
   float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
   float *gate = nullptr, *up = nullptr, *logits = nullptr;
+  float* logits_part = nullptr;  // tensor parallelism: this rank's vocabulary slice
   int32_t *ids = nullptr, *gen_out = nullptr, *n_out = nullptr;
   void* gscratch = nullptr;  // prefill GEMM: split activations
   size_t gscratch_bytes = 0;
@@ -181,7 +218,21 @@ struct TensorRef {
   size_t offset = 0;
 };
 
-int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tensors, int n) {
+// One uploaded piece of a tensor: all of it, a range of its rows, or a range
+// of its columns (the same block range of every row, packed).
+struct Piece {
+  const rpgc_tensor* t = nullptr;
+  int kind = 0;  // 0 whole, 1 rows [a, b), 2 columns [a, b)
+  int64_t a = 0, b = 0;
+  size_t offset = 0, bytes = 0;
+};
+
+// Uploads the model, or with world > 1 rank `rank`'s tensor-parallel shard:
+// q/k/v/gate/up and the untied output split by rows (heads, intermediate
+// rows, vocabulary), o and down by columns (the same block range of every
+// row), everything else whole.
+int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tensors, int n,
+               int32_t rank = 0, int32_t world = 1, const void* nccl_id = nullptr) {
   const rpgc_model_config& c = cfg;
   if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
       c.head_dim <= 0 || c.intermediate <= 0 || c.vocab <= 0)
@@ -196,8 +247,17 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
       fail(RPGC_E_ARG, "GQA group %d unsupported (1, 2, 4 or 8)", g);
   }
   if (c.hidden % 256 || c.intermediate % 32) fail(RPGC_E_ARG, "hidden/intermediate not block aligned");
-  if (!gemv_supported(c.hidden, true) || !gemv_supported(c.intermediate, false) ||
-      !gemv_supported((int64_t)c.n_heads * c.head_dim, false))
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    fail(RPGC_E_ARG, "tensor-parallel rank %d of %d", rank, world);
+  if (world > 1 && (c.n_heads % world || c.n_kv_heads % world || c.intermediate % world || c.vocab % world))
+    fail(RPGC_E_ARG, "heads %d, kv heads %d, intermediate %d and vocab %d must divide by %d ranks",
+         c.n_heads, c.n_kv_heads, c.intermediate, c.vocab, world);
+  rpgc_model_config cl = c;  // this rank's shapes
+  cl.n_heads /= world;
+  cl.n_kv_heads /= world;
+  cl.intermediate /= world;
+  if (!gemv_supported(c.hidden, true) || !gemv_supported(cl.intermediate, false) ||
+      !gemv_supported((int64_t)cl.n_heads * c.head_dim, false))
     fail(RPGC_E_ARG, "decode kernels need hidden, intermediate and heads*head_dim to be multiples of "
                      "128 within the decode kernel's limits");
   int ndev = 0;
@@ -235,19 +295,51 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
 
   auto model = std::make_unique<Model>();
   model->device = device;
-  model->c = c;
-  std::vector<const rpgc_tensor*> order;
+  model->c = cl;
+  model->cg = c;
+  model->tp_rank = rank;
+  model->tp_world = world;
+  std::vector<Piece> pieces;
+  std::unordered_map<const rpgc_tensor*, size_t> piece_of;
+  auto add = [&](const rpgc_tensor* t, int kind, int64_t a, int64_t b) {
+    Piece pc;
+    pc.t = t;
+    pc.kind = kind;
+    pc.a = a;
+    pc.b = b;
+    if (kind == 0) {
+      pc.bytes = (size_t)t->n_bytes;
+    } else {
+      const int64_t rows = t->dims[1], cols = t->dims[0];
+      pc.bytes = kind == 1 ? (size_t)((b - a) * row_bytes_of(t->type, cols))
+                           : (size_t)(rows * row_bytes_of(t->type, b - a));
+    }
+    piece_of[t] = pieces.size();
+    pieces.push_back(pc);
+  };
+  auto rows_of = [&](const rpgc_tensor* t) {  // this rank's row range
+    const int64_t r = t->dims[1] / world;
+    add(t, world > 1 ? 1 : 0, r * rank, r * (rank + 1));
+  };
+  auto cols_of = [&](const rpgc_tensor* t) {  // this rank's column range
+    const int64_t k = t->dims[0] / world;
+    int64_t be = 0, bb = 0;
+    if (!ggml_block(t->type, &be, &bb) || k % be)
+      fail(RPGC_E_ARG, "tensor %s: %lld columns per rank split a %lld-element block", t->name,
+           (long long)k, (long long)be);
+    add(t, world > 1 ? 2 : 0, k * rank, k * (rank + 1));
+  };
   const rpgc_tensor* emb = require("token_embd.weight");
   check_matrix(emb, c.vocab, H);
-  order.push_back(emb);
+  add(emb, 0, 0, 0);
   const rpgc_tensor* out = find("output.weight");
   if (out) {
     check_matrix(out, c.vocab, H);
-    order.push_back(out);
+    rows_of(out);
   }
   const rpgc_tensor* onorm = require("output_norm.weight");
   check_norm(onorm, H);
-  order.push_back(onorm);
+  add(onorm, 0, 0, 0);
   struct LT {
     const rpgc_tensor *an, *fn, *qn, *kn, *q, *k, *v, *o, *g, *u, *d;
   };
@@ -277,35 +369,70 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
     check_matrix(t.g, F, H);
     check_matrix(t.u, F, H);
     check_matrix(t.d, H, F);
-    for (const rpgc_tensor* x : {t.an, t.fn, t.qn, t.kn, t.q, t.k, t.v, t.o, t.g, t.u, t.d})
-      order.push_back(x);
+    for (const rpgc_tensor* x : {t.an, t.fn, t.qn, t.kn}) add(x, 0, 0, 0);
+    rows_of(t.q);
+    rows_of(t.k);
+    rows_of(t.v);
+    cols_of(t.o);
+    rows_of(t.g);
+    rows_of(t.u);
+    cols_of(t.d);
   }
-  std::unordered_map<const rpgc_tensor*, size_t> off;
   size_t total = 0;
-  for (const rpgc_tensor* t : order) {
-    off[t] = total;
-    total += ((size_t)t->n_bytes + 255) & ~size_t(255);
+  for (Piece& pc : pieces) {
+    pc.offset = total;
+    total += (pc.bytes + 255) & ~size_t(255);
   }
   DeviceGuard dg(device);
+  if (world > 1) {
+    const NcclApi* api = nccl_api();
+    if (!api) fail(RPGC_E_STATE, "tensor parallelism needs libnccl.so.2");
+    if (!nccl_id) fail(RPGC_E_ARG, "null NCCL id");
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof(id));
+    const ncclResult_t r = api->init_rank(&model->comm, world, id, rank);
+    if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclCommInitRank: %s", api->error_string(r));
+  }
   CK(cudaMalloc(&model->blob, total));
-  for (const rpgc_tensor* t : order) {
+  for (const Piece& pc : pieces) {
+    const rpgc_tensor* t = pc.t;
     if (!t->data) fail(RPGC_E_ARG, "tensor %s has no data", t->name);
-    CK(cudaMemcpy(model->blob + off[t], t->data, (size_t)t->n_bytes, cudaMemcpyHostToDevice));
+    const uint8_t* src = static_cast<const uint8_t*>(t->data);
+    if (pc.kind == 0) {
+      CK(cudaMemcpy(model->blob + pc.offset, src, pc.bytes, cudaMemcpyHostToDevice));
+    } else if (pc.kind == 1) {
+      const int64_t rb = row_bytes_of(t->type, t->dims[0]);
+      CK(cudaMemcpy(model->blob + pc.offset, src + pc.a * rb, pc.bytes, cudaMemcpyHostToDevice));
+    } else {
+      const int64_t rb = row_bytes_of(t->type, t->dims[0]), w = row_bytes_of(t->type, pc.b - pc.a);
+      const int64_t skip = row_bytes_of(t->type, pc.a);
+      CK(cudaMemcpy2D(model->blob + pc.offset, (size_t)w, src + skip, (size_t)rb, (size_t)w,
+                      (size_t)t->dims[1], cudaMemcpyHostToDevice));
+    }
   }
   model->weight_bytes = 0;
-  for (const rpgc_tensor* t : order) model->weight_bytes += t->n_bytes;
+  for (const Piece& pc : pieces) model->weight_bytes += (int64_t)pc.bytes;
   auto mat = [&](const rpgc_tensor* t) {
+    const Piece& pc = pieces[piece_of[t]];
     DevMatrix d;
     d.type = t->type;
-    d.rows = t->dims[1];
-    d.cols = t->dims[0];
+    d.rows = pc.kind == 1 ? pc.b - pc.a : t->dims[1];
+    d.cols = pc.kind == 2 ? pc.b - pc.a : t->dims[0];
     d.row_bytes = row_bytes_of(t->type, d.cols);
-    d.w = model->blob + off[t];
+    d.w = model->blob + pc.offset;
     return d;
   };
-  auto vec = [&](const rpgc_tensor* t) { return reinterpret_cast<const float*>(model->blob + off[t]); };
+  auto vec = [&](const rpgc_tensor* t) {
+    return reinterpret_cast<const float*>(model->blob + pieces[piece_of[t]].offset);
+  };
   model->embd = mat(emb);
-  model->lm_head = out ? mat(out) : model->embd;
+  if (out) {
+    model->lm_head = mat(out);
+  } else {  // tied: this rank's vocabulary rows of the embedding table
+    model->lm_head = model->embd;
+    model->lm_head.rows = c.vocab / world;
+    model->lm_head.w = model->embd.w + (int64_t)rank * model->lm_head.rows * model->embd.row_bytes;
+  }
   model->out_norm = vec(onorm);
   model->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -382,6 +509,7 @@ int32_t session_create(int32_t model, int32_t max_seq) {
   s->gate = s->alloc<float>(s->cap * F);
   s->up = s->alloc<float>(s->cap * F);
   s->logits = s->alloc<float>(c.vocab);
+  if (m->tp_world > 1) s->logits_part = s->alloc<float>(c.vocab / m->tp_world);
   {
     int64_t kmax = H > qd ? H : qd;
     kmax = kmax > F ? kmax : F;
@@ -420,6 +548,27 @@ GemvSeg seg_of(const DevMatrix& d, float* out, int32_t mode) {
   s.mode = mode;
   return s;
 }
+
+// ------------------------------------------------ tensor-parallel collectives
+// Sum of every rank's partial `buf` (count floats) in place.
+void tp_all_reduce(Session* s, float* buf, size_t count) {
+  const Model* m = s->m;
+  if (m->tp_world <= 1) return;
+  const ncclResult_t r = nccl_api()->all_reduce(buf, buf, count, ncclFloat, ncclSum, m->comm, s->stream);
+  if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclAllReduce: %s", nccl_api()->error_string(r));
+}
+// The ranks' vocabulary slices of the logits (logits_part) into s->logits.
+void tp_gather_logits(Session* s) {
+  const Model* m = s->m;
+  const ncclResult_t r = nccl_api()->all_gather(s->logits_part, s->logits, (size_t)m->c.vocab / m->tp_world,
+                                                ncclFloat, m->comm, s->stream);
+  if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclAllGather: %s", nccl_api()->error_string(r));
+}
+// Row-split matmuls (o, down) under tensor parallelism: rank 0 adds its
+// partial to the residual, the others store theirs, and the all-reduce sums
+// them into the new residual on every rank.
+int32_t residual_mode(const Session* s) { return s->m->tp_rank == 0 ? kAdd : kStore; }
+float* lm_head_out(Session* s) { return s->m->tp_world > 1 ? s->logits_part : s->logits; }
 
 // Bytes of the next launch's rows each CTA prefetches into L2 per matrix.
 constexpr int32_t kPrefetchBytes = 64 * 1024;
@@ -462,7 +611,7 @@ bool step_kernel_enabled() {
 void ensure_step_plan(Session* s) {
   if (s->step_planned) return;
   s->step_planned = true;
-  if (!step_kernel_enabled()) return;
+  if (!step_kernel_enabled() || s->m->tp_world > 1) return;  // collectives run between launches
   const Model* m = s->m;
   const rpgc_model_config& c = m->c;
   const size_t lc = s->layer_cache_floats();
@@ -577,10 +726,11 @@ void launch_layers_step(Session* s) {
     aa.pdl = true;
     check(attn_decode_launch(aa, cs), "attn decode");
     GemvArgs go = step_gemv(s, s->attn, qd, nullptr);
-    go.seg[0] = seg_of(L.o, s->x, kAdd);
+    go.seg[0] = seg_of(L.o, s->x, residual_mode(s));
     go.nseg = 1;
     prefetch_of(&go, {&L.gate, &L.up});
     check(gemv_launch(go, cs, true), "gemv o");
+    tp_all_reduce(s, s->x, c.hidden);
     GemvArgs gf = step_gemv(s, s->x, c.hidden, L.ffn_norm);
     gf.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
     gf.seg[1] = seg_of(L.up, s->gate, kStore);
@@ -588,7 +738,7 @@ void launch_layers_step(Session* s) {
     prefetch_of(&gf, {&L.down});
     check(gemv_launch(gf, cs, true), "gemv gate/up");
     GemvArgs gd = step_gemv(s, s->gate, c.intermediate, nullptr);
-    gd.seg[0] = seg_of(L.down, s->x, kAdd);
+    gd.seg[0] = seg_of(L.down, s->x, residual_mode(s));
     gd.nseg = 1;
     if (l + 1 < c.n_layers) {
       const DevLayer& N = m->layers[l + 1];
@@ -597,12 +747,14 @@ void launch_layers_step(Session* s) {
       prefetch_of(&gd, {&m->lm_head});
     }
     check(gemv_launch(gd, cs, true), "gemv down");
+    tp_all_reduce(s, s->x, c.hidden);
   }
   GemvArgs gl = step_gemv(s, s->x, c.hidden, m->out_norm);
-  gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+  gl.seg[0] = seg_of(m->lm_head, lm_head_out(s), kStore);
   gl.nseg = 1;
   prefetch_of(&gl, {&m->layers[0].q, &m->layers[0].k, &m->layers[0].v});  // the next step
   check(gemv_launch(gl, cs, true), "gemv lm_head");
+  if (m->tp_world > 1) tp_gather_logits(s);
 }
 
 // One decode step for ids[0] at st->pos (the host set the state).
@@ -628,9 +780,14 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
     check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
+    // q, k and v share their input: one fp16 split of it serves the three
+    // tensor-core GEMMs
+    const bool tq = gemm_uses_tc(L.q.type, nc, H, s->gscratch_bytes);
+    const bool tk = gemm_uses_tc(L.k.type, nc, H, s->gscratch_bytes);
+    const bool tv = gemm_uses_tc(L.v.type, nc, H, s->gscratch_bytes);
     check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, s->gscratch, s->gscratch_bytes, cs), "gemm q");
-    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs), "gemm k");
-    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs), "gemm v");
+    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs, tq && tk), "gemm k");
+    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs, (tq || tk) && tv && tk), "gemm v");
     QkvArgs qa{};
     qa.q = s->q;
     qa.k = s->k;
@@ -660,12 +817,19 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
     aa.pos0 = pos0;
     aa.n = nc;
     check(attn_prefill_launch(aa, cs), "attn prefill");
-    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, true, s->gscratch, s->gscratch_bytes, cs), "gemm o");
+    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm o");
+    tp_all_reduce(s, s->x, (size_t)nc * H);
     check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
     check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm gate");
-    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm up");
-    check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
-    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, true, s->gscratch, s->gscratch_bytes, cs), "gemm down");
+    if (gemm_uses_tc(L.gate.type, nc, H, s->gscratch_bytes) && gemm_uses_tc(L.up.type, nc, H, s->gscratch_bytes)) {
+      // same input as the gate projection; SwiGLU in the epilogue, in place
+      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true, s->gate), "gemm up");
+    } else {
+      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm up");
+      check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
+    }
+    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm down");
+    tp_all_reduce(s, s->x, (size_t)nc * H);
   }
 }
 
@@ -696,7 +860,10 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
   DeviceGuard dg(s->device);
   s->has_logits = false;
   float* all_dev = nullptr;
+  float* all_part = nullptr;  // tensor parallelism: [world][rows][vocab / world] gathered slices
+  const int64_t vl = c.vocab / m->tp_world;
   if (all) CK(cudaMalloc(&all_dev, (size_t)s->cap * c.vocab * sizeof(float)));
+  if (all && m->tp_world > 1) CK(cudaMalloc(&all_part, (size_t)(m->tp_world + 1) * s->cap * vl * sizeof(float)));
   try {
     for (int64_t t0 = 0; t0 < n; t0 += s->cap) {
       const int64_t nc = std::min<int64_t>(s->cap, n - t0);
@@ -712,22 +879,35 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
         if (all) {
           check(rmsnorm_rows_launch(s->x, m->out_norm, nc, c.hidden, c.rms_eps, s->h, s->stream),
                 "rmsnorm");
-          check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, c.hidden,
-                            m->lm_head.row_bytes, s->h, nc, all_dev, c.vocab, false, s->gscratch,
-                            s->gscratch_bytes, s->stream),
-                "gemm lm_head");
+          if (m->tp_world > 1) {  // this rank's slice, gathered, then interleaved by rows
+            float* mine = all_part + (size_t)m->tp_world * s->cap * vl;
+            check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, c.hidden,
+                              m->lm_head.row_bytes, s->h, nc, mine, vl, false, s->gscratch,
+                              s->gscratch_bytes, s->stream),
+                  "gemm lm_head");
+            const ncclResult_t r = nccl_api()->all_gather(mine, all_part, (size_t)nc * vl, ncclFloat,
+                                                          m->comm, s->stream);
+            if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclAllGather: %s", nccl_api()->error_string(r));
+            check(gather_vocab_launch(all_part, m->tp_world, nc, vl, all_dev, s->stream), "gather logits");
+          } else {
+            check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, c.hidden,
+                              m->lm_head.row_bytes, s->h, nc, all_dev, c.vocab, false, s->gscratch,
+                              s->gscratch_bytes, s->stream),
+                  "gemm lm_head");
+          }
           CK(cudaMemcpyAsync(all + t0 * c.vocab, all_dev, (size_t)nc * c.vocab * sizeof(float),
                              cudaMemcpyDeviceToHost, s->stream));
         }
         if (t0 + nc == n) {  // last row -> pending logits
           GemvArgs gl{};
-          gl.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+          gl.seg[0] = seg_of(m->lm_head, lm_head_out(s), kStore);
           gl.nseg = 1;
           gl.K = c.hidden;
           gl.x = s->x + (nc - 1) * c.hidden;
           gl.norm_w = m->out_norm;
           gl.eps = c.rms_eps;
           check(gemv_launch(gl, s->stream, false), "gemv lm_head");
+          if (m->tp_world > 1) tp_gather_logits(s);
         }
       }
       s->len += nc;
@@ -737,9 +917,11 @@ void forward(Session* s, const int32_t* ids, bool ids_on_device, int64_t n, floa
     if (last || all || !ids_on_device) CK(cudaStreamSynchronize(s->stream));
   } catch (...) {
     if (all_dev) cudaFree(all_dev);
+    if (all_part) cudaFree(all_part);
     throw;
   }
   if (all_dev) cudaFree(all_dev);
+  if (all_part) cudaFree(all_part);
   s->has_logits = true;
 }
 
@@ -907,6 +1089,27 @@ int32_t rpgc_model_upload(int device, const rpgc_model_config* cfg, const rpgc_t
   });
 }
 
+int rpgc_tp_id(void* id, int64_t bytes) {
+  return guard([&] {
+    if (!id || bytes < (int64_t)sizeof(ncclUniqueId)) fail(RPGC_E_ARG, "id buffer under %d bytes", (int)sizeof(ncclUniqueId));
+    const NcclApi* api = nccl_api();
+    if (!api) fail(RPGC_E_STATE, "tensor parallelism needs libnccl.so.2");
+    ncclUniqueId u;
+    const ncclResult_t r = api->get_id(&u);
+    if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclGetUniqueId: %s", api->error_string(r));
+    std::memcpy(id, &u, sizeof(u));
+    return RPGC_OK;
+  });
+}
+
+int32_t rpgc_model_upload_tp(int device, const rpgc_model_config* cfg, const rpgc_tensor* tensors,
+                             int32_t n_tensors, int32_t rank, int32_t world, const void* id) {
+  return guard([&] {
+    if (!cfg || !tensors || n_tensors <= 0) fail(RPGC_E_ARG, "null config or tensor table");
+    return upload(device, *cfg, tensors, n_tensors, rank, world, id);
+  });
+}
+
 int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos) {
   return guard([&] {
     if (!path || !*path) fail(RPGC_E_ARG, "empty path");
@@ -964,7 +1167,7 @@ int rpgc_model_get_config(int32_t model, rpgc_model_config* out) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!out) fail(RPGC_E_ARG, "null output");
     Model* m = model_locked(model);
-    *out = m->c;
+    *out = m->cg;
     out->max_pos = (int32_t)m->n_rope;
     return RPGC_OK;
   });

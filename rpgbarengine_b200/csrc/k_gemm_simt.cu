@@ -91,12 +91,18 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(uint32_t type, const uin
 
 size_t gemm_scratch_bytes(int64_t n, int64_t K) { return gemm_tc_scratch_bytes(n, K); }
 
+bool gemm_uses_tc(uint32_t type, int64_t n, int64_t K, size_t scratch_bytes) {
+  return scratch_bytes >= gemm_tc_scratch_bytes(n, K) && gemm_tc_supported(type, K);
+}
+
 cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K,
                         int64_t row_bytes, const float* X, int64_t n, float* out, int64_t ldo,
-                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s) {
-  if (scratch && scratch_bytes >= gemm_tc_scratch_bytes(n, K) && gemm_tc_supported(type, K))
+                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s,
+                        bool x_split_ready, const float* glu) {
+  if (scratch && gemm_uses_tc(type, n, K, scratch_bytes))
     return gemm_tc_launch(type, w, rows, K, row_bytes, X, n, out, ldo, accumulate, scratch,
-                          scratch_bytes, s);
+                          scratch_bytes, s, x_split_ready, glu);
+  if (glu) return cudaErrorInvalidValue;  // the fused SwiGLU is a tensor-core epilogue
   if (K % BK != 0 || (reinterpret_cast<uintptr_t>(X) & 15)) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
   gemm_simt_kernel<<<grid, 256, 0, s>>>(type, w, rows, K, row_bytes, X, n, out, ldo,

@@ -36,16 +36,24 @@ namespace rpgc {
 namespace {
 
 constexpr int TMt = 256;  // tokens per CTA
-constexpr int TNt = 128;  // weight rows per CTA
 constexpr int TKt = 64;   // K per stage (one 128-byte swizzle row of fp16)
 constexpr int kStg = 2;
-constexpr int kDeqWarps = 8;
-constexpr int kGThreads = (2 + kDeqWarps) * 32;
-constexpr uint32_t kTmemCols = 256;  // two 128 x 128 fp32 accumulators
 constexpr int kABytes = TMt * TKt * 2;   // one of Xh / Xl per stage
-constexpr int kWBytes = TNt * TKt * 2;   // one of Wh / Wl per stage
-constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
-constexpr int kGemmSmem = kStg * kStageBytes + 1024 + 1024;  // + barriers, + alignment slack
+
+// Geometry of a tile of TN weight rows (TN = 128 or 144: the launcher takes
+// the one that fills the SMs in fewer waves).  Two dequant threads per row.
+template <int TN>
+struct Tile {
+  static constexpr int kDeqWarps = TN / 16;
+  static constexpr int kThreads = (2 + kDeqWarps) * 32;
+  static constexpr int kWBytes = TN * TKt * 2;  // one of Wh / Wl per stage
+  static constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
+  static constexpr int kSmem = kStg * kStageBytes + 1024 + 1024;  // + barriers, + alignment slack
+  static constexpr uint32_t kTmemCols = 2 * TN <= 256 ? 256u : 512u;  // two 128 x TN accumulators
+  // instruction descriptor: fp16 x fp16 -> fp32, both K-major, M = 128, N = TN
+  static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  static_assert(TN % 16 == 0 && TN <= 256 && kSmem <= 227 * 1024, "tile");
+};
 
 struct GemmArgs {
   const uint8_t* w;
@@ -58,6 +66,7 @@ struct GemmArgs {
   int32_t* err;
   uint32_t type;
   int32_t accumulate;
+  const float* glu;       // ks == 1, optional: OUT = silu(glu) * (X W^T), glu in OUT's layout
 };
 
 // ------------------------------------------------------------ tcgen05 glue
@@ -69,14 +78,12 @@ __device__ __forceinline__ uint64_t sdesc(const void* p) {
          (2ull << 61);
 }
 
-// Instruction descriptor: fp16 x fp16 -> fp32, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(TNt >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -99,6 +106,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "%3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 16 consecutive TMEM columns of this warp's 32 lanes -> 16 registers.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers.
@@ -254,9 +276,13 @@ __device__ __forceinline__ void split8(const float* v, uint4* hi, uint4* lo) {
 // rows and the 128-byte swizzle (chunk index XOR row mod 8).
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-__global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_h,
-                                                               const __grid_constant__ CUtensorMap tm_l,
-                                                               const GemmArgs g) {
+template <int TN>
+__global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_h,
+                                                                        const __grid_constant__ CUtensorMap tm_l,
+                                                                        const GemmArgs g) {
+  using T = Tile<TN>;
+  constexpr int kStageBytes = T::kStageBytes, kWBytes = T::kWBytes, kDeqWarps = T::kDeqWarps;
+  constexpr uint32_t kTmemCols = T::kTmemCols;
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStg * kStageBytes);
@@ -271,7 +297,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   auto Wl = [&](int s) { return gsm + s * kStageBytes + 2 * kABytes + kWBytes; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * TNt;  // first weight row
+  const int64_t n0 = (int64_t)blockIdx.x * TN;   // first weight row
   const int t0 = (int)blockIdx.y * TMt;          // first token
   const int nk_all = (int)(g.K / TKt);
   const int kc0 = (int)((int64_t)nk_all * blockIdx.z / g.ks);  // this CTA's stages
@@ -325,10 +351,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
           for (int mb = 0; mb < 2; ++mb) {
             const uint64_t ah = sdesc(Ah(s) + mb * (128 * 128) + kk * 32);
             const uint64_t al = sdesc(Al(s) + mb * (128 * 128) + kk * 32);
-            const uint32_t d = tmem + (uint32_t)(mb * 128);
-            mma_f16(d, ah, bh, (c > 0 || kk > 0) ? 1u : 0u);
-            mma_f16(d, ah, bl, 1u);
-            mma_f16(d, al, bh, 1u);
+            const uint32_t d = tmem + (uint32_t)(mb * TN);
+            mma_f16(d, ah, bh, T::kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+            mma_f16(d, ah, bl, T::kIdesc, 1u);
+            mma_f16(d, al, bh, T::kIdesc, 1u);
           }
         }
         mma_commit(&empty[s]);  // the stage may be refilled once these MMAs are done
@@ -337,7 +363,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
     }
   } else {
     // ------------------------------------------------ weight dequant
-    const int dt = tid - 64;                 // 0..255
+    const int dt = tid - 64;                 // 0 .. 2 TN - 1
     const int r = dt >> 1, half = dt & 1;    // tile row, 32-element half of the stage's 64
     const int64_t gr = n0 + r;
     const uint8_t* row = g.w + gr * g.row_bytes;
@@ -377,26 +403,36 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       if (live && c + 2 < nk) fetch32(g.type, row, k0 + 2 * TKt, raw1);
     }
     // ------------------------------------------------ epilogue
+    // warps 2..9 read the accumulators (warp w reads TMEM lanes 32 (w % 4) ..
+    // of token half mb); with 144-row tiles the ninth dequant warp has none
     mbar_wait(acc_full, 0, g.err);
     tc_fence_after();
     const int ew = warp - 2, mb = ew >> 2, quarter = warp & 3;
-    const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
-    const int64_t t = t0 + tl;
-    const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
-    const bool part = g.ks > 1;
-    float* obase = part ? g.out + ((int64_t)blockIdx.z * g.n + t) * g.rows : g.out + t * g.ldo;
+    if (ew < 8) {
+      const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
+      const int64_t t = t0 + tl;
+      const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
+      const bool part = g.ks > 1;
+      float* obase = part ? g.out + ((int64_t)blockIdx.z * g.n + t) * g.rows : g.out + t * g.ldo;
+      const float* gbase = g.glu ? g.glu + t * g.ldo : nullptr;
 #pragma unroll 1
-    for (int j = 0; j < TNt / 32; ++j) {
-      float v[32];
-      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mb * 128 + 32 * j), v);
-      if (t < g.n) {
-        float* o = obase + n0 + 32 * j;
-        const int64_t lim = g.rows - (n0 + 32 * j);  // columns left in the matrix
+      for (int j = 0; j < TN / 16; ++j) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mb * TN + 16 * j), v);
+        if (t < g.n) {
+          float* o = obase + n0 + 16 * j;
+          const int64_t lim = g.rows - (n0 + 16 * j);  // columns left in the matrix
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < lim) {
-            const float y = v[i] * inv;
-            o[i] = (g.accumulate && !part) ? o[i] + y : y;
+          for (int i = 0; i < 16; ++i) {
+            if (i < lim) {
+              const float y = v[i] * inv;
+              if (gbase) {  // SwiGLU with the gate projection already in OUT's layout
+                const float gv = gbase[n0 + 16 * j + i];
+                o[i] = (gv / (1.0f + expf(-gv))) * y;
+              } else {
+                o[i] = (g.accumulate && !part) ? o[i] + y : y;
+              }
+            }
           }
         }
       }
@@ -493,9 +529,40 @@ bool gemm_tc_supported(uint32_t type, int64_t K) {
          (type == kQ4_K || type == kQ6_K || type == kQ8_0 || type == kF32);
 }
 
+namespace {
+
+template <int TN>
+cudaError_t launch_tile(const CUtensorMap& mh, const CUtensorMap& ml, const GemmArgs& g, dim3 grid,
+                        cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<TN>::kSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  gemm_tc_kernel<TN><<<grid, Tile<TN>::kThreads, Tile<TN>::kSmem, s>>>(mh, ml, g);
+  return cudaGetLastError();
+}
+
+// Split-K factor for a tile shape: enough K partitions to fill the GPU
+// once, at least 8 stages each, partial sums within the scratch.
+int64_t split_k(int64_t tiles, int64_t rows, int64_t K, int nsm) {
+  int64_t ks = tiles >= nsm ? 1 : nsm / tiles;
+  const int64_t nk = K / TKt;
+  if (ks > nk / 8) ks = nk / 8 > 0 ? nk / 8 : 1;
+  while (ks > 1 && ks * rows > kMaxPartRows) --ks;
+  return ks;
+}
+
+}  // namespace
+
 cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
                            const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
-                           void* scratch, size_t scratch_bytes, cudaStream_t s) {
+                           void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
+                           const float* glu) {
   if (!gemm_tc_supported(type, K) || n <= 0 || rows <= 0 ||
       scratch_bytes < gemm_tc_scratch_bytes(n, K) || (reinterpret_cast<uintptr_t>(scratch) & 255))
     return cudaErrorInvalidValue;
@@ -506,20 +573,17 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   float* part = reinterpret_cast<float*>(
       static_cast<uint8_t*>(scratch) +
       (((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255));
-  act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  count_launches(1);
+  cudaError_t e;
+  if (!x_split_ready) {  // else the scratch holds the split of this same X (the caller's promise)
+    act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    count_launches(1);
+  }
   CUtensorMap mh, ml;
   if (!make_x_map(&mh, xh, n, K) || !make_x_map(&ml, xl, n, K)) return cudaErrorInvalidValue;
-  static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-    if (e != cudaSuccess) return e;
-    configured[dev] = 1;
-  }
   GemmArgs g;
   g.w = w;
   g.rows = rows;
@@ -532,8 +596,7 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   g.err = nullptr;
   g.type = type;
   g.accumulate = accumulate ? 1 : 0;
-  // Split K when the tiles alone leave SMs idle: enough partitions to fill
-  // the GPU once, at least 8 stages each, partial sums within the scratch.
+  g.glu = glu;
   static int sms[64] = {0};
   if (dev >= 0 && dev < 64 && !sms[dev]) {
     int v = 0;
@@ -541,16 +604,26 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
     sms[dev] = v > 0 ? v : 148;
   }
   const int nsm = (dev >= 0 && dev < 64) ? sms[dev] : 148;
-  const int64_t tiles = ((rows + TNt - 1) / TNt) * ((n + TMt - 1) / TMt);
-  int64_t ks = tiles >= nsm ? 1 : nsm / tiles;
-  const int64_t nk = K / TKt;
-  if (ks > nk / 8) ks = nk / 8 > 0 ? nk / 8 : 1;
-  while (ks > 1 && ks * rows > kMaxPartRows) --ks;
+  // tile height: the one with the least work per SM (waves x rows per tile / K partitions)
+  const int64_t ttok = (n + TMt - 1) / TMt;
+  int64_t best_tn = 128, best_ks = 1;
+  double best_cost = 1e30;
+  for (const int64_t tn : {128, 144}) {
+    const int64_t tiles = ((rows + tn - 1) / tn) * ttok;
+    const int64_t ks = glu ? 1 : split_k(tiles, rows, K, nsm);
+    const int64_t waves = (tiles * ks + nsm - 1) / nsm;
+    const double cost = (double)waves * (double)tn / (double)ks;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best_tn = tn;
+      best_ks = ks;
+    }
+  }
+  const int64_t ks = best_ks;
   g.ks = (int32_t)ks;
   g.out = ks > 1 ? part : out;
-  dim3 grid((unsigned)((rows + TNt - 1) / TNt), (unsigned)((n + TMt - 1) / TMt), (unsigned)ks);
-  gemm_tc_kernel<<<grid, kGThreads, kGemmSmem, s>>>(mh, ml, g);
-  e = cudaGetLastError();
+  dim3 grid((unsigned)((rows + best_tn - 1) / best_tn), (unsigned)ttok, (unsigned)ks);
+  e = best_tn == 144 ? launch_tile<144>(mh, ml, g, grid, s) : launch_tile<128>(mh, ml, g, grid, s);
   if (e == cudaSuccess) count_launches(1);
   if (e != cudaSuccess || ks == 1) return e;
   const int64_t total = n * rows;

@@ -2,6 +2,8 @@
 // bookkeeping.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -123,6 +125,28 @@ cudaError_t state_set_launch(DecodeState* st, const DecodeState& v, cudaStream_t
 
 cudaError_t advance_launch(DecodeState* st, cudaStream_t s) {
   advance_kernel<<<1, 1, 0, s>>>(st);
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
+}
+
+// dst[t][r * vl + j] = src[r][t][j]: the ranks' vocabulary slices of nc
+// rows of logits, gathered rank-major, interleaved back into rows.
+__global__ void gather_vocab_kernel(const float* __restrict__ src, int world, int64_t nc, int64_t vl,
+                                    float* __restrict__ dst) {
+  const int64_t total = (int64_t)world * nc * vl;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (nc * vl), rem = i - r * nc * vl, t = rem / vl, j = rem - t * vl;
+    dst[t * world * vl + r * vl + j] = src[i];
+  }
+}
+
+cudaError_t gather_vocab_launch(const float* src, int world, int64_t nc, int64_t vl, float* dst,
+                                cudaStream_t s) {
+  const int64_t total = (int64_t)world * nc * vl;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+  gather_vocab_kernel<<<blocks, 256, 0, s>>>(src, world, nc, vl, dst);
   const cudaError_t e_ = cudaGetLastError();
   if (e_ == cudaSuccess) count_launches(1);
   return e_;

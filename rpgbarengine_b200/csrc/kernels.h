@@ -73,6 +73,11 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s, bool pdl);
 // RMSNorm gain when norm is set).
 bool gemv_supported(int64_t K, bool norm);
 
+// Tensor parallelism: rows of logits gathered rank-major ([world][nc][vl])
+// interleaved into [nc][world * vl].
+cudaError_t gather_vocab_launch(const float* src, int world, int64_t nc, int64_t vl, float* dst,
+                                cudaStream_t s);
+
 // ------------------------------------------------- persistent decode step
 // One matrix-vector phase of the step (up to three segments sharing x).
 struct StepGemv {
@@ -120,16 +125,24 @@ cudaError_t step_launch(const StepPlan* plan, const DecodeState* st, const float
 // Prefill matmul OUT[t][r] (+)= dot(X[t], W[r]).  With scratch of at least
 // gemm_scratch_bytes(n, K) bytes (256-byte aligned) and K a multiple of 64 it
 // runs on the tensor cores (tcgen05); otherwise on CUDA cores.
+// x_split_ready (tensor-core path): the scratch already holds the fp16 split
+// of this same X from the previous call (GEMMs that share their input).
+// glu (tensor-core path, no split-K): OUT = silu(glu) * (X W^T), glu in OUT's
+// layout (may be OUT itself): the SwiGLU of a gate projection fused.
 cudaError_t gemm_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K,
                         int64_t row_bytes, const float* X, int64_t n, float* out, int64_t ldo,
-                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s);
+                        bool accumulate, void* scratch, size_t scratch_bytes, cudaStream_t s,
+                        bool x_split_ready = false, const float* glu = nullptr);
+// Whether gemm_launch takes the tensor-core path for these arguments.
+bool gemm_uses_tc(uint32_t type, int64_t n, int64_t K, size_t scratch_bytes);
 size_t gemm_scratch_bytes(int64_t n, int64_t K);
 // tensor-core path (k_gemm_tc.cu)
 size_t gemm_tc_scratch_bytes(int64_t n, int64_t K);
 bool gemm_tc_supported(uint32_t type, int64_t K);
 cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
                            const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
-                           void* scratch, size_t scratch_bytes, cudaStream_t s);
+                           void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
+                           const float* glu);
 
 // -------------------------------------------------------------- others
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,

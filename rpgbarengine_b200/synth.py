@@ -96,9 +96,13 @@ TINY_MIX = Qwen3Shape("tiny-mix", 2, 512, 768, 4, 2, vocab=1024, context_length=
 TINY_Q8 = replace(QWEN3_1_7B_Q8_0, name="tiny-q8_0", n_layers=2, hidden=256, intermediate=512,
                   n_heads=2, n_kv_heads=1, vocab=768, context_length=1024)
 TINY_UNTIED = replace(TINY_MIX, name="tiny-untied", tied=False, t_out=Q6_K)
+# The 8B shape's block types and untied output, small enough for a 2-GPU
+# tensor-parallel parity test (every split block-aligned at 2 ranks).
+TINY_TP = replace(QWEN3_8B_Q8_0, name="tiny-tp-q8_0", n_layers=2, hidden=512, intermediate=1024,
+                  n_heads=4, n_kv_heads=2, vocab=1024, context_length=1024)
 
 SHAPES = {s.name: s for s in (QWEN3_1_7B_Q8_0, QWEN3_4B_Q4KM, QWEN3_8B_Q8_0, TINY_MIX, TINY_Q8,
-                              TINY_UNTIED)}
+                              TINY_UNTIED, TINY_TP)}
 
 
 def _f16_bytes(x: np.ndarray) -> np.ndarray:
