@@ -90,8 +90,8 @@ class Clocks:
 # same kernel on the same matrices): gate 14.08 MB, down 20.56 MB.
 # DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
 # dram__bytes_write.sum, config-2 model, 512-token prompt, context 516)
-STEP_TRAFFIC = None
-STEP_TRAFFIC_CTX = 516
+STEP_TRAFFIC = 2_832_019_712  # dram read + write of one step_kernel launch, ncu, context 514
+STEP_TRAFFIC_CTX = 514
 
 
 def decode_bytes_per_token(shape, ctx: int) -> float:
