@@ -6,8 +6,9 @@
 // src/model.cc:32-69): OUT[t][r] (+)= dot(X[t], W[r]).
 //
 // Precision.  The tensor cores multiply fp16 operands into fp32.  Each
-// weight is dequantised bit-exactly (the reference's fp32 value) and split
-// into fp16 hi + lo (W = Wh + Wl to 2^-22); each token row of X is scaled by
+// weight is dequantised to the reference's fp32 value (Q4_K: within one
+// rounding of it) and split into fp16 hi + lo (W = Wh + Wl to 2^-22); each
+// token row of X is scaled by
 // a power of two and split the same way (X s = Xh + Xl).  Three products
 // Xh Wh + Xh Wl + Xl Wh accumulate over the whole K in TMEM; the dropped
 // Xl Wl term and the fp16 roundings leave ~2^-21 of sum|a w|, inside the
@@ -189,18 +190,22 @@ __device__ __forceinline__ void fetch32(uint32_t type, const uint8_t* row, int64
   }
 }
 
-// Small non-negative integer -> float without the conversion unit: the
-// float with bits 0x4B000000 | q is 2^23 + q.
-__device__ __forceinline__ float small_int_f(uint32_t q) {
-  return __uint_as_float(0x4B000000u | q) - 8388608.0f;
+// Byte J of w as a float without the conversion unit: the float with bits
+// 0x4B000000 | byte is 2^23 + byte; `bias` removes 2^23 and any offset of
+// the format (exact: every operand is an integer below 2^24).
+template <int J>
+__device__ __forceinline__ float byte_as_f(uint32_t w, float bias) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + J)) - bias;
 }
 
 // kWScale * the 32 weights from their raw bytes: the reference's
-// DequantizeRow values (src/quant.cc:207-217, 327-354, 396-429), computed
-// with the same fp32 operations in the same order (no contraction) on scales
-// premultiplied by the power of two kWScale, which commutes with every
-// rounding.  The factor keeps the fp16 lo halves of the split out of the
-// subnormal range.  F32 rows are read here.
+// DequantizeRow values (src/quant.cc:207-217, 327-354, 396-429) on scales
+// premultiplied by the power of two kWScale (which commutes with every
+// rounding; it keeps the fp16 lo halves of the split out of the subnormal
+// range).  Q6_K and Q8_0 take the reference's single product, so they are
+// its values exactly; Q4_K's d*sc*q - dmin*m is one fused multiply-add, at
+// most one rounding (2^-24 relative) from the reference's two, far below the
+// split's 2^-22.  F32 rows are read here.
 constexpr float kWScale = 256.0f;
 __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, const uint8_t* row,
                                           int64_t k0, float* w) {
@@ -215,31 +220,43 @@ __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, cons
       m = (byte_of(r[1], r[2], r[3], j + 4) >> 4) | ((byte_of(r[1], r[2], r[3], j) >> 6) << 4);
     }
     const float d = f16_bits_to_f32(r[0] & 0xFFFFu), dmin = f16_bits_to_f32(r[0] >> 16);
-    const float ds = __fmul_rn(d, (float)sc) * kWScale, dm = __fmul_rn(dmin, (float)m) * kWScale;
+    const float ds = __fmul_rn(d, (float)sc) * kWScale, ndm = -(__fmul_rn(dmin, (float)m) * kWScale);
+    const uint32_t sh = 4u * (uint32_t)half;
 #pragma unroll
-    for (int l = 0; l < 32; ++l) {
-      const uint32_t b = (r[4 + (l >> 2)] >> (8 * (l & 3) + 4 * half)) & 15u;
-      w[l] = __fsub_rn(__fmul_rn(ds, small_int_f(b)), dm);
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t nb = (r[4 + i] >> sh) & 0x0F0F0F0Fu;  // four quants, one per byte
+      w[4 * i] = fmaf(ds, byte_as_f<0>(nb, 8388608.0f), ndm);
+      w[4 * i + 1] = fmaf(ds, byte_as_f<1>(nb, 8388608.0f), ndm);
+      w[4 * i + 2] = fmaf(ds, byte_as_f<2>(nb, 8388608.0f), ndm);
+      w[4 * i + 3] = fmaf(ds, byte_as_f<3>(nb, 8388608.0f), ndm);
     }
   } else if (type == kQ6_K) {
     const int qd = ((int)(k0 & 255) & 127) >> 5;
     const float d = f16_bits_to_f32(r[17] & 0xFFFFu);
     const float dsc0 = __fmul_rn(d, (float)(int)(int8_t)(r[16] & 0xFFu)) * kWScale;
     const float dsc1 = __fmul_rn(d, (float)(int)(int8_t)((r[16] >> 8) & 0xFFu)) * kWScale;
-    const int nsh = qd >= 2 ? 4 : 0;
+    const uint32_t nsh = qd >= 2 ? 4u : 0u, hsh = 2u * (uint32_t)qd;
 #pragma unroll
-    for (int l = 0; l < 32; ++l) {
-      const uint32_t nib = (r[l >> 2] >> (8 * (l & 3) + nsh)) & 15u;
-      const uint32_t hb = (r[8 + (l >> 2)] >> (8 * (l & 3) + 2 * qd)) & 3u;
-      const float q = small_int_f(nib | (hb << 4)) - 32.0f;  // exact
-      w[l] = __fmul_rn(l < 16 ? dsc0 : dsc1, q);
+    for (int i = 0; i < 8; ++i) {
+      // q + 32 = low 4 bits from ql, high 2 from qh, four per word
+      const uint32_t q = ((r[i] >> nsh) & 0x0F0F0F0Fu) | (((r[8 + i] >> hsh) & 0x03030303u) << 4);
+      const float dsc = i < 4 ? dsc0 : dsc1;
+      w[4 * i] = __fmul_rn(dsc, byte_as_f<0>(q, 8388640.0f));  // 2^23 + 32
+      w[4 * i + 1] = __fmul_rn(dsc, byte_as_f<1>(q, 8388640.0f));
+      w[4 * i + 2] = __fmul_rn(dsc, byte_as_f<2>(q, 8388640.0f));
+      w[4 * i + 3] = __fmul_rn(dsc, byte_as_f<3>(q, 8388640.0f));
     }
   } else if (type == kQ8_0) {
     const float d = f16_bits_to_f32(r[0] & 0xFFFFu) * kWScale;
+    uint32_t f[9];  // quants with the sign bit flipped: q + 128 per byte
 #pragma unroll
-    for (int l = 0; l < 32; ++l) {  // byte 2 + l of the block, signed
-      const uint32_t b = (r[(l + 2) >> 2] >> (8 * ((l + 2) & 3))) & 0xFFu;
-      w[l] = __fmul_rn(small_int_f(b ^ 0x80u) - 128.0f, d);
+    for (int i = 0; i < 9; ++i) f[i] = r[i] ^ 0x80808080u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // quant l = byte 2 + l of the block
+      w[4 * i] = __fmul_rn(byte_as_f<2>(f[i], 8388736.0f), d);  // 2^23 + 128
+      w[4 * i + 1] = __fmul_rn(byte_as_f<3>(f[i], 8388736.0f), d);
+      w[4 * i + 2] = __fmul_rn(byte_as_f<0>(f[i + 1], 8388736.0f), d);
+      w[4 * i + 3] = __fmul_rn(byte_as_f<1>(f[i + 1], 8388736.0f), d);
     }
   } else {  // F32
     const float4* p = reinterpret_cast<const float4*>(row + k0 * 4);
@@ -254,17 +271,15 @@ __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, cons
   }
 }
 
-// fp16 hi/lo split of 8 values packed for a 16-byte store.
-// hi = v rounded to 11 significant bits by integer arithmetic (exactly an
-// fp16 value in range), lo = v - hi exactly, then both packed to fp16.
+// fp16 hi/lo split of 8 values packed for a 16-byte store: hi = fp16(v)
+// (round to nearest), lo = fp16(v - hi), where v - hi is exact in fp32.
 __device__ __forceinline__ void split8(const float* v, uint4* hi, uint4* lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float a = __uint_as_float((__float_as_uint(v[2 * i]) + 0x1000u) & 0xFFFFE000u);
-    const float b = __uint_as_float((__float_as_uint(v[2 * i + 1]) + 0x1000u) & 0xFFFFE000u);
-    const __half2 ph = __floats2half2_rn(a, b);
-    const __half2 pl = __floats2half2_rn(v[2 * i] - a, v[2 * i + 1] - b);
+    const __half2 ph = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    const float2 f = __half22float2(ph);
+    const __half2 pl = __floats2half2_rn(v[2 * i] - f.x, v[2 * i + 1] - f.y);
     h[i] = *reinterpret_cast<const uint32_t*>(&ph);
     l[i] = *reinterpret_cast<const uint32_t*>(&pl);
   }
@@ -329,7 +344,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     if (lane == 0) {
       for (int c = 0; c < nk; ++c) {
         const int s = c % kStg;
-        if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
+        if (c >= kStg) mbar_wait_sleep(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
         mbar_arrive_expect_tx(&full_a[s], 2 * kABytes);
         tma_load_2d(Ah(s), &tm_h, (kc0 + c) * TKt, t0, &full_a[s]);
         tma_load_2d(Al(s), &tm_l, (kc0 + c) * TKt, t0, &full_a[s]);
@@ -341,8 +356,8 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       for (int c = 0; c < nk; ++c) {
         const int s = c % kStg;
         const uint32_t ph = (uint32_t)(c / kStg) & 1u;
-        mbar_wait(&full_a[s], ph, g.err);
-        mbar_wait(&full_w[s], ph, g.err);
+        mbar_wait_sleep(&full_a[s], ph, g.err);
+        mbar_wait_sleep(&full_w[s], ph, g.err);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < TKt / 16; ++kk) {
@@ -386,7 +401,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
         for (int i = 0; i < 32; ++i) w[i] = 0.0f;
       }
-      if (c >= kStg) mbar_wait(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
+      if (c >= kStg) mbar_wait_sleep(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 hi, lo;
@@ -405,7 +420,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     // ------------------------------------------------ epilogue
     // warps 2..9 read the accumulators (warp w reads TMEM lanes 32 (w % 4) ..
     // of token half mb); with 144-row tiles the ninth dequant warp has none
-    mbar_wait(acc_full, 0, g.err);
+    mbar_wait_sleep(acc_full, 0, g.err);
     tc_fence_after();
     const int ew = warp - 2, mb = ew >> 2, quarter = warp & 3;
     if (ew < 8) {
@@ -415,6 +430,9 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       const bool part = g.ks > 1;
       float* obase = part ? g.out + ((int64_t)blockIdx.z * g.n + t) * g.rows : g.out + t * g.ldo;
       const float* gbase = g.glu ? g.glu + t * g.ldo : nullptr;
+      // 16-byte accesses when the token's rows are 16-byte aligned (n0 and the
+      // 16-column runs keep that alignment)
+      const bool vec = ((reinterpret_cast<uintptr_t>(obase) | reinterpret_cast<uintptr_t>(gbase)) & 15) == 0;
 #pragma unroll 1
       for (int j = 0; j < TN / 16; ++j) {
         float v[16];
@@ -422,6 +440,29 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
         if (t < g.n) {
           float* o = obase + n0 + 16 * j;
           const int64_t lim = g.rows - (n0 + 16 * j);  // columns left in the matrix
+          if (lim >= 16 && vec) {  // whole 64-byte run of the token's row: 16-byte accesses
+            const float* gp = gbase ? gbase + n0 + 16 * j : nullptr;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float4 y = make_float4(v[4 * q] * inv, v[4 * q + 1] * inv, v[4 * q + 2] * inv, v[4 * q + 3] * inv);
+              float4* op = reinterpret_cast<float4*>(o) + q;
+              if (gp) {
+                const float4 gv = reinterpret_cast<const float4*>(gp)[q];
+                y.x *= gv.x / (1.0f + expf(-gv.x));
+                y.y *= gv.y / (1.0f + expf(-gv.y));
+                y.z *= gv.z / (1.0f + expf(-gv.z));
+                y.w *= gv.w / (1.0f + expf(-gv.w));
+              } else if (g.accumulate && !part) {
+                const float4 p = *op;
+                y.x += p.x;
+                y.y += p.y;
+                y.z += p.z;
+                y.w += p.w;
+              }
+              *op = y;
+            }
+            continue;
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             if (i < lim) {
