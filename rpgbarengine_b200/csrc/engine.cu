@@ -780,14 +780,21 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
     check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
-    // q, k and v share their input: one fp16 split of it serves the three
-    // tensor-core GEMMs
+    // q, k and v share their input: one fp16 split of it and one launch
+    // serve the three tensor-core GEMMs
     const bool tq = gemm_uses_tc(L.q.type, nc, H, s->gscratch_bytes);
     const bool tk = gemm_uses_tc(L.k.type, nc, H, s->gscratch_bytes);
     const bool tv = gemm_uses_tc(L.v.type, nc, H, s->gscratch_bytes);
-    check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, s->gscratch, s->gscratch_bytes, cs), "gemm q");
-    check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs, tq && tk), "gemm k");
-    check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs, (tq || tk) && tv && tk), "gemm v");
+    if (tq && tk && tv) {  // one launch over the three matrices' tiles
+      const GemmGroupMat qkv[3] = {{L.q.type, L.q.w, L.q.rows, L.q.row_bytes, s->q, qd},
+                                   {L.k.type, L.k.w, L.k.rows, L.k.row_bytes, s->k, kvd},
+                                   {L.v.type, L.v.w, L.v.rows, L.v.row_bytes, s->v, kvd}};
+      check(gemm_tc_launch_group(qkv, 3, H, s->h, nc, s->gscratch, s->gscratch_bytes, cs, false), "gemm qkv");
+    } else {
+      check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, s->gscratch, s->gscratch_bytes, cs), "gemm q");
+      check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs, tq && tk), "gemm k");
+      check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs, (tq || tk) && tv && tk), "gemm v");
+    }
     QkvArgs qa{};
     qa.q = s->q;
     qa.k = s->k;

@@ -256,17 +256,19 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
 }
 
 // --------------------------------------------------------------- prefill
-// grid (n_heads, ceil(n/64)), 256 threads; hd == 128.
+// grid (n_heads, ceil(n/64)), 256 threads, two CTAs per SM; hd == 128.  The
+// causal work of a query tile grows with its index, so blockIdx.y = 0 takes
+// the last (heaviest) tile: the long CTAs start in the first wave.
 constexpr int QT = 64, KT = 64, HD = 128;
 
-__global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(256, 2) attn_prefill_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) float fsm[];
   float* Qs = fsm;             // [HD][QT]
   float* Ks = Qs + HD * QT;    // [HD][KT]
   float* Vs = Ks + HD * KT;    // [KT][HD]
-  float* Ps = Vs + KT * HD;    // [KT][QT]
+  float* Ps = Ks;              // [KT][QT], over the key tile once the scores are taken
   const int h = blockIdx.x;
-  const int64_t qt0 = (int64_t)blockIdx.y * QT;
+  const int64_t qt0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * QT;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int G = a.n_heads / a.n_kv, kh = h / G;
   const float scale = 1.0f / sqrtf((float)HD);
@@ -352,6 +354,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
       l[i] = l[i] * corr[i] + rs;
       m[i] = mn;
     }
+    __syncthreads();  // every thread's scores are taken: the key tile becomes P
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       *reinterpret_cast<float4*>(Ps + (tx * 4 + j) * QT + ty * 4) =
@@ -477,7 +480,8 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.hd != HD || a.n_heads % a.n_kv || a.n <= 0) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)(HD * QT + HD * KT + KT * HD + KT * QT) * sizeof(float);
+  static_assert(KT * QT <= HD * KT, "P fits the key tile");
+  const size_t smem = (size_t)(HD * QT + HD * KT + KT * HD) * sizeof(float);
   static int configured = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -56,16 +56,25 @@ struct Tile {
   static_assert(TN % 16 == 0 && TN <= 256 && kSmem <= 227 * 1024, "tile");
 };
 
-struct GemmArgs {
+// One matrix of a launch: blockIdx.x counts the tiles of the matrices in order
+// (a group of matrices with the same input, e.g. q, k and v, is one launch).
+struct GemmMat {
   const uint8_t* w;
-  int64_t rows, K, row_bytes;
-  int64_t n;              // tokens
+  int64_t rows, row_bytes;
   float* out;             // ks == 1: OUT; else the partial sums [ks][n][rows]
   int64_t ldo;
-  int32_t ks;             // K partitions (gridDim.z)
+  uint32_t type;
+  int32_t tiles;          // row tiles of this matrix
+};
+
+struct GemmArgs {
+  GemmMat mat[3];
+  int32_t nmat;
+  int64_t K;
+  int64_t n;              // tokens
+  int32_t ks;             // K partitions (gridDim.z; 1 for a group)
   const float* inv_scale; // per token
   int32_t* err;
-  uint32_t type;
   int32_t accumulate;
   const float* glu;       // ks == 1, optional: OUT = silu(glu) * (X W^T), glu in OUT's layout
 };
@@ -312,7 +321,10 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
   auto Wl = [&](int s) { return gsm + s * kStageBytes + 2 * kABytes + kWBytes; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * TN;   // first weight row
+  int bx = (int)blockIdx.x, mi = 0;  // the matrix of this CTA and its tile there
+  while (mi + 1 < g.nmat && bx >= g.mat[mi].tiles) bx -= g.mat[mi++].tiles;
+  const GemmMat& M = g.mat[mi];
+  const int64_t n0 = (int64_t)bx * TN;           // first weight row
   const int t0 = (int)blockIdx.y * TMt;          // first token
   const int nk_all = (int)(g.K / TKt);
   const int kc0 = (int)((int64_t)nk_all * blockIdx.z / g.ks);  // this CTA's stages
@@ -381,22 +393,22 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     const int dt = tid - 64;                 // 0 .. 2 TN - 1
     const int r = dt >> 1, half = dt & 1;    // tile row, 32-element half of the stage's 64
     const int64_t gr = n0 + r;
-    const uint8_t* row = g.w + gr * g.row_bytes;
+    const uint8_t* row = M.w + gr * M.row_bytes;
     // Raw bytes run two stages ahead: the loads for stage c + 2 are issued
     // after stage c is published (the proxy fence would otherwise wait for
     // them), and consumed after stage c + 1 has been processed.
-    const bool live = gr < g.rows;
+    const bool live = gr < M.rows;
     uint32_t raw0[kRaw], raw1[kRaw];
     if (live) {
-      fetch32(g.type, row, (int64_t)kc0 * TKt + 32 * half, raw0);
-      if (nk > 1) fetch32(g.type, row, (int64_t)(kc0 + 1) * TKt + 32 * half, raw1);
+      fetch32(M.type, row, (int64_t)kc0 * TKt + 32 * half, raw0);
+      if (nk > 1) fetch32(M.type, row, (int64_t)(kc0 + 1) * TKt + 32 * half, raw1);
     }
     for (int c = 0; c < nk; ++c) {
       const int s = c % kStg;
       const int64_t k0 = (int64_t)(kc0 + c) * TKt + 32 * half;
       float w[32];
       if (live) {
-        convert32(g.type, raw0, row, k0, w);
+        convert32(M.type, raw0, row, k0, w);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) w[i] = 0.0f;
@@ -415,21 +427,24 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       if (lane == 0) mbar_arrive(&full_w[s]);
 #pragma unroll
       for (int i = 0; i < kRaw; ++i) raw0[i] = raw1[i];
-      if (live && c + 2 < nk) fetch32(g.type, row, k0 + 2 * TKt, raw1);
+      if (live && c + 2 < nk) fetch32(M.type, row, k0 + 2 * TKt, raw1);
     }
     // ------------------------------------------------ epilogue
-    // warps 2..9 read the accumulators (warp w reads TMEM lanes 32 (w % 4) ..
-    // of token half mb); with 144-row tiles the ninth dequant warp has none
+    // the dequant warps read the accumulators: warp w may read TMEM lanes
+    // 32 (w % 4) .. + 31 only, so the nq warps with one w % 4 share that
+    // quarter of both token halves mb (8 warps: one half each; 6 warps: the
+    // two warps alone on their quarter take both halves; 9: the ninth none)
     mbar_wait_sleep(acc_full, 0, g.err);
     tc_fence_after();
-    const int ew = warp - 2, mb = ew >> 2, quarter = warp & 3;
-    if (ew < 8) {
+    const int ew = warp - 2, quarter = warp & 3, nq = (kDeqWarps - (ew & 3) + 3) >> 2;
+#pragma unroll 1
+    for (int mb = ew >> 2; mb < 2; mb += nq) {
       const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
       const int64_t t = t0 + tl;
       const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
       const bool part = g.ks > 1;
-      float* obase = part ? g.out + ((int64_t)blockIdx.z * g.n + t) * g.rows : g.out + t * g.ldo;
-      const float* gbase = g.glu ? g.glu + t * g.ldo : nullptr;
+      float* obase = part ? M.out + ((int64_t)blockIdx.z * g.n + t) * M.rows : M.out + t * M.ldo;
+      const float* gbase = g.glu ? g.glu + t * M.ldo : nullptr;
       // 16-byte accesses when the token's rows are 16-byte aligned (n0 and the
       // 16-column runs keep that alignment)
       const bool vec = ((reinterpret_cast<uintptr_t>(obase) | reinterpret_cast<uintptr_t>(gbase)) & 15) == 0;
@@ -439,7 +454,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
         tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mb * TN + 16 * j), v);
         if (t < g.n) {
           float* o = obase + n0 + 16 * j;
-          const int64_t lim = g.rows - (n0 + 16 * j);  // columns left in the matrix
+          const int64_t lim = M.rows - (n0 + 16 * j);  // columns left in the matrix
           if (lim >= 16 && vec) {  // whole 64-byte run of the token's row: 16-byte accesses
             const float* gp = gbase ? gbase + n0 + 16 * j : nullptr;
 #pragma unroll
@@ -600,14 +615,22 @@ int64_t split_k(int64_t tiles, int64_t rows, int64_t K, int nsm) {
 
 }  // namespace
 
-cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
-                           const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
-                           void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
-                           const float* glu) {
-  if (!gemm_tc_supported(type, K) || n <= 0 || rows <= 0 ||
-      scratch_bytes < gemm_tc_scratch_bytes(n, K) || (reinterpret_cast<uintptr_t>(scratch) & 255))
+namespace {
+
+// One launch over the matrices mat[0..nmat) sharing the input X (n x K):
+// the activation split (unless the scratch already holds it), the tile
+// height with the least work per SM, split-K for a single matrix, the
+// partial-sum reduction.
+cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int64_t n, bool accumulate,
+                         void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
+                         const float* glu) {
+  if (nmat < 1 || nmat > 3 || n <= 0 || scratch_bytes < gemm_tc_scratch_bytes(n, K) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255) || (nmat > 1 && (glu || accumulate)))
     return cudaErrorInvalidValue;
-  if (type == kF32 && (row_bytes & 15)) return cudaErrorInvalidValue;
+  for (int i = 0; i < nmat; ++i) {
+    if (!gemm_tc_supported(mat[i].type, K) || mat[i].rows <= 0) return cudaErrorInvalidValue;
+    if (mat[i].type == kF32 && (mat[i].row_bytes & 15)) return cudaErrorInvalidValue;
+  }
   __half* xh = static_cast<__half*>(scratch);
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
@@ -625,19 +648,6 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   if (!make_x_map(&mh, xh, n, K) || !make_x_map(&ml, xl, n, K)) return cudaErrorInvalidValue;
   int dev = 0;
   cudaGetDevice(&dev);
-  GemmArgs g;
-  g.w = w;
-  g.rows = rows;
-  g.K = K;
-  g.row_bytes = row_bytes;
-  g.n = n;
-  g.out = out;
-  g.ldo = ldo;
-  g.inv_scale = inv;
-  g.err = nullptr;
-  g.type = type;
-  g.accumulate = accumulate ? 1 : 0;
-  g.glu = glu;
   static int sms[64] = {0};
   if (dev >= 0 && dev < 64 && !sms[dev]) {
     int v = 0;
@@ -649,9 +659,11 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   const int64_t ttok = (n + TMt - 1) / TMt;
   int64_t best_tn = 128, best_ks = 1;
   double best_cost = 1e30;
-  for (const int64_t tn : {128, 144}) {
-    const int64_t tiles = ((rows + tn - 1) / tn) * ttok;
-    const int64_t ks = glu ? 1 : split_k(tiles, rows, K, nsm);
+  for (const int64_t tn : {96, 128, 144}) {
+    int64_t tiles = 0;
+    for (int i = 0; i < nmat; ++i) tiles += (mat[i].rows + tn - 1) / tn;
+    tiles *= ttok;
+    const int64_t ks = (glu || nmat > 1) ? 1 : split_k(tiles, mat[0].rows, K, nsm);
     const int64_t waves = (tiles * ks + nsm - 1) / nsm;
     const double cost = (double)waves * (double)tn / (double)ks;
     if (cost < best_cost - 1e-9) {
@@ -660,19 +672,54 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
       best_ks = ks;
     }
   }
+  GemmArgs g;
+  int64_t tiles = 0;
+  for (int i = 0; i < 3; ++i) {
+    g.mat[i] = i < nmat ? mat[i] : mat[0];
+    g.mat[i].tiles = (int32_t)((g.mat[i].rows + best_tn - 1) / best_tn);
+    if (i < nmat) tiles += g.mat[i].tiles;
+  }
+  g.nmat = nmat;
+  g.K = K;
+  g.n = n;
+  g.inv_scale = inv;
+  g.err = nullptr;
+  g.accumulate = accumulate ? 1 : 0;
+  g.glu = glu;
   const int64_t ks = best_ks;
   g.ks = (int32_t)ks;
-  g.out = ks > 1 ? part : out;
-  dim3 grid((unsigned)((rows + best_tn - 1) / best_tn), (unsigned)ttok, (unsigned)ks);
-  e = best_tn == 144 ? launch_tile<144>(mh, ml, g, grid, s) : launch_tile<128>(mh, ml, g, grid, s);
+  if (ks > 1) g.mat[0].out = part;
+  dim3 grid((unsigned)tiles, (unsigned)ttok, (unsigned)ks);
+  e = best_tn == 144   ? launch_tile<144>(mh, ml, g, grid, s)
+      : best_tn == 128 ? launch_tile<128>(mh, ml, g, grid, s)
+                       : launch_tile<96>(mh, ml, g, grid, s);
   if (e == cudaSuccess) count_launches(1);
   if (e != cudaSuccess || ks == 1) return e;
-  const int64_t total = n * rows;
-  splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(part, (int)ks, n, rows, out, ldo,
-                                                                       accumulate ? 1 : 0);
+  const int64_t total = n * mat[0].rows;
+  splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(part, (int)ks, n, mat[0].rows,
+                                                                       mat[0].out, mat[0].ldo, accumulate ? 1 : 0);
   e = cudaGetLastError();
   if (e == cudaSuccess) count_launches(1);
   return e;
+}
+
+}  // namespace
+
+cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t K, int64_t row_bytes,
+                           const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
+                           void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
+                           const float* glu) {
+  GemmMat m{w, rows, row_bytes, out, ldo, type, 0};
+  return launch_group(&m, 1, K, X, n, accumulate, scratch, scratch_bytes, s, x_split_ready, glu);
+}
+
+cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, const float* X, int64_t n,
+                                 void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready) {
+  if (nmat < 1 || nmat > 3) return cudaErrorInvalidValue;
+  GemmMat m[3];
+  for (int i = 0; i < nmat; ++i)
+    m[i] = GemmMat{mats[i].w, mats[i].rows, mats[i].row_bytes, mats[i].out, mats[i].ldo, mats[i].type, 0};
+  return launch_group(m, nmat, K, X, n, false, scratch, scratch_bytes, s, x_split_ready, nullptr);
 }
 
 }  // namespace rpgc

@@ -143,6 +143,18 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
                            const float* X, int64_t n, float* out, int64_t ldo, bool accumulate,
                            void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
                            const float* glu);
+// Up to three matrices with the same input X (q, k and v) in one tensor-core
+// launch (no split-K): OUT_i[t][r] = dot(X[t], W_i[r]).  Every matrix must
+// pass gemm_uses_tc.
+struct GemmGroupMat {
+  uint32_t type;
+  const uint8_t* w;
+  int64_t rows, row_bytes;
+  float* out;
+  int64_t ldo;
+};
+cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, const float* X, int64_t n,
+                                 void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready);
 
 // -------------------------------------------------------------- others
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,
