@@ -779,9 +779,9 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
   const size_t lc = s->layer_cache_floats();
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
-    check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
-    // q, k and v share their input: one fp16 split of it and one launch
-    // serve the three tensor-core GEMMs
+    // q, k and v share their input: one fp16 split of the normalised rows
+    // (the RMSNorm fused into it) and one launch serve the three tensor-core
+    // GEMMs
     const bool tq = gemm_uses_tc(L.q.type, nc, H, s->gscratch_bytes);
     const bool tk = gemm_uses_tc(L.k.type, nc, H, s->gscratch_bytes);
     const bool tv = gemm_uses_tc(L.v.type, nc, H, s->gscratch_bytes);
@@ -789,8 +789,10 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
       const GemmGroupMat qkv[3] = {{L.q.type, L.q.w, L.q.rows, L.q.row_bytes, s->q, qd},
                                    {L.k.type, L.k.w, L.k.rows, L.k.row_bytes, s->k, kvd},
                                    {L.v.type, L.v.w, L.v.rows, L.v.row_bytes, s->v, kvd}};
-      check(gemm_tc_launch_group(qkv, 3, H, s->h, nc, s->gscratch, s->gscratch_bytes, cs, false), "gemm qkv");
+      check(gemm_tc_split_norm(s->x, L.attn_norm, c.rms_eps, nc, H, s->gscratch, s->gscratch_bytes, cs), "norm split");
+      check(gemm_tc_launch_group(qkv, 3, H, nullptr, nc, s->gscratch, s->gscratch_bytes, cs, true), "gemm qkv");
     } else {
+      check(rmsnorm_rows_launch(s->x, L.attn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
       check(gemm_launch(L.q.type, L.q.w, L.q.rows, H, L.q.row_bytes, s->h, nc, s->q, qd, false, s->gscratch, s->gscratch_bytes, cs), "gemm q");
       check(gemm_launch(L.k.type, L.k.w, L.k.rows, H, L.k.row_bytes, s->h, nc, s->k, kvd, false, s->gscratch, s->gscratch_bytes, cs, tq && tk), "gemm k");
       check(gemm_launch(L.v.type, L.v.w, L.v.rows, H, L.v.row_bytes, s->h, nc, s->v, kvd, false, s->gscratch, s->gscratch_bytes, cs, (tq || tk) && tv && tk), "gemm v");
@@ -826,12 +828,15 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
     check(attn_prefill_launch(aa, cs), "attn prefill");
     check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm o");
     tp_all_reduce(s, s->x, (size_t)nc * H);
-    check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
-    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm gate");
     if (gemm_uses_tc(L.gate.type, nc, H, s->gscratch_bytes) && gemm_uses_tc(L.up.type, nc, H, s->gscratch_bytes)) {
-      // same input as the gate projection; SwiGLU in the epilogue, in place
-      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true, s->gate), "gemm up");
+      // the normalised rows only as their fp16 split; the up projection has
+      // the gate projection's input and SwiGLU in its epilogue, in place
+      check(gemm_tc_split_norm(s->x, L.ffn_norm, c.rms_eps, nc, H, s->gscratch, s->gscratch_bytes, cs), "norm split");
+      check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, nullptr, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true), "gemm gate");
+      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, nullptr, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true, s->gate), "gemm up");
     } else {
+      check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
+      check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm gate");
       check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm up");
       check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
     }

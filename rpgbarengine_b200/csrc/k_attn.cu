@@ -6,6 +6,7 @@
 // (src/kv_cache.cc:29-33), AttentionFromCache with a softmax over [0, pos]
 // (src/qwen3.cc:79-117).
 #include <cooperative_groups.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "attn_dev.cuh"
@@ -256,20 +257,66 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
 }
 
 // --------------------------------------------------------------- prefill
-// grid (n_heads, ceil(n/64)), 256 threads, two CTAs per SM; hd == 128.  The
-// causal work of a query tile grows with its index, so blockIdx.y = 0 takes
-// the last (heaviest) tile: the long CTAs start in the first wave.
-constexpr int QT = 64, KT = 64, HD = 128;
+// Causal attention of n new tokens over the cache (keys [0, pos0 + t]) on the
+// tensor cores: warp-level mma.sync m16n8k16, fp16 operands, fp32
+// accumulators.  Scores and the probability-weighted sum keep fp32-class
+// accuracy by the three-product split used by the prefill matmul: every
+// operand x = xh + xl (fp16 hi, fp16 residual), products Ah Bh + Ah Bl + Al Bh
+// (the dropped Al Bl and the roundings leave ~2^-21 of sum |a b|).  The
+// online softmax (running max, rescaled sums) is fp32 in registers, as in the
+// reference's AttentionFromCache (src/qwen3.cc:79-117: scores q.k/sqrt(hd),
+// softmax, sum of p v).
+//
+// grid (n_heads, ceil(n/64)), 128 threads: warp w owns queries 16w..16w+15 of
+// the CTA's 64; per 64-key tile the CTA stages K and V as fp16 hi/lo rows
+// [key][dim] (padded to 136 halves: conflict-free ldmatrix); each warp then
+// forms S = Q K^T (16 x 64), the softmax update and O += P V (16 x 128), the
+// P fragments taken straight from the S accumulators.  blockIdx.y = 0 takes
+// the last (heaviest) query tile.  P enters the split scaled by 2^14 (p <= 1
+// stays below the fp16 maximum, and p down to 2^-38 keeps a normal lo half);
+// the final 1 / (2^14 l) removes it exactly.
+constexpr int QT = 64, KT = 64, HD = 128, KP = HD + 8;
+constexpr float kPScale = 16384.0f;
 
-__global__ void __launch_bounds__(256, 2) attn_prefill_kernel(const AttnArgs a) {
-  extern __shared__ __align__(16) float fsm[];
-  float* Qs = fsm;             // [HD][QT]
-  float* Ks = Qs + HD * QT;    // [HD][KT]
-  float* Vs = Ks + HD * KT;    // [KT][HD]
-  float* Ps = Ks;              // [KT][QT], over the key tile once the scores are taken
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// (a, b) -> fp16 pairs hi = fp16(a, b), lo = fp16(a - hi, b - hi).
+__device__ __forceinline__ void split2(float a, float b, uint32_t* hi, uint32_t* lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 f = __half22float2(h);
+  *hi = h2_bits(h);
+  *lo = h2_bits(__floats2half2_rn(a - f.x, b - f.y));
+}
+
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Four 8x8 fp16 matrices (rows of 16 bytes at the lanes' addresses).
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) __half hsm[];
+  __half* Kh = hsm;            // [KT][KP]
+  __half* Kl = Kh + KT * KP;
+  __half* Vh = Kl + KT * KP;
+  __half* Vl = Vh + KT * KP;
   const int h = blockIdx.x;
   const int64_t qt0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * QT;
-  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int G = a.n_heads / a.n_kv, kh = h / G;
   const float scale = 1.0f / sqrtf((float)HD);
   const int64_t qpos0 = a.pos0 + qt0;
@@ -278,113 +325,150 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(const AttnArgs a) 
   const float* kb = a.kc + (int64_t)kh * a.max_seq * HD;
   const float* vb = a.vc + (int64_t)kh * a.max_seq * HD;
 
-  for (int idx = tid; idx < QT * (HD / 4); idx += 256) {
-    const int i = idx % QT, c = idx / QT;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (i < nq) v = *reinterpret_cast<const float4*>(a.q + ((qt0 + i) * a.n_heads + h) * HD + 4 * c);
-    Qs[(4 * c + 0) * QT + i] = v.x;
-    Qs[(4 * c + 1) * QT + i] = v.y;
-    Qs[(4 * c + 2) * QT + i] = v.z;
-    Qs[(4 * c + 3) * QT + i] = v.w;
-  }
-  float m[4], l[4], o[4][8];
+  // the warp's query rows r0 = 16 w + g and r1 = r0 + 8 as A fragments, k16
+  // step kk: {(r0, 2t..), (r1, 2t..), (r0, 8+2t..), (r1, 8+2t..)} of dims 16kk..
+  const int r0 = 16 * warp + g;
+  uint32_t qh[8][4], ql[8][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m[i] = kNegBig;
-    l[i] = 0.0f;
+  for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[i][j] = 0.0f;
-  }
+    for (int e = 0; e < 4; ++e) {
+      const int row = r0 + 8 * (e & 1), col = 16 * kk + 8 * (e >> 1) + 2 * t;
+      float2 v = make_float2(0.f, 0.f);
+      if (row < nq) v = *reinterpret_cast<const float2*>(a.q + ((qt0 + row) * a.n_heads + h) * HD + col);
+      split2(v.x, v.y, &qh[kk][e], &ql[kk][e]);
+    }
+  float o[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+  float m0 = kNegBig, m1 = kNegBig, l0 = 0.0f, l1 = 0.0f;  // rows r0, r1 (l: this lane's columns)
+  const int64_t qp0 = qpos0 + r0, qp1 = qp0 + 8;
+  // ldmatrix row addresses: lane L gives row L & 7 of matrix L >> 3
+  const int mi = lane >> 3, mr = lane & 7;
+  const uint32_t kh_base = smem_u32(Kh), kl_base = smem_u32(Kl), vh_base = smem_u32(Vh), vl_base = smem_u32(Vl);
+  // S operand: matrices (keys +0, dims +0), (keys +0, dims +8), (keys +8, dims +0), (keys +8, dims +8)
+  const uint32_t koff = (uint32_t)(((8 * (mi >> 1) + mr) * KP + 8 * (mi & 1)) * 2);
+  // PV operand (transposed): (keys +0, dims +0), (keys +8, dims +0), (keys +0, dims +8), (keys +8, dims +8)
+  const uint32_t voff = (uint32_t)(((8 * (mi & 1) + mr) * KP + 8 * (mi >> 1)) * 2);
+
   for (int64_t k0 = 0; k0 < key_end; k0 += KT) {
+    __syncthreads();  // the previous tile's fragments are all read
+    for (int idx = tid; idx < KT * (HD / 4); idx += 128) {
+      const int j = idx >> 5, c = idx & 31;  // key j, dims 4c .. 4c + 3
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (k0 + j < key_end) {
+        kv = *reinterpret_cast<const float4*>(kb + (k0 + j) * HD + 4 * c);
+        vv = *reinterpret_cast<const float4*>(vb + (k0 + j) * HD + 4 * c);
+      }
+      uint32_t h0, l0w, h1, l1w;
+      split2(kv.x, kv.y, &h0, &l0w);
+      split2(kv.z, kv.w, &h1, &l1w);
+      *reinterpret_cast<uint2*>(Kh + j * KP + 4 * c) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(Kl + j * KP + 4 * c) = make_uint2(l0w, l1w);
+      split2(vv.x, vv.y, &h0, &l0w);
+      split2(vv.z, vv.w, &h1, &l1w);
+      *reinterpret_cast<uint2*>(Vh + j * KP + 4 * c) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(Vl + j * KP + 4 * c) = make_uint2(l0w, l1w);
+    }
     __syncthreads();
-    for (int idx = tid; idx < KT * (HD / 4); idx += 256) {
-      const int j = idx % KT, c = idx / KT;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + j < key_end) kv = *reinterpret_cast<const float4*>(kb + (k0 + j) * HD + 4 * c);
-      Ks[(4 * c + 0) * KT + j] = kv.x;
-      Ks[(4 * c + 1) * KT + j] = kv.y;
-      Ks[(4 * c + 2) * KT + j] = kv.z;
-      Ks[(4 * c + 3) * KT + j] = kv.w;
+    // ---- S = Q K^T: n-tile n = keys 8n .. 8n + 7 of the tile
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const uint32_t off = koff + (uint32_t)((16 * np * KP + 16 * kk) * 2);
+        uint32_t bh[4], bl[4];
+        ldsm4(kh_base + off, bh);
+        ldsm4(kl_base + off, bl);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float* c = sc[2 * np + q];
+          mma16816(c, qh[kk], bh[2 * q], bh[2 * q + 1]);
+          mma16816(c, qh[kk], bl[2 * q], bl[2 * q + 1]);
+          mma16816(c, ql[kk], bh[2 * q], bh[2 * q + 1]);
+        }
+      }
+    // ---- scale, causal mask, online softmax
+    float mx0 = kNegBig, mx1 = kNegBig;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int64_t key = k0 + 8 * n + 2 * t + (c & 1);
+        const int64_t qp = c < 2 ? qp0 : qp1;
+        const float v = (key <= qp && key < key_end) ? sc[n][c] * scale : kNegBig;
+        sc[n][c] = v;
+        if (c < 2) mx0 = fmaxf(mx0, v);
+        else mx1 = fmaxf(mx1, v);
+      }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float corr0 = expf(m0 - mn0), corr1 = expf(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    l0 *= corr0;
+    l1 *= corr1;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      o[d][0] *= corr0;
+      o[d][1] *= corr0;
+      o[d][2] *= corr1;
+      o[d][3] *= corr1;
     }
-    for (int idx = tid; idx < KT * (HD / 4); idx += 256) {
-      const int j = idx / (HD / 4), c = idx % (HD / 4);
-      float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + j < key_end) vv = *reinterpret_cast<const float4*>(vb + (k0 + j) * HD + 4 * c);
-      *reinterpret_cast<float4*>(Vs + j * HD + 4 * c) = vv;
-    }
-    __syncthreads();
-    float s[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
-#pragma unroll 8
-    for (int d = 0; d < HD; ++d) {
-      const float4 qv = *reinterpret_cast<const float4*>(Qs + d * QT + ty * 4);
-      const float4 kv = *reinterpret_cast<const float4*>(Ks + d * KT + tx * 4);
-      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qa[i], ka[j], s[i][j]);
-    }
-    float corr[4];
+    // ---- O += P V, k16 step i = keys 16i .. 16i + 15 = n-tiles 2i, 2i + 1
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int64_t qp = qpos0 + ty * 4 + i;
-      float rmax = kNegBig;
+      float p[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t kp = k0 + tx * 4 + j;
-        s[i][j] = (kp <= qp && kp < key_end) ? s[i][j] * scale : -INFINITY;
-        rmax = fmaxf(rmax, s[i][j]);
+      for (int q = 0; q < 2; ++q) {
+        p[4 * q] = expf(sc[2 * i + q][0] - m0);
+        p[4 * q + 1] = expf(sc[2 * i + q][1] - m0);
+        p[4 * q + 2] = expf(sc[2 * i + q][2] - m1);
+        p[4 * q + 3] = expf(sc[2 * i + q][3] - m1);
       }
+      l0 += (p[0] + p[1]) + (p[4] + p[5]);
+      l1 += (p[2] + p[3]) + (p[6] + p[7]);
+      uint32_t ah[4], al[4];
+      split2(p[0] * kPScale, p[1] * kPScale, &ah[0], &al[0]);  // (r0, keys 2t..)
+      split2(p[2] * kPScale, p[3] * kPScale, &ah[1], &al[1]);  // (r1, keys 2t..)
+      split2(p[4] * kPScale, p[5] * kPScale, &ah[2], &al[2]);  // (r0, keys 8+2t..)
+      split2(p[6] * kPScale, p[7] * kPScale, &ah[3], &al[3]);  // (r1, keys 8+2t..)
 #pragma unroll
-      for (int off = 1; off < 16; off <<= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
-      const float mn = fmaxf(m[i], rmax);
-      corr[i] = expf(m[i] - mn);
-      float rs = 0.0f;
+      for (int dp = 0; dp < 8; ++dp) {
+        const uint32_t off = voff + (uint32_t)((16 * i * KP + 16 * dp) * 2);
+        uint32_t bh[4], bl[4];
+        ldsm4_t(vh_base + off, bh);
+        ldsm4_t(vl_base + off, bl);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        s[i][j] = expf(s[i][j] - mn);
-        rs += s[i][j];
+        for (int q = 0; q < 2; ++q) {
+          float* c = o[2 * dp + q];
+          mma16816(c, ah, bh[2 * q], bh[2 * q + 1]);
+          mma16816(c, ah, bl[2 * q], bl[2 * q + 1]);
+          mma16816(c, al, bh[2 * q], bh[2 * q + 1]);
+        }
       }
-#pragma unroll
-      for (int off = 1; off < 16; off <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
-      l[i] = l[i] * corr[i] + rs;
-      m[i] = mn;
-    }
-    __syncthreads();  // every thread's scores are taken: the key tile becomes P
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      *reinterpret_cast<float4*>(Ps + (tx * 4 + j) * QT + ty * 4) =
-          make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[i][j] *= corr[i];
-    __syncthreads();
-#pragma unroll 4
-    for (int j = 0; j < KT; ++j) {
-      const float4 pv = *reinterpret_cast<const float4*>(Ps + j * QT + ty * 4);
-      const float4 va = *reinterpret_cast<const float4*>(Vs + j * HD + tx * 8);
-      const float4 vb2 = *reinterpret_cast<const float4*>(Vs + j * HD + tx * 8 + 4);
-      const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-      const float vr[8] = {va.x, va.y, va.z, va.w, vb2.x, vb2.y, vb2.z, vb2.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int d = 0; d < 8; ++d) o[i][d] = fmaf(pa[i], vr[d], o[i][d]);
     }
   }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.0f / (l0 * kPScale), inv1 = 1.0f / (l1 * kPScale);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t t = qt0 + ty * 4 + i;
-    if (t >= a.n) continue;
-    float* op = a.out + (t * a.n_heads + h) * HD + tx * 8;
-    const float inv = 1.0f / l[i];
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = r0 + 8 * hr;
+    if (row >= nq) continue;
+    float* op = a.out + ((qt0 + row) * a.n_heads + h) * HD + 2 * t;
+    const float inv = hr ? inv1 : inv0;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) op[d] = o[i][d] * inv;
+    for (int d = 0; d < 16; ++d)
+      *reinterpret_cast<float2*>(op + 8 * d) = make_float2(o[d][2 * hr] * inv, o[d][2 * hr + 1] * inv);
   }
 }
 
@@ -480,8 +564,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.hd != HD || a.n_heads % a.n_kv || a.n <= 0) return cudaErrorInvalidValue;
-  static_assert(KT * QT <= HD * KT, "P fits the key tile");
-  const size_t smem = (size_t)(HD * QT + HD * KT + KT * HD) * sizeof(float);
+  const size_t smem = (size_t)4 * KT * KP * sizeof(__half);
   static int configured = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -492,7 +575,7 @@ cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
     configured = dev;
   }
   dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + QT - 1) / QT));
-  attn_prefill_kernel<<<grid, 256, smem, s>>>(a);
+  attn_prefill_kernel<<<grid, 128, smem, s>>>(a);
   const cudaError_t e_ = cudaGetLastError();
   if (e_ == cudaSuccess) count_launches(1);
   return e_;

@@ -532,6 +532,44 @@ __global__ void __launch_bounds__(256) act_split_kernel(const float* __restrict_
   if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);  // undoes both scalings
 }
 
+// act_split_kernel with the RMSNorm of the row in front (src/kernels.h:56-63:
+// x * (1/sqrt(sum x^2 / K + eps), double sum) * w, the same float operations
+// as rmsnorm_rows_kernel): the normalised row exists only as its fp16 split.
+__global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict__ X, const float* __restrict__ w,
+                                                         int64_t K, float eps, __half* __restrict__ xh,
+                                                         __half* __restrict__ xl, float* __restrict__ inv_scale) {
+  __shared__ double dred[8];
+  __shared__ float red[8];
+  const int64_t t = blockIdx.x;
+  const float* x = X + t * K;
+  double ss = 0.0;
+  for (int64_t k = threadIdx.x; k < K; k += 256) ss += (double)x[k] * x[k];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) dred[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  double tot = 0.0;
+  for (int i = 0; i < 8; ++i) tot += dred[i];
+  const float nsc = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
+  float m = 0.0f;
+  for (int64_t k = threadIdx.x; k < K; k += 256) m = fmaxf(m, fabsf(x[k] * nsc * w[k]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mx = 0.0f;
+  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
+  int se = 141 - e;
+  se = se > 100 ? 100 : (se < -100 ? -100 : se);
+  const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
+  for (int64_t k = threadIdx.x; k < K; k += 256) {
+    const float v = (x[k] * nsc * w[k]) * s;
+    const __half h = __float2half_rn(v);
+    xh[t * K + k] = h;
+    xl[t * K + k] = __float2half_rn(v - __half2float(h));
+  }
+  if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);
+}
+
 // OUT[t][r] (+)= sum over the K partitions of the partial sums, in order.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int ks,
                                                             int64_t n, int64_t rows, float* out,
@@ -711,6 +749,20 @@ cudaError_t gemm_tc_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
                            const float* glu) {
   GemmMat m{w, rows, row_bytes, out, ldo, type, 0};
   return launch_group(&m, 1, K, X, n, accumulate, scratch, scratch_bytes, s, x_split_ready, glu);
+}
+
+cudaError_t gemm_tc_split_norm(const float* X, const float* norm_w, float eps, int64_t n, int64_t K,
+                               void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (n <= 0 || K <= 0 || !norm_w || scratch_bytes < gemm_tc_scratch_bytes(n, K) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255))
+    return cudaErrorInvalidValue;
+  __half* xh = static_cast<__half*>(scratch);
+  __half* xl = xh + n * K;
+  float* inv = reinterpret_cast<float*>(xl + n * K);
+  norm_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, norm_w, K, eps, xh, xl, inv);
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
+  return e;
 }
 
 cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, const float* X, int64_t n,

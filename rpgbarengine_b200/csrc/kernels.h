@@ -155,6 +155,10 @@ struct GemmGroupMat {
 };
 cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, const float* X, int64_t n,
                                  void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready);
+// The fp16 split of RMSNorm(X) * norm_w (rmsnorm_rows_launch's values) into
+// the tensor-core scratch, for the GEMMs that follow with x_split_ready.
+cudaError_t gemm_tc_split_norm(const float* X, const float* norm_w, float eps, int64_t n, int64_t K,
+                               void* scratch, size_t scratch_bytes, cudaStream_t s);
 
 // -------------------------------------------------------------- others
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,

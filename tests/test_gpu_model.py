@@ -44,8 +44,13 @@ def test_forward_logits_and_kv(orc, shape):
     k, v = s.read_kv()
     ok, ov = okv.arrays()
     n = len(ids)
-    assert rel_l2(k[:, :, :n], ok[:, :, :n]) <= 1e-5
-    assert rel_l2(v[:, :, :n], ov[:, :, :n]) <= 1e-5
+    # layer 0's rows come from the matmuls alone; later layers' rows inherit
+    # the attention's error (fp16 hi/lo three-product split on the tensor
+    # cores: ~2^-21 of sum |p v| per output, a few 1e-6 after the o projection)
+    assert rel_l2(k[0, :, :n], ok[0, :, :n]) <= 1e-5
+    assert rel_l2(v[0, :, :n], ov[0, :, :n]) <= 1e-5
+    assert rel_l2(k[:, :, :n], ok[:, :, :n]) <= 3e-5
+    assert rel_l2(v[:, :, :n], ov[:, :, :n]) <= 3e-5
     assert np.all(k[:, :, n:] == 0)
 
 
