@@ -19,9 +19,10 @@
 //   warp 1      TMEM allocation and the MMA issue (one thread): per 64-K
 //               stage 2 token blocks x 4 k16 steps x 3 products, M=128
 //               N=128 K=16 each, then tcgen05.commit frees the stage
-//   warps 2-9   dequantise the stage's weight tile into Wh / Wl (same
-//               swizzled K-major layout), then read the two 128x128 fp32
-//               accumulators back from TMEM and write OUT
+//   warps 2..   dequantise the stage's weight tile into Wh / Wl (same
+//               swizzled K-major layout; four threads per row), then read
+//               the two 128 x TN fp32 accumulators back from TMEM and
+//               write OUT
 // Two 96 KB stages; all waits are bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -41,11 +42,12 @@ constexpr int TKt = 64;   // K per stage (one 128-byte swizzle row of fp16)
 constexpr int kStg = 2;
 constexpr int kABytes = TMt * TKt * 2;   // one of Xh / Xl per stage
 
-// Geometry of a tile of TN weight rows (TN = 128 or 144: the launcher takes
-// the one that fills the SMs in fewer waves).  Two dequant threads per row.
+// Geometry of a tile of TN weight rows (TN = 96, 128 or 144: the launcher
+// takes the one with the least work per SM).  Four dequant threads per row,
+// 16 weights each per stage.
 template <int TN>
 struct Tile {
-  static constexpr int kDeqWarps = TN / 16;
+  static constexpr int kDeqWarps = TN / 8;
   static constexpr int kThreads = (2 + kDeqWarps) * 32;
   static constexpr int kWBytes = TN * TKt * 2;  // one of Wh / Wl per stage
   static constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
@@ -173,29 +175,29 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w0, uint32_t w1, uint32_t w
   return (w >> (8 * (k & 3))) & 0xFFu;
 }
 
-// Raw bytes of 32 weights [k0, k0 + 32) of one row (k0 a multiple of 32),
-// fetched one stage ahead of their use so that the global-memory latency
-// hides behind the previous stage's dequantisation.
-constexpr int kRaw = 20;  // words
-__device__ __forceinline__ void fetch32(uint32_t type, const uint8_t* row, int64_t k0, uint32_t* r) {
-  if (type == kQ4_K) {
+// Raw bytes of 16 weights [k0, k0 + 16) of one row (k0 a multiple of 16),
+// fetched two stages ahead of their use so that the global-memory latency
+// hides behind the dequantisation of the stages in between.
+constexpr int kRaw = 10;  // words
+__device__ __forceinline__ void fetch16(uint32_t type, const uint8_t* row, int64_t k0, uint32_t* r) {
+  if (type == kQ4_K) {  // header + 16 quant bytes (both nibble planes)
     const uint8_t* blk = row + (k0 >> 8) * 144;
-    const int g = (int)(k0 & 255) >> 6;
+    const int i0 = (int)(k0 & 255);
     const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * g));
-    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * g));
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (i0 >> 6) + (i0 & 31)));
     r[0] = hdr.x; r[1] = hdr.y; r[2] = hdr.z; r[3] = hdr.w;
-    r[4] = qa.x; r[5] = qa.y; r[6] = qa.z; r[7] = qa.w;
-    r[8] = qb.x; r[9] = qb.y; r[10] = qb.z; r[11] = qb.w;
-  } else if (type == kQ6_K) {
+    r[4] = q.x; r[5] = q.y; r[6] = q.z; r[7] = q.w;
+  } else if (type == kQ6_K) {  // 16 ql bytes, 16 qh bytes, the scale pair, d
     const uint8_t* blk = row + (k0 >> 8) * 210;
-    const int i0 = (int)(k0 & 255), h = i0 >> 7, qd = (i0 & 127) >> 5;
-    ldg_words<8>(blk + 64 * h + 32 * (qd & 1), r);
-    ldg_words<8>(blk + 128 + 32 * h, r + 8);
-    ldg_words<1>(blk + 192 + 8 * h + 2 * qd, r + 16);
-    ldg_words<1>(blk + 208, r + 17);
-  } else if (type == kQ8_0) {
-    ldg_words<9>(row + (k0 >> 5) * 34, r);
+    const int i0 = (int)(k0 & 255), h = i0 >> 7, qd = (i0 & 127) >> 5, o = i0 & 16;
+    ldg_words<4>(blk + 64 * h + 32 * (qd & 1) + o, r);
+    ldg_words<4>(blk + 128 + 32 * h + o, r + 4);
+    ldg_words<1>(blk + 192 + 8 * h + 2 * qd, r + 8);
+    ldg_words<1>(blk + 208, r + 9);
+  } else if (type == kQ8_0) {  // d, then the 16 quants from a word boundary
+    const uint8_t* blk = row + (k0 >> 5) * 34;
+    ldg_words<1>(blk, r);
+    ldg_words<4>(blk + 2 + (k0 & 16), r + 1);
   }
 }
 
@@ -216,7 +218,7 @@ __device__ __forceinline__ float byte_as_f(uint32_t w, float bias) {
 // most one rounding (2^-24 relative) from the reference's two, far below the
 // split's 2^-22.  F32 rows are read here.
 constexpr float kWScale = 256.0f;
-__device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, const uint8_t* row,
+__device__ __forceinline__ void convert16(uint32_t type, const uint32_t* r, const uint8_t* row,
                                           int64_t k0, float* w) {
   if (type == kQ4_K) {
     const int i0 = (int)(k0 & 255), g = i0 >> 6, half = (i0 >> 5) & 1, j = 2 * g + half;
@@ -232,7 +234,7 @@ __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, cons
     const float ds = __fmul_rn(d, (float)sc) * kWScale, ndm = -(__fmul_rn(dmin, (float)m) * kWScale);
     const uint32_t sh = 4u * (uint32_t)half;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       const uint32_t nb = (r[4 + i] >> sh) & 0x0F0F0F0Fu;  // four quants, one per byte
       w[4 * i] = fmaf(ds, byte_as_f<0>(nb, 8388608.0f), ndm);
       w[4 * i + 1] = fmaf(ds, byte_as_f<1>(nb, 8388608.0f), ndm);
@@ -240,16 +242,15 @@ __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, cons
       w[4 * i + 3] = fmaf(ds, byte_as_f<3>(nb, 8388608.0f), ndm);
     }
   } else if (type == kQ6_K) {
-    const int qd = ((int)(k0 & 255) & 127) >> 5;
-    const float d = f16_bits_to_f32(r[17] & 0xFFFFu);
-    const float dsc0 = __fmul_rn(d, (float)(int)(int8_t)(r[16] & 0xFFu)) * kWScale;
-    const float dsc1 = __fmul_rn(d, (float)(int)(int8_t)((r[16] >> 8) & 0xFFu)) * kWScale;
+    const int i0 = (int)(k0 & 255), qd = (i0 & 127) >> 5;
+    const float d = f16_bits_to_f32(r[9] & 0xFFFFu);
+    const uint32_t scb = (i0 & 16) ? (r[8] >> 8) & 0xFFu : r[8] & 0xFFu;  // 16 weights share one scale
+    const float dsc = __fmul_rn(d, (float)(int)(int8_t)scb) * kWScale;
     const uint32_t nsh = qd >= 2 ? 4u : 0u, hsh = 2u * (uint32_t)qd;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       // q + 32 = low 4 bits from ql, high 2 from qh, four per word
-      const uint32_t q = ((r[i] >> nsh) & 0x0F0F0F0Fu) | (((r[8 + i] >> hsh) & 0x03030303u) << 4);
-      const float dsc = i < 4 ? dsc0 : dsc1;
+      const uint32_t q = ((r[i] >> nsh) & 0x0F0F0F0Fu) | (((r[4 + i] >> hsh) & 0x03030303u) << 4);
       w[4 * i] = __fmul_rn(dsc, byte_as_f<0>(q, 8388640.0f));  // 2^23 + 32
       w[4 * i + 1] = __fmul_rn(dsc, byte_as_f<1>(q, 8388640.0f));
       w[4 * i + 2] = __fmul_rn(dsc, byte_as_f<2>(q, 8388640.0f));
@@ -257,20 +258,18 @@ __device__ __forceinline__ void convert32(uint32_t type, const uint32_t* r, cons
     }
   } else if (type == kQ8_0) {
     const float d = f16_bits_to_f32(r[0] & 0xFFFFu) * kWScale;
-    uint32_t f[9];  // quants with the sign bit flipped: q + 128 per byte
 #pragma unroll
-    for (int i = 0; i < 9; ++i) f[i] = r[i] ^ 0x80808080u;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {  // quant l = byte 2 + l of the block
-      w[4 * i] = __fmul_rn(byte_as_f<2>(f[i], 8388736.0f), d);  // 2^23 + 128
-      w[4 * i + 1] = __fmul_rn(byte_as_f<3>(f[i], 8388736.0f), d);
-      w[4 * i + 2] = __fmul_rn(byte_as_f<0>(f[i + 1], 8388736.0f), d);
-      w[4 * i + 3] = __fmul_rn(byte_as_f<1>(f[i + 1], 8388736.0f), d);
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t f = r[1 + i] ^ 0x80808080u;  // quants with the sign bit flipped: q + 128
+      w[4 * i] = __fmul_rn(byte_as_f<0>(f, 8388736.0f), d);  // 2^23 + 128
+      w[4 * i + 1] = __fmul_rn(byte_as_f<1>(f, 8388736.0f), d);
+      w[4 * i + 2] = __fmul_rn(byte_as_f<2>(f, 8388736.0f), d);
+      w[4 * i + 3] = __fmul_rn(byte_as_f<3>(f, 8388736.0f), d);
     }
   } else {  // F32
     const float4* p = reinterpret_cast<const float4*>(row + k0 * 4);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       const float4 v = __ldg(p + i);
       w[4 * i] = v.x * kWScale;
       w[4 * i + 1] = v.y * kWScale;
@@ -390,8 +389,8 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     }
   } else {
     // ------------------------------------------------ weight dequant
-    const int dt = tid - 64;                 // 0 .. 2 TN - 1
-    const int r = dt >> 1, half = dt & 1;    // tile row, 32-element half of the stage's 64
+    const int dt = tid - 64;                 // 0 .. 4 TN - 1
+    const int r = dt >> 2, qq = dt & 3;      // tile row, 16-element quarter of the stage's 64
     const int64_t gr = n0 + r;
     const uint8_t* row = M.w + gr * M.row_bytes;
     // Raw bytes run two stages ahead: the loads for stage c + 2 are issued
@@ -400,25 +399,25 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     const bool live = gr < M.rows;
     uint32_t raw0[kRaw], raw1[kRaw];
     if (live) {
-      fetch32(M.type, row, (int64_t)kc0 * TKt + 32 * half, raw0);
-      if (nk > 1) fetch32(M.type, row, (int64_t)(kc0 + 1) * TKt + 32 * half, raw1);
+      fetch16(M.type, row, (int64_t)kc0 * TKt + 16 * qq, raw0);
+      if (nk > 1) fetch16(M.type, row, (int64_t)(kc0 + 1) * TKt + 16 * qq, raw1);
     }
     for (int c = 0; c < nk; ++c) {
       const int s = c % kStg;
-      const int64_t k0 = (int64_t)(kc0 + c) * TKt + 32 * half;
-      float w[32];
+      const int64_t k0 = (int64_t)(kc0 + c) * TKt + 16 * qq;
+      float w[16];
       if (live) {
-        convert32(M.type, raw0, row, k0, w);
+        convert16(M.type, raw0, row, k0, w);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) w[i] = 0.0f;
+        for (int i = 0; i < 16; ++i) w[i] = 0.0f;
       }
       if (c >= kStg) mbar_wait_sleep(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         uint4 hi, lo;
         split8(w + 8 * q, &hi, &lo);
-        const uint32_t off = swz(r, 4 * half + q);
+        const uint32_t off = swz(r, 2 * qq + q);
         *reinterpret_cast<uint4*>(Wh(s) + off) = hi;
         *reinterpret_cast<uint4*>(Wl(s) + off) = lo;
       }
@@ -427,13 +426,13 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       if (lane == 0) mbar_arrive(&full_w[s]);
 #pragma unroll
       for (int i = 0; i < kRaw; ++i) raw0[i] = raw1[i];
-      if (live && c + 2 < nk) fetch32(M.type, row, k0 + 2 * TKt, raw1);
+      if (live && c + 2 < nk) fetch16(M.type, row, k0 + 2 * TKt, raw1);
     }
     // ------------------------------------------------ epilogue
     // the dequant warps read the accumulators: warp w may read TMEM lanes
     // 32 (w % 4) .. + 31 only, so the nq warps with one w % 4 share that
-    // quarter of both token halves mb (8 warps: one half each; 6 warps: the
-    // two warps alone on their quarter take both halves; 9: the ninth none)
+    // quarter of both token halves mb (the first eight warps take one
+    // (half, quarter) each, the others none)
     mbar_wait_sleep(acc_full, 0, g.err);
     tc_fence_after();
     const int ew = warp - 2, quarter = warp & 3, nq = (kDeqWarps - (ew & 3) + 3) >> 2;
