@@ -813,6 +813,7 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
     qa.eps = c.rms_eps;
     qa.pos0 = pos0;
     qa.n = nc;
+    qa.kv_only = 1;  // the attention kernel normalises and rotates q as it loads it
     check(qkv_rope_launch(qa, cs), "qkv rope");
     AttnArgs aa{};
     aa.q = s->q;
@@ -825,22 +826,28 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
     aa.hd = c.head_dim;
     aa.pos0 = pos0;
     aa.n = nc;
+    aa.q_norm = L.q_norm;
+    aa.rope = m->rope;
+    aa.eps = c.rms_eps;
     check(attn_prefill_launch(aa, cs), "attn prefill");
     check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, s->attn, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm o");
     tp_all_reduce(s, s->x, (size_t)nc * H);
-    if (gemm_uses_tc(L.gate.type, nc, H, s->gscratch_bytes) && gemm_uses_tc(L.up.type, nc, H, s->gscratch_bytes)) {
-      // the normalised rows only as their fp16 split; the up projection has
-      // the gate projection's input and SwiGLU in its epilogue, in place
+    if (gemm_uses_tc(L.gate.type, nc, H, s->gscratch_bytes) && gemm_uses_tc(L.up.type, nc, H, s->gscratch_bytes) &&
+        gemm_uses_tc(L.down.type, nc, F, s->gscratch_bytes)) {
+      // the normalised rows only as their fp16 split (gate and up share it);
+      // SwiGLU inside the split of the down projection's input
       check(gemm_tc_split_norm(s->x, L.ffn_norm, c.rms_eps, nc, H, s->gscratch, s->gscratch_bytes, cs), "norm split");
       check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, nullptr, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true), "gemm gate");
-      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, nullptr, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs, true, s->gate), "gemm up");
+      check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, nullptr, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs, true), "gemm up");
+      check(gemm_tc_split_glu(s->gate, s->up, nc, F, s->gscratch, s->gscratch_bytes, cs), "glu split");
+      check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, nullptr, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs, true), "gemm down");
     } else {
       check(rmsnorm_rows_launch(s->x, L.ffn_norm, nc, c.hidden, c.rms_eps, s->h, cs), "rmsnorm");
       check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, s->h, nc, s->gate, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm gate");
       check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, s->h, nc, s->up, F, false, s->gscratch, s->gscratch_bytes, cs), "gemm up");
       check(swiglu_launch(s->gate, s->up, nc * F, cs), "swiglu");
+      check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm down");
     }
-    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, s->gate, nc, s->x, H, m->tp_rank == 0, s->gscratch, s->gscratch_bytes, cs), "gemm down");
     tp_all_reduce(s, s->x, (size_t)nc * H);
   }
 }

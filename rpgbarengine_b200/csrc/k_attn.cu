@@ -27,7 +27,7 @@ __global__ void qkv_rope_kernel(const QkvArgs a) {
   __shared__ double red[8];
   __shared__ float y[256];
   const int64_t t = blockIdx.x;
-  const int h = blockIdx.y, i = threadIdx.x, hd = a.hd, half = hd >> 1;
+  const int h = (int)blockIdx.y + (a.kv_only ? a.n_heads : 0), i = threadIdx.x, hd = a.hd, half = hd >> 1;
   const int64_t pos = st ? (int64_t)st->pos : a.pos0 + t;
   const bool isq = h < a.n_heads;
   const int kh = h - a.n_heads;
@@ -327,15 +327,61 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) 
 
   // the warp's query rows r0 = 16 w + g and r1 = r0 + 8 as A fragments, k16
   // step kk: {(r0, 2t..), (r1, 2t..), (r0, 8+2t..), (r1, 8+2t..)} of dims 16kk..
+  // With a.q_norm the rows arrive raw and get the QK-norm and RoPE here, with
+  // qkv_rope_kernel's float operations: the four lanes of a quad hold a row's
+  // 128 dims (sum of squares over the quad, in double), and dims i and i + 64
+  // sit in steps kk and kk + 4 of the same lane.
   const int r0 = 16 * warp + g;
   uint32_t qh[8][4], ql[8][4];
+  const float* qrow[2];
+  float qsc[2] = {1.0f, 1.0f};
+  const float* qcs[2] = {nullptr, nullptr};
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = r0 + 8 * hr;
+    qrow[hr] = row < nq ? a.q + ((qt0 + row) * a.n_heads + h) * HD : nullptr;
+    if (a.q_norm) {
+      double ss = 0.0;
+      if (qrow[hr])
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const float2 v = *reinterpret_cast<const float2*>(qrow[hr] + 16 * kk + 8 * hf + 2 * t);
+            ss += (double)v.x * v.x + (double)v.y * v.y;
+          }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      qsc[hr] = (float)(1.0 / sqrt(ss / (double)HD + (double)a.eps));
+      qcs[hr] = a.rope + (row < nq ? qpos0 + row : qpos0) * HD;  // hd/2 cos then hd/2 sin
+    }
+  }
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int row = r0 + 8 * (e & 1), col = 16 * kk + 8 * (e >> 1) + 2 * t;
+      const int hr = e & 1, col = 16 * kk + 8 * (e >> 1) + 2 * t;
       float2 v = make_float2(0.f, 0.f);
-      if (row < nq) v = *reinterpret_cast<const float2*>(a.q + ((qt0 + row) * a.n_heads + h) * HD + col);
+      if (qrow[hr]) {
+        v = *reinterpret_cast<const float2*>(qrow[hr] + col);
+        if (a.q_norm) {
+          const int pc = col ^ 64;  // the rotation partner dims
+          const float2 pv = *reinterpret_cast<const float2*>(qrow[hr] + pc);
+          const float2 gv = *reinterpret_cast<const float2*>(a.q_norm + col);
+          const float2 gp = *reinterpret_cast<const float2*>(a.q_norm + pc);
+          const float y0 = v.x * qsc[hr] * gv.x, y1 = v.y * qsc[hr] * gv.y;
+          const float p0 = pv.x * qsc[hr] * gp.x, p1 = pv.y * qsc[hr] * gp.y;
+          const int j = col & 63;
+          const float c0 = qcs[hr][j], c1 = qcs[hr][j + 1], s0 = qcs[hr][64 + j], s1 = qcs[hr][64 + j + 1];
+          if (col < 64) {
+            v.x = __fsub_rn(__fmul_rn(y0, c0), __fmul_rn(p0, s0));
+            v.y = __fsub_rn(__fmul_rn(y1, c1), __fmul_rn(p1, s1));
+          } else {
+            v.x = __fadd_rn(__fmul_rn(y0, c0), __fmul_rn(p0, s0));
+            v.y = __fadd_rn(__fmul_rn(y1, c1), __fmul_rn(p1, s1));
+          }
+        }
+      }
       split2(v.x, v.y, &qh[kk][e], &ql[kk][e]);
     }
   float o[16][4];
@@ -476,7 +522,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) 
 
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s) {
   if (a.hd > 256 || (a.hd & 31) || a.n <= 0) return cudaErrorInvalidValue;
-  dim3 grid((unsigned)a.n, (unsigned)(a.n_heads + a.n_kv));
+  dim3 grid((unsigned)a.n, (unsigned)(a.kv_only ? a.n_kv : a.n_heads + a.n_kv));
   qkv_rope_kernel<<<grid, a.hd, 0, s>>>(a);
   const cudaError_t e_ = cudaGetLastError();
   if (e_ == cudaSuccess) count_launches(1);

@@ -569,15 +569,75 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict
   if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);
 }
 
+// act_split_kernel of silu(gate) * up (src/kernels.h:82-92, the same float
+// expression as swiglu_kernel): the down projection's input exists only as
+// its fp16 split.
+__global__ void __launch_bounds__(256) glu_split_kernel(const float* __restrict__ G, const float* __restrict__ U,
+                                                        int64_t K, __half* __restrict__ xh, __half* __restrict__ xl,
+                                                        float* __restrict__ inv_scale) {
+  __shared__ float red[8];
+  const int64_t t = blockIdx.x;
+  const float* g = G + t * K;
+  const float* u = U + t * K;
+  float m = 0.0f;
+  for (int64_t k = threadIdx.x; k < K; k += 256) {
+    const float v = g[k];
+    m = fmaxf(m, fabsf((v / (1.0f + expf(-v))) * u[k]));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mx = 0.0f;
+  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
+  int se = 141 - e;
+  se = se > 100 ? 100 : (se < -100 ? -100 : se);
+  const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
+  for (int64_t k = threadIdx.x; k < K; k += 256) {
+    const float v = g[k];
+    const float y = ((v / (1.0f + expf(-v))) * u[k]) * s;
+    const __half h = __float2half_rn(y);
+    xh[t * K + k] = h;
+    xl[t * K + k] = __float2half_rn(y - __half2float(h));
+  }
+  if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);
+}
+
 // OUT[t][r] (+)= sum over the K partitions of the partial sums, in order.
+// vec: four consecutive outputs per thread (16-byte accesses; the launcher
+// checks that rows, ldo and OUT allow them), else one.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int ks,
                                                             int64_t n, int64_t rows, float* out,
-                                                            int64_t ldo, int accumulate) {
+                                                            int64_t ldo, int accumulate, int vec) {
+  const int64_t total = n * rows;
+  if (vec) {
+    const int64_t i = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
+    if (i >= total) return;
+    const int64_t t = i / rows, r = i - t * rows;
+    float4 y = __ldcs(reinterpret_cast<const float4*>(part + i));
+    for (int p = 1; p < ks; ++p) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + (int64_t)p * total + i));
+      y.x += v.x;
+      y.y += v.y;
+      y.z += v.z;
+      y.w += v.w;
+    }
+    float4* o = reinterpret_cast<float4*>(out + t * ldo + r);
+    if (accumulate) {
+      const float4 c = *o;
+      y.x = c.x + y.x;
+      y.y = c.y + y.y;
+      y.z = c.z + y.z;
+      y.w = c.w + y.w;
+    }
+    *o = y;
+    return;
+  }
   const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  if (i >= n * rows) return;
+  if (i >= total) return;
   const int64_t t = i / rows, r = i - t * rows;
   float y = 0.0f;
-  for (int p = 0; p < ks; ++p) y += part[(int64_t)p * n * rows + i];
+  for (int p = 0; p < ks; ++p) y += part[(int64_t)p * total + i];
   float* o = out + t * ldo + r;
   *o = accumulate ? *o + y : y;
 }
@@ -733,8 +793,11 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
   if (e == cudaSuccess) count_launches(1);
   if (e != cudaSuccess || ks == 1) return e;
   const int64_t total = n * mat[0].rows;
-  splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(part, (int)ks, n, mat[0].rows,
-                                                                       mat[0].out, mat[0].ldo, accumulate ? 1 : 0);
+  const bool vec = (mat[0].rows & 3) == 0 && (mat[0].ldo & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(mat[0].out) & 15) == 0;
+  const int64_t threads = vec ? (total + 3) / 4 : total;
+  splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      part, (int)ks, n, mat[0].rows, mat[0].out, mat[0].ldo, accumulate ? 1 : 0, vec ? 1 : 0);
   e = cudaGetLastError();
   if (e == cudaSuccess) count_launches(1);
   return e;
@@ -759,6 +822,20 @@ cudaError_t gemm_tc_split_norm(const float* X, const float* norm_w, float eps, i
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
   norm_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, norm_w, K, eps, xh, xl, inv);
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
+  return e;
+}
+
+cudaError_t gemm_tc_split_glu(const float* gate, const float* up, int64_t n, int64_t K, void* scratch,
+                              size_t scratch_bytes, cudaStream_t s) {
+  if (n <= 0 || K <= 0 || scratch_bytes < gemm_tc_scratch_bytes(n, K) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255))
+    return cudaErrorInvalidValue;
+  __half* xh = static_cast<__half*>(scratch);
+  __half* xl = xh + n * K;
+  float* inv = reinterpret_cast<float*>(xl + n * K);
+  glu_split_kernel<<<(unsigned)n, 256, 0, s>>>(gate, up, K, xh, xl, inv);
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) count_launches(1);
   return e;

@@ -159,6 +159,10 @@ cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, 
 // the tensor-core scratch, for the GEMMs that follow with x_split_ready.
 cudaError_t gemm_tc_split_norm(const float* X, const float* norm_w, float eps, int64_t n, int64_t K,
                                void* scratch, size_t scratch_bytes, cudaStream_t s);
+// The fp16 split of silu(gate) * up (swiglu_launch's values) into the
+// tensor-core scratch, for the down projection with x_split_ready.
+cudaError_t gemm_tc_split_glu(const float* gate, const float* up, int64_t n, int64_t K, void* scratch,
+                              size_t scratch_bytes, cudaStream_t s);
 
 // -------------------------------------------------------------- others
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,
@@ -189,6 +193,7 @@ struct QkvArgs {
   int64_t pos0;
   int64_t n;
   const DecodeState* state;
+  int32_t kv_only;     // 1: only the k/v heads (the attention normalises and rotates q)
 };
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s);
 
