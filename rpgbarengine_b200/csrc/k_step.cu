@@ -148,12 +148,18 @@ __device__ __forceinline__ void phase_wait(const StepParams& P, uint32_t target,
   csync();
 }
 
+// Release add: the barrier orders every consumer's stores of the phase before
+// thread 0's release, which is cumulative at GPU scope (no separate fence).
 __device__ __forceinline__ void phase_signal(const StepParams& P, int tid) {
   csync();  // every consumer's output of this phase is written
-  if (tid == 0) {
-    __threadfence();
-    atomicAdd(P.ctr, 1u);
-  }
+  if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
+}
+
+// Acquire-release add returning the old value (one round trip).
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // ============================================================== producer
@@ -599,11 +605,7 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
   csync();
   if (tid == 0) {
     int last = 0;
-    if (has_item) {
-      __threadfence();
-      last = atomicAdd(A.head_ctr + kh, 1u) == (uint32_t)P.splits - 1u;
-      if (last) __threadfence();
-    }
+    if (has_item) last = atom_add_acq_rel(A.head_ctr + kh, 1u) == (uint32_t)P.splits - 1u;
     *flag = last;
   }
   csync();
