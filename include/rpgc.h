@@ -171,7 +171,7 @@ RPGC_API int rpgc_matvec(uint32_t type, const void* w, int64_t rows, int64_t col
                          const float* x, float* y, void* stream);
 /* OUT[t*rows + r] = dot(X[t], W[r]) (QuantMatrix::MatMulBatch,
  * src/model.cc:39-69; MatMulBlocked, src/matmul.h:55).  n == 1 takes the
- * decode kernel, n > 1 the prefill kernel. */
+ * decode kernel, n > 1 the prefill kernel.  X must be 16-byte aligned. */
 RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t cols,
                          const float* X, int64_t n, float* OUT, void* stream);
 /* AttentionFromCache for one query token (src/qwen3.cc:79-117, seq = 1):

@@ -502,105 +502,115 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
   }
 }
 
-// Per token: power-of-two scale s (max |x| s in [2^14, 2^15)), Xh = fp16(x s),
-// Xl = fp16(x s - Xh), 1/s.
-__global__ void __launch_bounds__(256) act_split_kernel(const float* __restrict__ X, int64_t K,
-                                                        __half* __restrict__ xh, __half* __restrict__ xl,
-                                                        float* __restrict__ inv_scale) {
+// Per token row: the values v (mode kPlain: x; kNorm: the RMSNorm of x,
+// src/kernels.h:56-63, x * (1/sqrt(sum x^2 / K + eps), double sum) * w;
+// kGlu: silu(gate) * up, src/kernels.h:82-92, as swiglu_kernel), a
+// power-of-two scale s (max |v| s in [2^14, 2^15)), Xh = fp16(v s), Xl =
+// fp16(v s - Xh), 1/s.  The row is read once with 16-byte loads into shared
+// memory (every load of a thread in flight together), reduced, then split
+// from there.  K is a multiple of 4.
+enum SplitMode { kPlain = 0, kNorm = 1, kGlu = 2 };
+
+template <int MODE>
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                         int64_t K, float eps, __half* __restrict__ xh,
+                                                         __half* __restrict__ xl, float* __restrict__ inv_scale) {
+  extern __shared__ __align__(16) float vrow[];  // [K]
+  __shared__ double dred[8];
   __shared__ float red[8];
   const int64_t t = blockIdx.x;
-  const float* x = X + t * K;
+  const int64_t K4 = K >> 2;
+  const float4* a4 = reinterpret_cast<const float4*>(A + t * K);
+  const float4* b4 = MODE == kGlu ? reinterpret_cast<const float4*>(B + t * K) : nullptr;
+  float4* v4 = reinterpret_cast<float4*>(vrow);
   float m = 0.0f;
-  for (int64_t k = threadIdx.x; k < K; k += 256) m = fmaxf(m, fabsf(x[k]));
+  double ss = 0.0;
+#pragma unroll 4
+  for (int64_t i = threadIdx.x; i < K4; i += 256) {
+    float4 v = a4[i];
+    if (MODE == kGlu) {
+      const float4 u = b4[i];
+      v.x = (v.x / (1.0f + expf(-v.x))) * u.x;
+      v.y = (v.y / (1.0f + expf(-v.y))) * u.y;
+      v.z = (v.z / (1.0f + expf(-v.z))) * u.z;
+      v.w = (v.w / (1.0f + expf(-v.w))) * u.w;
+    }
+    if (MODE == kNorm)
+      ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    else
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    v4[i] = v;
+  }
+  if (MODE == kNorm) {
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) dred[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < 8; ++i) tot += dred[i];
+    const float nsc = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
+    const float4* w4 = reinterpret_cast<const float4*>(B);
+#pragma unroll 4
+    for (int64_t i = threadIdx.x; i < K4; i += 256) {  // each thread rereads its own entries
+      float4 v = v4[i];
+      const float4 w = w4[i];
+      v.x = v.x * nsc * w.x;
+      v.y = v.y * nsc * w.y;
+      v.z = v.z * nsc * w.z;
+      v.w = v.w * nsc * w.w;
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      v4[i] = v;
+    }
+  }
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   float mx = 0.0f;
   for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
   const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);  // biased exponent of the max
-  // scale 2^(141 - e): max |x| s in [2^14, 2^15); clamped to stay finite
+  // scale 2^(141 - e): max |v| s in [2^14, 2^15); clamped to stay finite
   int se = 141 - e;
   se = se > 100 ? 100 : (se < -100 ? -100 : se);
   const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
-  for (int64_t k = threadIdx.x; k < K; k += 256) {
-    const float v = x[k] * s;
-    const __half h = __float2half_rn(v);
-    xh[t * K + k] = h;
-    xl[t * K + k] = __float2half_rn(v - __half2float(h));
+  uint2* h2 = reinterpret_cast<uint2*>(xh + t * K);
+  uint2* l2 = reinterpret_cast<uint2*>(xl + t * K);
+#pragma unroll 4
+  for (int64_t i = threadIdx.x; i < K4; i += 256) {
+    const float4 v = v4[i];
+    const float y[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const __half2 hh = __floats2half2_rn(y[2 * k], y[2 * k + 1]);
+      const float2 hf = __half22float2(hh);
+      const __half2 ll = __floats2half2_rn(y[2 * k] - hf.x, y[2 * k + 1] - hf.y);
+      hw[k] = *reinterpret_cast<const uint32_t*>(&hh);
+      lw[k] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    h2[i] = make_uint2(hw[0], hw[1]);
+    l2[i] = make_uint2(lw[0], lw[1]);
   }
   if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);  // undoes both scalings
 }
 
-// act_split_kernel with the RMSNorm of the row in front (src/kernels.h:56-63:
-// x * (1/sqrt(sum x^2 / K + eps), double sum) * w, the same float operations
-// as rmsnorm_rows_kernel): the normalised row exists only as its fp16 split.
-__global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict__ X, const float* __restrict__ w,
-                                                         int64_t K, float eps, __half* __restrict__ xh,
-                                                         __half* __restrict__ xl, float* __restrict__ inv_scale) {
-  __shared__ double dred[8];
-  __shared__ float red[8];
-  const int64_t t = blockIdx.x;
-  const float* x = X + t * K;
-  double ss = 0.0;
-  for (int64_t k = threadIdx.x; k < K; k += 256) ss += (double)x[k] * x[k];
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) dred[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  double tot = 0.0;
-  for (int i = 0; i < 8; ++i) tot += dred[i];
-  const float nsc = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
-  float m = 0.0f;
-  for (int64_t k = threadIdx.x; k < K; k += 256) m = fmaxf(m, fabsf(x[k] * nsc * w[k]));
-  m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  float mx = 0.0f;
-  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
-  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
-  int se = 141 - e;
-  se = se > 100 ? 100 : (se < -100 ? -100 : se);
-  const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
-  for (int64_t k = threadIdx.x; k < K; k += 256) {
-    const float v = (x[k] * nsc * w[k]) * s;
-    const __half h = __float2half_rn(v);
-    xh[t * K + k] = h;
-    xl[t * K + k] = __float2half_rn(v - __half2float(h));
+template <int MODE>
+cudaError_t split_rows_launch(const float* A, const float* B, int64_t n, int64_t K, float eps, __half* xh,
+                              __half* xl, float* inv, cudaStream_t s) {
+  if (K % 4 || K * 4 > 227 * 1024 || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15))
+    return cudaErrorInvalidValue;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem = (int)(K * 4);
+  if (smem > 48 * 1024 && dev >= 0 && dev < 64 && configured[dev] < smem) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(split_rows_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = smem;
   }
-  if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);
-}
-
-// act_split_kernel of silu(gate) * up (src/kernels.h:82-92, the same float
-// expression as swiglu_kernel): the down projection's input exists only as
-// its fp16 split.
-__global__ void __launch_bounds__(256) glu_split_kernel(const float* __restrict__ G, const float* __restrict__ U,
-                                                        int64_t K, __half* __restrict__ xh, __half* __restrict__ xl,
-                                                        float* __restrict__ inv_scale) {
-  __shared__ float red[8];
-  const int64_t t = blockIdx.x;
-  const float* g = G + t * K;
-  const float* u = U + t * K;
-  float m = 0.0f;
-  for (int64_t k = threadIdx.x; k < K; k += 256) {
-    const float v = g[k];
-    m = fmaxf(m, fabsf((v / (1.0f + expf(-v))) * u[k]));
-  }
-  m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  float mx = 0.0f;
-  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
-  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
-  int se = 141 - e;
-  se = se > 100 ? 100 : (se < -100 ? -100 : se);
-  const float s = (e == 0 || e == 255) ? 1.0f : exp2f((float)se);
-  for (int64_t k = threadIdx.x; k < K; k += 256) {
-    const float v = g[k];
-    const float y = ((v / (1.0f + expf(-v))) * u[k]) * s;
-    const __half h = __float2half_rn(y);
-    xh[t * K + k] = h;
-    xl[t * K + k] = __float2half_rn(y - __half2float(h));
-  }
-  if (threadIdx.x == 0) inv_scale[t] = 1.0f / (s * kWScale);
+  split_rows_kernel<MODE><<<(unsigned)n, 256, smem, s>>>(A, B, K, eps, xh, xl, inv);
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) count_launches(1);
+  return e;
 }
 
 // OUT[t][r] (+)= sum over the K partitions of the partial sums, in order.
@@ -736,10 +746,8 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
       (((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255));
   cudaError_t e;
   if (!x_split_ready) {  // else the scratch holds the split of this same X (the caller's promise)
-    act_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, K, xh, xl, inv);
-    e = cudaGetLastError();
+    e = split_rows_launch<kPlain>(X, nullptr, n, K, 0.0f, xh, xl, inv, s);
     if (e != cudaSuccess) return e;
-    count_launches(1);
   }
   CUtensorMap mh, ml;
   if (!make_x_map(&mh, xh, n, K) || !make_x_map(&ml, xl, n, K)) return cudaErrorInvalidValue;
@@ -821,10 +829,7 @@ cudaError_t gemm_tc_split_norm(const float* X, const float* norm_w, float eps, i
   __half* xh = static_cast<__half*>(scratch);
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
-  norm_split_kernel<<<(unsigned)n, 256, 0, s>>>(X, norm_w, K, eps, xh, xl, inv);
-  const cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) count_launches(1);
-  return e;
+  return split_rows_launch<kNorm>(X, norm_w, n, K, eps, xh, xl, inv, s);
 }
 
 cudaError_t gemm_tc_split_glu(const float* gate, const float* up, int64_t n, int64_t K, void* scratch,
@@ -835,10 +840,7 @@ cudaError_t gemm_tc_split_glu(const float* gate, const float* up, int64_t n, int
   __half* xh = static_cast<__half*>(scratch);
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
-  glu_split_kernel<<<(unsigned)n, 256, 0, s>>>(gate, up, K, xh, xl, inv);
-  const cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) count_launches(1);
-  return e;
+  return split_rows_launch<kGlu>(gate, up, n, K, 0.0f, xh, xl, inv, s);
 }
 
 cudaError_t gemm_tc_launch_group(const GemmGroupMat* mats, int nmat, int64_t K, const float* X, int64_t n,
