@@ -17,6 +17,7 @@ again by every decode step, so no L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
   python bench.py --workload tp8b --steps 1 --warmup 1   # config 4, under torchrun
+  python bench.py --workload microbench --steps 5          # config 1 matmul kernels
 
 N > 1: one process per GPU (torchrun), each rank runs its own independent
 session (sessions shard with no communication), value = all ranks' tokens /
@@ -400,6 +401,87 @@ def run_tp8b(args):
     }))
 
 
+MB_SHAPES = [(6144, 2048), (2048, 6144), (9728, 2560), (151936, 2560)]  # rows x cols
+MB_BATCH = 64
+
+
+def run_microbench(args):
+    """the fused-dequant matmuls per quant type (Q4_K, Q6_K,
+    Q8_0) at rows x cols 6144x2048, 2048x6144, 9728x2560 and 151936x2560, on
+    f32 N(0,1) activations at batch 1 (rpgc_matvec, the decode GEMV: HBM
+    roofline) and batch 64 (rpgc_matmul, the tensor-core GEMM: useful
+    TFLOP/s).  Every call reads its own copy of the weights (the copies
+    together exceed L2); the calls are captured in a CUDA graph so that the
+    time is device time only (CUDA events around graph replays)."""
+    import torch
+
+    import rpgbarengine_b200 as rb
+    from rpgbarengine_b200 import gguf, synth
+
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    torch.cuda.set_device(dev)
+    hbm, bf16, src = peaks()
+    gen = torch.Generator(device=f"cuda:{dev}")
+    gen.manual_seed(SEED_WEIGHTS)
+    rows_out = []
+    stream = torch.cuda.Stream(device=dev)
+    for ty, tname in ((gguf.Q4_K, "Q4_K"), (gguf.Q6_K, "Q6_K"), (gguf.Q8_0, "Q8_0")):
+        for rows, cols in MB_SHAPES:
+            w0 = synth.random_blocks_torch(ty, rows, cols, gen, f"cuda:{dev}")
+            copies = max(1, int(np.ceil(256e6 / w0.numel())))
+            ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+            wbytes = rows * gguf.row_bytes(ty, cols)
+            line = {"type": tname, "rows": rows, "cols": cols, "weight_mb": round(wbytes / 1e6, 2)}
+            for n in (1, MB_BATCH):
+                X = torch.randn(n, cols, device=f"cuda:{dev}", generator=gen)
+                out = torch.empty(n, rows, device=f"cuda:{dev}")
+                reps = max(len(ws), 8)
+
+                def calls():
+                    for i in range(reps):
+                        rb.matmul_batch(ty, ws[i % len(ws)], rows, cols, X, out=out)
+                with torch.cuda.stream(stream):
+                    calls()  # warm-up (module load, attributes, allocator)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    calls()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):  # replays and events on one stream
+                    g.replay()
+                    stream.synchronize()
+                    e0.record(stream)
+                    for _ in range(args.steps):
+                        g.replay()
+                    e1.record(stream)
+                torch.cuda.synchronize(dev)
+                us = e0.elapsed_time(e1) * 1e3 / (args.steps * reps)
+                if n == 1:
+                    gbs = (wbytes + 4 * (cols + rows)) / (us * 1e-6) / 1e9
+                    line.update(gemv_us=round(us, 2), gemv_gbs=round(gbs, 1), gemv_frac=round(gbs / hbm, 4))
+                else:
+                    tf = 2.0 * rows * cols * n / (us * 1e-6) / 1e12
+                    line.update(gemm64_us=round(us, 2), gemm64_tflops=round(tf, 2),
+                                gemm64_frac=round(tf / bf16, 4))
+                del g
+            rows_out.append(line)
+            del ws, w0
+            torch.cuda.empty_cache()
+    fr = [r["gemv_frac"] for r in rows_out]
+    print(json.dumps({
+        "metric": "config-1 fused-dequant GEMV (batch 1, HBM roofline) / GEMM (batch 64) microbench",
+        "value": round(float(np.mean(fr)), 4), "unit": "mean GEMV fraction of measured HBM copy bandwidth",
+        "n_gpus": 1, "steps": args.steps, "warmup": 1, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 dp4a + fp32 (GEMV), fp16 hi/lo tcgen05 + fp32 (GEMM)",
+        "data": "synthetic", "config": {"workload": "config1: Q4_K/Q6_K/Q8_0 x 4 shapes, batch 1 and 64",
+                                        "l2": "each call reads its own weight copy; copies > 256 MB"},
+        "peak_hbm_gbs": hbm, "peak_bf16_tflops": bf16, "peak_source": src,
+        "table": rows_out,
+    }))
+
+
 def reference_sample(shape, threads, prompt_n, decode_n, reps, path=None):
     """Time the reference's own code (oracle/_ref) on a bounded sample of the
     workload: prompt_n-token prefill + decode_n greedy tokens, reps times."""
@@ -487,14 +569,17 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config2", "tp8b"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "tp8b", "microbench"],
                     help="config2 (default): the 4B decode/prefill benchmark; tp8b: BASELINE "
-                         "config 4, the 8B shape tensor-parallel over the torchrun ranks")
+                         "config 4, the 8B shape tensor-parallel over the torchrun ranks; "
+                         "microbench: BASELINE config 1, the matmul kernels per quant type")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "tp8b":
         run_tp8b(args)
+    elif args.workload == "microbench":
+        run_microbench(args)
     else:
         run_gpu(args)
 

@@ -172,6 +172,40 @@ def build_tensors(shape: Qwen3Shape, seed: int) -> list:
     return out + norm_tensors(shape)
 
 
+def random_blocks_torch(ggml_type: int, rows: int, cols: int, gen, device):
+    """random_blocks drawn by torch on `device` (a uint8 tensor there): the
+    same block layout and distributions (Q8_0: fp16 d in [1e-4, 2e-4], quants
+    in [-127, 127]; Q4_K: d in [1e-3, 4e-3], dmin in [0, 1e-3], random scale
+    and quant bytes; Q6_K: random ql/qh, int8 scales in [-32, 31], d in
+    [1e-3, 4e-3]), a different stream of numbers."""
+    import torch
+
+    def f16(n, lo, hi):
+        return torch.empty(n, dtype=torch.float32, device=device).uniform_(lo, hi, generator=gen) \
+            .to(torch.float16).view(torch.uint8).view(n, 2)
+
+    if ggml_type == Q8_0:
+        nb = rows * cols // 32
+        blk = torch.empty((nb, 34), dtype=torch.uint8, device=device)
+        blk[:, 0:2] = f16(nb, 1e-4, 2e-4)
+        blk[:, 2:] = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device=device,
+                                   generator=gen).view(torch.uint8)
+    elif ggml_type == Q4_K:
+        nb = rows * cols // 256
+        blk = torch.randint(0, 256, (nb, 144), dtype=torch.uint8, device=device, generator=gen)
+        blk[:, 0:2] = f16(nb, 1e-3, 4e-3)
+        blk[:, 2:4] = f16(nb, 0.0, 1e-3)
+    elif ggml_type == Q6_K:
+        nb = rows * cols // 256
+        blk = torch.randint(0, 256, (nb, 210), dtype=torch.uint8, device=device, generator=gen)
+        blk[:, 192:208] = torch.randint(-32, 32, (nb, 16), dtype=torch.int8, device=device,
+                                        generator=gen).view(torch.uint8)
+        blk[:, 208:210] = f16(nb, 1e-3, 4e-3)
+    else:
+        raise ValueError(f"no torch generator for ggml type {ggml_type}")
+    return blk.view(-1)
+
+
 def build_tensors_torch(shape: Qwen3Shape, seed: int, device) -> list:
     """build_tensors for all-Q8_0 shapes (the 8B benchmark shape), the random
     blocks drawn by torch on `device` (8.7 GB in seconds instead of minutes)
@@ -185,14 +219,9 @@ def build_tensors_torch(shape: Qwen3Shape, seed: int, device) -> list:
     for name, ty, rows, cols in shape.matrices():
         if ty != Q8_0:
             raise ValueError("build_tensors_torch covers Q8_0 matrices only")
-        nb = rows * cols // 32
-        blk = torch.empty((nb, 34), dtype=torch.uint8, device=device)
-        d = torch.empty(nb, dtype=torch.float32, device=device).uniform_(1e-4, 2e-4, generator=gen)
-        blk[:, 0:2] = d.to(torch.float16).view(torch.uint8).view(nb, 2)
-        blk[:, 2:] = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device=device,
-                                   generator=gen).view(torch.uint8)
-        out.append(Tensor(name, ty, (cols, rows), blk.view(-1).cpu().numpy()))
-        del blk, d
+        blk = random_blocks_torch(ty, rows, cols, gen, device)
+        out.append(Tensor(name, ty, (cols, rows), blk.cpu().numpy()))
+        del blk
     return out + norm_tensors(shape)
 
 

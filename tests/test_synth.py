@@ -47,3 +47,29 @@ def test_torch_builder_rejects_k_quants():
     pytest.importorskip("torch")
     with pytest.raises(ValueError):
         synth.build_tensors_torch(synth.TINY_MIX, 1, "cpu")
+
+
+@pytest.mark.parametrize("ty", [gguf.Q4_K, gguf.Q6_K, gguf.Q8_0])
+def test_torch_blocks_have_the_benchmark_fields(ty):
+    torch = pytest.importorskip("torch")
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(3)
+    rows, cols = 64, 512
+    b = synth.random_blocks_torch(ty, rows, cols, gen, "cpu").numpy()
+    assert b.nbytes == rows * gguf.row_bytes(ty, cols)
+    if ty == gguf.Q8_0:
+        d, q = _q8_fields(b)
+        assert d.min() >= np.float32(np.float16(1e-4)) and d.max() <= np.float32(np.float16(2e-4))
+        assert q.min() >= -127
+        return
+    blk = b.reshape(-1, 144 if ty == gguf.Q4_K else 210)
+    if ty == gguf.Q4_K:
+        d = blk[:, 0:2].copy().view("<f2").astype(np.float32)
+        dmin = blk[:, 2:4].copy().view("<f2").astype(np.float32)
+        assert d.min() >= np.float32(np.float16(1e-3)) and d.max() <= np.float32(np.float16(4e-3))
+        assert dmin.min() >= 0 and dmin.max() <= np.float32(np.float16(1e-3))
+    else:
+        sc = blk[:, 192:208].view(np.int8)
+        d = blk[:, 208:210].copy().view("<f2").astype(np.float32)
+        assert sc.min() >= -32 and sc.max() <= 31
+        assert d.min() >= np.float32(np.float16(1e-3)) and d.max() <= np.float32(np.float16(4e-3))
