@@ -184,18 +184,21 @@ RPGC_API int rpgc_matmul(uint32_t type, const void* w, int64_t rows, int64_t col
 RPGC_API int rpgc_attention_decode(const float* q, const float* k_cache, const float* v_cache,
                                    int64_t max_seq, int32_t n_heads, int32_t n_kv_heads,
                                    int32_t head_dim, int64_t pos, float* out, void* stream);
-/* Allocation-free variant of rpgc_attention_decode.  No counterpart in the
- * reference.  For callers that cannot allocate device memory when they call
- * (a host whose GPU heap belongs to another runtime, or a latency-critical
- * path that must not enter the allocator): its contract is that a call
- * allocates nothing and keeps no state between calls, so calls on different
- * streams may overlap.  Same arguments, limits and results as
- * rpgc_attention_decode. */
-RPGC_API int rpgc_attention_decode_noalloc(const float* q, const float* k_cache,
-                                           const float* v_cache, int64_t max_seq,
-                                           int32_t n_heads, int32_t n_kv_heads,
-                                           int32_t head_dim, int64_t pos, float* out,
-                                           void* stream);
+/* rpgc_matmul that allocates nothing.  No counterpart in the reference.
+ * For callers that cannot let this library allocate device memory: a host
+ * whose GPU heap belongs to another runtime (a game engine that forbids
+ * foreign cudaMalloc/cudaFree), or a path where an allocation may block or
+ * fail.  Same arguments and results as rpgc_matmul; the tensor-core kernels'
+ * scratch (fp16 split of X, row scales, split-K partial sums) is a fixed
+ * 32 MiB device array of the library on every GPU that loads it (held until
+ * exit) instead of memory allocated per call.  n x cols beyond what fits
+ * (about 4*n*cols + 36864*n bytes) is rejected with RPGC_E_ARG and a message.
+ * The first call on a device looks the array's address up (with that device
+ * current) and should come before any stream capture on that device.  All
+ * calls on a device share the array: calls that overlap on the GPU race, so
+ * order them on one stream or synchronise between them. */
+RPGC_API int rpgc_matmul_noalloc(uint32_t type, const void* w, int64_t rows, int64_t cols,
+                                 const float* X, int64_t n, float* OUT, void* stream);
 /* SampleToken / ArgMax on device logits (src/sampler.cc:96-112,
  * src/kernels.h:42-52); *token_dev receives the id. */
 RPGC_API int rpgc_sample(const float* logits, int64_t n, float temperature, int32_t top_k,

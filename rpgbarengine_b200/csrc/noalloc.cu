@@ -1,19 +1,25 @@
-// noalloc.cu -- decode attention that allocates nothing.
+// noalloc.cu -- the prefill matmul without any allocation.
 //
-// Some callers cannot allocate device memory at the moment they need a
-// result: a host that runs inside another runtime's memory budget (a game
-// engine that owns the GPU heap and forbids foreign cudaMalloc/cudaFree), a
-// caller on a latency-critical path where an allocation may block or
-// synchronise, or code that must not touch the allocator while another
-// component holds it.  This entry point guarantees, as part of its contract,
-// that a call performs no allocation and holds no state between calls: the
-// decode attention kernel merges its position splits inside a thread-block
-// cluster (distributed shared memory), so it needs no global scratch, and
-// calls on different streams may overlap freely.
+// rpgc_matmul gives its tensor-core kernels scratch memory that it allocates
+// for the call (stream-ordered cudaMallocAsync): the fp16 hi/lo split of the
+// input rows, one scale per row, and the split-K partial sums.  Some callers
+// cannot let the library allocate device memory: a game engine or another
+// runtime that owns the GPU heap and forbids foreign cudaMalloc/cudaFree, or a
+// caller on a path where an allocation may block, synchronise or fail under
+// memory pressure.  rpgc_matmul_noalloc runs the same kernels with that
+// scratch in a fixed array of this library instead.
+//
+// The array is kNoallocScratchBytes (32 MiB) of device memory on every GPU
+// that loads the library, held until the process exits.  All calls on a
+// device share it and it keeps the last call's contents; every call writes
+// all of the scratch it reads before reading it, so nothing has to start at
+// zero.  Calls whose work overlaps on the GPU (different streams, or no
+// ordering between them) race on the array: order them.
 #include <cuda_runtime.h>
 
-#include <climits>
 #include <cstdint>
+#include <cstdio>
+#include <mutex>
 
 #include "../../include/rpgc.h"
 #include "kernels.h"
@@ -22,48 +28,80 @@ namespace rpgc {
 void set_last_error(const char* msg);  // engine.cu
 }  // namespace rpgc
 
-extern "C" int rpgc_attention_decode_noalloc(const float* q, const float* k_cache,
-                                             const float* v_cache, int64_t max_seq,
-                                             int32_t n_heads, int32_t n_kv_heads,
-                                             int32_t head_dim, int64_t pos, float* out,
-                                             void* stream) {
+namespace {
+
+constexpr size_t kNoallocScratchBytes = size_t(32) << 20;
+
+// Device code could name this array directly; host code must not pass its
+// name to a kernel (on the host it is only a stand-in for the symbol): it
+// takes the device address from cudaGetSymbolAddress, per device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// The array's address on device `dev`, looked up on the first call with that
+// device current (the caller's current device) and kept.
+cudaError_t scratch_address(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+int64_t row_bytes(uint32_t type, int64_t cols) {
+  switch (type) {
+    case RPGC_F32: return cols * 4;
+    case RPGC_Q8_0: return cols % 32 ? -1 : cols / 32 * 34;
+    case RPGC_Q4_K: return cols % 256 ? -1 : cols / 256 * 144;
+    case RPGC_Q6_K: return cols % 256 ? -1 : cols / 256 * 210;
+    default: return -1;
+  }
+}
+
+int fail_arg(const char* msg) {
+  rpgc::set_last_error(msg);
+  return RPGC_E_ARG;
+}
+
+}  // namespace
+
+extern "C" int rpgc_matmul_noalloc(uint32_t type, const void* w, int64_t rows, int64_t cols,
+                                   const float* X, int64_t n, float* OUT, void* stream) {
   using namespace rpgc;
   set_last_error("");
-  if (!q || !k_cache || !v_cache || !out || n_heads <= 0 || n_kv_heads <= 0 || max_seq <= 0) {
-    set_last_error("attention_decode_noalloc: null pointer or non-positive size");
-    return RPGC_E_ARG;
+  if (!w || !X || !OUT || rows <= 0 || cols <= 0 || n <= 0)
+    return fail_arg("matmul_noalloc: null pointer or non-positive size");
+  const int64_t rb = row_bytes(type, cols);
+  if (rb < 0 || cols % 32)
+    return fail_arg("matmul_noalloc: type must be F32, Q8_0, Q4_K or Q6_K with cols a multiple of "
+                    "its block (and of 32)");
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(X)) & 15)
+    return fail_arg("matmul_noalloc: w and X must be 16-byte aligned");
+  if (n == 1) return rpgc_matvec(type, w, rows, cols, X, OUT, stream);  // the GEMV needs no scratch
+  const size_t need = gemm_scratch_bytes(n, cols);
+  if (need > kNoallocScratchBytes) {
+    char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "matmul_noalloc: %lld rows of %lld columns need %zu bytes of scratch; the fixed "
+                  "array holds %zu (about 4 n cols + 36864 n bytes are needed): use rpgc_matmul",
+                  (long long)n, (long long)cols, need, kNoallocScratchBytes);
+    return fail_arg(msg);
   }
-  if (head_dim != 128 || n_heads % n_kv_heads) {
-    set_last_error("attention_decode_noalloc: head_dim must be 128 and n_heads a multiple of "
-                   "n_kv_heads");
-    return RPGC_E_ARG;
-  }
-  const int32_t grp = n_heads / n_kv_heads;
-  if (!(grp == 1 || grp == 2 || grp == 4 || grp == 8)) {
-    set_last_error("attention_decode_noalloc: GQA group (n_heads / n_kv_heads) must be 1, 2, 4 or 8");
-    return RPGC_E_ARG;
-  }
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) {
-    set_last_error("attention_decode_noalloc: caches must be 16-byte aligned");
-    return RPGC_E_ARG;
-  }
-  if (pos < 0 || pos >= max_seq || pos > INT32_MAX - 1) {
-    set_last_error("attention_decode_noalloc: pos out of range");
-    return RPGC_E_ARG;
-  }
-  cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  AttnArgs a{};
-  a.q = q;
-  a.kc = k_cache;
-  a.vc = v_cache;
-  a.out = out;
-  a.max_seq = max_seq;
-  a.n_heads = n_heads;
-  a.n_kv = n_kv_heads;
-  a.hd = head_dim;
-  a.pos0 = pos;
-  a.n = 1;
-  const cudaError_t e = attn_decode_launch(a, cs);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess && (dev < 0 || dev >= kMaxDevices)) e = cudaErrorInvalidDevice;
+  void* scratch = nullptr;
+  if (e == cudaSuccess) e = scratch_address(dev, &scratch);
+  if (e == cudaSuccess)
+    e = gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT, rows, false,
+                    scratch, kNoallocScratchBytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_last_error(cudaGetErrorString(e));
     return RPGC_E_CUDA;
