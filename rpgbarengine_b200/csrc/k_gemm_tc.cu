@@ -601,7 +601,7 @@ cudaError_t split_rows_launch(const float* A, const float* B, int64_t n, int64_t
   int dev = 0;
   cudaGetDevice(&dev);
   const int smem = (int)(K * 4);
-  if (smem > 48 * 1024 && dev >= 0 && dev < 64 && configured[dev] < smem) {
+  if (dev >= 0 && dev < 64 && configured[dev] < smem) {  // dynamic + static above 48 KB needs the opt-in
     const cudaError_t e =
         cudaFuncSetAttribute(split_rows_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

@@ -85,7 +85,8 @@ def test_matvec_activation_edge_values(orc):
 
 @pytest.mark.parametrize("ty", TYPES)
 @pytest.mark.parametrize("rows,cols,n", [(6144, 2048, 64), (2048, 6144, 64), (9728, 2560, 64),
-                                         (37, 512, 11), (5, 768, 9)])
+                                         (37, 512, 11), (5, 768, 9),
+                                         (300, 12288, 8)])  # the 8B down projection's input width
 def test_matmul_row_gate(orc, ty, rows, cols, n):
     w = legal_random(ty, rows, cols, rows + cols + n)
     X = np.random.default_rng(n).standard_normal((n, cols)).astype(np.float32)
