@@ -521,7 +521,7 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
       reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = knew;
       reinterpret_cast<float4*>(Vs + (pos - t0) * 128)[lane] = vnew;
     }
-    csync();
+    if (owner) csync();  // the patched row is visible to every scoring warp (CTA-uniform condition)
     if (warp < kAttnWarps) {
       for (int pb = warp * PB; pb < tn; pb += kAttnWarps * PB) {
         float val[32];
