@@ -18,6 +18,7 @@ again by every decode step, so no L2 flush is needed between steps.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
   python bench.py --workload tp8b --steps 1 --warmup 1   # config 4, under torchrun
   python bench.py --workload microbench --steps 5          # config 1 matmul kernels
+  python bench.py --workload sessions64                    # config 3, under torchrun for N > 1
 
 N > 1: one process per GPU (torchrun), each rank runs its own independent
 session (sessions shard with no communication), value = all ranks' tokens /
@@ -139,6 +140,7 @@ def run_gpu(args):
     ids_dev = torch.from_numpy(ids_host).to(f"cuda:{dev}")
     out_dev = torch.zeros(DECODE + 8, dtype=torch.int32, device=f"cuda:{dev}")
     n_dev = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    torch.cuda.synchronize(dev)  # the ids are on the device before the session's own stream reads them
 
     def ev():
         return torch.cuda.Event(enable_timing=True)
@@ -313,6 +315,7 @@ def run_tp8b(args):
     ids = torch.from_numpy(synth.prompt_ids(SEED_PROMPT, TP_PROMPT)).to(f"cuda:{dev}")
     out_dev = torch.zeros(TP_DECODE + 8, dtype=torch.int32, device=f"cuda:{dev}")
     n_dev = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    torch.cuda.synchronize(dev)  # the ids are on the device before the session's own stream reads them
 
     def ev():
         return torch.cuda.Event(enable_timing=True)
@@ -398,6 +401,139 @@ def run_tp8b(args):
                          "sample": "not run for config 4 (the reference's 4096-token CPU "
                                    "prefill alone takes minutes); see the config-2 line"},
         "build_s": round(build_s, 1),
+    }))
+
+
+S3_SESSIONS, S3_PREFIX, S3_UNIQUE, S3_DECODE = 64, 256, 768, 128
+
+
+def run_sessions64(args):
+    """64 independent sessions of the 4B shape, each
+    prefilled to 1024 tokens of which the first 256 are a shared prefix, then
+    128 greedy decode tokens per session; the sessions are sharded over the
+    torchrun ranks with no communication.  Each rank computes the shared
+    prefix once and copies its KV into every session on the device
+    (rpgc_session_copy_prefix), prefills the 768 unique tokens, and decodes
+    the sessions one after another (there is no batched multi-session decode:
+    every token streams the weights).  Device time from CUDA events on each
+    session's stream, one session at a time (each synchronised before the next
+    starts, so the intervals do not overlap), summed over the rank's sessions,
+    max over ranks."""
+    import torch
+
+    import rpgbarengine_b200 as rb
+    from rpgbarengine_b200 import dist as rdist
+    from rpgbarengine_b200 import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dev = local
+    shape = synth.QWEN3_4B_Q4KM
+    model = rb.Model.upload(shape, synth.build_tensors(shape, SEED_WEIGHTS), dev, 4096)
+    max_seq = S3_PREFIX + S3_UNIQUE + S3_DECODE + 8
+    mine = rdist.shard_sessions(S3_SESSIONS, rank, world)
+    shared = torch.from_numpy(synth.prompt_ids(SEED_PROMPT, S3_PREFIX)).to(f"cuda:{dev}")
+    unique = {i: torch.from_numpy(synth.prompt_ids(rdist.session_seed(SEED_PROMPT, 1000 + i), S3_UNIQUE))
+              .to(f"cuda:{dev}") for i in mine}
+    out_dev = torch.zeros(S3_DECODE + 8, dtype=torch.int32, device=f"cuda:{dev}")
+    n_dev = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    # torch's copies run on its own stream; the sessions' streams do not wait for it
+    torch.cuda.synchronize(dev)
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def run(indices):
+        pre = ev(), ev()
+        psess = model.session(S3_PREFIX + 8)
+        pstream = torch.cuda.ExternalStream(psess.stream_ptr, device=dev)
+        pre[0].record(pstream)
+        psess.forward_device(shared.data_ptr(), S3_PREFIX)
+        pre[1].record(pstream)
+        pstream.synchronize()
+        sessions, pre_ms = [], []
+        for i in indices:
+            s = model.session(max_seq)
+            st = torch.cuda.ExternalStream(s.stream_ptr, device=dev)
+            ids = unique[i]
+            e = ev(), ev()
+            e[0].record(st)
+            s.copy_prefix_from(psess, S3_PREFIX)
+            s.forward_device(ids.data_ptr(), S3_UNIQUE)
+            e[1].record(st)
+            st.synchronize()  # one session at a time: the intervals must not overlap
+            sessions.append((s, st, ids))
+            pre_ms.append(e)
+        for s, st, ids in sessions:  # each session's decode graph, captured outside the timing
+            s.generate_device(1, out_dev.data_ptr(), n_dev.data_ptr())
+            s.set_len(S3_PREFIX + S3_UNIQUE - 1)  # prefix reuse: back to the prompt
+            s.forward_device(ids.data_ptr() + 4 * (S3_UNIQUE - 1), 1)
+            st.synchronize()
+        dec = []
+        for s, st, _ in sessions:
+            e = ev(), ev()
+            e[0].record(st)
+            s.generate_device(S3_DECODE, out_dev.data_ptr(), n_dev.data_ptr())
+            e[1].record(st)
+            st.synchronize()
+            dec.append(e)
+        torch.cuda.synchronize(dev)
+        p_ms = pre[0].elapsed_time(pre[1]) + sum(a.elapsed_time(b) for a, b in pre_ms)
+        d_ms = sum(a.elapsed_time(b) for a, b in dec)
+        for s, _, _ in sessions:
+            s.close()
+        psess.close()
+        return p_ms, d_ms
+
+    run(mine[:1])  # warm-up: graphs, plans, module loads
+    if dist:
+        dist.barrier()
+    clocks = Clocks(dev) if rank == 0 else None
+    kl0 = rb.kernel_launches()
+    pre_ms, dec_ms = run(mine)
+    launches = rb.kernel_launches() - kl0
+    clk = clocks.stop() if clocks else None
+    pre_ms, dec_ms = rdist.max_over_ranks([pre_ms, dec_ms], dist, f"cuda:{dev}")
+    if dist:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    hbm, _, src = peaks()
+    n_tok = S3_SESSIONS * S3_DECODE
+    value = n_tok / (dec_ms / 1e3)
+    ctx = S3_PREFIX + S3_UNIQUE + S3_DECODE / 2.0
+    bytes_tok = decode_bytes_per_token(shape, ctx)
+    achieved = bytes_tok * n_tok / world / (dec_ms / 1e3) / 1e9  # per GPU
+    batched_ideal = hbm * 1e9 / (shape.weight_bytes(per_token=True) / S3_SESSIONS +
+                                 decode_bytes_per_token(shape, ctx) - shape.weight_bytes(per_token=True))
+    print(json.dumps({
+        "metric": "config-3 aggregate decode tok/s, 64 sessions with a shared 256-token prefix",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": 1,
+        "ms_per_step": round(pre_ms + dec_ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 dp4a + fp32 (decode), fp16 hi/lo tcgen05 + fp32 (prefill)",
+        "data": "synthetic",
+        "config": {"workload": "config3: qwen3-4b q4_k_m-mix, 64 sessions x (256 shared + 768 unique "
+                               "prefill, 128 greedy decode), sessions sharded over the GPUs",
+                   "model": shape.name, "global_batch": S3_SESSIONS, "seq_len": max_seq - 8,
+                   "parallelism": f"sessions x{world} (no communication)",
+                   "prefix": "computed once per GPU, KV copied device-to-device into each session",
+                   "decode": "sessions one after another (no batched multi-session decode)"},
+        "prefill_tok_s": round(S3_SESSIONS * S3_UNIQUE / (pre_ms / 1e3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "peak_source": src,
+                     "kernel": "step_kernel per session token: weights + the session's KV at ~1088",
+                     "batched_ideal_tok_s_per_gpu": round(batched_ideal, 1)},
+        "gpu_launches": launches, "clocks": clk,
+        "cpu_baseline": {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                         "sample": "see the config-2 line (the reference decodes sessions one at a time)"},
     }))
 
 
@@ -569,10 +705,11 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config2", "tp8b", "microbench"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "tp8b", "microbench", "sessions64"],
                     help="config2 (default): the 4B decode/prefill benchmark; tp8b: BASELINE "
                          "config 4, the 8B shape tensor-parallel over the torchrun ranks; "
-                         "microbench: BASELINE config 1, the matmul kernels per quant type")
+                         "microbench: BASELINE config 1, the matmul kernels per quant type; "
+                         "sessions64: BASELINE config 3, 64 sessions with a shared prefix")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -580,6 +717,8 @@ def main():
         run_tp8b(args)
     elif args.workload == "microbench":
         run_microbench(args)
+    elif args.workload == "sessions64":
+        run_sessions64(args)
     else:
         run_gpu(args)
 

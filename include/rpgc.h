@@ -132,6 +132,14 @@ RPGC_API int64_t rpgc_session_len(int32_t session);
 /* Prefix reuse: positions [0, len) stay valid (src/engine.cc:425-431,
  * src/kv_cache.h:63-69).  Invalidates the pending logits. */
 RPGC_API int rpgc_session_set_len(int32_t session, int64_t len);
+/* Shared-prefix reuse across sessions of one model: copies KV positions
+ * [0, n) of every layer and kv head from session src into session dst on the
+ * device and sets dst's length to n (pending logits invalidated, so a
+ * rpgc_forward of the rest follows).  The reference reuses a prefix only
+ * within one session (LCP, src/engine.cc:383-448); this lets many sessions
+ * that open with the same tokens (a shared system prompt) compute them once.
+ * n <= rpgc_session_len(src); n > dst's capacity is RPGC_E_CONTEXT_FULL. */
+RPGC_API int rpgc_session_copy_prefix(int32_t dst, int32_t src, int64_t n);
 /* cudaStream_t of the session, as void* (for event timing). */
 RPGC_API void* rpgc_session_stream(int32_t session);
 /* Copies the cache to host arrays of n_layers*n_kv_heads*max_seq*head_dim
@@ -154,6 +162,10 @@ RPGC_API int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* 
  * logits (the benchmark's kernel-only leg).  ids_dev: n int32 on the device;
  * out_ids_dev: max_tokens int32 on the device; n_out stays on the device too
  * (n_out_dev, one int32).  Asynchronous on the session stream. */
+/* The ids must be on the device before the session's stream reads them (the
+ * caller orders its own copy, e.g. by synchronising).  They are not checked on
+ * the host: an id outside the vocabulary embeds as zeros and the next
+ * rpgc_session_sync returns RPGC_E_ARG. */
 RPGC_API int rpgc_forward_device(int32_t session, const int32_t* ids_dev, int64_t n);
 RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
                                   int32_t* out_ids_dev, int32_t* n_out_dev);

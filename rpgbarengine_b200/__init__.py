@@ -94,6 +94,7 @@ def lib() -> C.CDLL:
         "rpgc_forward": ([i32, vp, i64, vp, vp], C.c_int),
         "rpgc_generate": ([i32, C.POINTER(GenOpts), vp, C.POINTER(i32)], C.c_int),
         "rpgc_forward_device": ([i32, vp, i64], C.c_int),
+        "rpgc_session_copy_prefix": ([i32, i32, i64], C.c_int),
         "rpgc_generate_device": ([i32, C.POINTER(GenOpts), vp, vp], C.c_int),
         "rpgc_session_sync": ([i32], C.c_int),
         "rpgc_dequantize_rows": ([u32, vp, i64, i64, vp, vp], C.c_int),
@@ -218,6 +219,11 @@ class Session:
 
     def reset(self):
         self.set_len(0)
+
+    def copy_prefix_from(self, src: "Session", n: int):
+        """KV positions [0, n) of `src` copied into this session on the device
+        (rpgc_session_copy_prefix); a forward of the remaining tokens follows."""
+        _check(lib().rpgc_session_copy_prefix(self.handle, src.handle, n))
 
     @property
     def stream_ptr(self) -> int:

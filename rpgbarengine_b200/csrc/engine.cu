@@ -760,8 +760,8 @@ void launch_layers_step(Session* s) {
 // One decode step for ids[0] at st->pos (the host set the state).
 void launch_step(Session* s) {
   const Model* m = s->m;
-  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, m->c.hidden, s->ids, 1, s->x,
-                     nullptr, s->stream),
+  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, m->embd.rows, m->c.hidden, s->ids, 1,
+                     s->x, nullptr, &s->st->error, s->stream),
         "embed");
   launch_layers_step(s);
 }
@@ -773,8 +773,8 @@ void launch_prefill(Session* s, int64_t nc, int64_t pos0) {
   cudaStream_t cs = s->stream;
   const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
                 kvd = (int64_t)c.n_kv_heads * c.head_dim;
-  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, c.hidden, s->ids, nc, s->x,
-                     nullptr, cs),
+  check(embed_launch(m->embd.type, m->embd.w, m->embd.row_bytes, m->embd.rows, c.hidden, s->ids, nc,
+                     s->x, nullptr, &s->st->error, cs),
         "embed");
   const size_t lc = s->layer_cache_floats();
   for (int l = 0; l < c.n_layers; ++l) {
@@ -1038,6 +1038,7 @@ int finish_generate(Session* s, const rpgc_gen_opts& o, int64_t steps, int32_t* 
   CK(cudaMemcpyAsync(s->st_host, s->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   const DecodeState h = *s->st_host;
+  if (h.error & kErrBadToken) fail(RPGC_E_ARG, "a device-resident token id was outside the vocabulary");
   if (h.error) fail(RPGC_E_TIMEOUT, "a device wait gave up during generation (flags %d)", h.error);
   if (h.n_gen < 0 || h.n_gen > steps) fail(RPGC_E_CUDA, "inconsistent decode state");
   if (h.n_gen > 0) CK(cudaMemcpy(out, s->gen_out, h.n_gen * sizeof(int32_t), cudaMemcpyDeviceToHost));
@@ -1275,6 +1276,44 @@ int rpgc_session_set_len(int32_t session, int64_t len) {
   });
 }
 
+int rpgc_session_copy_prefix(int32_t dst, int32_t src, int64_t n) {
+  return guard([&] {
+    Session* d = require_session(dst);
+    Session* s = require_session(src);
+    if (d == s) fail(RPGC_E_ARG, "source and destination are the same session");
+    if (d->m != s->m) fail(RPGC_E_ARG, "the sessions belong to different models");
+    std::scoped_lock lk(d->mu, s->mu);
+    if (n < 0 || n > s->len)
+      fail(RPGC_E_ARG, "prefix of %lld positions, the source holds %lld", (long long)n, (long long)s->len);
+    if (n > d->max_seq)
+      fail(RPGC_E_CONTEXT_FULL, "prefix of %lld positions, capacity %lld", (long long)n, (long long)d->max_seq);
+    DeviceGuard dg(d->device);
+    if (n > 0) {
+      // rows [0, n) of every (layer, kv head) block: one strided copy per cache,
+      // ordered after the source's writes and before its next ones
+      const Model* m = d->m;
+      const size_t hd = (size_t)m->c.head_dim, blocks = (size_t)m->c.n_layers * m->c.n_kv_heads;
+      const size_t wbytes = (size_t)n * hd * sizeof(float);
+      cudaEvent_t ev = nullptr;
+      CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      CK(cudaEventRecord(ev, s->stream));
+      CK(cudaStreamWaitEvent(d->stream, ev, 0));
+      CK(cudaMemcpy2DAsync(d->kc, (size_t)d->max_seq * hd * sizeof(float), s->kc,
+                           (size_t)s->max_seq * hd * sizeof(float), wbytes, blocks,
+                           cudaMemcpyDeviceToDevice, d->stream));
+      CK(cudaMemcpy2DAsync(d->vc, (size_t)d->max_seq * hd * sizeof(float), s->vc,
+                           (size_t)s->max_seq * hd * sizeof(float), wbytes, blocks,
+                           cudaMemcpyDeviceToDevice, d->stream));
+      CK(cudaEventRecord(ev, d->stream));
+      CK(cudaStreamWaitEvent(s->stream, ev, 0));
+      CK(cudaEventDestroy(ev));
+    }
+    d->len = n;
+    d->has_logits = false;
+    return RPGC_OK;
+  });
+}
+
 void* rpgc_session_stream(int32_t session) {
   void* p = nullptr;
   guard([&] {
@@ -1356,6 +1395,11 @@ int rpgc_session_sync(int32_t session) {
     DeviceGuard dg(s->device);
     CK(cudaStreamSynchronize(s->stream));
     CK(cudaMemcpy(s->st_host, s->st, sizeof(DecodeState), cudaMemcpyDeviceToHost));
+    if (s->st_host->error & kErrBadToken) {  // reported once
+      const int32_t zero = 0;
+      CK(cudaMemcpy(&s->st->error, &zero, sizeof(zero), cudaMemcpyHostToDevice));
+      fail(RPGC_E_ARG, "a device-resident token id was outside the vocabulary (embedded as zeros)");
+    }
     if (s->st_host->error) fail(RPGC_E_TIMEOUT, "a device wait gave up (flags %d)", s->st_host->error);
     return RPGC_OK;
   });

@@ -24,12 +24,18 @@ __global__ void dequant_kernel(uint32_t type, const uint8_t* __restrict__ w, int
 // Embedding lookup = dequantise one row per token (QuantMatrix::Row,
 // src/model.cc:32-37).
 __global__ void embed_kernel(uint32_t type, const uint8_t* __restrict__ embd, int64_t row_bytes,
-                             int32_t hidden, const int32_t* __restrict__ ids,
-                             float* __restrict__ x, const DecodeState* st) {
+                             int64_t n_rows, int32_t hidden, const int32_t* __restrict__ ids,
+                             float* __restrict__ x, const DecodeState* st, int32_t* err) {
   grid_dep_wait();
   if (st && !st->active) return;
   const int64_t t = blockIdx.y;
   const int32_t id = st ? st->token : ids[t];
+  if (id < 0 || (int64_t)id >= n_rows) {  // device-resident ids never passed a host check
+    if (err && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, kErrBadToken);
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < hidden; e += gridDim.x * blockDim.x)
+      x[t * hidden + e] = 0.0f;
+    return;
+  }
   const uint8_t* row = embd + (int64_t)id * row_bytes;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < hidden; e += gridDim.x * blockDim.x)
     x[t * hidden + e] = deq_elem(type, row, e);
@@ -89,11 +95,11 @@ cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_
   return e_;
 }
 
-cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int32_t hidden,
-                         const int32_t* ids, int64_t n, float* x, const DecodeState* st,
-                         cudaStream_t s) {
+cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int64_t n_rows,
+                         int32_t hidden, const int32_t* ids, int64_t n, float* x,
+                         const DecodeState* st, int32_t* err, cudaStream_t s) {
   dim3 grid((hidden + 255) / 256, (unsigned)n);
-  embed_kernel<<<grid, 256, 0, s>>>(type, embd, row_bytes, hidden, ids, x, st);
+  embed_kernel<<<grid, 256, 0, s>>>(type, embd, row_bytes, n_rows, hidden, ids, x, st, err);
   const cudaError_t e_ = cudaGetLastError();
   if (e_ == cudaSuccess) count_launches(1);
   return e_;

@@ -8,6 +8,9 @@ namespace rpgc {
 
 // Decode-loop state living in device memory, so that one captured CUDA graph
 // serves every step (the position and the stop status are read in-kernel).
+// DecodeState::error flags besides the bounded-wait timeout (common.cuh)
+constexpr int32_t kErrBadToken = 2;  // a device-resident token id outside the embedding table
+
 struct DecodeState {
   int32_t pos;        // KV length = position of the token being forwarded
   int32_t start_pos;  // KV length when generation started
@@ -168,10 +171,11 @@ cudaError_t gemm_tc_split_glu(const float* gate, const float* up, int64_t n, int
 cudaError_t dequant_launch(uint32_t type, const uint8_t* w, int64_t rows, int64_t cols,
                            int64_t row_bytes, float* out, cudaStream_t s);
 // x[t] = dequant(embd row ids[t]); ids on device.  state (optional): take the
-// single id from state->token and skip when inactive.
-cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int32_t hidden,
-                         const int32_t* ids, int64_t n, float* x, const DecodeState* state,
-                         cudaStream_t s);
+// single id from state->token and skip when inactive.  An id outside
+// [0, n_rows) embeds as zeros and sets kErrBadToken in *err (optional).
+cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, int64_t n_rows,
+                         int32_t hidden, const int32_t* ids, int64_t n, float* x,
+                         const DecodeState* state, int32_t* err, cudaStream_t s);
 cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
                                 float* out, cudaStream_t s);
 cudaError_t swiglu_launch(float* gate, const float* up, int64_t count, cudaStream_t s);

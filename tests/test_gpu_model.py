@@ -162,3 +162,68 @@ def test_config0_full_size(orc):
     got = s.generate(32)
     want, wl = om.generate(okv, want_l, 32, want_logits=True)
     compare_tokens(got, want, wl)
+
+
+def test_copy_prefix_then_forward_matches_one_session(orc):
+    # config 3's shared prefix: session b takes positions [0, 20) from a on
+    # the device, forwards the rest, and must agree with a's own forward
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    ids = synth.prompt_ids(5, 48, shape.vocab)
+    a = gm.session(128)
+    full = a.forward_full(ids, all_rows=True)
+    b = gm.session(96)
+    b.copy_prefix_from(a, 20)
+    assert b.len == 20
+    rest = b.forward_full(ids[20:], all_rows=True)
+    assert b.len == len(ids)
+    for t in range(len(ids) - 20):
+        assert rel_l2(rest[t], full[20 + t]) <= 1e-4, t
+    okv = om.kv(96)
+    want = om.forward(ids, okv, all_rows=True)
+    assert rel_l2(rest[-1], want[-1]) <= LOGIT_REL_L2
+    ref, ref_logits = om.generate(okv, want[-1], 8, want_logits=True)
+    compare_tokens(list(b.generate(8)), ref, ref_logits)
+    # the source is untouched and keeps going
+    assert a.len == len(ids)
+    k_a, _ = a.read_kv()
+    k_b, _ = b.read_kv()
+    assert np.array_equal(k_a[:, :, :20], k_b[:, :, :20])
+
+
+def test_copy_prefix_rejects_bad_requests(orc):
+    gm, _ = pair(orc, synth.TINY_MIX)
+    a = gm.session(64)
+    a.forward_full(synth.prompt_ids(6, 10, synth.TINY_MIX.vocab))
+    b = gm.session(64)
+    with pytest.raises(rb.RpgcError):
+        b.copy_prefix_from(a, 11)  # more than the source holds
+    with pytest.raises(rb.RpgcError):
+        b.copy_prefix_from(b, 1)  # itself
+    small = gm.session(4)
+    with pytest.raises(rb.ContextFull):
+        small.copy_prefix_from(a, 10)
+    other, _ = pair(orc, synth.TINY_Q8)
+    c = other.session(64)
+    with pytest.raises(rb.RpgcError):
+        c.copy_prefix_from(a, 5)  # another model
+    b.copy_prefix_from(a, 0)
+    assert b.len == 0
+
+
+def test_out_of_range_device_ids_are_reported_not_faulted(orc):
+    # ids given on the device skip the host's range check: the embedding
+    # kernel must not read outside the table, and the session reports it
+    torch = pytest.importorskip("torch")
+    gm, _ = pair(orc, synth.TINY_MIX)
+    s = gm.session(64)
+    ids = torch.tensor([3, synth.TINY_MIX.vocab + 12345, 7, -4], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    s.forward_device(ids.data_ptr(), 4)
+    with pytest.raises(rb.RpgcError) as e:
+        s.sync()
+    assert e.value.code == rb.E_ARG and "vocabulary" in str(e.value)
+    s.sync()  # reported once; the session stays usable
+    s.set_len(0)
+    good = synth.prompt_ids(8, 6, synth.TINY_MIX.vocab)
+    assert np.isfinite(s.forward_full(good)).all()
