@@ -169,6 +169,18 @@ RPGC_API int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* 
 RPGC_API int rpgc_forward_device(int32_t session, const int32_t* ids_dev, int64_t n);
 RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
                                   int32_t* out_ids_dev, int32_t* n_out_dev);
+/* Batched multi-session decode: max_tokens steps that each decode one token
+ * for every one of the n sessions (1 .. 256, one model, each with pending
+ * logits and room for max_tokens more positions) at once, with the same
+ * options for all (each session keeps its own position, stop state and
+ * seeded draws, as rpgc_generate would give it).  The reference decodes one
+ * session at a time (Generate, src/qwen3.cc:302-355, per session); here the
+ * weight stream is shared: the matmuls run on the tensor cores over the n
+ * session rows, the attention reads each session's own cache.  out_ids holds
+ * n x max_tokens ids (row i = session i, n_out[i] valid); afterwards each
+ * session is as after rpgc_generate.  Not for tensor-parallel models. */
+RPGC_API int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts,
+                                 int32_t* out_ids, int32_t* n_out);
 RPGC_API int rpgc_session_sync(int32_t session);
 
 /* ------------------------------------------------ kernel entry points */

@@ -95,6 +95,7 @@ def lib() -> C.CDLL:
         "rpgc_generate": ([i32, C.POINTER(GenOpts), vp, C.POINTER(i32)], C.c_int),
         "rpgc_forward_device": ([i32, vp, i64], C.c_int),
         "rpgc_session_copy_prefix": ([i32, i32, i64], C.c_int),
+        "rpgc_generate_batch": ([vp, i32, C.POINTER(GenOpts), vp, vp], C.c_int),
         "rpgc_generate_device": ([i32, C.POINTER(GenOpts), vp, vp], C.c_int),
         "rpgc_session_sync": ([i32], C.c_int),
         "rpgc_dequantize_rows": ([u32, vp, i64, i64, vp, vp], C.c_int),
@@ -294,6 +295,21 @@ def _stream(stream) -> int:
         import torch
         return int(torch.cuda.current_stream().cuda_stream)
     return int(stream)
+
+
+def generate_batch(sessions, max_tokens: int, stop_ids=(), temperature: float = 0.0, top_k: int = 0,
+                   top_p: float = 1.0, seed: int = 0) -> list:
+    """rpgc_generate_batch: max_tokens steps decoding one token for every
+    session at once; returns one array of generated ids per session."""
+    n = len(sessions)
+    handles = (C.c_int32 * n)(*[s.handle for s in sessions])
+    stop = (C.c_int32 * max(1, len(stop_ids)))(*stop_ids)
+    o = GenOpts(max_tokens, stop, len(stop_ids), temperature, top_k, top_p, seed)
+    out = np.zeros((n, max_tokens), np.int32)
+    n_out = np.zeros(n, np.int32)
+    _check(lib().rpgc_generate_batch(C.cast(handles, C.c_void_p), n, C.byref(o), out.ctypes.data,
+                                     n_out.ctypes.data))
+    return [out[i, : n_out[i]].copy() for i in range(n)]
 
 
 def tp_unique_id() -> bytes:

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <atomic>
 #include <climits>
 #include <cstdlib>
@@ -1070,6 +1071,70 @@ int guard(F&& f) {
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
+constexpr int32_t kMaxBatch = 256;
+
+struct BatchBufs {
+  std::vector<void*> ptrs;
+  cudaStream_t stream = nullptr;  // the batch's work is finished before the buffers go
+  template <typename T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, count * sizeof(T)));
+    ptrs.push_back(p);
+    return static_cast<T*>(p);
+  }
+  ~BatchBufs() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : ptrs) cudaFree(p);
+  }
+};
+
+void batch_layers(const Model* m, int32_t n, float* x, float* q, float* k, float* v, float* attn, float* gate,
+                  float* up, void* scratch, size_t sbytes, const AttnBatchEntry* entries, int32_t* err,
+                  cudaStream_t cs) {
+  const rpgc_model_config& c = m->c;
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
+                kvd = (int64_t)c.n_kv_heads * c.head_dim;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m->layers[l];
+    const GemmGroupMat qkv[3] = {{L.q.type, L.q.w, L.q.rows, L.q.row_bytes, q, qd},
+                                 {L.k.type, L.k.w, L.k.rows, L.k.row_bytes, k, kvd},
+                                 {L.v.type, L.v.w, L.v.rows, L.v.row_bytes, v, kvd}};
+    check(gemm_tc_split_norm(x, L.attn_norm, c.rms_eps, n, H, scratch, sbytes, cs), "norm split");
+    check(gemm_tc_launch_group(qkv, 3, H, nullptr, n, scratch, sbytes, cs, true), "gemm qkv");
+    AttnArgs aa{};
+    aa.q = q;
+    aa.k_new = k;
+    aa.v_new = v;
+    aa.out = attn;
+    aa.n_heads = c.n_heads;
+    aa.n_kv = c.n_kv_heads;
+    aa.hd = c.head_dim;
+    aa.q_norm = L.q_norm;
+    aa.k_norm = L.k_norm;
+    aa.rope = m->rope;
+    aa.eps = c.rms_eps;
+    aa.err = err;
+    aa.batch = entries;
+    aa.nbatch = n;
+    aa.layer = l;
+    check(attn_decode_launch(aa, cs), "attention");
+    check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, attn, n, x, H, true, scratch, sbytes, cs),
+          "gemm o");
+    check(gemm_tc_split_norm(x, L.ffn_norm, c.rms_eps, n, H, scratch, sbytes, cs), "norm split");
+    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, nullptr, n, gate, F, false, scratch,
+                      sbytes, cs, true),
+          "gemm gate");
+    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, nullptr, n, up, F, false, scratch, sbytes,
+                      cs, true),
+          "gemm up");
+    check(gemm_tc_split_glu(gate, up, n, F, scratch, sbytes, cs), "glu split");
+    check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, nullptr, n, x, H, true, scratch,
+                      sbytes, cs, true),
+          "gemm down");
+  }
+}
+
 }  // namespace
 
 // Lets other translation units of the library report through rpgc_last_error().
@@ -1365,6 +1430,135 @@ int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids, 
     std::lock_guard<std::mutex> lk(s->mu);
     const int64_t steps = generate(s, *opts, true);
     return finish_generate(s, *opts, steps, out_ids, n_out);
+  });
+}
+
+// Batched multi-session decode: one step decodes one token for each of the n
+// sessions at once.  The sessions' rows share the weight stream: the matmuls
+// run on the tensor cores over n rows (the prefill kernels), the attention is
+// the decode kernel with one grid slice per session (its own cache, position
+// and state), the sampler one block per session.
+int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts, int32_t* out_ids,
+                        int32_t* n_out) {
+  return guard([&] {
+    if (!sessions || !opts || !out_ids || !n_out) fail(RPGC_E_ARG, "null argument");
+    if (n < 1 || n > kMaxBatch) fail(RPGC_E_ARG, "batch of %d sessions (1 .. %d)", n, kMaxBatch);
+    const rpgc_gen_opts& o = *opts;
+    if (o.max_tokens <= 0) fail(RPGC_E_ARG, "max_tokens must be positive, got %d", o.max_tokens);
+    if (o.n_stop < 0 || o.n_stop > RPGC_MAX_STOP) fail(RPGC_E_ARG, "at most %d stop ids", RPGC_MAX_STOP);
+    if (o.n_stop > 0 && !o.stop_ids) fail(RPGC_E_ARG, "stop_ids is NULL");
+    for (int32_t i = 0; i < n; ++i) n_out[i] = 0;
+    std::vector<Session*> ss((size_t)n);
+    for (int32_t i = 0; i < n; ++i) {
+      ss[i] = require_session(sessions[i]);
+      for (int32_t j = 0; j < i; ++j)
+        if (ss[j] == ss[i]) fail(RPGC_E_ARG, "session %d appears twice in the batch", sessions[i]);
+      if (ss[i]->m != ss[0]->m) fail(RPGC_E_ARG, "the sessions of a batch must share one model");
+    }
+    const Model* m = ss[0]->m;
+    const rpgc_model_config& c = m->c;
+    if (m->tp_world > 1) fail(RPGC_E_ARG, "tensor-parallel models decode one session at a time");
+    std::vector<Session*> order(ss);  // lock in address order (no lock-order inversion)
+    std::sort(order.begin(), order.end());
+    std::vector<std::unique_lock<std::mutex>> locks;
+    for (Session* s : order) locks.emplace_back(s->mu);
+    for (int32_t i = 0; i < n; ++i) {
+      if (!ss[i]->has_logits) fail(RPGC_E_STATE, "session %d has no pending logits: call rpgc_forward first", sessions[i]);
+      if (ss[i]->max_seq - ss[i]->len < o.max_tokens)
+        fail(RPGC_E_CONTEXT_FULL, "session %d has room for %lld more tokens, max_tokens is %d", sessions[i],
+             (long long)(ss[i]->max_seq - ss[i]->len), o.max_tokens);
+    }
+    const int64_t H = c.hidden, F = c.intermediate, V = c.vocab, qd = (int64_t)c.n_heads * c.head_dim,
+                  kvd = (int64_t)c.n_kv_heads * c.head_dim;
+    const int64_t kmax = std::max(H, std::max(qd, F));
+    if (!gemm_uses_tc(m->layers[0].q.type, n, H, gemm_scratch_bytes(n, kmax)) || H % 64 || F % 64 || qd % 64)
+      fail(RPGC_E_ARG, "batched decode needs the tensor-core matmul shapes (hidden, q width, FFN multiples of 64)");
+    DeviceGuard dg(m->device);
+    cudaStream_t bs = ss[0]->stream;  // the batch runs on the first session's stream
+    cudaEvent_t ev = nullptr;
+    CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    struct EvGuard {
+      cudaEvent_t e;
+      ~EvGuard() { cudaEventDestroy(e); }
+    } evg{ev};
+    BatchBufs B;
+    B.stream = bs;
+    float* x = B.alloc<float>((size_t)n * H);
+    float* h = B.alloc<float>((size_t)n * H);
+    float* q = B.alloc<float>((size_t)n * qd);
+    float* k = B.alloc<float>((size_t)n * kvd);
+    float* v = B.alloc<float>((size_t)n * kvd);
+    float* attn = B.alloc<float>((size_t)n * qd);
+    float* gate = B.alloc<float>((size_t)n * F);
+    float* up = B.alloc<float>((size_t)n * F);
+    float* logits = B.alloc<float>((size_t)n * V);
+    const size_t sbytes = gemm_scratch_bytes(n, kmax);
+    void* scratch = B.alloc<uint8_t>(sbytes);
+    DecodeState** states = B.alloc<DecodeState*>((size_t)n);
+    int32_t** outs = B.alloc<int32_t*>((size_t)n);
+    int32_t** nouts = B.alloc<int32_t*>((size_t)n);
+    float** dst = B.alloc<float*>((size_t)n);
+    AttnBatchEntry* entries = B.alloc<AttnBatchEntry>((size_t)n);
+    std::vector<DecodeState*> hs((size_t)n);
+    std::vector<int32_t*> ho((size_t)n), hn((size_t)n);
+    std::vector<float*> hd((size_t)n);
+    std::vector<AttnBatchEntry> he((size_t)n);
+    for (int32_t i = 0; i < n; ++i) {
+      Session* s = ss[i];
+      DecodeState st;
+      std::memset(&st, 0, sizeof(st));
+      st.pos = (int32_t)s->len;
+      st.start_pos = (int32_t)s->len;
+      st.active = 1;
+      st.max_tokens = o.max_tokens;
+      st.n_stop = o.n_stop;
+      for (int j = 0; j < o.n_stop; ++j) st.stop_ids[j] = o.stop_ids[j];
+      st.temperature = o.temperature;
+      st.top_k = o.top_k;
+      st.top_p = o.top_p;
+      st.seed = o.seed;
+      check(state_set_launch(s->st, st, s->stream), "state");
+      CK(cudaEventRecord(ev, s->stream));  // the session's own work comes first
+      CK(cudaStreamWaitEvent(bs, ev, 0));
+      CK(cudaMemcpyAsync(logits + (size_t)i * V, s->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, bs));
+      hs[i] = s->st;
+      ho[i] = s->gen_out;
+      hn[i] = s->n_out;
+      hd[i] = s->logits;
+      he[i] = AttnBatchEntry{s->st, s->kc, s->vc, s->max_seq};
+    }
+    CK(cudaMemcpy(states, hs.data(), n * sizeof(DecodeState*), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(outs, ho.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(nouts, hn.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dst, hd.data(), n * sizeof(float*), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(entries, he.data(), n * sizeof(AttnBatchEntry), cudaMemcpyHostToDevice));
+    SampleArgs sa{};
+    sa.logits = logits;
+    sa.n = V;
+    sa.embd = m->embd.w;
+    sa.embd_row_bytes = m->embd.row_bytes;
+    sa.embd_type = m->embd.type;
+    sa.hidden = (int32_t)H;
+    sa.x = x;
+    sa.states = states;
+    sa.out_ids_b = outs;
+    sa.n_out_b = nouts;
+    sa.nbatch = n;
+    for (int32_t step = 0; step < o.max_tokens; ++step) {
+      check(sample_launch(sa, bs), "sample");
+      batch_layers(m, n, x, q, k, v, attn, gate, up, scratch, sbytes, entries, &ss[0]->st->error, bs);
+      check(rmsnorm_rows_launch(x, m->out_norm, n, c.hidden, c.rms_eps, h, bs), "rmsnorm");
+      check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, H, m->lm_head.row_bytes, h, n, logits, V,
+                        false, scratch, sbytes, bs),
+            "gemm lm_head");
+      check(commit_rows_launch(logits, V, dst, states, n, bs), "commit logits");
+    }
+    CK(cudaEventRecord(ev, bs));
+    for (int32_t i = 0; i < n; ++i) CK(cudaStreamWaitEvent(ss[i]->stream, ev, 0));
+    for (int32_t i = 0; i < n; ++i)
+      finish_generate(ss[i], o, o.max_tokens, out_ids + (size_t)i * o.max_tokens, n_out + i);
+    CK(cudaStreamSynchronize(bs));  // the buffers are freed after the batch's last kernel
+    return RPGC_OK;
   });
 }
 

@@ -85,7 +85,21 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   __shared__ __align__(16) float cpart[G][132];  // merged o[128], m, l of this CTA
   __shared__ __align__(8) uint64_t bar;
 
-  const DecodeState* st = a.state;
+  // batched decode: session z = blockIdx.z (its rows of q / k_new / v_new /
+  // out, its cache and state); otherwise z = 0 and the single-session fields
+  const int64_t z = blockIdx.z;
+  const AttnBatchEntry* be = a.batch ? a.batch + z : nullptr;
+  const DecodeState* st = be ? be->state : a.state;
+  const int64_t max_seq = be ? be->max_seq : a.max_seq;
+  const int64_t loff = be ? (int64_t)a.layer * a.n_kv * max_seq * 128 : 0;
+  const float* kcache = be ? be->kc + loff : a.kc;
+  const float* vcache = be ? be->vc + loff : a.vc;
+  float* kc_w = be ? be->kc + loff : a.kc_w;
+  float* vc_w = be ? be->vc + loff : a.vc_w;
+  const float* qz = a.q + z * a.n_heads * 128;
+  const float* knz = a.k_new ? a.k_new + z * a.n_kv * 128 : nullptr;
+  const float* vnz = a.v_new ? a.v_new + z * a.n_kv * 128 : nullptr;
+  float* outz = a.out + z * a.n_heads * 128;
   cg::cluster_group cluster = cg::this_cluster();
   const int S = (int)gridDim.y, split = (int)blockIdx.y, kh = (int)blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -102,8 +116,8 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   const bool fused = a.q_norm != nullptr;
   const bool owner = fused && c0 <= pos && pos < c1;  // this split holds the new token
   const float* cs = fused ? a.rope + (int64_t)pos * 128 : nullptr;
-  const float* kb = a.kc + (int64_t)kh * a.max_seq * 128;
-  const float* vb = a.vc + (int64_t)kh * a.max_seq * 128;
+  const float* kb = kcache + (int64_t)kh * max_seq * 128;
+  const float* vb = vcache + (int64_t)kh * max_seq * 128;
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -124,19 +138,19 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   }
   // query heads of this kv head (normalised and rotated when fused)
   for (int g = warp; g < G; g += kAWarps) {
-    float4 v = *reinterpret_cast<const float4*>(a.q + (kh * G + g) * 128 + 4 * lane);
+    float4 v = *reinterpret_cast<const float4*>(qz + (kh * G + g) * 128 + 4 * lane);
     if (fused) v = norm_rope_head(v, a.q_norm, cs, a.eps, lane);
     *reinterpret_cast<float4*>(&qs[g][4 * lane]) = v;
   }
   float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
   if (owner && warp == kAWarps - 1) {
     // the new token's k/v: normalise + rotate k, write both into the cache
-    knew = *reinterpret_cast<const float4*>(a.k_new + kh * 128 + 4 * lane);
+    knew = *reinterpret_cast<const float4*>(knz + kh * 128 + 4 * lane);
     knew = norm_rope_head(knew, a.k_norm, cs, a.eps, lane);
-    vnew = *reinterpret_cast<const float4*>(a.v_new + kh * 128 + 4 * lane);
-    const int64_t off = ((int64_t)kh * a.max_seq + pos) * 128 + 4 * lane;
-    *reinterpret_cast<float4*>(a.kc_w + off) = knew;
-    *reinterpret_cast<float4*>(a.vc_w + off) = vnew;
+    vnew = *reinterpret_cast<const float4*>(vnz + kh * 128 + 4 * lane);
+    const int64_t off = ((int64_t)kh * max_seq + pos) * 128 + 4 * lane;
+    *reinterpret_cast<float4*>(kc_w + off) = knew;
+    *reinterpret_cast<float4*>(vc_w + off) = vnew;
   }
   __syncthreads();
 
@@ -250,7 +264,7 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
         O += rp[d] * f;
         Ls += rp[129] * f;
       }
-      a.out[(kh * G + g) * 128 + d] = O / Ls;
+      outz[(kh * G + g) * 128 + d] = O / Ls;
     }
   }
   cluster.sync();  // keep every CTA's shared memory alive until rank 0 is done
@@ -572,7 +586,7 @@ template <int G>
 cudaError_t launch_decode(const AttnArgs& a, cudaStream_t s) {
   const int S = cluster_size<G>();
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)S);
+  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)S, (unsigned)(a.batch ? a.nbatch : 1));
   cfg.blockDim = dim3(kAWarps * 32);
   cfg.dynamicSmemBytes = 2 * kTileP * 128 * sizeof(float);
   cfg.stream = s;
@@ -595,9 +609,10 @@ cudaError_t launch_decode(const AttnArgs& a, cudaStream_t s) {
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
   const int G = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
   if (a.hd != 128 || a.n_kv <= 0 || a.n_heads % a.n_kv) return cudaErrorInvalidValue;
-  if ((reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15)
+  if (!a.batch && ((reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15))
     return cudaErrorInvalidValue;
-  if (a.q_norm && (!a.k_norm || !a.rope || !a.k_new || !a.v_new || !a.kc_w || !a.vc_w))
+  if (a.batch && (a.nbatch < 1 || a.nbatch > 65535 || !a.q_norm)) return cudaErrorInvalidValue;
+  if (a.q_norm && (!a.k_norm || !a.rope || !a.k_new || !a.v_new || (!a.batch && (!a.kc_w || !a.vc_w))))
     return cudaErrorInvalidValue;
   switch (G) {
     case 1: return launch_decode<1>(a, s);

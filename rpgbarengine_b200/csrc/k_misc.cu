@@ -105,6 +105,28 @@ cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, 
   return e_;
 }
 
+// Batched decode: row b of src goes to dst[b] when session b took part in
+// this step (its state is active), so a session that has stopped keeps the
+// logits of its last real step.
+__global__ void commit_rows_kernel(const float* __restrict__ src, int64_t n_cols, float* const* dst,
+                                   DecodeState* const* states) {
+  const int64_t b = blockIdx.y;
+  if (!states[b]->active) return;
+  const float* s = src + b * n_cols;
+  float* d = dst[b];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_cols; i += (int64_t)gridDim.x * blockDim.x)
+    d[i] = s[i];
+}
+
+cudaError_t commit_rows_launch(const float* src, int64_t n_cols, float* const* dst, DecodeState* const* states,
+                               int32_t n, cudaStream_t s) {
+  if (n < 1 || n > 65535 || n_cols <= 0) return cudaErrorInvalidValue;
+  commit_rows_kernel<<<dim3(64, (unsigned)n), 256, 0, s>>>(src, n_cols, dst, states);
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
+}
+
 cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
                                 float* out, cudaStream_t s) {
   rmsnorm_rows_kernel<<<(unsigned)n, 256, 0, s>>>(x, w, dim, eps, out);

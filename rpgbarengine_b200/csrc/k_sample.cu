@@ -438,7 +438,14 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) uint8_t raw[];
   Smem& S = *reinterpret_cast<Smem*>(raw);
   grid_dep_wait();
-  DecodeState* st = a.state;
+  // batched decode: block b is session b (its logits row, state, outputs and
+  // embedding row); otherwise the single-session fields
+  const int b = (int)blockIdx.x;
+  DecodeState* st = a.states ? a.states[b] : a.state;
+  const float* logits = a.logits + (int64_t)b * a.n;
+  int32_t* out_ids = a.states ? a.out_ids_b[b] : a.out_ids;
+  int32_t* n_out = a.states ? a.n_out_b[b] : a.n_out;
+  float* xrow = a.x ? a.x + (int64_t)b * a.hidden : nullptr;
   float T = a.temperature, top_p = a.top_p, u = a.u;
   int top_k = a.top_k;
   int pos = 0;
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int j = threadIdx.x; j < n; j += NT) {
-      const float v = a.logits[j];
+      const float v = logits[j];
       if (v > bv) {  // a thread's indices increase, so strict > keeps the first
         bv = v;
         bi = j;
@@ -470,23 +477,23 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
     tok = block_argmax(S, bv, bi);
     if (tok == 0x7fffffff) tok = 0;
   } else {
-    tok = sample_probs(S, a.logits, n, T, top_k, top_p, u);
+    tok = sample_probs(S, logits, n, T, top_k, top_p, u);
   }
-  if (st && a.x) {  // the decode step continues with this token's embedding row
+  if (st && xrow) {  // the decode step continues with this token's embedding row
     const uint8_t* row = a.embd + (int64_t)tok * a.embd_row_bytes;
-    for (int e = threadIdx.x; e < a.hidden; e += NT) a.x[e] = deq_elem(a.embd_type, row, e);
+    for (int e = threadIdx.x; e < a.hidden; e += NT) xrow[e] = deq_elem(a.embd_type, row, e);
   }
   if (threadIdx.x == 0) {
     if (st) {
       st->pos = pos;
       st->token = tok;
-      a.out_ids[st->n_gen] = tok;
+      out_ids[st->n_gen] = tok;
       st->n_gen += 1;
       st->active = 1;
       bool stop = false;
       for (int i = 0; i < st->n_stop; ++i) stop |= (st->stop_ids[i] == tok);
       if (stop || st->n_gen >= st->max_tokens) st->done = 1;
-      if (a.n_out) *a.n_out = st->n_gen;
+      if (n_out) *n_out = st->n_gen;
     } else {
       *a.token_out = tok;
     }
@@ -506,8 +513,9 @@ cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
     configured = dev;
   }
   if (a.n <= 0 || a.n > 0x7ffffff0) return cudaErrorInvalidValue;
+  if (a.states && (a.nbatch < 1 || !a.out_ids_b || !a.n_out_b)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(a.states ? (unsigned)a.nbatch : 1u);
   cfg.blockDim = dim3(NT);
   cfg.dynamicSmemBytes = sizeof(Smem);
   cfg.stream = s;

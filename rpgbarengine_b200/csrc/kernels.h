@@ -178,6 +178,10 @@ cudaError_t embed_launch(uint32_t type, const uint8_t* embd, int64_t row_bytes, 
                          const DecodeState* state, int32_t* err, cudaStream_t s);
 cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
                                 float* out, cudaStream_t s);
+// Batched decode: dst[b][0, n_cols) = src row b for every session b whose
+// state is active (device arrays of n pointers).
+cudaError_t commit_rows_launch(const float* src, int64_t n_cols, float* const* dst, DecodeState* const* states,
+                               int32_t n, cudaStream_t s);
 cudaError_t swiglu_launch(float* gate, const float* up, int64_t count, cudaStream_t s);
 
 // Per token t (position pos0+t, or state->pos when state != null): RMSNorm
@@ -201,6 +205,14 @@ struct QkvArgs {
 };
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s);
 
+// One session of a batched decode step (attention over its own cache).
+struct AttnBatchEntry {
+  const DecodeState* state;  // position, active flag
+  float* kc;                 // the session's K cache, layer 0 ([layers][n_kv][max_seq][hd])
+  float* vc;
+  int64_t max_seq;
+};
+
 struct AttnArgs {
   const float* q;      // [n][n_heads*hd] (decode with q_norm: raw projections)
   const float* kc;     // layer cache [n_kv][max_seq][hd]
@@ -222,6 +234,11 @@ struct AttnArgs {
   float* vc_w;
   float eps;
   bool pdl;
+  // batched decode (optional): nbatch sessions, blockIdx.z = session z, whose
+  // q / k_new / v_new / out rows are row z of those arrays and whose cache is
+  // layer `layer` of batch[z] (state, kc, vc, max_seq replace the fields above)
+  const AttnBatchEntry* batch;
+  int32_t nbatch, layer;
 };
 // Decode attention needs no scratch: the splits of a kv head form one
 // thread-block cluster and merge in distributed shared memory.  Group sizes
@@ -251,6 +268,13 @@ struct SampleArgs {
   int32_t hidden;
   float* x;
   bool pdl;
+  // batched decode (optional): nbatch blocks, block b samples logits row b
+  // (logits + b * n) for session b: states[b], out_ids_b[b], n_out_b[b], and
+  // writes the embedding into x + b * hidden
+  DecodeState* const* states;
+  int32_t* const* out_ids_b;
+  int32_t* const* n_out_b;
+  int32_t nbatch;
 };
 cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s);
 // state->pos += 1 when active (end of a decode step).

@@ -227,3 +227,59 @@ def test_out_of_range_device_ids_are_reported_not_faulted(orc):
     s.set_len(0)
     good = synth.prompt_ids(8, 6, synth.TINY_MIX.vocab)
     assert np.isfinite(s.forward_full(good)).all()
+
+
+def test_generate_batch_matches_each_session_alone(orc):
+    # three sessions with different prompt lengths decode together; each must
+    # produce what the oracle gives it alone (greedy, then seeded sampling)
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    prompts = [synth.prompt_ids(40 + i, n, shape.vocab) for i, n in enumerate((9, 23, 5))]
+    for opts in (dict(), dict(temperature=0.8, top_k=40, top_p=0.9, seed=77)):
+        sess = [gm.session(64) for _ in prompts]
+        for s, p in zip(sess, prompts):
+            s.forward_full(p)
+        got = rb.generate_batch(sess, 10, **opts)
+        for s, p, g in zip(sess, prompts, got):
+            okv = om.kv(64)
+            first = om.forward(p, okv)[-1]
+            ref, ref_logits = om.generate(okv, first, 10, want_logits=True, **opts)
+            compare_tokens(list(g), ref, ref_logits)
+            assert s.len == len(p) + len(g)
+        # the sessions carry on singly after the batch
+        nxt = sess[1].generate(3)
+        assert len(nxt) == 3
+
+
+def test_generate_batch_stops_sessions_independently(orc):
+    # a stop id taken from session a's own greedy continuation: a stops on it
+    # (the stop token is kept), b runs on unless it meets it too
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    p0, p1 = synth.prompt_ids(50, 12, shape.vocab), synth.prompt_ids(51, 7, shape.vocab)
+    okv = om.kv(64)
+    ref0, _ = om.generate(okv, om.forward(p0, okv)[-1], 6, want_logits=True)
+    stop = [int(ref0[2])]
+    a, b = gm.session(64), gm.session(64)
+    a.forward_full(p0)
+    b.forward_full(p1)
+    got = rb.generate_batch([a, b], 6, stop_ids=stop)
+    for s, p, g in ((a, p0, got[0]), (b, p1, got[1])):
+        kv = om.kv(64)
+        ref, ref_logits = om.generate(kv, om.forward(p, kv)[-1], 6, stop_ids=stop, want_logits=True)
+        compare_tokens(list(g), ref, ref_logits)
+        assert s.len == len(p) + len(g)
+    assert len(got[0]) <= 3
+
+
+def test_generate_batch_rejects_bad_batches(orc):
+    gm, _ = pair(orc, synth.TINY_MIX)
+    a = gm.session(16)
+    a.forward_full(synth.prompt_ids(52, 10, synth.TINY_MIX.vocab))
+    with pytest.raises(rb.RpgcError):
+        rb.generate_batch([a, a], 2)  # twice
+    with pytest.raises(rb.ContextFull):
+        rb.generate_batch([a], 7)  # room for 6
+    fresh = gm.session(16)
+    with pytest.raises(rb.RpgcError):
+        rb.generate_batch([a, fresh], 2)  # fresh has no pending logits
