@@ -584,7 +584,23 @@ int cluster_size() {
 
 template <int G>
 cudaError_t launch_decode(const AttnArgs& a, cudaStream_t s) {
-  const int S = cluster_size<G>();
+  int S = cluster_size<G>();
+  if (a.batch) {
+    // a batch has parallelism across sessions: split a session's positions only
+    // as far as needed for two CTAs per SM (fewer splits, fewer merges; 64
+    // sessions of the 4B shape decode 1.6x faster unsplit than in 16 splits)
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int nsm = 148;
+    if (dev >= 0 && dev < 64) {
+      if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+      if (sms[dev] > 0) nsm = sms[dev];
+    }
+    int want = 1;
+    while (want < S && (int64_t)a.n_kv * want * a.nbatch < 2 * nsm) want *= 2;
+    S = want;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)S, (unsigned)(a.batch ? a.nbatch : 1));
   cfg.blockDim = dim3(kAWarps * 32);

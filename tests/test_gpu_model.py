@@ -251,6 +251,24 @@ def test_generate_batch_matches_each_session_alone(orc):
         assert len(nxt) == 3
 
 
+@pytest.mark.parametrize("n_sessions", [24, 150])
+def test_generate_batch_many_sessions(orc, n_sessions):
+    # large batches split each session's positions less (2 kv heads: 24 sessions
+    # take 8 splits, 150 take none); every session still matches the oracle
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    prompts = [synth.prompt_ids(300 + i, 3 + i % 7, shape.vocab) for i in range(n_sessions)]
+    sess = [gm.session(16) for _ in prompts]
+    for s, p in zip(sess, prompts):
+        s.forward_full(p)
+    got = rb.generate_batch(sess, 4)
+    for p, g in zip(prompts, got):
+        okv = om.kv(16)
+        first = om.forward(p, okv)[-1]
+        ref, ref_logits = om.generate(okv, first, 4, want_logits=True)
+        compare_tokens(list(g), ref, ref_logits)
+
+
 def test_generate_batch_stops_sessions_independently(orc):
     # a stop id taken from session a's own greedy continuation: a stops on it
     # (the stop token is kept), b runs on unless it meets it too
