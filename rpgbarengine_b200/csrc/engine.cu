@@ -1492,7 +1492,10 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
     float* gate = B.alloc<float>((size_t)n * F);
     float* up = B.alloc<float>((size_t)n * F);
     float* logits = B.alloc<float>((size_t)n * V);
-    const size_t sbytes = gemm_scratch_bytes(n, kmax);
+    // room for split-K partial sums of up to 8 partitions of the widest
+    // matrix per token: a few dozen session rows fill the GPU only with K split
+    const size_t sbytes =
+        gemm_scratch_bytes(n, kmax) + (size_t)n * 8 * (size_t)std::max<int64_t>(F, std::max<int64_t>(H, qd)) * sizeof(float);
     void* scratch = B.alloc<uint8_t>(sbytes);
     DecodeState** states = B.alloc<DecodeState*>((size_t)n);
     int32_t** outs = B.alloc<int32_t*>((size_t)n);

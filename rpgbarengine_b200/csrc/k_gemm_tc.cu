@@ -17,8 +17,10 @@
 // Data path (one CTA per 256 tokens x 128 weight rows):
 //   warp 0      TMA of the Xh / Xl tiles (SWIZZLE_128B, 64 K x 256 tokens)
 //   warp 1      TMEM allocation and the MMA issue (one thread): per 64-K
-//               stage 2 token blocks x 4 k16 steps x 3 products, M=128
-//               N=128 K=16 each, then tcgen05.commit frees the stage
+//               stage 2 token blocks (1 when the tile's second 128 tokens
+//               are past n, e.g. a batched decode step) x 4 k16 steps x 3
+//               products, M=128 N=128 K=16 each, then tcgen05.commit frees
+//               the stage
 //   warps 2..   dequantise the stage's weight tile into Wh / Wl (same
 //               swizzled K-major layout; four threads per row), then read
 //               the two 128 x TN fp32 accumulators back from TMEM and
@@ -326,6 +328,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
   const int64_t n0 = (int64_t)bx * TN;           // first weight row
   const int t0 = (int)blockIdx.y * TMt;          // first token
   const int nk_all = (int)(g.K / TKt);
+  const int nmb = g.n - t0 > 128 ? 2 : 1;        // 128-token halves holding live tokens
   const int kc0 = (int)((int64_t)nk_all * blockIdx.z / g.ks);  // this CTA's stages
   const int nk = (int)((int64_t)nk_all * (blockIdx.z + 1) / g.ks) - kc0;
 
@@ -375,6 +378,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
           const uint64_t bh = sdesc(Wh(s) + kk * 32), bl = sdesc(Wl(s) + kk * 32);
 #pragma unroll
           for (int mb = 0; mb < 2; ++mb) {
+            if (mb >= nmb) break;  // a half past the last token: no MMAs for it
             const uint64_t ah = sdesc(Ah(s) + mb * (128 * 128) + kk * 32);
             const uint64_t al = sdesc(Al(s) + mb * (128 * 128) + kk * 32);
             const uint32_t d = tmem + (uint32_t)(mb * TN);
@@ -402,12 +406,15 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       fetch16(M.type, row, (int64_t)kc0 * TKt + 16 * qq, raw0);
       if (nk > 1) fetch16(M.type, row, (int64_t)(kc0 + 1) * TKt + 16 * qq, raw1);
     }
-    for (int c = 0; c < nk; ++c) {
+    // stage c converts the raw words fetched two stages earlier, then fetches
+    // stage c + 2 into the same registers (even stages raw0, odd raw1: the
+    // loop runs two stages per pass so that no register copy waits on a load)
+    auto stage = [&](int c, uint32_t* raw) {
       const int s = c % kStg;
       const int64_t k0 = (int64_t)(kc0 + c) * TKt + 16 * qq;
       float w[16];
       if (live) {
-        convert16(M.type, raw0, row, k0, w);
+        convert16(M.type, raw, row, k0, w);
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) w[i] = 0.0f;
@@ -424,9 +431,12 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMA
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_w[s]);
-#pragma unroll
-      for (int i = 0; i < kRaw; ++i) raw0[i] = raw1[i];
-      if (live && c + 2 < nk) fetch16(M.type, row, k0 + 2 * TKt, raw1);
+      if (live && c + 2 < nk) fetch16(M.type, row, k0 + 2 * TKt, raw);
+    };
+    static_assert(kStg == 2, "the raw words alternate between two register sets");
+    for (int c = 0; c < nk; c += 2) {
+      stage(c, raw0);
+      if (c + 1 < nk) stage(c + 1, raw1);
     }
     // ------------------------------------------------ epilogue
     // the dequant warps read the accumulators: warp w may read TMEM lanes
@@ -437,7 +447,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     tc_fence_after();
     const int ew = warp - 2, quarter = warp & 3, nq = (kDeqWarps - (ew & 3) + 3) >> 2;
 #pragma unroll 1
-    for (int mb = ew >> 2; mb < 2; mb += nq) {
+    for (int mb = ew >> 2; mb < nmb; mb += nq) {
       const int tl = mb * 128 + quarter * 32 + lane;  // token row of the tile = TMEM lane
       const int64_t t = t0 + tl;
       const float inv = t < g.n ? g.inv_scale[t] : 0.0f;
@@ -711,12 +721,13 @@ cudaError_t launch_tile(const CUtensorMap& mh, const CUtensorMap& ml, const Gemm
 }
 
 // Split-K factor for a tile shape: enough K partitions to fill the GPU
-// once, at least 8 stages each, partial sums within the scratch.
-int64_t split_k(int64_t tiles, int64_t rows, int64_t K, int nsm) {
+// once, at least 8 stages each, the partial sums (ks x rows per token)
+// within the part_rows the scratch holds per token.
+int64_t split_k(int64_t tiles, int64_t rows, int64_t K, int nsm, int64_t part_rows) {
   int64_t ks = tiles >= nsm ? 1 : nsm / tiles;
   const int64_t nk = K / TKt;
   if (ks > nk / 8) ks = nk / 8 > 0 ? nk / 8 : 1;
-  while (ks > 1 && ks * rows > kMaxPartRows) --ks;
+  while (ks > 1 && ks * rows > part_rows) --ks;
   return ks;
 }
 
@@ -741,9 +752,11 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
   __half* xh = static_cast<__half*>(scratch);
   __half* xl = xh + n * K;
   float* inv = reinterpret_cast<float*>(xl + n * K);
-  float* part = reinterpret_cast<float*>(
-      static_cast<uint8_t*>(scratch) +
-      (((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255));
+  const size_t part_off = ((size_t)2 * n * K * sizeof(__half) + (size_t)n * sizeof(float) + 255) & ~(size_t)255;
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + part_off);
+  // rows of partial sums per token the scratch holds past the split (at least
+  // kMaxPartRows; more when the caller passes a larger scratch)
+  const int64_t part_rows = (int64_t)((scratch_bytes - part_off) / sizeof(float) / (size_t)n);
   cudaError_t e;
   if (!x_split_ready) {  // else the scratch holds the split of this same X (the caller's promise)
     e = split_rows_launch<kPlain>(X, nullptr, n, K, 0.0f, xh, xl, inv, s);
@@ -768,7 +781,7 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
     int64_t tiles = 0;
     for (int i = 0; i < nmat; ++i) tiles += (mat[i].rows + tn - 1) / tn;
     tiles *= ttok;
-    const int64_t ks = (glu || nmat > 1) ? 1 : split_k(tiles, mat[0].rows, K, nsm);
+    const int64_t ks = (glu || nmat > 1) ? 1 : split_k(tiles, mat[0].rows, K, nsm, part_rows);
     const int64_t waves = (tiles * ks + nsm - 1) / nsm;
     const double cost = (double)waves * (double)tn / (double)ks;
     if (cost < best_cost - 1e-9) {
