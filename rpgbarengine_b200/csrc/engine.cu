@@ -1122,12 +1122,11 @@ void batch_layers(const Model* m, int32_t n, float* x, float* q, float* k, float
     check(gemm_launch(L.o.type, L.o.w, L.o.rows, qd, L.o.row_bytes, attn, n, x, H, true, scratch, sbytes, cs),
           "gemm o");
     check(gemm_tc_split_norm(x, L.ffn_norm, c.rms_eps, n, H, scratch, sbytes, cs), "norm split");
-    check(gemm_launch(L.gate.type, L.gate.w, L.gate.rows, H, L.gate.row_bytes, nullptr, n, gate, F, false, scratch,
-                      sbytes, cs, true),
-          "gemm gate");
-    check(gemm_launch(L.up.type, L.up.w, L.up.rows, H, L.up.row_bytes, nullptr, n, up, F, false, scratch, sbytes,
-                      cs, true),
-          "gemm up");
+    // gate and up share their input: one launch (at a few dozen rows each
+    // alone would need split-K and a reduction to fill the GPU)
+    const GemmGroupMat gu[2] = {{L.gate.type, L.gate.w, L.gate.rows, L.gate.row_bytes, gate, F},
+                                {L.up.type, L.up.w, L.up.rows, L.up.row_bytes, up, F}};
+    check(gemm_tc_launch_group(gu, 2, H, nullptr, n, scratch, sbytes, cs, true), "gemm gate+up");
     check(gemm_tc_split_glu(gate, up, n, F, scratch, sbytes, cs), "glu split");
     check(gemm_launch(L.down.type, L.down.w, L.down.rows, F, L.down.row_bytes, nullptr, n, x, H, true, scratch,
                       sbytes, cs, true),
@@ -1547,7 +1546,7 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
     sa.out_ids_b = outs;
     sa.n_out_b = nouts;
     sa.nbatch = n;
-    for (int32_t step = 0; step < o.max_tokens; ++step) {
+    auto one_step = [&] {
       check(sample_launch(sa, bs), "sample");
       batch_layers(m, n, x, q, k, v, attn, gate, up, scratch, sbytes, entries, &ss[0]->st->error, bs);
       check(rmsnorm_rows_launch(x, m->out_norm, n, c.hidden, c.rms_eps, h, bs), "rmsnorm");
@@ -1555,6 +1554,45 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
                         false, scratch, sbytes, bs),
             "gemm lm_head");
       check(commit_rows_launch(logits, V, dst, states, n, bs), "commit logits");
+    };
+    // The first step runs as plain launches (one-time kernel attributes are
+    // set there); the others replay a graph of one step, captured once: every
+    // argument of a step (positions, states, buffers) lives on the device, so
+    // one graph serves every step, and ~13 launches per layer cost one.
+    one_step();
+    if (o.max_tokens > 1) {
+      cudaGraph_t g = nullptr;
+      int64_t nk = 0;
+      CK(cudaStreamBeginCapture(bs, cudaStreamCaptureModeThreadLocal));
+      t_capture_count = &nk;
+      try {
+        one_step();
+      } catch (...) {
+        t_capture_count = nullptr;
+        cudaStreamEndCapture(bs, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      t_capture_count = nullptr;
+      CK(cudaStreamEndCapture(bs, &g));
+      struct ExecGuard {  // destroyed after the stream has run every launch of it
+        cudaGraphExec_t e = nullptr;
+        cudaStream_t s = nullptr;
+        ~ExecGuard() {
+          if (e) {
+            cudaStreamSynchronize(s);
+            cudaGraphExecDestroy(e);
+          }
+        }
+      } ge;
+      ge.s = bs;
+      const cudaError_t e = cudaGraphInstantiate(&ge.e, g, 0);
+      cudaGraphDestroy(g);
+      CK(e);
+      for (int32_t step = 1; step < o.max_tokens; ++step) {
+        CK(cudaGraphLaunch(ge.e, bs));
+        count_launches(nk);
+      }
     }
     CK(cudaEventRecord(ev, bs));
     for (int32_t i = 0; i < n; ++i) CK(cudaStreamWaitEvent(ss[i]->stream, ev, 0));

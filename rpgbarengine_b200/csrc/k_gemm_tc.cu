@@ -521,13 +521,14 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
 // from there.  K is a multiple of 4.
 enum SplitMode { kPlain = 0, kNorm = 1, kGlu = 2 };
 
-template <int MODE>
-__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ A, const float* __restrict__ B,
+template <int MODE, int NT>
+__global__ void __launch_bounds__(NT, 1) split_rows_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                          int64_t K, float eps, __half* __restrict__ xh,
                                                          __half* __restrict__ xl, float* __restrict__ inv_scale) {
   extern __shared__ __align__(16) float vrow[];  // [K]
-  __shared__ double dred[8];
-  __shared__ float red[8];
+  constexpr int NW = NT / 32;
+  __shared__ double dred[NW];
+  __shared__ float red[NW];
   const int64_t t = blockIdx.x;
   const int64_t K4 = K >> 2;
   const float4* a4 = reinterpret_cast<const float4*>(A + t * K);
@@ -536,7 +537,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
   float m = 0.0f;
   double ss = 0.0;
 #pragma unroll 4
-  for (int64_t i = threadIdx.x; i < K4; i += 256) {
+  for (int64_t i = threadIdx.x; i < K4; i += NT) {
     float4 v = a4[i];
     if (MODE == kGlu) {
       const float4 u = b4[i];
@@ -556,11 +557,11 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     if ((threadIdx.x & 31) == 0) dred[threadIdx.x >> 5] = ss;
     __syncthreads();
     double tot = 0.0;
-    for (int i = 0; i < 8; ++i) tot += dred[i];
+    for (int i = 0; i < NW; ++i) tot += dred[i];
     const float nsc = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
     const float4* w4 = reinterpret_cast<const float4*>(B);
 #pragma unroll 4
-    for (int64_t i = threadIdx.x; i < K4; i += 256) {  // each thread rereads its own entries
+    for (int64_t i = threadIdx.x; i < K4; i += NT) {  // each thread rereads its own entries
       float4 v = v4[i];
       const float4 w = w4[i];
       v.x = v.x * nsc * w.x;
@@ -575,7 +576,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   float mx = 0.0f;
-  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+  for (int i = 0; i < NW; ++i) mx = fmaxf(mx, red[i]);
   const int e = (int)((__float_as_uint(mx) >> 23) & 0xFFu);  // biased exponent of the max
   // scale 2^(141 - e): max |v| s in [2^14, 2^15); clamped to stay finite
   int se = 141 - e;
@@ -584,7 +585,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
   uint2* h2 = reinterpret_cast<uint2*>(xh + t * K);
   uint2* l2 = reinterpret_cast<uint2*>(xl + t * K);
 #pragma unroll 4
-  for (int64_t i = threadIdx.x; i < K4; i += 256) {
+  for (int64_t i = threadIdx.x; i < K4; i += NT) {
     const float4 v = v4[i];
     const float y[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
     uint32_t hw[2], lw[2];
@@ -612,12 +613,18 @@ cudaError_t split_rows_launch(const float* A, const float* B, int64_t n, int64_t
   cudaGetDevice(&dev);
   const int smem = (int)(K * 4);
   if (dev >= 0 && dev < 64 && configured[dev] < smem) {  // dynamic + static above 48 KB needs the opt-in
-    const cudaError_t e =
-        cudaFuncSetAttribute(split_rows_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(split_rows_kernel<MODE, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(split_rows_kernel<MODE, 1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
-  split_rows_kernel<MODE><<<(unsigned)n, 256, smem, s>>>(A, B, K, eps, xh, xl, inv);
+  // a few hundred rows or more fill the GPU at 256 threads a row; fewer
+  // (a batched decode step's session rows) take 1024 threads a row
+  if (n >= 256)
+    split_rows_kernel<MODE, 256><<<(unsigned)n, 256, smem, s>>>(A, B, K, eps, xh, xl, inv);
+  else
+    split_rows_kernel<MODE, 1024><<<(unsigned)n, 1024, smem, s>>>(A, B, K, eps, xh, xl, inv);
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) count_launches(1);
   return e;
@@ -737,8 +744,8 @@ namespace {
 
 // One launch over the matrices mat[0..nmat) sharing the input X (n x K):
 // the activation split (unless the scratch already holds it), the tile
-// height with the least work per SM, split-K for a single matrix, the
-// partial-sum reduction.
+// height with the least work per SM, split-K (a group's matrices split
+// alike), the partial-sum reductions.
 cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int64_t n, bool accumulate,
                          void* scratch, size_t scratch_bytes, cudaStream_t s, bool x_split_ready,
                          const float* glu) {
@@ -777,11 +784,13 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
   const int64_t ttok = (n + TMt - 1) / TMt;
   int64_t best_tn = 128, best_ks = 1;
   double best_cost = 1e30;
+  int64_t all_rows = 0;  // partial sums of a group hold every matrix's rows
+  for (int i = 0; i < nmat; ++i) all_rows += mat[i].rows;
   for (const int64_t tn : {96, 128, 144}) {
     int64_t tiles = 0;
     for (int i = 0; i < nmat; ++i) tiles += (mat[i].rows + tn - 1) / tn;
     tiles *= ttok;
-    const int64_t ks = (glu || nmat > 1) ? 1 : split_k(tiles, mat[0].rows, K, nsm, part_rows);
+    const int64_t ks = glu ? 1 : split_k(tiles, all_rows, K, nsm, part_rows);
     const int64_t waves = (tiles * ks + nsm - 1) / nsm;
     const double cost = (double)waves * (double)tn / (double)ks;
     if (cost < best_cost - 1e-9) {
@@ -806,22 +815,31 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
   g.glu = glu;
   const int64_t ks = best_ks;
   g.ks = (int32_t)ks;
-  if (ks > 1) g.mat[0].out = part;
+  // split K: matrix i's partial sums [ks][n][rows_i] follow those of the
+  // matrices before it
+  float* mpart[3] = {part, part, part};
+  for (int i = 1; i < nmat; ++i) mpart[i] = mpart[i - 1] + ks * n * mat[i - 1].rows;
+  if (ks > 1)
+    for (int i = 0; i < nmat; ++i) g.mat[i].out = mpart[i];
   dim3 grid((unsigned)tiles, (unsigned)ttok, (unsigned)ks);
   e = best_tn == 144   ? launch_tile<144>(mh, ml, g, grid, s)
       : best_tn == 128 ? launch_tile<128>(mh, ml, g, grid, s)
                        : launch_tile<96>(mh, ml, g, grid, s);
   if (e == cudaSuccess) count_launches(1);
   if (e != cudaSuccess || ks == 1) return e;
-  const int64_t total = n * mat[0].rows;
-  const bool vec = (mat[0].rows & 3) == 0 && (mat[0].ldo & 3) == 0 &&
-                   (reinterpret_cast<uintptr_t>(mat[0].out) & 15) == 0;
-  const int64_t threads = vec ? (total + 3) / 4 : total;
-  splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
-      part, (int)ks, n, mat[0].rows, mat[0].out, mat[0].ldo, accumulate ? 1 : 0, vec ? 1 : 0);
-  e = cudaGetLastError();
-  if (e == cudaSuccess) count_launches(1);
-  return e;
+  for (int i = 0; i < nmat; ++i) {
+    const int64_t total = n * mat[i].rows;
+    const bool vec = (mat[i].rows & 3) == 0 && (mat[i].ldo & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(mat[i].out) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(mpart[i]) & 15) == 0;
+    const int64_t threads = vec ? (total + 3) / 4 : total;
+    splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+        mpart[i], (int)ks, n, mat[i].rows, mat[i].out, mat[i].ldo, accumulate ? 1 : 0, vec ? 1 : 0);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    count_launches(1);
+  }
+  return cudaSuccess;
 }
 
 }  // namespace

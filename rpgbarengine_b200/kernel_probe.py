@@ -9,6 +9,7 @@ mix) shapes, for timing and profiler captures of a single kernel.
   python -m rpgbarengine_b200.kernel_probe gemm-down 512 # Q6_K 2560 x 9728
   python -m rpgbarengine_b200.kernel_probe attn 767      # decode attention, 32 / 8 heads, pos 767
   python -m rpgbarengine_b200.kernel_probe step 4        # config-2 model: 512-token prefill, 4 decode steps
+  python -m rpgbarengine_b200.kernel_probe batch 64      # 64 sessions at position 1024, batched steps
 
 Weights are seeded random blocks of the benchmark's distributions; each
 launch reads its own weight copy, the copies together larger than L2.
@@ -56,6 +57,26 @@ def main(argv):
         sess = model.session(800)
         sess.forward_full(synth.prompt_ids(42, 512))
         print("tokens", sess.generate(arg or 4))
+        return
+    elif kind == "batch":  # batched decode: one 1024-token prefill copied into every session
+        shape = synth.QWEN3_4B_Q4KM
+        model = rb.Model.upload(shape, synth.build_tensors(shape, 1234), 0, 4096)
+        n = arg or 64
+        first = model.session(1100)
+        first.forward_full(synth.prompt_ids(42, 1024))
+        sess = [first]
+        for i in range(1, n):
+            s = model.session(1100)
+            s.copy_prefix_from(first, 1024)
+            s.forward_full([7 + i])
+            sess.append(s)
+        torch.cuda.synchronize()
+        # a profiler started with --profile-from-start off sees the batched steps only
+        torch.cuda.profiler.start()
+        rb.generate_batch(sess, reps)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("batch", n, "steps", reps)
         return
     elif kind == "attn":
         pos = arg or 767
