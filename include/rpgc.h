@@ -178,7 +178,9 @@ RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
  * weight stream is shared: the matmuls run on the tensor cores over the n
  * session rows, the attention reads each session's own cache.  out_ids holds
  * n x max_tokens ids (row i = session i, n_out[i] valid); afterwards each
- * session is as after rpgc_generate.  Not for tensor-parallel models. */
+ * session is as after rpgc_generate.  Not for tensor-parallel models.  Steps
+ * after the first replay a CUDA graph of one step captured on the first
+ * session's stream, which therefore must not be under stream capture. */
 RPGC_API int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts,
                                  int32_t* out_ids, int32_t* n_out);
 RPGC_API int rpgc_session_sync(int32_t session);
