@@ -183,6 +183,25 @@ RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
  * session's stream, which therefore must not be under stream capture. */
 RPGC_API int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts,
                                  int32_t* out_ids, int32_t* n_out);
+/* Batching behind rpgc_generate (no counterpart in the reference, whose
+ * engine generates for one session per call, src/engine.cc:349-515): with
+ * max_batch >= 2, rpgc_generate calls on sessions of this model made
+ * concurrently from different host threads are gathered, up to max_batch
+ * sessions, waiting at most window_us microseconds for more once the first
+ * arrives, and decoded as one batch (as rpgc_generate_batch, each call with
+ * its own options, stop ids and max_tokens).  Each call returns when its
+ * batch ends, with its own ids and status; a call that arrives while a
+ * batch runs joins the next one.  A call alone after the window decodes
+ * unbatched.  Calls that are not eligible (no pending logits, less room
+ * than max_tokens, invalid options) run unbatched and report their errors
+ * as before.  Batched tokens match an unbatched call's within the parity
+ * tolerance (the matmuls run on the tensor cores).  max_batch 0 or 1 turns
+ * batching off (the default); max_batch 2 .. 256, window_us 0 .. 1000000.
+ * Not for tensor-parallel models. */
+RPGC_API int rpgc_model_set_batching(int32_t model, int32_t max_batch, int32_t window_us);
+/* Batches of two or more sessions run so far for this model, and the
+ * rpgc_generate calls they served. */
+RPGC_API int rpgc_model_batching_stats(int32_t model, int64_t* batches, int64_t* requests);
 RPGC_API int rpgc_session_sync(int32_t session);
 
 /* ------------------------------------------------ kernel entry points */

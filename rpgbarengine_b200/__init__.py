@@ -96,6 +96,8 @@ def lib() -> C.CDLL:
         "rpgc_forward_device": ([i32, vp, i64], C.c_int),
         "rpgc_session_copy_prefix": ([i32, i32, i64], C.c_int),
         "rpgc_generate_batch": ([vp, i32, C.POINTER(GenOpts), vp, vp], C.c_int),
+        "rpgc_model_set_batching": ([i32, i32, i32], C.c_int),
+        "rpgc_model_batching_stats": ([i32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)], C.c_int),
         "rpgc_generate_device": ([i32, C.POINTER(GenOpts), vp, vp], C.c_int),
         "rpgc_session_sync": ([i32], C.c_int),
         "rpgc_dequantize_rows": ([u32, vp, i64, i64, vp, vp], C.c_int),
@@ -187,6 +189,18 @@ class Model:
     @property
     def weight_bytes(self) -> int:
         return int(_check(lib().rpgc_model_weight_bytes(self.handle)))
+
+    def set_batching(self, max_batch: int, window_us: int = 2000):
+        """rpgc_model_set_batching: gather concurrent generate calls on this
+        model's sessions (from different threads) into batched decodes of up
+        to max_batch sessions; 0 or 1 turns it off."""
+        _check(lib().rpgc_model_set_batching(self.handle, max_batch, window_us))
+
+    def batching_stats(self):
+        """(batches of two or more sessions run, generate calls they served)."""
+        b, r = C.c_int64(0), C.c_int64(0)
+        _check(lib().rpgc_model_batching_stats(self.handle, C.byref(b), C.byref(r)))
+        return b.value, r.value
 
     def session(self, max_seq: int) -> "Session":
         return Session(self, max_seq)

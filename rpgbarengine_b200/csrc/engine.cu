@@ -13,7 +13,10 @@
 #include <cstdio>
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <climits>
+#include <condition_variable>
+#include <deque>
 #include <cstdlib>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -99,6 +102,20 @@ const NcclApi* nccl_api() {
   return ok ? &api : nullptr;
 }
 
+struct BatchRequest;
+
+// Gathers concurrent rpgc_generate calls on sessions of one model into
+// batched decode steps (rpgc_model_set_batching).
+struct Batcher {
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<BatchRequest*> pending;
+  bool leading = false;  // a caller is gathering or running a batch
+  int32_t max_batch = 0;  // 0: off
+  int32_t window_us = 0;
+  int64_t batches = 0, requests = 0;  // batches of two or more sessions run, and their requests
+};
+
 struct Model {
   int device = 0;
   rpgc_model_config c{};   // this rank's shapes (heads, kv heads, intermediate of its shard)
@@ -113,6 +130,7 @@ struct Model {
   float* rope = nullptr;
   int64_t n_rope = 0;
   std::vector<int32_t> sessions;
+  Batcher batcher;
   ~Model() {
     int prev = 0;
     cudaGetDevice(&prev);
@@ -1134,6 +1152,298 @@ void batch_layers(const Model* m, int32_t n, float* x, float* q, float* k, float
   }
 }
 
+// The shapes batched decode needs: the tensor-core matmuls over the session
+// rows (hidden, q width and FFN width multiples of 64, a supported type).
+bool batch_shapes_ok(const Model* m) {
+  const rpgc_model_config& c = m->c;
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim;
+  const int64_t kmax = std::max(H, std::max(qd, F));
+  return m->tp_world == 1 && !m->layers.empty() && H % 64 == 0 && F % 64 == 0 && qd % 64 == 0 &&
+         gemm_uses_tc(m->layers[0].q.type, 2, H, gemm_scratch_bytes(2, kmax));
+}
+
+// Batched multi-session decode: one step decodes one token for each session
+// at once.  The sessions' rows share the weight stream: the matmuls run on
+// the tensor cores over the session rows (the prefill kernels), the attention
+// is the decode kernel with one grid slice per session (its own cache,
+// position and state), the sampler one block per session.  Session i decodes
+// with opts[i] (its own stop ids, sampling, seed and max_tokens: it goes
+// inactive after its own count while the batch runs the largest).  The caller
+// holds every session's lock and has checked pending logits and room for
+// opts[i].max_tokens; afterwards every session's stream is ordered after the
+// batch, and the caller finishes each session (finish_generate).
+void batch_decode(const std::vector<Session*>& ss, const std::vector<rpgc_gen_opts>& opts) {
+  const int32_t n = (int32_t)ss.size();
+  const Model* m = ss[0]->m;
+  const rpgc_model_config& c = m->c;
+  int32_t steps = 0;
+  for (const rpgc_gen_opts& o : opts) steps = std::max(steps, o.max_tokens);
+  const int64_t H = c.hidden, F = c.intermediate, V = c.vocab, qd = (int64_t)c.n_heads * c.head_dim,
+                kvd = (int64_t)c.n_kv_heads * c.head_dim;
+  const int64_t kmax = std::max(H, std::max(qd, F));
+  if (!batch_shapes_ok(m))
+    fail(RPGC_E_ARG, "batched decode needs the tensor-core matmul shapes (hidden, q width, FFN multiples of 64)");
+  DeviceGuard dg(m->device);
+  cudaStream_t bs = ss[0]->stream;  // the batch runs on the first session's stream
+  cudaEvent_t ev = nullptr;
+  CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  struct EvGuard {
+    cudaEvent_t e;
+    ~EvGuard() { cudaEventDestroy(e); }
+  } evg{ev};
+  BatchBufs B;
+  B.stream = bs;
+  float* x = B.alloc<float>((size_t)n * H);
+  float* h = B.alloc<float>((size_t)n * H);
+  float* q = B.alloc<float>((size_t)n * qd);
+  float* k = B.alloc<float>((size_t)n * kvd);
+  float* v = B.alloc<float>((size_t)n * kvd);
+  float* attn = B.alloc<float>((size_t)n * qd);
+  float* gate = B.alloc<float>((size_t)n * F);
+  float* up = B.alloc<float>((size_t)n * F);
+  float* logits = B.alloc<float>((size_t)n * V);
+  // room for split-K partial sums of up to 8 partitions of the widest
+  // matrix per token: a few dozen session rows fill the GPU only with K split
+  const size_t sbytes =
+      gemm_scratch_bytes(n, kmax) + (size_t)n * 8 * (size_t)std::max<int64_t>(F, std::max<int64_t>(H, qd)) * sizeof(float);
+  void* scratch = B.alloc<uint8_t>(sbytes);
+  DecodeState** states = B.alloc<DecodeState*>((size_t)n);
+  int32_t** outs = B.alloc<int32_t*>((size_t)n);
+  int32_t** nouts = B.alloc<int32_t*>((size_t)n);
+  float** dst = B.alloc<float*>((size_t)n);
+  AttnBatchEntry* entries = B.alloc<AttnBatchEntry>((size_t)n);
+  std::vector<DecodeState*> hs((size_t)n);
+  std::vector<int32_t*> ho((size_t)n), hn((size_t)n);
+  std::vector<float*> hd((size_t)n);
+  std::vector<AttnBatchEntry> he((size_t)n);
+  for (int32_t i = 0; i < n; ++i) {
+    Session* s = ss[i];
+    const rpgc_gen_opts& o = opts[(size_t)i];
+    DecodeState st;
+    std::memset(&st, 0, sizeof(st));
+    st.pos = (int32_t)s->len;
+    st.start_pos = (int32_t)s->len;
+    st.active = 1;
+    st.max_tokens = o.max_tokens;
+    st.n_stop = o.n_stop;
+    for (int j = 0; j < o.n_stop; ++j) st.stop_ids[j] = o.stop_ids[j];
+    st.temperature = o.temperature;
+    st.top_k = o.top_k;
+    st.top_p = o.top_p;
+    st.seed = o.seed;
+    check(state_set_launch(s->st, st, s->stream), "state");
+    CK(cudaEventRecord(ev, s->stream));  // the session's own work comes first
+    CK(cudaStreamWaitEvent(bs, ev, 0));
+    CK(cudaMemcpyAsync(logits + (size_t)i * V, s->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, bs));
+    hs[i] = s->st;
+    ho[i] = s->gen_out;
+    hn[i] = s->n_out;
+    hd[i] = s->logits;
+    he[i] = AttnBatchEntry{s->st, s->kc, s->vc, s->max_seq};
+  }
+  CK(cudaMemcpy(states, hs.data(), n * sizeof(DecodeState*), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(outs, ho.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(nouts, hn.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dst, hd.data(), n * sizeof(float*), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(entries, he.data(), n * sizeof(AttnBatchEntry), cudaMemcpyHostToDevice));
+  SampleArgs sa{};
+  sa.logits = logits;
+  sa.n = V;
+  sa.embd = m->embd.w;
+  sa.embd_row_bytes = m->embd.row_bytes;
+  sa.embd_type = m->embd.type;
+  sa.hidden = (int32_t)H;
+  sa.x = x;
+  sa.states = states;
+  sa.out_ids_b = outs;
+  sa.n_out_b = nouts;
+  sa.nbatch = n;
+  auto one_step = [&] {
+    check(sample_launch(sa, bs), "sample");
+    batch_layers(m, n, x, q, k, v, attn, gate, up, scratch, sbytes, entries, &ss[0]->st->error, bs);
+    check(rmsnorm_rows_launch(x, m->out_norm, n, c.hidden, c.rms_eps, h, bs), "rmsnorm");
+    check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, H, m->lm_head.row_bytes, h, n, logits, V,
+                      false, scratch, sbytes, bs),
+          "gemm lm_head");
+    check(commit_rows_launch(logits, V, dst, states, n, bs), "commit logits");
+  };
+  // The first step runs as plain launches (one-time kernel attributes are
+  // set there); the others replay a graph of one step, captured once: every
+  // argument of a step (positions, states, buffers) lives on the device, so
+  // one graph serves every step, and ~13 launches per layer cost one.
+  one_step();
+  if (steps > 1) {
+    cudaGraph_t g = nullptr;
+    int64_t nk = 0;
+    CK(cudaStreamBeginCapture(bs, cudaStreamCaptureModeThreadLocal));
+    t_capture_count = &nk;
+    try {
+      one_step();
+    } catch (...) {
+      t_capture_count = nullptr;
+      cudaStreamEndCapture(bs, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    t_capture_count = nullptr;
+    CK(cudaStreamEndCapture(bs, &g));
+    struct ExecGuard {  // destroyed after the stream has run every launch of it
+      cudaGraphExec_t e = nullptr;
+      cudaStream_t s = nullptr;
+      ~ExecGuard() {
+        if (e) {
+          cudaStreamSynchronize(s);
+          cudaGraphExecDestroy(e);
+        }
+      }
+    } ge;
+    ge.s = bs;
+    const cudaError_t e = cudaGraphInstantiate(&ge.e, g, 0);
+    cudaGraphDestroy(g);
+    CK(e);
+    for (int32_t step = 1; step < steps; ++step) {
+      CK(cudaGraphLaunch(ge.e, bs));
+      count_launches(nk);
+    }
+  }
+  CK(cudaEventRecord(ev, bs));
+  for (int32_t i = 0; i < n; ++i) CK(cudaStreamWaitEvent(ss[i]->stream, ev, 0));
+}
+
+// One rpgc_generate call waiting to join a batch (rpgc_model_set_batching).
+struct BatchRequest {
+  Session* s = nullptr;
+  rpgc_gen_opts o{};
+  int32_t* out = nullptr;
+  int32_t* n_out = nullptr;
+  bool done = false;  // set by the caller that ran its batch, under the batcher's lock
+  int code = RPGC_OK;
+  std::string msg;
+};
+
+// Runs a gathered batch; each request records its own outcome.  One request
+// alone decodes as an unbatched rpgc_generate (the persistent step kernel).
+void serve_batch(const std::vector<BatchRequest*>& batch) {
+  auto record_all = [&](int code, const char* msg) {
+    for (BatchRequest* r : batch) {
+      r->code = code;
+      r->msg = msg;
+    }
+  };
+  auto run = [](BatchRequest* r, auto&& f) {
+    try {
+      f();
+    } catch (const Error& e) {
+      r->code = e.code;
+      r->msg = e.what();
+    } catch (const std::exception& e) {
+      r->code = RPGC_E_CUDA;
+      r->msg = e.what();
+    } catch (...) {
+      r->code = RPGC_E_CUDA;
+      r->msg = "unknown exception";
+    }
+  };
+  if (batch.size() == 1) {
+    BatchRequest* r = batch[0];
+    run(r, [&] {
+      std::lock_guard<std::mutex> lk(r->s->mu);
+      const int64_t steps = generate(r->s, r->o, true);
+      finish_generate(r->s, r->o, steps, r->out, r->n_out);
+    });
+    return;
+  }
+  std::vector<Session*> ss;
+  std::vector<rpgc_gen_opts> opts;
+  for (BatchRequest* r : batch) {
+    ss.push_back(r->s);
+    opts.push_back(r->o);
+  }
+  std::vector<Session*> order(ss);  // lock in address order (no lock-order inversion)
+  std::sort(order.begin(), order.end());
+  std::vector<std::unique_lock<std::mutex>> locks;
+  for (Session* s : order) locks.emplace_back(s->mu);
+  try {
+    DeviceGuard dg(ss[0]->m->device);
+    for (size_t i = 0; i < ss.size(); ++i)
+      if (!ss[i]->has_logits || ss[i]->max_seq - ss[i]->len < opts[i].max_tokens)
+        fail(RPGC_E_STATE, "a session of the batch changed while it waited");
+    batch_decode(ss, opts);
+    for (size_t i = 0; i < ss.size(); ++i)
+      run(batch[i], [&] { finish_generate(ss[i], opts[i], opts[i].max_tokens, batch[i]->out, batch[i]->n_out); });
+    cudaStreamSynchronize(ss[0]->stream);
+  } catch (const Error& e) {
+    record_all(e.code, e.what());
+  } catch (const std::exception& e) {
+    record_all(RPGC_E_CUDA, e.what());
+  } catch (...) {
+    record_all(RPGC_E_CUDA, "unknown exception");
+  }
+}
+
+// Whether an rpgc_generate call joins its model's batches: batching on, the
+// model batchable, valid options, pending logits and room for max_tokens (a
+// call that fails any of these runs unbatched, which reports its errors).
+bool batch_eligible(Session* s, const rpgc_gen_opts& o) {
+  Model* m = s->m;
+  {
+    std::lock_guard<std::mutex> lk(m->batcher.mu);
+    if (m->batcher.max_batch < 2) return false;
+  }
+  if (!batch_shapes_ok(m)) return false;
+  if (o.max_tokens <= 0 || o.n_stop < 0 || o.n_stop > RPGC_MAX_STOP || (o.n_stop > 0 && !o.stop_ids)) return false;
+  std::lock_guard<std::mutex> lk(s->mu);
+  return s->has_logits && s->max_seq - s->len >= o.max_tokens;
+}
+
+// rpgc_generate with batching on: the call queues its request; the first
+// caller to find no batch running leads: it waits up to the window (or until
+// max_batch requests of distinct sessions are queued), takes them in arrival
+// order with its own first, runs them as one batch and wakes the others.
+// Requests left over lead the next batch.
+int batched_generate(Session* s, const rpgc_gen_opts& o, int32_t* out, int32_t* n_out) {
+  Batcher& b = s->m->batcher;
+  BatchRequest r;
+  r.s = s;
+  r.o = o;
+  r.out = out;
+  r.n_out = n_out;
+  std::unique_lock<std::mutex> lk(b.mu);
+  b.pending.push_back(&r);
+  b.cv.notify_all();
+  while (!r.done && b.leading) b.cv.wait(lk);
+  if (!r.done) {
+    b.leading = true;
+    const int32_t maxb = std::max<int32_t>(2, b.max_batch);
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(b.window_us);
+    b.cv.wait_until(lk, deadline, [&] { return (int32_t)b.pending.size() >= maxb; });
+    std::vector<BatchRequest*> batch{&r};
+    b.pending.erase(std::find(b.pending.begin(), b.pending.end(), &r));
+    for (auto it = b.pending.begin(); it != b.pending.end() && (int32_t)batch.size() < maxb;) {
+      bool dup = false;  // one call at a time per session: a second one waits for the next batch
+      for (BatchRequest* q : batch) dup |= q->s == (*it)->s;
+      if (dup) {
+        ++it;
+        continue;
+      }
+      batch.push_back(*it);
+      it = b.pending.erase(it);
+    }
+    if (batch.size() > 1) {
+      b.batches += 1;
+      b.requests += (int64_t)batch.size();
+    }
+    lk.unlock();
+    serve_batch(batch);
+    lk.lock();
+    for (BatchRequest* q : batch) q->done = true;
+    b.leading = false;
+    b.cv.notify_all();
+  }
+  if (r.code != RPGC_OK) throw Error(r.code, r.msg);
+  return RPGC_OK;
+}
+
 }  // namespace
 
 // Lets other translation units of the library report through rpgc_last_error().
@@ -1426,17 +1736,14 @@ int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids, 
     if (!opts || !out_ids || !n_out) fail(RPGC_E_ARG, "null argument");
     *n_out = 0;
     Session* s = require_session(session);
+    if (batch_eligible(s, *opts)) return batched_generate(s, *opts, out_ids, n_out);
     std::lock_guard<std::mutex> lk(s->mu);
     const int64_t steps = generate(s, *opts, true);
     return finish_generate(s, *opts, steps, out_ids, n_out);
   });
 }
 
-// Batched multi-session decode: one step decodes one token for each of the n
-// sessions at once.  The sessions' rows share the weight stream: the matmuls
-// run on the tensor cores over n rows (the prefill kernels), the attention is
-// the decode kernel with one grid slice per session (its own cache, position
-// and state), the sampler one block per session.
+// Batched multi-session decode with one set of options (batch_decode).
 int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts, int32_t* out_ids,
                         int32_t* n_out) {
   return guard([&] {
@@ -1455,7 +1762,6 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
       if (ss[i]->m != ss[0]->m) fail(RPGC_E_ARG, "the sessions of a batch must share one model");
     }
     const Model* m = ss[0]->m;
-    const rpgc_model_config& c = m->c;
     if (m->tp_world > 1) fail(RPGC_E_ARG, "tensor-parallel models decode one session at a time");
     std::vector<Session*> order(ss);  // lock in address order (no lock-order inversion)
     std::sort(order.begin(), order.end());
@@ -1467,138 +1773,44 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
         fail(RPGC_E_CONTEXT_FULL, "session %d has room for %lld more tokens, max_tokens is %d", sessions[i],
              (long long)(ss[i]->max_seq - ss[i]->len), o.max_tokens);
     }
-    const int64_t H = c.hidden, F = c.intermediate, V = c.vocab, qd = (int64_t)c.n_heads * c.head_dim,
-                  kvd = (int64_t)c.n_kv_heads * c.head_dim;
-    const int64_t kmax = std::max(H, std::max(qd, F));
-    if (!gemm_uses_tc(m->layers[0].q.type, n, H, gemm_scratch_bytes(n, kmax)) || H % 64 || F % 64 || qd % 64)
-      fail(RPGC_E_ARG, "batched decode needs the tensor-core matmul shapes (hidden, q width, FFN multiples of 64)");
     DeviceGuard dg(m->device);
-    cudaStream_t bs = ss[0]->stream;  // the batch runs on the first session's stream
-    cudaEvent_t ev = nullptr;
-    CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-    struct EvGuard {
-      cudaEvent_t e;
-      ~EvGuard() { cudaEventDestroy(e); }
-    } evg{ev};
-    BatchBufs B;
-    B.stream = bs;
-    float* x = B.alloc<float>((size_t)n * H);
-    float* h = B.alloc<float>((size_t)n * H);
-    float* q = B.alloc<float>((size_t)n * qd);
-    float* k = B.alloc<float>((size_t)n * kvd);
-    float* v = B.alloc<float>((size_t)n * kvd);
-    float* attn = B.alloc<float>((size_t)n * qd);
-    float* gate = B.alloc<float>((size_t)n * F);
-    float* up = B.alloc<float>((size_t)n * F);
-    float* logits = B.alloc<float>((size_t)n * V);
-    // room for split-K partial sums of up to 8 partitions of the widest
-    // matrix per token: a few dozen session rows fill the GPU only with K split
-    const size_t sbytes =
-        gemm_scratch_bytes(n, kmax) + (size_t)n * 8 * (size_t)std::max<int64_t>(F, std::max<int64_t>(H, qd)) * sizeof(float);
-    void* scratch = B.alloc<uint8_t>(sbytes);
-    DecodeState** states = B.alloc<DecodeState*>((size_t)n);
-    int32_t** outs = B.alloc<int32_t*>((size_t)n);
-    int32_t** nouts = B.alloc<int32_t*>((size_t)n);
-    float** dst = B.alloc<float*>((size_t)n);
-    AttnBatchEntry* entries = B.alloc<AttnBatchEntry>((size_t)n);
-    std::vector<DecodeState*> hs((size_t)n);
-    std::vector<int32_t*> ho((size_t)n), hn((size_t)n);
-    std::vector<float*> hd((size_t)n);
-    std::vector<AttnBatchEntry> he((size_t)n);
-    for (int32_t i = 0; i < n; ++i) {
-      Session* s = ss[i];
-      DecodeState st;
-      std::memset(&st, 0, sizeof(st));
-      st.pos = (int32_t)s->len;
-      st.start_pos = (int32_t)s->len;
-      st.active = 1;
-      st.max_tokens = o.max_tokens;
-      st.n_stop = o.n_stop;
-      for (int j = 0; j < o.n_stop; ++j) st.stop_ids[j] = o.stop_ids[j];
-      st.temperature = o.temperature;
-      st.top_k = o.top_k;
-      st.top_p = o.top_p;
-      st.seed = o.seed;
-      check(state_set_launch(s->st, st, s->stream), "state");
-      CK(cudaEventRecord(ev, s->stream));  // the session's own work comes first
-      CK(cudaStreamWaitEvent(bs, ev, 0));
-      CK(cudaMemcpyAsync(logits + (size_t)i * V, s->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, bs));
-      hs[i] = s->st;
-      ho[i] = s->gen_out;
-      hn[i] = s->n_out;
-      hd[i] = s->logits;
-      he[i] = AttnBatchEntry{s->st, s->kc, s->vc, s->max_seq};
-    }
-    CK(cudaMemcpy(states, hs.data(), n * sizeof(DecodeState*), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(outs, ho.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(nouts, hn.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(dst, hd.data(), n * sizeof(float*), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(entries, he.data(), n * sizeof(AttnBatchEntry), cudaMemcpyHostToDevice));
-    SampleArgs sa{};
-    sa.logits = logits;
-    sa.n = V;
-    sa.embd = m->embd.w;
-    sa.embd_row_bytes = m->embd.row_bytes;
-    sa.embd_type = m->embd.type;
-    sa.hidden = (int32_t)H;
-    sa.x = x;
-    sa.states = states;
-    sa.out_ids_b = outs;
-    sa.n_out_b = nouts;
-    sa.nbatch = n;
-    auto one_step = [&] {
-      check(sample_launch(sa, bs), "sample");
-      batch_layers(m, n, x, q, k, v, attn, gate, up, scratch, sbytes, entries, &ss[0]->st->error, bs);
-      check(rmsnorm_rows_launch(x, m->out_norm, n, c.hidden, c.rms_eps, h, bs), "rmsnorm");
-      check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, H, m->lm_head.row_bytes, h, n, logits, V,
-                        false, scratch, sbytes, bs),
-            "gemm lm_head");
-      check(commit_rows_launch(logits, V, dst, states, n, bs), "commit logits");
-    };
-    // The first step runs as plain launches (one-time kernel attributes are
-    // set there); the others replay a graph of one step, captured once: every
-    // argument of a step (positions, states, buffers) lives on the device, so
-    // one graph serves every step, and ~13 launches per layer cost one.
-    one_step();
-    if (o.max_tokens > 1) {
-      cudaGraph_t g = nullptr;
-      int64_t nk = 0;
-      CK(cudaStreamBeginCapture(bs, cudaStreamCaptureModeThreadLocal));
-      t_capture_count = &nk;
-      try {
-        one_step();
-      } catch (...) {
-        t_capture_count = nullptr;
-        cudaStreamEndCapture(bs, &g);
-        if (g) cudaGraphDestroy(g);
-        throw;
-      }
-      t_capture_count = nullptr;
-      CK(cudaStreamEndCapture(bs, &g));
-      struct ExecGuard {  // destroyed after the stream has run every launch of it
-        cudaGraphExec_t e = nullptr;
-        cudaStream_t s = nullptr;
-        ~ExecGuard() {
-          if (e) {
-            cudaStreamSynchronize(s);
-            cudaGraphExecDestroy(e);
-          }
-        }
-      } ge;
-      ge.s = bs;
-      const cudaError_t e = cudaGraphInstantiate(&ge.e, g, 0);
-      cudaGraphDestroy(g);
-      CK(e);
-      for (int32_t step = 1; step < o.max_tokens; ++step) {
-        CK(cudaGraphLaunch(ge.e, bs));
-        count_launches(nk);
-      }
-    }
-    CK(cudaEventRecord(ev, bs));
-    for (int32_t i = 0; i < n; ++i) CK(cudaStreamWaitEvent(ss[i]->stream, ev, 0));
+    batch_decode(ss, std::vector<rpgc_gen_opts>((size_t)n, o));
     for (int32_t i = 0; i < n; ++i)
       finish_generate(ss[i], o, o.max_tokens, out_ids + (size_t)i * o.max_tokens, n_out + i);
-    CK(cudaStreamSynchronize(bs));  // the buffers are freed after the batch's last kernel
+    CK(cudaStreamSynchronize(ss[0]->stream));
+    return RPGC_OK;
+  });
+}
+
+int rpgc_model_set_batching(int32_t model, int32_t max_batch, int32_t window_us) {
+  return guard([&] {
+    if (max_batch < 0 || max_batch > kMaxBatch) fail(RPGC_E_ARG, "max_batch %d outside 0 .. %d", max_batch, kMaxBatch);
+    if (window_us < 0 || window_us > 1000000) fail(RPGC_E_ARG, "window_us %d outside 0 .. 1000000", window_us);
+    Model* m = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      m = model_locked(model);
+    }
+    if (max_batch > 1 && !batch_shapes_ok(m))
+      fail(RPGC_E_ARG, "this model cannot batch sessions (tensor-parallel, or not the tensor-core matmul shapes)");
+    std::lock_guard<std::mutex> lk(m->batcher.mu);
+    m->batcher.max_batch = max_batch > 1 ? max_batch : 0;
+    m->batcher.window_us = window_us;
+    return RPGC_OK;
+  });
+}
+
+int rpgc_model_batching_stats(int32_t model, int64_t* batches, int64_t* requests) {
+  return guard([&] {
+    if (!batches || !requests) fail(RPGC_E_ARG, "null argument");
+    Model* m = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      m = model_locked(model);
+    }
+    std::lock_guard<std::mutex> lk(m->batcher.mu);
+    *batches = m->batcher.batches;
+    *requests = m->batcher.requests;
     return RPGC_OK;
   });
 }

@@ -301,3 +301,74 @@ def test_generate_batch_rejects_bad_batches(orc):
     fresh = gm.session(16)
     with pytest.raises(rb.RpgcError):
         rb.generate_batch([a, fresh], 2)  # fresh has no pending logits
+
+
+def test_generate_calls_from_threads_are_batched(orc):
+    # rpgc_generate from six threads on one model's sessions, each call with
+    # its own length, sampling options and stop ids, with batching on: the
+    # calls meet in batches (the model's counters say so) and each result
+    # matches the oracle for its session alone
+    import threading
+
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    prompts = [synth.prompt_ids(500 + i, 4 + 3 * i, shape.vocab) for i in range(6)]
+    opts = [dict(), dict(temperature=0.8, top_k=40, top_p=0.9, seed=11), dict(),
+            dict(temperature=0.7, top_k=0, top_p=0.8, seed=12), dict(), dict(temperature=1.0, seed=13)]
+    lengths = [3 + i for i in range(6)]
+    okv = om.kv(64)
+    ref2, _ = om.generate(okv, om.forward(prompts[2], okv)[-1], lengths[2], want_logits=True)
+    opts[2]["stop_ids"] = [int(ref2[1])]  # call 2 stops on its second token
+    sess = [gm.session(64) for _ in prompts]
+    for s, p in zip(sess, prompts):
+        s.forward_full(p)
+    got, errs = [None] * 6, []
+    start = threading.Barrier(6)
+
+    def run(i):
+        try:
+            start.wait()
+            got[i] = sess[i].generate(lengths[i], **opts[i])
+        except Exception as e:  # reported below
+            errs.append(e)
+
+    gm.set_batching(8, 200000)  # all six calls arrive well inside the window
+    try:
+        threads = [threading.Thread(target=run, args=(i,)) for i in range(6)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(120)
+    finally:
+        gm.set_batching(0)
+    assert not errs, errs
+    batches, requests = gm.batching_stats()
+    assert batches >= 1 and requests >= 4, (batches, requests)
+    for s, p, n, o, g in zip(sess, prompts, lengths, opts, got):
+        kv = om.kv(64)
+        ref, ref_logits = om.generate(kv, om.forward(p, kv)[-1], n, want_logits=True, **o)
+        compare_tokens(list(g), ref, ref_logits)
+        assert s.len == len(p) + len(g)
+    assert len(got[2]) <= 2
+    # off again: a call decodes alone and the counters stay
+    assert len(sess[0].generate(2)) == 2
+    assert gm.batching_stats() == (batches, requests)
+
+
+def test_batching_setting_is_checked(orc):
+    gm, _ = pair(orc, synth.TINY_MIX)
+    with pytest.raises(rb.RpgcError):
+        gm.set_batching(257, 0)
+    with pytest.raises(rb.RpgcError):
+        gm.set_batching(4, -1)
+    gm.set_batching(4, 100)
+    try:
+        # a call that is not eligible (no pending logits) runs unbatched and reports its error
+        s = gm.session(16)
+        with pytest.raises(rb.RpgcError):
+            s.generate(2)
+        # one eligible call alone: the window passes, it decodes unbatched
+        s.forward_full(synth.prompt_ids(53, 5, synth.TINY_MIX.vocab))
+        assert len(s.generate(3)) == 3
+    finally:
+        gm.set_batching(0)
