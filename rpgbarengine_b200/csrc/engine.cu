@@ -26,6 +26,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -246,6 +247,99 @@ struct Piece {
   size_t offset = 0, bytes = 0;
 };
 
+// One host-to-device copy of the upload: `rows` rows of `width` bytes,
+// `stride` apart in the source, packed at dst.
+struct CopyJob {
+  uint8_t* dst;
+  const uint8_t* src;
+  size_t width, stride, rows;
+};
+
+// Copies the pieces into the device blob through pinned staging memory: up to
+// 8 host threads, each with two pinned buffers and its own stream, take the
+// chunks round-robin; a thread fills one buffer from the source (page faults
+// of a mapped file and the copy run in parallel across threads) while the
+// other buffer's DMA runs.  Chunks are 1-8 MB (smaller models get smaller
+// chunks, so every upload runs this path).
+void upload_pieces(uint8_t* blob, const std::vector<Piece>& pieces, int device) {
+  size_t total = 0;
+  for (const Piece& pc : pieces) total += pc.bytes;
+  const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
+  const int T = std::max(1, std::min(8, hw));
+  size_t chunk = (total / (size_t)(4 * T) + 65535) & ~size_t(65535);
+  chunk = std::min<size_t>(std::max<size_t>(chunk, 1u << 20), 8u << 20);
+  std::vector<CopyJob> jobs;
+  for (const Piece& pc : pieces) {
+    const rpgc_tensor* t = pc.t;
+    if (!t->data) fail(RPGC_E_ARG, "tensor %s has no data", t->name);
+    const uint8_t* src = static_cast<const uint8_t*>(t->data);
+    uint8_t* dst = blob + pc.offset;
+    if (pc.kind == 2) {  // the same column range of every row
+      const size_t rb = (size_t)row_bytes_of(t->type, t->dims[0]), w = (size_t)row_bytes_of(t->type, pc.b - pc.a);
+      src += row_bytes_of(t->type, pc.a);
+      const size_t rows = (size_t)t->dims[1], per = std::max<size_t>(1, chunk / w);
+      for (size_t r = 0; r < rows; r += per)
+        jobs.push_back(CopyJob{dst + r * w, src + r * rb, w, rb, std::min(per, rows - r)});
+    } else {
+      if (pc.kind == 1) src += pc.a * row_bytes_of(t->type, t->dims[0]);
+      for (size_t o = 0; o < pc.bytes; o += chunk) {
+        const size_t n = std::min(chunk, pc.bytes - o);
+        jobs.push_back(CopyJob{dst + o, src + o, n, n, 1});
+      }
+    }
+  }
+  if (jobs.empty()) return;
+  size_t buf_bytes = 0;
+  for (const CopyJob& j : jobs) buf_bytes = std::max(buf_bytes, j.width * j.rows);
+  const int nth = (int)std::min<size_t>((size_t)T, jobs.size());
+  std::atomic<bool> failed{false};
+  std::mutex emu;
+  std::string err;
+  auto note = [&](cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(emu);
+    if (err.empty()) err = std::string(what) + ": " + cudaGetErrorString(e);
+    failed = true;
+    return true;
+  };
+  auto worker = [&](int i) {
+    if (note(cudaSetDevice(device), "cudaSetDevice")) return;
+    cudaStream_t st = nullptr;
+    uint8_t* buf[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    bool ok = !note(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int b = 0; ok && b < 2; ++b) {
+      ok = !note(cudaHostAlloc(reinterpret_cast<void**>(&buf[b]), buf_bytes, cudaHostAllocDefault), "cudaHostAlloc");
+      if (ok) ok = !note(cudaEventCreateWithFlags(&ev[b], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    int k = 0;
+    for (size_t j = (size_t)i; ok && !failed && j < jobs.size(); j += (size_t)nth, ++k) {
+      const int b = k & 1;
+      if (k >= 2 && note(cudaEventSynchronize(ev[b]), "upload copy")) break;  // the buffer's last copy is done
+      const CopyJob& J = jobs[j];
+      if (J.rows == 1 || J.stride == J.width) {
+        std::memcpy(buf[b], J.src, J.width * J.rows);
+      } else {
+        for (size_t r = 0; r < J.rows; ++r) std::memcpy(buf[b] + r * J.width, J.src + r * J.stride, J.width);
+      }
+      if (note(cudaMemcpyAsync(J.dst, buf[b], J.width * J.rows, cudaMemcpyHostToDevice, st), "cudaMemcpyAsync"))
+        break;
+      if (note(cudaEventRecord(ev[b], st), "cudaEventRecord")) break;
+    }
+    if (st) note(cudaStreamSynchronize(st), "upload copy");
+    for (int b = 0; b < 2; ++b) {
+      if (ev[b]) cudaEventDestroy(ev[b]);
+      if (buf[b]) cudaFreeHost(buf[b]);
+    }
+    if (st) cudaStreamDestroy(st);
+  };
+  std::vector<std::thread> th;
+  for (int i = 1; i < nth; ++i) th.emplace_back(worker, i);
+  worker(0);
+  for (std::thread& t : th) t.join();
+  if (failed) fail(RPGC_E_CUDA, "model upload: %s", err.c_str());
+}
+
 // Uploads the model, or with world > 1 rank `rank`'s tensor-parallel shard:
 // q/k/v/gate/up and the untied output split by rows (heads, intermediate
 // rows, vocabulary), o and down by columns (the same block range of every
@@ -413,22 +507,7 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
     if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclCommInitRank: %s", api->error_string(r));
   }
   CK(cudaMalloc(&model->blob, total));
-  for (const Piece& pc : pieces) {
-    const rpgc_tensor* t = pc.t;
-    if (!t->data) fail(RPGC_E_ARG, "tensor %s has no data", t->name);
-    const uint8_t* src = static_cast<const uint8_t*>(t->data);
-    if (pc.kind == 0) {
-      CK(cudaMemcpy(model->blob + pc.offset, src, pc.bytes, cudaMemcpyHostToDevice));
-    } else if (pc.kind == 1) {
-      const int64_t rb = row_bytes_of(t->type, t->dims[0]);
-      CK(cudaMemcpy(model->blob + pc.offset, src + pc.a * rb, pc.bytes, cudaMemcpyHostToDevice));
-    } else {
-      const int64_t rb = row_bytes_of(t->type, t->dims[0]), w = row_bytes_of(t->type, pc.b - pc.a);
-      const int64_t skip = row_bytes_of(t->type, pc.a);
-      CK(cudaMemcpy2D(model->blob + pc.offset, (size_t)w, src + skip, (size_t)rb, (size_t)w,
-                      (size_t)t->dims[1], cudaMemcpyHostToDevice));
-    }
-  }
+  upload_pieces(model->blob, pieces, device);
   model->weight_bytes = 0;
   for (const Piece& pc : pieces) model->weight_bytes += (int64_t)pc.bytes;
   auto mat = [&](const rpgc_tensor* t) {
@@ -1434,7 +1513,14 @@ int batched_generate(Session* s, const rpgc_gen_opts& o, int32_t* out, int32_t* 
       b.requests += (int64_t)batch.size();
     }
     lk.unlock();
-    serve_batch(batch);
+    try {  // every request gets an outcome, and leadership is always handed back
+      serve_batch(batch);
+    } catch (...) {
+      for (BatchRequest* q : batch) {
+        q->code = RPGC_E_CUDA;
+        q->msg = "batched decode failed before it started";
+      }
+    }
     lk.lock();
     for (BatchRequest* q : batch) q->done = true;
     b.leading = false;

@@ -372,3 +372,29 @@ def test_batching_setting_is_checked(orc):
         assert len(s.generate(3)) == 3
     finally:
         gm.set_batching(0)
+
+
+# Hidden 1024 and FFN 2048 give the matmuls 16-32 stages of K: the grouped
+# launches (q/k/v, gate+up) and the single ones split K at small token counts
+# (partial sums per matrix), which the 512-wide tiny shapes never do.
+MID = synth.Qwen3Shape("mid-mix", 1, 1024, 2048, 8, 2, vocab=1024, context_length=1024)
+
+
+def test_split_k_shapes_prefill_and_batch(orc):
+    gm, om = pair(orc, MID)
+    prompts = [synth.prompt_ids(700 + i, n, MID.vocab) for i, n in enumerate((40, 9, 130, 17, 66, 3))]
+    sess = []
+    for p in prompts:
+        s = gm.session(200)
+        got = s.forward_full(p, all_rows=True)
+        okv = om.kv(200)
+        want = om.forward(p, okv, all_rows=True)
+        for t in range(len(p)):
+            assert rel_l2(got[t], want[t]) <= LOGIT_REL_L2, (len(p), t)
+        sess.append(s)
+    got = rb.generate_batch(sess, 6)
+    for s, p, g in zip(sess, prompts, got):
+        okv = om.kv(200)
+        ref, ref_logits = om.generate(okv, om.forward(p, okv)[-1], 6, want_logits=True)
+        compare_tokens(list(g), ref, ref_logits)
+        assert s.len == len(p) + len(g)
