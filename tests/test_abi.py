@@ -71,3 +71,29 @@ def test_gguf_python_roundtrip():
         b = f.tensor(a.name)
         assert b.ggml_type == a.ggml_type and tuple(b.dims) == tuple(a.dims)
         assert np.array_equal(np.asarray(b.data), a.data)
+
+
+def test_batching_entry_points_check_arguments_without_gpu():
+    # argument and handle checks run before any device work
+    import ctypes as C
+    L = rb.lib()
+    assert L.rpgc_model_set_batching(12345, 257, 0) == rb.E_ARG  # above 256 sessions
+    assert b"max_batch" in L.rpgc_last_error()
+    assert L.rpgc_model_set_batching(12345, 4, -1) == rb.E_ARG
+    assert L.rpgc_model_set_batching(12345, 4, 1000001) == rb.E_ARG
+    assert L.rpgc_model_set_batching(12345, 4, 100) == rb.E_STATE  # no such model
+    assert b"model handle" in L.rpgc_last_error()
+    b, r = C.c_int64(-1), C.c_int64(-1)
+    assert L.rpgc_model_batching_stats(12345, C.byref(b), C.byref(r)) == rb.E_STATE
+    assert L.rpgc_model_batching_stats(12345, None, None) == rb.E_ARG
+    o = rb.GenOpts(4, None, 0, 0.0, 0, 1.0, 0)
+    out = np.zeros(8, np.int32)
+    n_out = np.zeros(2, np.int32)
+    sessions = np.array([12345, 12346], np.int32)
+    assert L.rpgc_generate_batch(None, 2, C.byref(o), out.ctypes.data, n_out.ctypes.data) == rb.E_ARG
+    assert L.rpgc_generate_batch(sessions.ctypes.data, 0, C.byref(o), out.ctypes.data,
+                                 n_out.ctypes.data) == rb.E_ARG  # empty batch
+    assert L.rpgc_generate_batch(sessions.ctypes.data, 257, C.byref(o), out.ctypes.data,
+                                 n_out.ctypes.data) == rb.E_ARG
+    assert L.rpgc_generate_batch(sessions.ctypes.data, 2, C.byref(o), out.ctypes.data,
+                                 n_out.ctypes.data) == rb.E_STATE  # unknown sessions
