@@ -155,7 +155,10 @@ RPGC_API int rpgc_forward(int32_t session, const int32_t* ids, int64_t n, float*
 /* Generate (src/qwen3.cc:302-355): device-resident decode loop starting from
  * the pending last-row logits; each picked token (the stop token included) is
  * forwarded, so len grows by *n_out.  u = CounterUniform(seed, len) per step
- * (src/sampler.cc:24-34).  out_ids needs max_tokens slots. */
+ * (src/sampler.cc:24-34).  out_ids needs max_tokens slots.  With batching on
+ * for the session's model (rpgc_model_set_batching), concurrent calls from
+ * other threads may decode together with this one; the call still returns
+ * only its own session's ids and status. */
 RPGC_API int rpgc_generate(int32_t session, const rpgc_gen_opts* opts, int32_t* out_ids,
                            int32_t* n_out);
 /* Same two calls with device-resident ids / results and no host transfer of
