@@ -1,4 +1,4 @@
-"""Benchmark: Qwen3-4B Q4_K_M-mix token loop on B200.
+"""Benchmark: Qwen3-4B Q4_K_M-mix token loop on B200 (the default workload, config2).
 
 One step = one session pass over the config-2 workload: a 512-token prefill of
 seeded uniform ids, then 256 greedy decode steps, then (prefix reuse back to
@@ -16,9 +16,9 @@ again by every decode step, so no L2 flush is needed between steps.
          KV bytes read) / time per token, over the measured copy bandwidth.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-  python bench.py --workload tp8b --steps 1 --warmup 1   # config 4, under torchrun
-  python bench.py --workload microbench --steps 5          # config 1 matmul kernels
-  python bench.py --workload sessions64                    # config 3, under torchrun for N > 1
+  python bench.py --workload tp8b --steps 1 --warmup 1   # 8B Q8_0 tensor parallel, under torchrun
+  python bench.py --workload microbench --steps 5          # matmul kernels per quant type
+  python bench.py --workload sessions64                    # 64 sessions, under torchrun for N > 1
 
 N > 1: one process per GPU (torchrun), each rank runs its own independent
 session (sessions shard with no communication), value = all ranks' tokens /
@@ -92,7 +92,7 @@ class Clocks:
 # capture of each shape (gpu__time_duration / dram__bytes_*.sum pass of the
 # same kernel on the same matrices): gate 14.08 MB, down 20.56 MB.
 # DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
-# dram__bytes_write.sum, config-2 model, 512-token prompt, context 516)
+# dram__bytes_write.sum, the 4B Q4_K_M-mix model, 512-token prompt, context 516)
 STEP_TRAFFIC = 2_832_019_712  # dram read + write of one step_kernel launch, ncu, context 514
 STEP_TRAFFIC_CTX = 514
 
@@ -126,6 +126,7 @@ def run_gpu(args):
     dev = local
 
     shape = synth.QWEN3_4B_Q4KM
+    prompt_n, decode_n = args.prompt, args.decode  # the benchmark's 512 and 256 unless profiling a small case
     t0 = time.time()
     tensors = synth.build_tensors(shape, SEED_WEIGHTS)
     # the per-tensor pageable copy (one synchronous host-to-device copy per
@@ -142,14 +143,14 @@ def run_gpu(args):
     upload_s = time.time() - t_up
     del tensors
     build_s = time.time() - t0
-    max_seq = PROMPT + DECODE + 8
+    max_seq = prompt_n + decode_n + 8
     sess = model.session(max_seq)
     stream = torch.cuda.ExternalStream(sess.stream_ptr, device=dev)
     # one session per rank: global session index = rank
     (session,) = rdist.shard_sessions(world, rank, world)
-    ids_host = synth.prompt_ids(rdist.session_seed(SEED_PROMPT, session), PROMPT)
+    ids_host = synth.prompt_ids(rdist.session_seed(SEED_PROMPT, session), prompt_n)
     ids_dev = torch.from_numpy(ids_host).to(f"cuda:{dev}")
-    out_dev = torch.zeros(DECODE + 8, dtype=torch.int32, device=f"cuda:{dev}")
+    out_dev = torch.zeros(decode_n + 8, dtype=torch.int32, device=f"cuda:{dev}")
     n_dev = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
     torch.cuda.synchronize(dev)  # the ids are on the device before the session's own stream reads them
 
@@ -159,15 +160,15 @@ def run_gpu(args):
     def device_step(marks):
         sess.set_len(0)
         marks[0].record(stream)
-        sess.forward_device(ids_dev.data_ptr(), PROMPT)
+        sess.forward_device(ids_dev.data_ptr(), prompt_n)
         marks[1].record(stream)
-        sess.generate_device(DECODE, out_dev.data_ptr(), n_dev.data_ptr())
-        sess.set_len(PROMPT)  # prefix reuse: back to the prompt
+        sess.generate_device(decode_n, out_dev.data_ptr(), n_dev.data_ptr())
+        sess.set_len(prompt_n)  # prefix reuse: back to the prompt
         # logits for the sampled run: forward the last prompt token again
-        sess.set_len(PROMPT - 1)
-        sess.forward_device(ids_dev.data_ptr() + 4 * (PROMPT - 1), 1)
+        sess.set_len(prompt_n - 1)
+        sess.forward_device(ids_dev.data_ptr() + 4 * (prompt_n - 1), 1)
         marks[2].record(stream)
-        sess.generate_device(DECODE, out_dev.data_ptr(), n_dev.data_ptr(), **SAMPLED)
+        sess.generate_device(decode_n, out_dev.data_ptr(), n_dev.data_ptr(), **SAMPLED)
         marks[3].record(stream)
 
     def barrier():
@@ -203,10 +204,10 @@ def run_gpu(args):
     for _ in range(e2e_steps):
         sess.set_len(0)
         sess.forward_full(ids_pinned.numpy())
-        sess.generate(DECODE)
-        sess.set_len(PROMPT - 1)
-        sess.forward_full(ids_pinned.numpy()[PROMPT - 1:])
-        sess.generate(DECODE, **SAMPLED)
+        sess.generate(decode_n)
+        sess.set_len(prompt_n - 1)
+        sess.forward_full(ids_pinned.numpy()[prompt_n - 1:])
+        sess.generate(decode_n, **SAMPLED)
     barrier()
     e2e_s = time.perf_counter() - e0
     hbm, _, src = peaks()
@@ -218,23 +219,23 @@ def run_gpu(args):
     if rank != 0:
         return
 
-    n_dec = 2 * DECODE * args.steps * world
+    n_dec = 2 * decode_n * args.steps * world
     value = n_dec / (dec_ms / 1e3)
-    prefill_tok_s = PROMPT * args.steps * world / (pre_ms / 1e3)
-    ctx_avg = PROMPT + DECODE / 2.0
+    prefill_tok_s = prompt_n * args.steps * world / (pre_ms / 1e3)
+    ctx_avg = prompt_n + decode_n / 2.0
     bytes_tok = decode_bytes_per_token(shape, ctx_avg)
-    per_tok_s = (dec_ms / 1e3) / (2 * DECODE * args.steps)
+    per_tok_s = (dec_ms / 1e3) / (2 * decode_n * args.steps)
     achieved = bytes_tok / per_tok_s / 1e9
     layer_macs = shape.n_layers * (shape.hidden * (shape.q_dim + 2 * shape.kv_dim) +
                                    shape.q_dim * shape.hidden + 3 * shape.hidden * shape.intermediate)
-    attn_flops = shape.n_layers * shape.n_heads * shape.head_dim * 4 * (PROMPT * (PROMPT + 1) / 2)
-    prefill_flops = 2 * layer_macs * PROMPT + 2 * shape.vocab * shape.hidden + attn_flops
-    if world == 1:  # the host cores' reference sample, timed at N=1 only
+    attn_flops = shape.n_layers * shape.n_heads * shape.head_dim * 4 * (prompt_n * (prompt_n + 1) / 2)
+    prefill_flops = 2 * layer_macs * prompt_n + 2 * shape.vocab * shape.hidden + attn_flops
+    if world == 1 and not args.skip_cpu:  # the host cores' reference sample, timed at N=1 only
         cpu = cpu_baseline(shape, args)
     else:
         cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-               "sample": "timed at N=1 only"}
-    e2e_tok = e2e_steps * 2 * DECODE * world / e2e_s
+               "sample": "timed at N=1 only" if world > 1 else "skipped (--skip-cpu)"}
+    e2e_tok = e2e_steps * 2 * decode_n * world / e2e_s
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -250,7 +251,7 @@ def run_gpu(args):
         "data": "synthetic",
         "config": {"workload": "config2: qwen3-4b q4_k_m-mix, 512-tok prefill + 256 greedy + 256 "
                                "sampled (T0.7 k20 p0.8) decode per session",
-                   "model": shape.name, "global_batch": world, "seq_len": PROMPT + DECODE,
+                   "model": shape.name, "global_batch": world, "seq_len": prompt_n + decode_n,
                    "parallelism": f"sessions x{world} (no communication)",
                    "weights": "raw Q4_K/Q6_K blocks in HBM", "kv": "fp32",
                    "decode_math": "dp4a on 24-bit fixed-point activation limbs, fp32 scales",
@@ -259,8 +260,8 @@ def run_gpu(args):
         "prefill_tok_s": round(prefill_tok_s, 1),
         "prefill_ms": round(pre_ms / args.steps, 3),
         "prefill_tflops": round(prefill_flops / (pre_ms / args.steps / 1e3) / 1e12, 2),
-        "greedy_tok_s": round(DECODE * args.steps * world / (greedy_ms / 1e3), 2),
-        "sampled_tok_s": round(DECODE * args.steps * world / (sampled_ms / 1e3), 2),
+        "greedy_tok_s": round(decode_n * args.steps * world / (greedy_ms / 1e3), 2),
+        "sampled_tok_s": round(decode_n * args.steps * world / (sampled_ms / 1e3), 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4),
                      "traffic": (int(STEP_TRAFFIC + (bytes_tok - decode_bytes_per_token(shape, STEP_TRAFFIC_CTX)))
@@ -275,8 +276,8 @@ def run_gpu(args):
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
                                        f"context {STEP_TRAFFIC_CTX}, KV bytes scaled to the mean context"},
         "e2e": {"value": round(e2e_tok, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": 4 * (PROMPT + 1),
-                "d2h_bytes_per_step": 4 * (2 * shape.vocab + 2 * DECODE)},
+                "h2d_bytes_per_step": 4 * (prompt_n + 1),
+                "d2h_bytes_per_step": 4 * (2 * shape.vocab + 2 * decode_n)},
         "gpu_launches": launches,
         "clocks": clk,
         "cpu_baseline": cpu,
@@ -284,7 +285,7 @@ def run_gpu(args):
         "upload": {"seconds": round(upload_s, 3), "gb": round(model.weight_bytes / 1e9, 3),
                    "gbs": round(model.weight_bytes / 1e9 / upload_s, 2),
                    "pageable_per_tensor_gbs": round(model.weight_bytes / 1e9 / pageable_s, 2),
-                   "what": "rpgc_model_upload of the config-2 weights from resident host arrays "
+                   "what": "rpgc_model_upload of the 4B Q4_K_M-mix weights from resident host arrays "
                            "(pinned staging, host threads) vs one pageable copy per tensor"},
     }
     print(json.dumps(line))
@@ -295,7 +296,7 @@ TP_METRIC = "Qwen3-8B Q8_0 tensor-parallel decode tok/s (% HBM roofline); 4096-t
 
 
 def run_tp8b(args):
-    """the 8B shape (Q8_0, untied output), a 4096-token
+    """The tp8b workload: the 8B shape (Q8_0, untied output), a 4096-token
     prefill of seeded uniform ids then 128 greedy decode steps, one session
     tensor-parallel over the torchrun ranks (rpgc_model_upload_tp; NCCL
     all-reduce after the row-split o and down projections, vocabulary slices
@@ -418,8 +419,8 @@ def run_tp8b(args):
         "gpu_launches": launches,
         "clocks": clk,
         "cpu_baseline": {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-                         "sample": "not run for config 4 (the reference's 4096-token CPU "
-                                   "prefill alone takes minutes); see the config-2 line"},
+                         "sample": "not run for the tp8b workload (the reference's 4096-token CPU "
+                                   "prefill alone takes minutes); see the config2 line"},
         "build_s": round(build_s, 1),
     }))
 
@@ -428,7 +429,7 @@ S3_SESSIONS, S3_PREFIX, S3_UNIQUE, S3_DECODE = 64, 256, 768, 128
 
 
 def run_sessions64(args):
-    """64 independent sessions of the 4B shape, each
+    """The sessions64 workload: 64 independent sessions of the 4B shape, each
     prefilled to 1024 tokens of which the first 256 are a shared prefix, then
     128 greedy decode tokens per session; the sessions are sharded over the
     torchrun ranks with no communication.  Each rank computes the shared
@@ -540,7 +541,7 @@ def run_sessions64(args):
     batched_ideal = hbm * 1e9 / (shape.weight_bytes(per_token=True) / S3_SESSIONS +
                                  decode_bytes_per_token(shape, ctx) - shape.weight_bytes(per_token=True))
     print(json.dumps({
-        "metric": "config-3 aggregate decode tok/s, 64 sessions with a shared 256-token prefix",
+        "metric": "sessions64 aggregate decode tok/s, 64 sessions with a shared 256-token prefix",
         "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": 1,
         "ms_per_step": round(pre_ms + dec_ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 dp4a + fp32 (decode), fp16 hi/lo tcgen05 + fp32 (prefill)",
@@ -563,11 +564,10 @@ def run_sessions64(args):
 
 
 MB_SHAPES = [(6144, 2048), (2048, 6144), (9728, 2560), (151936, 2560)]  # rows x cols
-MB_BATCH = 64
 
 
 def run_microbench(args):
-    """the fused-dequant matmuls per quant type (Q4_K, Q6_K,
+    """The microbench workload: the fused-dequant matmuls per quant type (Q4_K, Q6_K,
     Q8_0) at rows x cols 6144x2048, 2048x6144, 9728x2560 and 151936x2560, on
     f32 N(0,1) activations at batch 1 (rpgc_matvec, the decode GEMV: HBM
     roofline) and batch 64 (rpgc_matmul, the tensor-core GEMM: useful
@@ -588,14 +588,20 @@ def run_microbench(args):
     gen.manual_seed(SEED_WEIGHTS)
     rows_out = []
     stream = torch.cuda.Stream(device=dev)
-    for ty, tname in ((gguf.Q4_K, "Q4_K"), (gguf.Q6_K, "Q6_K"), (gguf.Q8_0, "Q8_0")):
-        for rows, cols in MB_SHAPES:
+    cases = [(ty, tname, rows, cols) for ty, tname in ((gguf.Q4_K, "Q4_K"), (gguf.Q6_K, "Q6_K"), (gguf.Q8_0, "Q8_0"))
+             for rows, cols in MB_SHAPES]
+    if args.mb_only:  # one case, for a profiler capture
+        tname, _, rc = args.mb_only.partition(":")
+        rows, cols = (int(v) for v in rc.split("x"))
+        cases = [(getattr(gguf, tname), tname, rows, cols)]
+    for ty, tname, rows, cols in cases:
+        if True:
             w0 = synth.random_blocks_torch(ty, rows, cols, gen, f"cuda:{dev}")
             copies = max(1, int(np.ceil(256e6 / w0.numel())))
             ws = [w0] + [w0.clone() for _ in range(copies - 1)]
             wbytes = rows * gguf.row_bytes(ty, cols)
             line = {"type": tname, "rows": rows, "cols": cols, "weight_mb": round(wbytes / 1e6, 2)}
-            for n in (1, MB_BATCH):
+            for n in (1, args.mb_batch):
                 X = torch.randn(n, cols, device=f"cuda:{dev}", generator=gen)
                 out = torch.empty(n, rows, device=f"cuda:{dev}")
                 reps = max(len(ws), 8)
@@ -624,7 +630,7 @@ def run_microbench(args):
                     line.update(gemv_us=round(us, 2), gemv_gbs=round(gbs, 1), gemv_frac=round(gbs / hbm, 4))
                 else:
                     tf = 2.0 * rows * cols * n / (us * 1e-6) / 1e12
-                    line.update(gemm64_us=round(us, 2), gemm64_tflops=round(tf, 2),
+                    line.update(gemm_rows=n, gemm64_us=round(us, 2), gemm64_tflops=round(tf, 2),
                                 gemm64_frac=round(tf / bf16, 4))
                 del g
             rows_out.append(line)
@@ -632,7 +638,7 @@ def run_microbench(args):
             torch.cuda.empty_cache()
     fr = [r["gemv_frac"] for r in rows_out]
     print(json.dumps({
-        "metric": "config-1 fused-dequant GEMV (batch 1, HBM roofline) / GEMM (batch 64) microbench",
+        "metric": "microbench: fused-dequant GEMV (batch 1, HBM roofline) / GEMM (batch 64) per quant type",
         "value": round(float(np.mean(fr)), 4), "unit": "mean GEMV fraction of measured HBM copy bandwidth",
         "n_gpus": 1, "steps": args.steps, "warmup": 1, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 dp4a + fp32 (GEMV), fp16 hi/lo tcgen05 + fp32 (GEMM)",
@@ -643,9 +649,16 @@ def run_microbench(args):
     }))
 
 
-def reference_sample(shape, threads, prompt_n, decode_n, reps, path=None):
-    """Time the reference's own code (oracle/_ref) on a bounded sample of the
-    workload: prompt_n-token prefill + decode_n greedy tokens, reps times."""
+REF_DECODE = 8  # greedy and sampled tokens per reference step, each run from position PROMPT
+
+
+def reference_decode(shape, threads, reps, warmup, path=None):
+    """Time the reference's own code (oracle/_ref) at the benchmark's context:
+    one PROMPT-token prefill (ForwardFull over the seeded prompt, timed once),
+    then per step, from position PROMPT (the cache set back to the prompt as
+    the GPU step does), REF_DECODE greedy tokens and REF_DECODE sampled tokens
+    at the benchmark's sampling options.  Returns decode tok/s over the timed
+    steps (greedy + sampled tokens / their time) and the prefill tok/s."""
     from oracle import Reference
     from rpgbarengine_b200 import synth
 
@@ -656,22 +669,26 @@ def reference_sample(shape, threads, prompt_n, decode_n, reps, path=None):
         synth.write_model(path, shape, SEED_WEIGHTS)
     ref = Reference()
     m = ref.load(path, threads, 4096)
-    ids = synth.prompt_ids(SEED_PROMPT, prompt_n)
-    pre_s = dec_s = 0.0
-    for _ in range(reps):
-        kv = m.kv(prompt_n + decode_n + 8)
+    ids = synth.prompt_ids(SEED_PROMPT, PROMPT)
+    kv = m.kv(PROMPT + 2 * REF_DECODE + 8)
+    t = time.perf_counter()
+    first = m.forward(ids, kv)[-1].copy()
+    pre_s = time.perf_counter() - t
+    dec_s = 0.0
+    for k in range(warmup + reps):
         t = time.perf_counter()
-        lg = m.forward(ids, kv)
-        t1 = time.perf_counter()
-        m.generate(kv, lg[-1], decode_n)
-        t2 = time.perf_counter()
-        pre_s += t1 - t
-        dec_s += t2 - t1
-    del m
+        kv.set_len(PROMPT)
+        m.generate(kv, first, REF_DECODE)
+        kv.set_len(PROMPT)
+        m.generate(kv, first, REF_DECODE, **SAMPLED)
+        if k >= warmup:
+            dec_s += time.perf_counter() - t
+    kern = ref.kernel
+    del kv, m
     if tmp:
         os.remove(path)
         os.rmdir(tmp)
-    return reps * decode_n / dec_s, reps * prompt_n / pre_s, ref.kernel
+    return reps * 2 * REF_DECODE / dec_s, PROMPT / pre_s, kern
 
 
 def cpu_baseline(shape, args):
@@ -681,10 +698,11 @@ def cpu_baseline(shape, args):
                 "sample": "oracle/_ref not built"}
     threads = os.cpu_count() or 1
     os.environ.setdefault("RPGBAR_ENGINE_LOG", "off")
-    dec, pre, kern = reference_sample(shape, threads, 32, 8, 1)
+    dec, pre, kern = reference_decode(shape, threads, 1, 0)
     return {"value": round(dec, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-            "sample": f"reference ({kern}) on config2 weights: 32-token prefill "
-                      f"({pre:.2f} tok/s) + 8 greedy decode tokens",
+            "sample": f"reference ({kern}) on the same weights: the {PROMPT}-token prefill "
+                      f"({pre:.2f} tok/s), then {REF_DECODE} greedy + {REF_DECODE} sampled decode "
+                      f"tokens from position {PROMPT}",
             "prefill_tok_s": round(pre, 3)}
 
 
@@ -700,22 +718,20 @@ def run_reference(args):
     os.environ.setdefault("RPGBAR_ENGINE_LOG", "off")
     shape = synth.QWEN3_4B_Q4KM
     threads = os.cpu_count() or 1
-    tmp = tempfile.mkdtemp(prefix="rpgref_")
-    path = os.path.join(tmp, "model.gguf")
-    synth.write_model(path, shape, SEED_WEIGHTS)
-    prompt_n, decode_n = 16, 4
-    reference_sample(shape, threads, prompt_n, decode_n, max(1, args.warmup // 3), path)
-    dec, pre, kern = reference_sample(shape, threads, prompt_n, decode_n, args.steps, path)
-    os.remove(path)
-    os.rmdir(tmp)
-    sample = (f"reference ({kern}) on config2 weights, {threads} threads: per step a "
-              f"{prompt_n}-token prefill ({pre:.2f} tok/s) + {decode_n} greedy decode tokens")
+    dec, pre, kern = reference_decode(shape, threads, args.steps, args.warmup)
+    sample = (f"reference ({kern}) on the same weights, {threads} threads: one {PROMPT}-token "
+              f"prefill ({pre:.2f} tok/s), then per step {REF_DECODE} greedy + {REF_DECODE} sampled "
+              f"(T0.7 k20 p0.8) decode tokens from position {PROMPT}")
     print(json.dumps({
         "metric": METRIC, "value": round(dec, 3), "unit": "tok/s", "impl": "reference",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 sample (CPU reference)", "model": shape.name},
+        "config": {"workload": "config2: qwen3-4b q4_k_m-mix, 512-tok prefill, then greedy and sampled "
+                               "(T0.7 k20 p0.8) decode from position 512 (CPU reference: "
+                               f"{REF_DECODE} + {REF_DECODE} tokens per step)",
+                   "model": shape.name, "seq_len": PROMPT + REF_DECODE,
+                   "seed_weights": SEED_WEIGHTS, "seed_prompt": SEED_PROMPT},
         "prefill_tok_s": round(pre, 3),
         "cpu_baseline": {"value": round(dec, 3), "unit": "tok/s", "cores": threads,
                          "kind": "reference", "sample": sample},
@@ -730,11 +746,19 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT,
+                    help="config2 prompt tokens (the benchmark's 512; smaller only for profiler captures)")
+    ap.add_argument("--decode", type=int, default=DECODE,
+                    help="config2 greedy and sampled tokens per step (the benchmark's 256)")
+    ap.add_argument("--skip-cpu", action="store_true",
+                    help="leave out the CPU reference sample (profiler captures)")
+    ap.add_argument("--mb-batch", type=int, default=64, help="microbench: token rows of the matmul leg")
+    ap.add_argument("--mb-only", default="",
+                    help="microbench: one case TYPE:ROWSxCOLS (e.g. Q4_K:9728x2560), for profiler captures")
     ap.add_argument("--workload", default="config2", choices=["config2", "tp8b", "microbench", "sessions64"],
-                    help="config2 (default): the 4B decode/prefill benchmark; tp8b: BASELINE "
-                         "config 4, the 8B shape tensor-parallel over the torchrun ranks; "
-                         "microbench: BASELINE config 1, the matmul kernels per quant type; "
-                         "sessions64: BASELINE config 3, 64 sessions with a shared prefix")
+                    help="config2 (default): the 4B decode/prefill benchmark; tp8b: the 8B Q8_0 "
+                         "shape tensor-parallel over the torchrun ranks; microbench: the matmul "
+                         "kernels per quant type; sessions64: 64 sessions with a shared prefix")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

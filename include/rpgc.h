@@ -181,9 +181,12 @@ RPGC_API int rpgc_generate_device(int32_t session, const rpgc_gen_opts* opts,
  * weight stream is shared: the matmuls run on the tensor cores over the n
  * session rows, the attention reads each session's own cache.  out_ids holds
  * n x max_tokens ids (row i = session i, n_out[i] valid); afterwards each
- * session is as after rpgc_generate.  Not for tensor-parallel models.  Steps
- * after the first replay a CUDA graph of one step captured on the first
- * session's stream, which therefore must not be under stream capture. */
+ * session is as after rpgc_generate.  Each session is finished with its own
+ * outcome; the call returns the first failure (a failed session's n_out is
+ * 0 and its length unchanged).  Not for tensor-parallel models.  Steps replay
+ * a CUDA graph of one step, captured on the first session's stream by the
+ * first batch of each size (the model keeps the graphs and the batch buffers
+ * between batches), so that stream must not be under stream capture. */
 RPGC_API int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts* opts,
                                  int32_t* out_ids, int32_t* n_out);
 /* Batching behind rpgc_generate (no counterpart in the reference, whose
@@ -205,7 +208,85 @@ RPGC_API int rpgc_model_set_batching(int32_t model, int32_t max_batch, int32_t w
 /* Batches of two or more sessions run so far for this model, and the
  * rpgc_generate calls they served. */
 RPGC_API int rpgc_model_batching_stats(int32_t model, int64_t* batches, int64_t* requests);
+/* Test hook, no counterpart in the reference: in the next batched decode (on
+ * any model), the session at position `index` of the batch has its
+ * attention thread blocks of layer 0 wait, at every step, on a barrier that
+ * nothing completes.  The bounded wait gives up and flags that session only:
+ * its call (or its entry of rpgc_generate_batch) fails with RPGC_E_TIMEOUT
+ * while the other sessions complete.  -1 clears a pending stall.  For tests of
+ * the failure path; nothing else sets it. */
+RPGC_API int rpgc_test_stall_next_batch(int32_t index);
 RPGC_API int rpgc_session_sync(int32_t session);
+
+/* ------------------------------------------- token-level engine sessions */
+/* The reference's public session calls (rpg_engine_session_create / _reset /
+ * _destroy / _generate, include/rpg_engine.h:52-117, src/engine.cc:259-515)
+ * with the text side left to the host: the host renders the chat template,
+ * tokenises, and passes each turn's whole prompt as token ids (with the BOS
+ * id when the model adds one); it receives the completion as token ids and
+ * decodes and parses it.  Between the two, the engine does what the
+ * reference does: longest-common-prefix reuse of the session's cache, the
+ * capacity check before the cache is touched, reset on a failed forward,
+ * the model's and the caller's stop ids, sampling with top_k 0 and top_p
+ * 0.95, and the finish reason by tokens.  Handles start at 1 and are never
+ * reused; destroying an unknown handle is a no-op; one generate at a time
+ * per session (the host serialises, include/rpg_engine.h:13-14). */
+typedef struct rpgc_engine_session_opts {
+  int32_t max_seq;        /* cache positions; 0: the model's RoPE positions (src/engine.cc:264-268) */
+  int32_t max_tokens;     /* default per request; 0: 256; narrowed to max_seq - 1 (:272-286) */
+  float temperature;      /* default; clamped to [0, 2], 0 = greedy (:295-303) */
+  uint64_t seed;          /* default seed (:304-305) */
+  const int32_t* stop_ids; /* the session's single-token stop strings, as ids (:288-293, 456) */
+  int32_t n_stop;
+} rpgc_engine_session_opts;
+
+typedef struct rpgc_engine_request {
+  int32_t max_tokens;      /* <= 0: the session's (src/engine.cc:399-400) */
+  int32_t set_temperature; /* nonzero: temperature below, else the session's (:404-410) */
+  float temperature;       /* clamped to [0, 2] */
+  int32_t set_seed;        /* nonzero: seed below, else the session's (:411) */
+  uint64_t seed;
+  const int32_t* stop_ids; /* the request's single-token stop strings, as ids (:455) */
+  int32_t n_stop;
+} rpgc_engine_request;
+
+#define RPGC_FINISH_STOP 0   /* a stop id ended it, or it ended short of max_tokens */
+#define RPGC_FINISH_LENGTH 1 /* max_tokens ids and the last is not a stop id */
+typedef struct rpgc_engine_result {
+  int32_t n_out;         /* generated ids (usage.completion_tokens) */
+  int32_t finish;        /* RPGC_FINISH_*, by tokens (src/engine.cc:477-487); "tool_calls" and a
+                            completion cut inside a tool call or think block are the host
+                            parser's call */
+  int64_t prompt_tokens; /* usage.prompt_tokens */
+  int64_t reused;        /* prompt positions served from the cache (the common prefix) */
+} rpgc_engine_result;
+
+/* rpg_engine_session_create (src/engine.cc:259-308) on a model of this
+ * library; opts NULL = every default.  Returns a handle >= 1. */
+RPGC_API int32_t rpgc_engine_session_create(int32_t model, const rpgc_engine_session_opts* opts);
+/* rpg_engine_session_destroy (src/engine.cc:310-323). */
+RPGC_API int rpgc_engine_session_destroy(int32_t session);
+/* rpg_engine_session_reset (src/engine.cc:336-346): length 0, memory kept. */
+RPGC_API int rpgc_engine_session_reset(int32_t session);
+/* The ids the session's cache holds (prompt and generated ids of its turns
+ * so far): copies up to cap of them into ids (may be NULL), returns how many
+ * there are (< 0: error). */
+RPGC_API int64_t rpgc_engine_session_cached(int32_t session, int32_t* ids, int64_t cap);
+/* rpg_engine_generate (src/engine.cc:349-515) on token ids: prompt ids[0, n)
+ * is the whole conversation so far, rendered and tokenised by the host; req
+ * NULL = the session's defaults.  out_ids needs room for max_tokens ids.  A
+ * prompt + max_tokens + 4 beyond the session's positions is
+ * RPGC_E_CONTEXT_FULL with the cache untouched; a forward that fails resets
+ * the session's cache. */
+RPGC_API int rpgc_engine_generate(int32_t session, const int32_t* ids, int64_t n,
+                                  const rpgc_engine_request* req, int32_t* out_ids, int32_t out_cap,
+                                  rpgc_engine_result* res);
+/* The model's end-of-sequence and <|im_end|> ids, the engine's model-level
+ * stop ids (src/model.cc:187, src/engine.cc:451-454): read from a GGUF's
+ * tokenizer.ggml.eos_token_id and vocabulary by rpgc_model_load_gguf, -1
+ * (none) for a model uploaded from a tensor table until set here. */
+RPGC_API int rpgc_model_set_special_ids(int32_t model, int32_t eos_id, int32_t im_end_id);
+RPGC_API int rpgc_model_special_ids(int32_t model, int32_t* eos_id, int32_t* im_end_id);
 
 /* ------------------------------------------------ kernel entry points */
 /* DequantizeRow (src/quant.h:65) over rows*cols elements, bit-exact. */
@@ -241,8 +322,10 @@ RPGC_API int rpgc_attention_decode(const float* q, const float* k_cache, const f
  * 32 MiB device array of the library on every GPU that loads it (held until
  * exit) instead of memory allocated per call.  n x cols beyond what fits
  * (about 4*n*cols + 36864*n bytes) is rejected with RPGC_E_ARG and a message.
- * The first call on a device looks the array's address up (with that device
- * current) and should come before any stream capture on that device.  All
+ * Every call looks the array's address up on the current device (an address
+ * kept from an earlier call could be stale after a device reset); the first
+ * call on a device may load the library's device code there, so it should
+ * come before any stream capture on that device.  All
  * calls on a device share the array: calls that overlap on the GPU race, so
  * order them on one stream or synchronise between them. */
 RPGC_API int rpgc_matmul_noalloc(uint32_t type, const void* w, int64_t rows, int64_t cols,

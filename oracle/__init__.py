@@ -277,6 +277,74 @@ class OracleKv:
         return k.copy(), v.copy()
 
 
+class OracleEngineSession:
+    """The reference's per-turn session logic (src/engine.cc:383-487) replayed
+    over the oracle's forward and generate, on token ids: the checker for the
+    library's token-level engine (rpgc_engine_generate).
+
+    Cached ids and the LCP (src/engine.cc:383-397), options from the request
+    else the session (:399-411), the capacity check before the cache is
+    touched (:412-419), the cache cut to the prefix and the rest forwarded,
+    reset on a failed forward (:421-448), stop ids eos / <|im_end|> / request /
+    session (:451-456), top_k 0 and top_p 0.95 (:463-467), the finish reason
+    by tokens (:477-487)."""
+
+    DEFAULT_MAX_TOKENS, SEQ_MARGIN, TOP_K, TOP_P, MAX_T = 256, 4, 0, 0.95, 2.0
+
+    def __init__(self, m: OracleModel, max_seq: int, max_tokens: int = 0, temperature: float = 0.0,
+                 seed: int = 0, stop_ids=(), eos_id: int = -1, im_end_id: int = -1):
+        self.m, self.max_seq = m, max_seq
+        self.kv = m.kv(max_seq)
+        self.cached = []
+        mt = max_tokens or self.DEFAULT_MAX_TOKENS
+        self.max_tokens = min(mt, max_seq - 1)
+        self.temperature = self._clamp(temperature)
+        self.seed = seed
+        self.stop = list(stop_ids)
+        self.eos_id, self.im_end_id = eos_id, im_end_id
+
+    @classmethod
+    def _clamp(cls, t):
+        return 0.0 if not t > 0 else min(t, cls.MAX_T)
+
+    def reset(self):
+        self.kv.set_len(0)
+        self.cached = []
+
+    def generate(self, ids, max_tokens=0, temperature=None, seed=None, stop_ids=()):
+        ids = [int(i) for i in ids]
+        n = len(ids)
+        if n == 0:
+            raise ValueError("the prompt is empty")
+        assert len(self.cached) == self.kv.len
+        lcp = 0
+        while lcp < len(self.cached) and lcp < n and self.cached[lcp] == ids[lcp]:
+            lcp += 1
+        if lcp == n:
+            lcp = n - 1
+        mt = max_tokens if max_tokens > 0 else self.max_tokens
+        t = self._clamp(self.temperature if temperature is None else temperature)
+        sd = self.seed if seed is None else seed
+        stop = []
+        for i in [self.eos_id, self.im_end_id] + list(stop_ids) + self.stop:
+            if i >= 0 and i not in stop:
+                stop.append(int(i))
+        if n + mt + self.SEQ_MARGIN > self.max_seq:
+            raise OverflowError("sequence too long")
+        if any(i < 0 or i >= self.m.shape.vocab for i in ids):
+            self.reset()  # the forward fails: the cache is not reused
+            raise ValueError("prompt id outside the vocabulary")
+        self.kv.set_len(lcp)
+        first = self.m.forward(np.asarray(ids[lcp:], np.int32), self.kv)[0]
+        self.cached = list(ids)
+        gen = [int(x) for x in self.m.generate(self.kv, first, mt, stop_ids=stop, temperature=t,
+                                               top_k=self.TOP_K, top_p=self.TOP_P, seed=sd)]
+        self.cached += gen
+        stopped = bool(gen) and gen[-1] in stop
+        finish = "length" if len(gen) >= mt and not stopped else "stop"
+        return gen, finish, n, lcp
+
+
 class Reference:
     """The reference's own code (oracle/_ref/librpgref.so), when built.
 

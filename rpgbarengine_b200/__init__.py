@@ -60,6 +60,24 @@ class GenOpts(C.Structure):
                 ("top_p", C.c_float), ("seed", C.c_uint64)]
 
 
+class EngineSessionOpts(C.Structure):
+    _fields_ = [("max_seq", C.c_int32), ("max_tokens", C.c_int32), ("temperature", C.c_float),
+                ("seed", C.c_uint64), ("stop_ids", C.POINTER(C.c_int32)), ("n_stop", C.c_int32)]
+
+
+class EngineRequest(C.Structure):
+    _fields_ = [("max_tokens", C.c_int32), ("set_temperature", C.c_int32), ("temperature", C.c_float),
+                ("set_seed", C.c_int32), ("seed", C.c_uint64), ("stop_ids", C.POINTER(C.c_int32)),
+                ("n_stop", C.c_int32)]
+
+
+class EngineResult(C.Structure):
+    _fields_ = [("n_out", C.c_int32), ("finish", C.c_int32), ("prompt_tokens", C.c_int64),
+                ("reused", C.c_int64)]
+
+
+FINISH = {0: "stop", 1: "length"}
+
 _lib = None
 
 
@@ -100,6 +118,15 @@ def lib() -> C.CDLL:
         "rpgc_model_batching_stats": ([i32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)], C.c_int),
         "rpgc_generate_device": ([i32, C.POINTER(GenOpts), vp, vp], C.c_int),
         "rpgc_session_sync": ([i32], C.c_int),
+        "rpgc_test_stall_next_batch": ([i32], C.c_int),
+        "rpgc_engine_session_create": ([i32, C.POINTER(EngineSessionOpts)], i32),
+        "rpgc_engine_session_destroy": ([i32], C.c_int),
+        "rpgc_engine_session_reset": ([i32], C.c_int),
+        "rpgc_engine_session_cached": ([i32, vp, i64], i64),
+        "rpgc_engine_generate": ([i32, vp, i64, C.POINTER(EngineRequest), vp, i32,
+                                  C.POINTER(EngineResult)], C.c_int),
+        "rpgc_model_set_special_ids": ([i32, i32, i32], C.c_int),
+        "rpgc_model_special_ids": ([i32, C.POINTER(i32), C.POINTER(i32)], C.c_int),
         "rpgc_dequantize_rows": ([u32, vp, i64, i64, vp, vp], C.c_int),
         "rpgc_matvec": ([u32, vp, i64, i64, vp, vp, vp], C.c_int),
         "rpgc_matmul": ([u32, vp, i64, i64, vp, i64, vp, vp], C.c_int),
@@ -204,6 +231,19 @@ class Model:
 
     def session(self, max_seq: int) -> "Session":
         return Session(self, max_seq)
+
+    def set_special_ids(self, eos_id: int, im_end_id: int):
+        """The model-level stop ids of the token-level engine (-1: none)."""
+        _check(lib().rpgc_model_set_special_ids(self.handle, eos_id, im_end_id))
+
+    @property
+    def special_ids(self):
+        e, i = C.c_int32(-1), C.c_int32(-1)
+        _check(lib().rpgc_model_special_ids(self.handle, C.byref(e), C.byref(i)))
+        return e.value, i.value
+
+    def engine_session(self, **kw) -> "EngineSession":
+        return EngineSession(self, **kw)
 
     def free(self):
         if self.handle:
@@ -385,3 +425,55 @@ def attention_decode(q, k_cache, v_cache, pos: int, n_heads: int, n_kv_heads: in
 
 
 row_bytes = _gguf.row_bytes
+
+
+def _ids_array(ids):
+    a = (C.c_int32 * max(1, len(ids)))(*[int(i) for i in ids])
+    return a, len(ids)
+
+
+class EngineSession:
+    """Token-level engine session (rpgc_engine_*): the reference's
+    rpg_engine_session_* / rpg_engine_generate (src/engine.cc:259-515) with
+    prompts and completions as token ids; the host keeps the text side."""
+
+    def __init__(self, model: Model, max_seq: int = 0, max_tokens: int = 0, temperature: float = 0.0,
+                 seed: int = 0, stop_ids=()):
+        self.model = model
+        self._stop = _ids_array(stop_ids)
+        o = EngineSessionOpts(max_seq, max_tokens, temperature, seed, self._stop[0], self._stop[1])
+        self.handle = _check(lib().rpgc_engine_session_create(model.handle, C.byref(o)))
+
+    def generate(self, ids, max_tokens: int = 0, temperature=None, seed=None, stop_ids=(), out_cap=None):
+        """One turn: ids = the whole prompt so far.  Returns (completion ids,
+        finish "stop"/"length", prompt_tokens, reused prefix length)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+        stop = _ids_array(stop_ids)
+        req = EngineRequest(max_tokens, temperature is not None, temperature or 0.0, seed is not None,
+                            seed or 0, stop[0], stop[1])
+        cap = out_cap if out_cap is not None else max(max_tokens, 1 << 16)
+        out = np.zeros(max(1, cap), np.int32)
+        res = EngineResult()
+        _check(lib().rpgc_engine_generate(self.handle, ids.ctypes.data, ids.size, C.byref(req),
+                                          out.ctypes.data, cap, C.byref(res)))
+        return out[: res.n_out].copy(), FINISH[res.finish], int(res.prompt_tokens), int(res.reused)
+
+    def reset(self):
+        _check(lib().rpgc_engine_session_reset(self.handle))
+
+    def cached(self) -> np.ndarray:
+        n = _check(lib().rpgc_engine_session_cached(self.handle, None, 0))
+        out = np.zeros(max(1, n), np.int32)
+        _check(lib().rpgc_engine_session_cached(self.handle, out.ctypes.data, n))
+        return out[:n]
+
+    def close(self):
+        if self.handle:
+            lib().rpgc_engine_session_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

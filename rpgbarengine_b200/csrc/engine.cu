@@ -22,6 +22,7 @@
 #include <nccl.h>
 #include <cstring>
 #include <initializer_list>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
@@ -117,6 +118,43 @@ struct Batcher {
   int64_t batches = 0, requests = 0;  // batches of two or more sessions run, and their requests
 };
 
+// Device buffers and captured step graphs of batched decode, kept on the
+// model between batches and grown when a larger batch arrives: after the
+// first batch of a size, a batch neither allocates nor frees device memory
+// (cudaFree synchronises the whole device, which would stall every other
+// session's stream).  One batch at a time per model uses them (mu is held
+// across batch_decode).
+struct BatchCache {
+  std::mutex mu;
+  int32_t cap = 0;  // sessions the buffers hold
+  std::vector<void*> ptrs;
+  float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+  float *gate = nullptr, *up = nullptr, *logits = nullptr;
+  void* scratch = nullptr;
+  DecodeState** states = nullptr;
+  int32_t** outs = nullptr;
+  int32_t** nouts = nullptr;
+  float** dst = nullptr;
+  AttnBatchEntry* entries = nullptr;
+  int32_t* n_active = nullptr;       // device: sessions still active (early end)
+  int32_t* n_active_host = nullptr;  // pinned copy
+  struct StepGraph {
+    cudaGraphExec_t exec = nullptr;
+    int64_t kernels = 0;
+  };
+  std::map<int32_t, StepGraph> graphs;  // batch size -> one captured step over these buffers
+  // Frees everything (the device is current; no batch is running).
+  void release() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+    for (void* p : ptrs) cudaFree(p);
+    ptrs.clear();
+    if (n_active_host) cudaFreeHost(n_active_host);
+    n_active_host = nullptr;
+    cap = 0;
+  }
+};
+
 struct Model {
   int device = 0;
   rpgc_model_config c{};   // this rank's shapes (heads, kv heads, intermediate of its shard)
@@ -131,11 +169,16 @@ struct Model {
   float* rope = nullptr;
   int64_t n_rope = 0;
   std::vector<int32_t> sessions;
+  // end-of-sequence and <|im_end|> token ids (-1: none), the model-level stop
+  // ids of the token-level engine (src/model.cc:187, src/engine.cc:451-454)
+  int32_t eos_id = -1, im_end_id = -1;
   Batcher batcher;
+  BatchCache bcache;
   ~Model() {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
+    bcache.release();
     if (blob) cudaFree(blob);
     if (rope) cudaFree(rope);
     if (comm && nccl_api()) nccl_api()->destroy(comm);
@@ -1136,8 +1179,13 @@ int finish_generate(Session* s, const rpgc_gen_opts& o, int64_t steps, int32_t* 
   CK(cudaMemcpyAsync(s->st_host, s->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   const DecodeState h = *s->st_host;
-  if (h.error & kErrBadToken) fail(RPGC_E_ARG, "a device-resident token id was outside the vocabulary");
-  if (h.error) fail(RPGC_E_TIMEOUT, "a device wait gave up during generation (flags %d)", h.error);
+  if (h.error) {
+    // the pending logits and the cache rows past len no longer match len:
+    // the session needs a forward before its next generate
+    s->has_logits = false;
+    if (h.error & kErrBadToken) fail(RPGC_E_ARG, "a device-resident token id was outside the vocabulary");
+    fail(RPGC_E_TIMEOUT, "a device wait gave up during generation (flags %d)", h.error);
+  }
   if (h.n_gen < 0 || h.n_gen > steps) fail(RPGC_E_CUDA, "inconsistent decode state");
   if (h.n_gen > 0) CK(cudaMemcpy(out, s->gen_out, h.n_gen * sizeof(int32_t), cudaMemcpyDeviceToHost));
   *n_out = h.n_gen;
@@ -1170,25 +1218,56 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 constexpr int32_t kMaxBatch = 256;
 
-struct BatchBufs {
-  std::vector<void*> ptrs;
-  cudaStream_t stream = nullptr;  // the batch's work is finished before the buffers go
-  template <typename T>
-  T* alloc(size_t count) {
+// Room for split-K partial sums of up to 8 partitions of the widest matrix
+// per token: a few dozen session rows fill the GPU only with K split.
+size_t batch_scratch_bytes(const rpgc_model_config& c, int32_t n) {
+  const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim;
+  const int64_t kmax = std::max(H, std::max(qd, F));
+  return gemm_scratch_bytes(n, kmax) + (size_t)n * 8 * (size_t)kmax * sizeof(float);
+}
+
+// The model's batch buffers, grown to hold n sessions (the caller holds
+// bc.mu; the model's device is current; no batch is running).
+void batch_buffers(Model* m, int32_t n) {
+  BatchCache& bc = m->bcache;
+  if (bc.cap >= n) return;
+  bc.release();
+  const int32_t cap = std::min<int32_t>(kMaxBatch, std::max<int32_t>(n, 8 * ((n + 7) / 8)));
+  const rpgc_model_config& c = m->c;
+  const size_t H = c.hidden, F = c.intermediate, V = c.vocab, qd = (size_t)c.n_heads * c.head_dim,
+               kvd = (size_t)c.n_kv_heads * c.head_dim, N = (size_t)cap;
+  auto alloc = [&](size_t bytes) {
     void* p = nullptr;
-    CK(cudaMalloc(&p, count * sizeof(T)));
-    ptrs.push_back(p);
-    return static_cast<T*>(p);
-  }
-  ~BatchBufs() {
-    if (stream) cudaStreamSynchronize(stream);
-    for (void* p : ptrs) cudaFree(p);
-  }
-};
+    CK(cudaMalloc(&p, bytes));
+    bc.ptrs.push_back(p);
+    return p;
+  };
+  bc.x = static_cast<float*>(alloc(N * H * 4));
+  bc.h = static_cast<float*>(alloc(N * H * 4));
+  bc.q = static_cast<float*>(alloc(N * qd * 4));
+  bc.k = static_cast<float*>(alloc(N * kvd * 4));
+  bc.v = static_cast<float*>(alloc(N * kvd * 4));
+  bc.attn = static_cast<float*>(alloc(N * qd * 4));
+  bc.gate = static_cast<float*>(alloc(N * F * 4));
+  bc.up = static_cast<float*>(alloc(N * F * 4));
+  bc.logits = static_cast<float*>(alloc(N * V * 4));
+  bc.scratch = alloc(batch_scratch_bytes(c, cap));
+  bc.states = static_cast<DecodeState**>(alloc(N * sizeof(DecodeState*)));
+  bc.outs = static_cast<int32_t**>(alloc(N * sizeof(int32_t*)));
+  bc.nouts = static_cast<int32_t**>(alloc(N * sizeof(int32_t*)));
+  bc.dst = static_cast<float**>(alloc(N * sizeof(float*)));
+  bc.entries = static_cast<AttnBatchEntry*>(alloc(N * sizeof(AttnBatchEntry)));
+  bc.n_active = static_cast<int32_t*>(alloc(sizeof(int32_t)));
+  CK(cudaMallocHost(&bc.n_active_host, sizeof(int32_t)));
+  bc.cap = cap;
+}
+
+// Test hook (rpgc_test_stall_next_batch): index of the session whose
+// attention waits time out in the next batched decode, -1 for none.
+std::atomic<int32_t> g_test_stall{-1};
 
 void batch_layers(const Model* m, int32_t n, float* x, float* q, float* k, float* v, float* attn, float* gate,
-                  float* up, void* scratch, size_t sbytes, const AttnBatchEntry* entries, int32_t* err,
-                  cudaStream_t cs) {
+                  float* up, void* scratch, size_t sbytes, const AttnBatchEntry* entries, cudaStream_t cs) {
   const rpgc_model_config& c = m->c;
   const int64_t H = c.hidden, F = c.intermediate, qd = (int64_t)c.n_heads * c.head_dim,
                 kvd = (int64_t)c.n_kv_heads * c.head_dim;
@@ -1211,7 +1290,7 @@ void batch_layers(const Model* m, int32_t n, float* x, float* q, float* k, float
     aa.k_norm = L.k_norm;
     aa.rope = m->rope;
     aa.eps = c.rms_eps;
-    aa.err = err;
+    aa.err = nullptr;  // each entry carries its session's error flags
     aa.batch = entries;
     aa.nbatch = n;
     aa.layer = l;
@@ -1253,16 +1332,20 @@ bool batch_shapes_ok(const Model* m) {
 // batch, and the caller finishes each session (finish_generate).
 void batch_decode(const std::vector<Session*>& ss, const std::vector<rpgc_gen_opts>& opts) {
   const int32_t n = (int32_t)ss.size();
-  const Model* m = ss[0]->m;
+  Model* m = ss[0]->m;
   const rpgc_model_config& c = m->c;
   int32_t steps = 0;
+  bool early = false;  // a session may go inactive before the last step
   for (const rpgc_gen_opts& o : opts) steps = std::max(steps, o.max_tokens);
-  const int64_t H = c.hidden, F = c.intermediate, V = c.vocab, qd = (int64_t)c.n_heads * c.head_dim,
-                kvd = (int64_t)c.n_kv_heads * c.head_dim;
-  const int64_t kmax = std::max(H, std::max(qd, F));
+  for (const rpgc_gen_opts& o : opts) early |= o.n_stop > 0 || o.max_tokens < steps;
+  const int64_t H = c.hidden, V = c.vocab;
   if (!batch_shapes_ok(m))
     fail(RPGC_E_ARG, "batched decode needs the tensor-core matmul shapes (hidden, q width, FFN multiples of 64)");
   DeviceGuard dg(m->device);
+  BatchCache& bc = m->bcache;
+  std::lock_guard<std::mutex> blk(bc.mu);
+  batch_buffers(m, n);
+  const size_t sbytes = batch_scratch_bytes(c, n);
   cudaStream_t bs = ss[0]->stream;  // the batch runs on the first session's stream
   cudaEvent_t ev = nullptr;
   CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
@@ -1270,27 +1353,7 @@ void batch_decode(const std::vector<Session*>& ss, const std::vector<rpgc_gen_op
     cudaEvent_t e;
     ~EvGuard() { cudaEventDestroy(e); }
   } evg{ev};
-  BatchBufs B;
-  B.stream = bs;
-  float* x = B.alloc<float>((size_t)n * H);
-  float* h = B.alloc<float>((size_t)n * H);
-  float* q = B.alloc<float>((size_t)n * qd);
-  float* k = B.alloc<float>((size_t)n * kvd);
-  float* v = B.alloc<float>((size_t)n * kvd);
-  float* attn = B.alloc<float>((size_t)n * qd);
-  float* gate = B.alloc<float>((size_t)n * F);
-  float* up = B.alloc<float>((size_t)n * F);
-  float* logits = B.alloc<float>((size_t)n * V);
-  // room for split-K partial sums of up to 8 partitions of the widest
-  // matrix per token: a few dozen session rows fill the GPU only with K split
-  const size_t sbytes =
-      gemm_scratch_bytes(n, kmax) + (size_t)n * 8 * (size_t)std::max<int64_t>(F, std::max<int64_t>(H, qd)) * sizeof(float);
-  void* scratch = B.alloc<uint8_t>(sbytes);
-  DecodeState** states = B.alloc<DecodeState*>((size_t)n);
-  int32_t** outs = B.alloc<int32_t*>((size_t)n);
-  int32_t** nouts = B.alloc<int32_t*>((size_t)n);
-  float** dst = B.alloc<float*>((size_t)n);
-  AttnBatchEntry* entries = B.alloc<AttnBatchEntry>((size_t)n);
+  const int32_t stall = g_test_stall.exchange(-1);
   std::vector<DecodeState*> hs((size_t)n);
   std::vector<int32_t*> ho((size_t)n), hn((size_t)n);
   std::vector<float*> hd((size_t)n);
@@ -1313,80 +1376,94 @@ void batch_decode(const std::vector<Session*>& ss, const std::vector<rpgc_gen_op
     check(state_set_launch(s->st, st, s->stream), "state");
     CK(cudaEventRecord(ev, s->stream));  // the session's own work comes first
     CK(cudaStreamWaitEvent(bs, ev, 0));
-    CK(cudaMemcpyAsync(logits + (size_t)i * V, s->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, bs));
+    CK(cudaMemcpyAsync(bc.logits + (size_t)i * V, s->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, bs));
     hs[i] = s->st;
     ho[i] = s->gen_out;
     hn[i] = s->n_out;
     hd[i] = s->logits;
-    he[i] = AttnBatchEntry{s->st, s->kc, s->vc, s->max_seq};
+    he[i] = AttnBatchEntry{s->st, s->kc, s->vc, s->max_seq, &s->st->error, i == stall ? 1 : 0};
   }
-  CK(cudaMemcpy(states, hs.data(), n * sizeof(DecodeState*), cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(outs, ho.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(nouts, hn.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(dst, hd.data(), n * sizeof(float*), cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(entries, he.data(), n * sizeof(AttnBatchEntry), cudaMemcpyHostToDevice));
+  // the session table of this batch, ordered on the batch stream (the
+  // previous batch on these buffers has finished: its callers synchronised)
+  CK(cudaMemcpyAsync(bc.states, hs.data(), n * sizeof(DecodeState*), cudaMemcpyHostToDevice, bs));
+  CK(cudaMemcpyAsync(bc.outs, ho.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice, bs));
+  CK(cudaMemcpyAsync(bc.nouts, hn.data(), n * sizeof(int32_t*), cudaMemcpyHostToDevice, bs));
+  CK(cudaMemcpyAsync(bc.dst, hd.data(), n * sizeof(float*), cudaMemcpyHostToDevice, bs));
+  CK(cudaMemcpyAsync(bc.entries, he.data(), n * sizeof(AttnBatchEntry), cudaMemcpyHostToDevice, bs));
+  CK(cudaStreamSynchronize(bs));  // the pageable host tables are read before they go
   SampleArgs sa{};
-  sa.logits = logits;
+  sa.logits = bc.logits;
   sa.n = V;
   sa.embd = m->embd.w;
   sa.embd_row_bytes = m->embd.row_bytes;
   sa.embd_type = m->embd.type;
   sa.hidden = (int32_t)H;
-  sa.x = x;
-  sa.states = states;
-  sa.out_ids_b = outs;
-  sa.n_out_b = nouts;
+  sa.x = bc.x;
+  sa.states = bc.states;
+  sa.out_ids_b = bc.outs;
+  sa.n_out_b = bc.nouts;
   sa.nbatch = n;
   auto one_step = [&] {
     check(sample_launch(sa, bs), "sample");
-    batch_layers(m, n, x, q, k, v, attn, gate, up, scratch, sbytes, entries, &ss[0]->st->error, bs);
-    check(rmsnorm_rows_launch(x, m->out_norm, n, c.hidden, c.rms_eps, h, bs), "rmsnorm");
-    check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, H, m->lm_head.row_bytes, h, n, logits, V,
-                      false, scratch, sbytes, bs),
+    batch_layers(m, n, bc.x, bc.q, bc.k, bc.v, bc.attn, bc.gate, bc.up, bc.scratch, sbytes, bc.entries, bs);
+    check(rmsnorm_rows_launch(bc.x, m->out_norm, n, c.hidden, c.rms_eps, bc.h, bs), "rmsnorm");
+    check(gemm_launch(m->lm_head.type, m->lm_head.w, m->lm_head.rows, H, m->lm_head.row_bytes, bc.h, n, bc.logits,
+                      V, false, bc.scratch, sbytes, bs),
           "gemm lm_head");
-    check(commit_rows_launch(logits, V, dst, states, n, bs), "commit logits");
+    check(commit_rows_launch(bc.logits, V, bc.dst, bc.states, n, bs), "commit logits");
   };
-  // The first step runs as plain launches (one-time kernel attributes are
-  // set there); the others replay a graph of one step, captured once: every
-  // argument of a step (positions, states, buffers) lives on the device, so
-  // one graph serves every step, and ~13 launches per layer cost one.
-  one_step();
-  if (steps > 1) {
-    cudaGraph_t g = nullptr;
-    int64_t nk = 0;
-    CK(cudaStreamBeginCapture(bs, cudaStreamCaptureModeThreadLocal));
-    t_capture_count = &nk;
-    try {
-      one_step();
-    } catch (...) {
-      t_capture_count = nullptr;
-      cudaStreamEndCapture(bs, &g);
-      if (g) cudaGraphDestroy(g);
-      throw;
-    }
-    t_capture_count = nullptr;
-    CK(cudaStreamEndCapture(bs, &g));
-    struct ExecGuard {  // destroyed after the stream has run every launch of it
-      cudaGraphExec_t e = nullptr;
-      cudaStream_t s = nullptr;
-      ~ExecGuard() {
-        if (e) {
-          cudaStreamSynchronize(s);
-          cudaGraphExecDestroy(e);
-        }
+  // Every argument of a step (positions, states, buffers) lives on the
+  // device, so one captured graph of a step serves every step of every batch
+  // of this size on these buffers (~13 launches per layer cost one).  The
+  // first batch of a size runs its first step as plain launches (one-time
+  // kernel attributes are set there) and captures the graph after it.
+  int32_t done_steps = 0;
+  auto it = bc.graphs.find(n);
+  if (it == bc.graphs.end()) {
+    one_step();
+    done_steps = 1;
+    if (steps > 1) {
+      cudaGraph_t g = nullptr;
+      int64_t nk = 0;
+      CK(cudaStreamBeginCapture(bs, cudaStreamCaptureModeThreadLocal));
+      t_capture_count = &nk;
+      try {
+        one_step();
+      } catch (...) {
+        t_capture_count = nullptr;
+        cudaStreamEndCapture(bs, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
       }
-    } ge;
-    ge.s = bs;
-    const cudaError_t e = cudaGraphInstantiate(&ge.e, g, 0);
-    cudaGraphDestroy(g);
-    CK(e);
-    for (int32_t step = 1; step < steps; ++step) {
-      CK(cudaGraphLaunch(ge.e, bs));
-      count_launches(nk);
+      t_capture_count = nullptr;
+      CK(cudaStreamEndCapture(bs, &g));
+      BatchCache::StepGraph sg;
+      const cudaError_t e = cudaGraphInstantiate(&sg.exec, g, 0);
+      cudaGraphDestroy(g);
+      CK(e);
+      sg.kernels = nk;
+      it = bc.graphs.emplace(n, sg).first;
+    }
+  }
+  // Replays; with stop ids or unequal lengths, every 8 steps the host reads
+  // how many sessions are still active and ends the batch once none is.
+  for (int32_t step = done_steps; step < steps;) {
+    const int32_t nb = std::min<int32_t>(8, steps - step);
+    for (int32_t j = 0; j < nb; ++j) {
+      CK(cudaGraphLaunch(it->second.exec, bs));
+      count_launches(it->second.kernels);
+    }
+    step += nb;
+    if (early && step < steps) {
+      check(count_active_launch(bc.states, n, bc.n_active, bs), "count active");
+      CK(cudaMemcpyAsync(bc.n_active_host, bc.n_active, sizeof(int32_t), cudaMemcpyDeviceToHost, bs));
+      CK(cudaStreamSynchronize(bs));
+      if (*bc.n_active_host == 0) break;
     }
   }
   CK(cudaEventRecord(ev, bs));
   for (int32_t i = 0; i < n; ++i) CK(cudaStreamWaitEvent(ss[i]->stream, ev, 0));
+  CK(cudaStreamSynchronize(bs));  // the buffers serve the next batch only after this one
 }
 
 // One rpgc_generate call waiting to join a batch (rpgc_model_set_batching).
@@ -1638,7 +1715,43 @@ int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos) {
       for (const auto& x : tab)
         if (std::string(x.name) == "token_embd.weight" && x.n_dims == 2) c.vocab = (int32_t)x.dims[1];
     }
-    return upload(device, c, tab.data(), (int32_t)tab.size());
+    const int32_t eos = (int32_t)r.Int("tokenizer.ggml.eos_token_id", -1);
+    int32_t im_end = -1;  // Tokenizer::IdOf("<|im_end|>") over the vocabulary
+    if (const GgufValue* tv = r.Find("tokenizer.ggml.tokens"))
+      for (size_t k = 0; k < tv->strs.size(); ++k)
+        if (tv->strs[k] == "<|im_end|>") {
+          im_end = (int32_t)k;
+          break;
+        }
+    const int32_t h = upload(device, c, tab.data(), (int32_t)tab.size());
+    std::lock_guard<std::mutex> lk(g_mu);
+    Model* m = model_locked(h);
+    m->eos_id = eos >= 0 && eos < c.vocab ? eos : -1;
+    m->im_end_id = im_end < c.vocab ? im_end : -1;
+    return h;
+  });
+}
+
+int rpgc_model_set_special_ids(int32_t model, int32_t eos_id, int32_t im_end_id) {
+  return guard([&] {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Model* m = model_locked(model);
+    if (eos_id < -1 || eos_id >= m->c.vocab || im_end_id < -1 || im_end_id >= m->c.vocab)
+      fail(RPGC_E_ARG, "special ids %d, %d outside -1 .. %d", eos_id, im_end_id, m->c.vocab - 1);
+    m->eos_id = eos_id;
+    m->im_end_id = im_end_id;
+    return RPGC_OK;
+  });
+}
+
+int rpgc_model_special_ids(int32_t model, int32_t* eos_id, int32_t* im_end_id) {
+  return guard([&] {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!eos_id || !im_end_id) fail(RPGC_E_ARG, "null output");
+    const Model* m = model_locked(model);
+    *eos_id = m->eos_id;
+    *im_end_id = m->im_end_id;
+    return RPGC_OK;
   });
 }
 
@@ -1861,9 +1974,23 @@ int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_gen_opts*
     }
     DeviceGuard dg(m->device);
     batch_decode(ss, std::vector<rpgc_gen_opts>((size_t)n, o));
-    for (int32_t i = 0; i < n; ++i)
-      finish_generate(ss[i], o, o.max_tokens, out_ids + (size_t)i * o.max_tokens, n_out + i);
+    // every session is finished with its own outcome; the call reports the
+    // first failure (n_out of a failed session stays 0, its length unchanged)
+    int code = RPGC_OK;
+    std::string msg;
+    for (int32_t i = 0; i < n; ++i) {
+      try {
+        finish_generate(ss[i], o, o.max_tokens, out_ids + (size_t)i * o.max_tokens, n_out + i);
+      } catch (const Error& e) {
+        n_out[i] = 0;
+        if (code == RPGC_OK) {
+          code = e.code;
+          msg = "session " + std::to_string(sessions[i]) + ": " + e.what();
+        }
+      }
+    }
     CK(cudaStreamSynchronize(ss[0]->stream));
+    if (code != RPGC_OK) throw Error(code, msg);
     return RPGC_OK;
   });
 }
@@ -1897,6 +2024,14 @@ int rpgc_model_batching_stats(int32_t model, int64_t* batches, int64_t* requests
     std::lock_guard<std::mutex> lk(m->batcher.mu);
     *batches = m->batcher.batches;
     *requests = m->batcher.requests;
+    return RPGC_OK;
+  });
+}
+
+int rpgc_test_stall_next_batch(int32_t index) {
+  return guard([&] {
+    if (index < -1 || index >= kMaxBatch) fail(RPGC_E_ARG, "index %d outside -1 .. %d", index, kMaxBatch - 1);
+    g_test_stall.store(index);
     return RPGC_OK;
   });
 }

@@ -8,6 +8,7 @@
 
 #include <cstring>
 #include <stdexcept>
+#include <unordered_set>
 
 namespace rpgc {
 
@@ -48,8 +49,8 @@ struct Cursor {
     pos += sizeof(T);
     return v;
   }
-  std::string str(bool v1) {
-    const uint64_t len = v1 ? get<uint32_t>() : get<uint64_t>();
+  std::string str() {
+    const uint64_t len = get<uint64_t>();
     if (len > (1ull << 31)) throw std::runtime_error("GGUF: string length out of range");
     need(len);
     std::string s(reinterpret_cast<const char*>(p + pos), len);
@@ -58,7 +59,7 @@ struct Cursor {
   }
 };
 
-void skip_or_read(Cursor& c, uint32_t type, GgufValue* out, bool v1, int depth) {
+void skip_or_read(Cursor& c, uint32_t type, GgufValue* out, int depth) {
   GgufValue v;
   switch (type) {
     case 0: v.kind = GgufValue::kInt; v.i = c.get<uint8_t>(); break;
@@ -69,18 +70,23 @@ void skip_or_read(Cursor& c, uint32_t type, GgufValue* out, bool v1, int depth) 
     case 5: v.kind = GgufValue::kInt; v.i = c.get<int32_t>(); break;
     case 6: v.kind = GgufValue::kFloat; v.f = c.get<float>(); break;
     case 7: v.kind = GgufValue::kBool; v.b = c.get<uint8_t>() != 0; break;
-    case 8: v.kind = GgufValue::kString; v.s = c.str(v1); break;
+    case 8: v.kind = GgufValue::kString; v.s = c.str(); break;
     case 10: v.kind = GgufValue::kInt; v.i = (int64_t)c.get<uint64_t>(); break;
     case 11: v.kind = GgufValue::kInt; v.i = c.get<int64_t>(); break;
     case 12: v.kind = GgufValue::kFloat; v.f = c.get<double>(); break;
     case 9: {
       if (depth > 2) throw std::runtime_error("GGUF: nested arrays too deep");
       const uint32_t et = c.get<uint32_t>();
-      const uint64_t n = v1 ? c.get<uint32_t>() : c.get<uint64_t>();
+      const uint64_t n = c.get<uint64_t>();
       if (n >= (1ull << 32)) throw std::runtime_error("GGUF: array length out of range");
       v.kind = GgufValue::kArray;
       v.array_len = n;
-      for (uint64_t k = 0; k < n; ++k) skip_or_read(c, et, nullptr, v1, depth + 1);
+      if (et == 8 && depth == 0 && out) {  // strings: kept (the vocabulary)
+        v.strs.reserve(n);
+        for (uint64_t k = 0; k < n; ++k) v.strs.push_back(c.str());
+        break;
+      }
+      for (uint64_t k = 0; k < n; ++k) skip_or_read(c, et, nullptr, depth + 1);
       break;
     }
     default:
@@ -114,23 +120,31 @@ void GgufReader::Open(const std::string& path) {
   if (c.get<uint32_t>() != 0x46554747u) throw std::runtime_error("bad GGUF magic: " + path);
   const uint32_t version = c.get<uint32_t>();
   if (version < 1 || version > 3) throw std::runtime_error("unsupported GGUF version");
+  // Version 1 differs only in the two counts (32-bit); strings, array
+  // lengths and dimensions are 64-bit in every version, as the reference
+  // reads them (src/gguf.cc:84-93, 124).
   const bool v1 = version == 1;
   const uint64_t n_t = v1 ? c.get<uint32_t>() : c.get<uint64_t>();
   const uint64_t n_kv = v1 ? c.get<uint32_t>() : c.get<uint64_t>();
   for (uint64_t i = 0; i < n_kv; ++i) {
-    const std::string key = c.str(v1);
+    const std::string key = c.str();
     GgufValue v;
-    skip_or_read(c, c.get<uint32_t>(), &v, v1, 0);
+    skip_or_read(c, c.get<uint32_t>(), &v, 0);
     meta_[key] = std::move(v);
   }
+  if (Str("general.architecture", "").empty())
+    throw std::runtime_error("GGUF: general.architecture missing");  // src/gguf.cc:105-106
+  std::unordered_set<std::string> names;
   for (uint64_t i = 0; i < n_t; ++i) {
     GgufTensorInfo t;
-    t.name = c.str(v1);
+    t.name = c.str();
+    if (!names.insert(t.name).second)  // src/gguf.cc:139-141
+      throw std::runtime_error("GGUF: duplicate tensor name " + t.name);
     const uint32_t nd = c.get<uint32_t>();
     if (nd < 1 || nd > 4) throw std::runtime_error("GGUF: bad n_dims for " + t.name);
     t.n_elements = 1;
     for (uint32_t d = 0; d < nd; ++d) {
-      const uint64_t dim = v1 ? c.get<uint32_t>() : c.get<uint64_t>();
+      const uint64_t dim = c.get<uint64_t>();
       if (dim == 0 || dim >= (1ull << 40)) throw std::runtime_error("GGUF: bad dim for " + t.name);
       t.dims.push_back((int64_t)dim);
       t.n_elements *= (int64_t)dim;

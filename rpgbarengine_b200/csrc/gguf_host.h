@@ -21,6 +21,7 @@ struct GgufValue {
   bool b = false;
   std::string s;
   size_t array_len = 0;
+  std::vector<std::string> strs;  // elements of a top-level array of strings
 };
 
 struct GgufTensorInfo {

@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   const float* knz = a.k_new ? a.k_new + z * a.n_kv * 128 : nullptr;
   const float* vnz = a.v_new ? a.v_new + z * a.n_kv * 128 : nullptr;
   float* outz = a.out + z * a.n_heads * 128;
+  int32_t* err = be ? be->err : a.err;  // a batched session's waits report to that session
   cg::cluster_group cluster = cg::this_cluster();
   const int S = (int)gridDim.y, split = (int)blockIdx.y, kh = (int)blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -132,8 +133,16 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
   }
   grid_dep_wait();
   grid_dep_launch();
+  if (be && be->stall && a.layer == 0 && tid == 0) {
+    // test hook: a bounded wait on a barrier that nothing completes gives up
+    // and flags this session's error, which its caller reports
+    __shared__ __align__(8) uint64_t never;
+    mbar_init(&never, 1);
+    fence_barrier_init();
+    mbar_wait(&never, 0, err);
+  }
   if (st && !st->active) {  // the whole cluster leaves together, copies drained
-    if (tid == 0 && c0 < c1) mbar_wait(&bar, 0, a.err);
+    if (tid == 0 && c0 < c1) mbar_wait(&bar, 0, err);
     return;
   }
   // query heads of this kv head (normalised and rotated when fused)
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(kAWarps * 32, 2) attn_decode_kernel(const Attn
       bulk_g2s(Ks, kb + (int64_t)t0 * 128, bytes, &bar, pol);
       bulk_g2s(Vs, vb + (int64_t)t0 * 128, bytes, &bar, pol);
     }
-    mbar_wait(&bar, phase, a.err);
+    mbar_wait(&bar, phase, err);
     phase ^= 1u;
     if (owner && warp == kAWarps - 1 && pos >= t0 && pos < t0 + tn) {
       reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = knew;

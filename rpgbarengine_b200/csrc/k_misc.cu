@@ -127,6 +127,29 @@ cudaError_t commit_rows_launch(const float* src, int64_t n_cols, float* const* d
   return e_;
 }
 
+// Batched decode: how many of the n sessions are still active (one block).
+__global__ void count_active_kernel(DecodeState* const* states, int32_t n, int32_t* out) {
+  int c = 0;
+  for (int32_t b = threadIdx.x; b < n; b += blockDim.x) c += states[b]->active ? 1 : 0;
+  c = __reduce_add_sync(0xffffffffu, c);
+  __shared__ int part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    *out = t;
+  }
+}
+
+cudaError_t count_active_launch(DecodeState* const* states, int32_t n, int32_t* out, cudaStream_t s) {
+  if (n < 1) return cudaErrorInvalidValue;
+  count_active_kernel<<<1, 256, 0, s>>>(states, n, out);
+  const cudaError_t e_ = cudaGetLastError();
+  if (e_ == cudaSuccess) count_launches(1);
+  return e_;
+}
+
 cudaError_t rmsnorm_rows_launch(const float* x, const float* w, int64_t n, int32_t dim, float eps,
                                 float* out, cudaStream_t s) {
   rmsnorm_rows_kernel<<<(unsigned)n, 256, 0, s>>>(x, w, dim, eps, out);

@@ -211,6 +211,8 @@ struct AttnBatchEntry {
   float* kc;                 // the session's K cache, layer 0 ([layers][n_kv][max_seq][hd])
   float* vc;
   int64_t max_seq;
+  int32_t* err;              // the session's own error flags (a wait that gives up in its slice)
+  int32_t stall;             // test hook: this session's layer-0 CTAs wait on a barrier nothing completes
 };
 
 struct AttnArgs {
@@ -282,5 +284,7 @@ cudaError_t advance_launch(DecodeState* st, cudaStream_t s);
 // *st = v, ordered on the stream (the value travels as a kernel parameter, so
 // the host may reuse its copy immediately).
 cudaError_t state_set_launch(DecodeState* st, const DecodeState& v, cudaStream_t s);
+// Number of active sessions among states[0, n) into *out (batched decode's early end).
+cudaError_t count_active_launch(DecodeState* const* states, int32_t n, int32_t* out, cudaStream_t s);
 
 }  // namespace rpgc

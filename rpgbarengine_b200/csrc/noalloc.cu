@@ -19,7 +19,6 @@
 
 #include <cstdint>
 #include <cstdio>
-#include <mutex>
 
 #include "../../include/rpgc.h"
 #include "kernels.h"
@@ -37,21 +36,16 @@ constexpr size_t kNoallocScratchBytes = size_t(32) << 20;
 // takes the device address from cudaGetSymbolAddress, per device.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// The array's address on device `dev`, looked up on the first call with that
-// device current (the caller's current device) and kept.
-cudaError_t scratch_address(int dev, void** out) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    g_scratch_ptr[dev] = p;
-  }
-  *out = g_scratch_ptr[dev];
+// The array's address on the current device, looked up on every call with
+// that device current.  The lookup is cheap, and an address kept from an
+// earlier call could be stale: after cudaDeviceReset, or under another
+// driver context on the same ordinal, the module (and the array) is loaded
+// again at another address.
+cudaError_t scratch_address(void** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  *out = p;
   return cudaSuccess;
 }
 
@@ -94,11 +88,8 @@ extern "C" int rpgc_matmul_noalloc(uint32_t type, const void* w, int64_t rows, i
                   (long long)n, (long long)cols, need, kNoallocScratchBytes);
     return fail_arg(msg);
   }
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess && (dev < 0 || dev >= kMaxDevices)) e = cudaErrorInvalidDevice;
   void* scratch = nullptr;
-  if (e == cudaSuccess) e = scratch_address(dev, &scratch);
+  cudaError_t e = scratch_address(&scratch);
   if (e == cudaSuccess)
     e = gemm_launch(type, static_cast<const uint8_t*>(w), rows, cols, rb, X, n, OUT, rows, false,
                     scratch, kNoallocScratchBytes, static_cast<cudaStream_t>(stream));

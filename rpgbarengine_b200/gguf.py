@@ -97,15 +97,19 @@ def _w_value(f, v):
         raise TypeError(f"unsupported metadata value {type(v)}")
 
 
-def write(path: str, meta: dict, tensors: list) -> None:
-    """Write a GGUF v3 file. meta values: bool/int/float/str or lists of them."""
+def write(path: str, meta: dict, tensors: list, version: int = 3) -> None:
+    """Write a GGUF file (v3 by default; v1 differs only in its two 32-bit
+    counts).  meta values: bool/int/float/str or lists of them."""
     offsets, off = [], 0
     for t in tensors:
         offsets.append(off)
         off += t.n_bytes
         off = (off + ALIGN - 1) // ALIGN * ALIGN
     with open(path, "wb") as f:
-        f.write(struct.pack("<IIQQ", GGUF_MAGIC, 3, len(tensors), len(meta)))
+        if version == 1:
+            f.write(struct.pack("<IIII", GGUF_MAGIC, 1, len(tensors), len(meta)))
+        else:
+            f.write(struct.pack("<IIQQ", GGUF_MAGIC, version, len(tensors), len(meta)))
         for k, v in meta.items():
             _w_str(f, k)
             _w_value(f, v)

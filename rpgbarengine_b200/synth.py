@@ -83,7 +83,7 @@ class Qwen3Shape:
         return tot
 
 
-# BASELINE configurations.
+# The benchmarked shapes: 1.7B all-Q8_0 (tied), 4B Q4_K_M mix (tied), 8B all-Q8_0 (untied).
 QWEN3_1_7B_Q8_0 = Qwen3Shape("qwen3-1.7b-q8_0", 28, 2048, 6144, 16, 8,
                              t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0, t_gate=Q8_0, t_up=Q8_0,
                              t_down=Q8_0, t_embd=Q8_0)

@@ -59,6 +59,33 @@ def test_gguf_parse_reaches_device_check():
     assert "device" in str(e.value).lower()
 
 
+def test_gguf_reader_matches_the_reference_on_odd_files():
+    # src/gguf.cc:84-93, 105-106, 124, 139-141: version 1 changes only the two
+    # counts; a duplicate tensor name and a missing architecture are rejected
+    if rb.device_count() > 0:
+        pytest.skip("a GPU is present")
+    d = tempfile.mkdtemp()
+    shape = synth.TINY_MIX
+    tens = synth.build_tensors(shape, 1)
+    meta = synth.metadata(shape)
+    p1 = os.path.join(d, "v1.gguf")
+    rb.gguf.write(p1, meta, tens, version=1)
+    assert len(rb.gguf.read(p1).tensors) == len(tens)
+    with pytest.raises(rb.RpgcError) as e:
+        rb.Model.load_gguf(p1)
+    assert "device" in str(e.value).lower()  # parsed; only the device is missing
+    p2 = os.path.join(d, "dup.gguf")
+    rb.gguf.write(p2, meta, tens + [tens[-1]])
+    with pytest.raises(rb.RpgcError) as e:
+        rb.Model.load_gguf(p2)
+    assert e.value.code == rb.E_IO and "duplicate" in str(e.value)
+    p3 = os.path.join(d, "noarch.gguf")
+    rb.gguf.write(p3, {k: v for k, v in meta.items() if k != "general.architecture"}, tens)
+    with pytest.raises(rb.RpgcError) as e:
+        rb.Model.load_gguf(p3)
+    assert e.value.code == rb.E_IO and "architecture" in str(e.value)
+
+
 def test_gguf_python_roundtrip():
     d = tempfile.mkdtemp()
     p = os.path.join(d, "t.gguf")

@@ -10,7 +10,7 @@ from rpgbarengine_b200 import gguf, synth  # noqa: E402
 from tests.gpu_util import ROW_GATE, row_gate  # noqa: E402
 
 TYPES = [gguf.Q8_0, gguf.Q4_K, gguf.Q6_K]
-# config-1 shapes (rows x cols) plus ragged ones: odd row counts, partial tiles,
+# the microbench shapes (rows x cols) plus ragged ones: odd row counts, partial tiles,
 # odd block counts per row (unaligned Q6_K rows)
 SHAPES = [(6144, 2048), (2048, 6144), (9728, 2560), (37, 512), (5, 768), (33, 256)]
 

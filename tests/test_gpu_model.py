@@ -149,7 +149,7 @@ def test_gguf_load_matches_upload(orc, tmp_path):
 
 @pytest.mark.slow
 def test_config0_full_size(orc):
-    """Qwen3-1.7B shape, Q8_0, 32-token prompt + 32 greedy."""
+    """Qwen3-1.7B shape, all Q8_0, full size: 32-token prompt + 32 greedy tokens."""
     shape = synth.QWEN3_1_7B_Q8_0
     orc.set_threads(os.cpu_count() or 8)
     gm, om = pair(orc, shape, seed=0, max_pos=4096)
@@ -165,7 +165,7 @@ def test_config0_full_size(orc):
 
 
 def test_copy_prefix_then_forward_matches_one_session(orc):
-    # config 3's shared prefix: session b takes positions [0, 20) from a on
+    # a shared prefix across sessions: session b takes positions [0, 20) from a on
     # the device, forwards the rest, and must agree with a's own forward
     shape = synth.TINY_MIX
     gm, om = pair(orc, shape)
@@ -398,3 +398,39 @@ def test_split_k_shapes_prefill_and_batch(orc):
         ref, ref_logits = om.generate(okv, om.forward(p, okv)[-1], 6, want_logits=True)
         compare_tokens(list(g), ref, ref_logits)
         assert s.len == len(p) + len(g)
+
+
+def test_batched_wait_that_gives_up_fails_only_its_session(orc):
+    # a bounded device wait that runs out in one session's slice of the
+    # batched attention (the test hook makes session 1's layer-0 blocks wait
+    # on a barrier nothing completes) flags that session alone: the call
+    # reports RPGC_E_TIMEOUT, the other sessions finish with their tokens
+    import ctypes as C
+
+    shape = synth.TINY_MIX
+    gm, om = pair(orc, shape)
+    prompts = [synth.prompt_ids(60 + i, n, shape.vocab) for i, n in enumerate((6, 9, 4))]
+    sess = [gm.session(64) for _ in prompts]
+    for s, p in zip(sess, prompts):
+        s.forward_full(p)
+    L = rb.lib()
+    assert L.rpgc_test_stall_next_batch(1) == rb.OK
+    handles = (C.c_int32 * 3)(*[s.handle for s in sess])
+    o = rb.GenOpts(3, None, 0, 0.0, 0, 1.0, 0)
+    out = np.zeros((3, 3), np.int32)
+    n_out = np.zeros(3, np.int32)
+    rc = L.rpgc_generate_batch(C.cast(handles, C.c_void_p), 3, C.byref(o), out.ctypes.data, n_out.ctypes.data)
+    assert rc == rb.E_TIMEOUT, L.rpgc_last_error()
+    assert f"session {sess[1].handle}".encode() in L.rpgc_last_error()
+    assert n_out[1] == 0 and sess[1].len == len(prompts[1])
+    for i in (0, 2):
+        assert n_out[i] == 3 and sess[i].len == len(prompts[i]) + 3
+        okv = om.kv(64)
+        ref, ref_logits = om.generate(okv, om.forward(prompts[i], okv)[-1], 3, want_logits=True)
+        compare_tokens(list(out[i]), ref, ref_logits)
+    # the failed session needs a forward before it generates again; then it works
+    with pytest.raises(rb.RpgcError):
+        sess[1].generate(2)
+    sess[1].set_len(len(prompts[1]) - 1)
+    sess[1].forward_full(prompts[1][-1:])
+    assert len(sess[1].generate(2)) == 2

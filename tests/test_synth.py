@@ -1,5 +1,5 @@
 """Synthetic model builders on CPU: the torch-drawn Q8_0 tensors that the
-config-4 benchmark uploads (same table, layout and value ranges as
+tp8b benchmark uploads (same table, layout and value ranges as
 build_tensors, which the oracle tests use)."""
 import numpy as np
 import pytest
