@@ -268,8 +268,9 @@ def run_gpu(args):
                                  if STEP_TRAFFIC else None),
                      "peak_source": src,
                      "kernel": "step_kernel: one launch per decode token runs all 36 layers and the "
-                               "lm_head (the graph's other launch, the single-block sampler, is "
-                               "under 1% of the step)",
+                               "lm_head, whose phase also leaves per-CTA argmax / top-32 candidates; "
+                               "the time per launch is the whole decode step (step_kernel + the "
+                               "single-block sampler that reads the candidates), greedy and sampled",
                      "algorithmic_bytes_per_launch": int(bytes_tok),
                      "launch_us": round(per_tok_s * 1e6, 2),
                      "timing": "CUDA events on the session stream around the decode loops",

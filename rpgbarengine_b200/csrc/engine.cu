@@ -209,6 +209,7 @@ struct Session {
   StepPlan* step_plan = nullptr;
   bool step_planned = false;
   float* step_part = nullptr;     // attention partials
+  LogitCands cands{};             // the step kernel's lm_head candidates for the sampler
   uint32_t* step_ctr = nullptr;   // step counter + per-layer head counters
   size_t step_ctr_bytes = 0;
   std::vector<void*> allocs;
@@ -807,6 +808,7 @@ void ensure_step_plan(Session* s) {
   StepPhaseIn h = gemv_phase(s->x, c.hidden, m->out_norm);
   h.g.seg[0] = seg_of(m->lm_head, s->logits, kStore);
   h.g.nseg = 1;
+  h.cand = 1;
   ph.push_back(h);
   StepPlan* plan = nullptr;
   if (step_plan_create(ph.data(), (int)ph.size(), c.n_heads, c.n_kv_heads, s->max_seq, s->device, &plan) !=
@@ -816,6 +818,12 @@ void ensure_step_plan(Session* s) {
   }
   s->step_plan = plan;
   s->step_part = s->alloc<float>(step_part_floats(plan));
+  const int ctas = step_plan_grid(plan);
+  s->cands.ctas = ctas;
+  s->cands.val = s->alloc<float>((size_t)ctas * kCandK);
+  s->cands.idx = s->alloc<int32_t>((size_t)ctas * kCandK);
+  s->cands.max_val = s->alloc<float>((size_t)ctas);
+  s->cands.max_idx = s->alloc<int32_t>((size_t)ctas);
 }
 
 // Transformer layers + lm_head of one decode step for the token whose
@@ -826,7 +834,7 @@ void launch_layers_step(Session* s) {
   if (s->step_plan) {
     CK(cudaMemsetAsync(s->step_ctr, 0, s->step_ctr_bytes, s->stream));
     check(step_launch(s->step_plan, s->st, s->m->rope, s->m->c.rms_eps, s->step_part, s->step_ctr,
-                      &s->st->error, s->stream),
+                      &s->st->error, &s->cands, s->stream),
           "decode step");
     return;
   }
@@ -1111,6 +1119,7 @@ void capture_step_graph(Session* s) {
     sa.hidden = m->c.hidden;
     sa.x = s->x;
     sa.pdl = true;
+    sa.cands = s->cands;  // ctas 0 without a step plan: the full sweep
     check(sample_launch(sa, s->stream), "sample");
     launch_layers_step(s);
   } catch (...) {

@@ -212,9 +212,9 @@ int rpgc_engine_generate(int32_t h, const int32_t* ids, int64_t n, const rpgc_en
     int r = rpgc_model_get_config(s->model, &c);
     if (r != RPGC_OK) fail_rc(r, "engine generate");
     if (!ids || n <= 0) fail(RPGC_E_ARG, "the prompt is empty");  // src/engine.cc:378
-    for (int64_t i = 0; i < n; ++i)
-      if (ids[i] < 0 || ids[i] >= c.vocab)
-        fail(RPGC_E_ARG, "prompt id %d at %lld outside the vocabulary (%d)", ids[i], (long long)i, c.vocab);
+    // prompt ids are checked by the forward, as the reference's ForwardFull
+    // checks them (src/qwen3.cc:253-254): an id outside the vocabulary is a
+    // failed forward, which resets the cache
 
     // 1. the longest common prefix with the cache (src/engine.cc:383-397)
     const int64_t cached = (int64_t)s->cached_ids.size();

@@ -24,7 +24,7 @@ namespace rpgc {
 namespace {
 
 constexpr int NT = 1024;
-constexpr int kCap = 4096;  // compacted survivors held in shared memory
+constexpr int kCap = 4864;  // compacted survivors held in shared memory (>= 148 CTAs x kCandK candidates)
 constexpr double kFix = 4611686018427387904.0;  // 2^62
 
 struct Smem {
@@ -170,8 +170,50 @@ __device__ __forceinline__ float v_p(const View& v, int j) {  // softmax output 
   return expf(v_s(v, j) - v.mx) * v.inv;
 }
 
-__device__ int sample_probs(Smem& S, const float* logits, int n, float T, int top_k, float top_p,
-                            float u) {
+// k-th largest value of V's elements [0, m) (4-pass radix select over the
+// order-preserving keys; the count of equal values decides, as nth_element's
+// "keep >= k-th" does).
+__device__ float kth_largest(Smem& S, const View& V, int m, int k) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  int krem = k;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    clear_hist(S, false);
+    const int w = tid >> 5;
+    for (int j = tid; j < m; j += NT) {
+      const uint32_t kk = fkey(v_s(V, j));
+      if ((kk & pmask) == prefix) atomicAdd(&S.cnt[w][(kk >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 256) {
+      uint32_t c = 0;
+      for (int ww = 0; ww < 32; ++ww) c += S.cnt[ww][tid];
+      S.cnt[0][tid] = c;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int above = 0, b = 255;
+      for (; b > 0; --b) {
+        const int c = (int)S.cnt[0][b];
+        if (above + c >= krem) break;
+        above += c;
+      }
+      S.bcast_i[1] = b;
+      S.bcast_i[2] = krem - above;
+    }
+    __syncthreads();
+    prefix |= (uint32_t)S.bcast_i[1] << shift;
+    pmask |= 255u << shift;
+    krem = S.bcast_i[2];
+    __syncthreads();
+  }
+  return unfkey(prefix);
+}
+
+// The full vocabulary with temperature and top-k applied: survivors
+// compacted (index order kept) when they fit shared memory.
+__device__ View view_full(Smem& S, const float* logits, int n, float T, int top_k) {
   const int tid = threadIdx.x;
   View V;
   V.logits = logits;
@@ -182,42 +224,8 @@ __device__ int sample_probs(Smem& S, const float* logits, int n, float T, int to
   V.val = S.cval;
   V.kth = -INFINITY;
   V.m = n;
-  // ---------------- top-k: k-th largest value by radix select
   if (top_k > 1 && top_k < n) {
-    uint32_t prefix = 0, pmask = 0;
-    int krem = top_k;
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      clear_hist(S, false);
-      const int w = tid >> 5;
-      for (int j = tid; j < n; j += NT) {
-        const uint32_t k = fkey(v_s(V, j));
-        if ((k & pmask) == prefix) atomicAdd(&S.cnt[w][(k >> shift) & 255u], 1u);
-      }
-      __syncthreads();
-      if (tid < 256) {
-        uint32_t c = 0;
-        for (int ww = 0; ww < 32; ++ww) c += S.cnt[ww][tid];
-        S.cnt[0][tid] = c;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        int above = 0, b = 255;
-        for (; b > 0; --b) {
-          const int c = (int)S.cnt[0][b];
-          if (above + c >= krem) break;
-          above += c;
-        }
-        S.bcast_i[1] = b;
-        S.bcast_i[2] = krem - above;
-      }
-      __syncthreads();
-      prefix |= (uint32_t)S.bcast_i[1] << shift;
-      pmask |= 255u << shift;
-      krem = S.bcast_i[2];
-      __syncthreads();
-    }
-    V.kth = unfkey(prefix);
+    V.kth = kth_largest(S, V, n, top_k);
     // compact survivors in index order when they fit: warp w owns a
     // contiguous index range, read 32 consecutive logits per round
     // (coalesced); ballots give each survivor its slot.
@@ -261,6 +269,12 @@ __device__ int sample_probs(Smem& S, const float* logits, int n, float T, int to
       V.kth = -INFINITY;  // survivors only
     }
   }
+  return V;
+}
+
+// softmax -> top-p -> renormalise -> inverse CDF over the view's elements.
+__device__ int sample_view(Smem& S, View V, float top_p, float u) {
+  const int tid = threadIdx.x;
   const int m = V.m;
   const int C = (m + NT - 1) / NT, j0 = tid * C, j1 = min(m, j0 + C);
   // ---------------- softmax
@@ -434,6 +448,112 @@ __device__ int sample_probs(Smem& S, const float* logits, int n, float T, int to
   return tok;
 }
 
+__device__ int sample_probs(Smem& S, const float* logits, int n, float T, int top_k, float top_p, float u) {
+  return sample_view(S, view_full(S, logits, n, T, top_k), top_p, u);
+}
+
+// The top-k survivors from the decode step's candidates (LogitCands): the
+// valid entries of every CTA's list (index order within a CTA, CTAs in
+// vocabulary order, so index order overall), the k-th largest of their
+// scaled values, and the survivors >= it.  Returns false -- the caller then
+// takes the full vocabulary -- when a CTA whose list is full has its
+// smallest listed value >= the k-th: it may hold more such elements than it
+// listed (ties), which only the full sweep sees.
+__device__ bool view_cands(Smem& S, const LogitCands& c, float T, int top_k, View* out) {
+  const int tid = threadIdx.x;
+  const float invT = 1.0f / T;
+  const bool scaled = (T != 1.0f);
+  const int slots = c.ctas * kCandK;  // <= kCap (checked by the caller)
+  constexpr int kPer = (kCap + NT - 1) / NT;
+  // 1. the valid entries, compacted in slot order (each thread's chunk read, then written)
+  const int C = (slots + NT - 1) / NT, s0 = tid * C, s1 = min(slots, s0 + C);
+  float vv[kPer];
+  int vi[kPer];
+  int nv = 0;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int sl = s0 + q;
+    vi[q] = -1;
+    vv[q] = 0.0f;
+    if (sl < s1) {
+      const int i = c.idx[sl];
+      if (i >= 0) {
+        const float raw = c.val[sl];
+        vv[q] = scaled ? raw * invT : raw;
+        vi[q] = i;
+        ++nv;
+      }
+    }
+  }
+  int m;
+  const int base = block_excl_scan<int>(S.ired, nv, &m);
+  {
+    int o = base;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q)
+      if (vi[q] >= 0) {
+        S.cidx[o] = vi[q];
+        S.cval[o] = vv[q];
+        ++o;
+      }
+  }
+  __syncthreads();
+  View V;
+  V.logits = nullptr;
+  V.scaled = false;
+  V.invT = 1.0f;
+  V.compact = true;
+  V.idx = S.cidx;
+  V.val = S.cval;
+  V.kth = -INFINITY;
+  V.m = m;
+  if (top_k >= m) return false;  // every list short, so m is the vocabulary: no filtering to do here
+  const float kth = kth_largest(S, V, m, top_k);
+  // 2. a full list whose smallest value reaches the k-th: possibly incomplete
+  bool risky = false;
+  if (tid < c.ctas && c.idx[tid * kCandK + kCandK - 1] >= 0) {
+    float lo = INFINITY;
+    for (int q = 0; q < kCandK; ++q) {
+      const float raw = c.val[tid * kCandK + q];
+      lo = fminf(lo, scaled ? raw * invT : raw);
+    }
+    risky = lo >= kth;
+  }
+  if (__syncthreads_or(risky)) return false;
+  // 3. survivors >= k-th, order kept
+  const int C2 = (m + NT - 1) / NT, j0 = tid * C2, j1 = min(m, j0 + C2);
+  float sv[kPer];
+  int si[kPer];
+  int ns = 0;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int j = j0 + q;
+    si[q] = -1;
+    sv[q] = 0.0f;
+    if (j < j1 && S.cval[j] >= kth) {
+      sv[q] = S.cval[j];
+      si[q] = S.cidx[j];
+      ++ns;
+    }
+  }
+  int total;
+  const int b2 = block_excl_scan<int>(S.ired, ns, &total);  // its barriers order the reads before the writes
+  {
+    int o = b2;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q)
+      if (si[q] >= 0) {
+        S.cidx[o] = si[q];
+        S.cval[o] = sv[q];
+        ++o;
+      }
+  }
+  __syncthreads();
+  V.m = total;
+  *out = V;
+  return true;
+}
+
 __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) uint8_t raw[];
   Smem& S = *reinterpret_cast<Smem*>(raw);
@@ -463,21 +583,38 @@ __global__ void __launch_bounds__(NT) sample_kernel(const SampleArgs a) {
     u = counter_uniform(st->seed, (uint64_t)pos);
   }
   const int n = (int)a.n;
-  int tok;
-  if (!(T > 0.0f)) {  // greedy: first index of the maximum (coalesced sweep)
+  // the step kernel's candidates of these logits, when it left the kind the
+  // options need and no CTA saw a NaN (max_idx -2): then the sweep of the
+  // whole vocabulary is skipped
+  const LogitCands& cd = a.cands;
+  int cmode = (st && cd.max_idx && cd.ctas > 0 && cd.ctas <= NT && cd.ctas * kCandK <= kCap) ? st->cand_ok : 0;
+  if (__syncthreads_or(cmode > 0 && threadIdx.x < cd.ctas && cd.max_idx[threadIdx.x] == -2)) cmode = 0;
+  int tok = -1;
+  if (!(T > 0.0f)) {  // greedy: first index of the maximum
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int j = threadIdx.x; j < n; j += NT) {
-      const float v = logits[j];
-      if (v > bv) {  // a thread's indices increase, so strict > keeps the first
-        bv = v;
-        bi = j;
+    if (cmode >= 1) {  // the CTAs' maxima, in vocabulary order
+      if (threadIdx.x < cd.ctas && cd.max_idx[threadIdx.x] >= 0) {
+        bv = cd.max_val[threadIdx.x];
+        bi = cd.max_idx[threadIdx.x];
+      }
+    } else {
+      for (int j = threadIdx.x; j < n; j += NT) {  // coalesced sweep
+        const float v = logits[j];
+        if (v > bv) {  // a thread's indices increase, so strict > keeps the first
+          bv = v;
+          bi = j;
+        }
       }
     }
     tok = block_argmax(S, bv, bi);
     if (tok == 0x7fffffff) tok = 0;
   } else {
-    tok = sample_probs(S, logits, n, T, top_k, top_p, u);
+    View V;
+    if (cmode == 2 && top_k > 1 && top_k <= kCandK && top_k < n && view_cands(S, cd, T, top_k, &V))
+      tok = sample_view(S, V, top_p, u);
+    else
+      tok = sample_probs(S, logits, n, T, top_k, top_p, u);
   }
   if (st && xrow) {  // the decode step continues with this token's embedding row
     const uint8_t* row = a.embd + (int64_t)tok * a.embd_row_bytes;

@@ -76,6 +76,7 @@ struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
 
 struct PhaseDev {
   int32_t kind;    // 0 matrix-vector, 1 attention
+  int32_t cand;    // lm_head: leave the sampler's candidates (LogitCands)
   int32_t nseg, K, U, S, nls, red_floats, half_bytes;
   int32_t deferred;  // 1: every partial of the phase fits the buffers: one reduction at the end
   GemvSeg seg[3];
@@ -88,7 +89,8 @@ struct PhaseDev {
 struct StepParams {
   const PhaseDev* ph;
   int32_t nph;
-  const DecodeState* st;
+  DecodeState* st;
+  LogitCands cands;  // val null: none
   const float* rope;
   float eps;
   int32_t n_kv, splits;
@@ -635,6 +637,138 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
   }
 }
 
+// ------------------------------------------------- sampler candidates
+// 64-bit order key of a logit: larger value first, ties to the lower index.
+// Key 0 is padding (a NaN is reported by the CTA instead of listed).
+__device__ __forceinline__ uint64_t cand_key(float v, int32_t i) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((uint64_t)k << 32) | (uint32_t)(0x7FFFFFFF - i);
+}
+__device__ __forceinline__ float cand_value(uint64_t key) {
+  const uint32_t k = (uint32_t)(key >> 32);
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+__device__ __forceinline__ int32_t cand_index(uint64_t key) { return 0x7FFFFFFF - (int32_t)(uint32_t)key; }
+
+__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+  return ((uint64_t)hi << 32) | lo;
+}
+// One compare-exchange stage (block size k, distance j) of a bitonic network
+// over the warp's 32 keys, descending overall.
+__device__ __forceinline__ uint64_t bitonic_step(uint64_t key, int lane, int k, int j) {
+  const uint64_t o = shfl_xor64(key, j);
+  const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+  return keep_max ? (key > o ? key : o) : (key < o ? key : o);
+}
+__device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) key = bitonic_step(key, lane, k, j);
+  return key;
+}
+// The 32 largest of two descending lists, descending: the elementwise max
+// against the other list reversed is bitonic; one merge network sorts it.
+__device__ __forceinline__ uint64_t warp_merge_desc(uint64_t a, uint64_t b, int lane) {
+  const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)b, 31 - lane);
+  const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(b >> 32), 31 - lane);
+  const uint64_t br = ((uint64_t)hi << 32) | lo;
+  uint64_t key = a > br ? a : br;
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) key = bitonic_step(key, lane, 32, j);
+  return key;
+}
+
+// After the lm_head phase: this CTA's rows of the logits -> the first index
+// of its maximum and, when the sampler draws with 1 < top_k <= kCandK, its
+// kCandK largest (ties to the lower index) in index order.  Sets
+// st->cand_ok; a NaN among the rows marks max_idx -2 (the sampler then
+// sweeps the whole vocabulary, as it does for the options this skips).
+__device__ __noinline__ void cand_phase(const StepParams& P, const PhaseDev& ph, int lane, int warp,
+                                        uint64_t* lists, int* flags) {
+  DecodeState* st = P.st;
+  const int mode = !st ? 0 : !(st->temperature > 0.0f) ? 1 : (st->top_k > 1 && st->top_k <= kCandK) ? 2 : 0;
+  const int c = (int)blockIdx.x;
+  if (mode == 0 || c >= P.cands.ctas) return;  // uniform over the CTA
+  csync();  // the phase's row totals are stored
+  const GemvSeg& G = ph.seg[0];
+  int32_t lo, hi;
+  seg_rows((int32_t)G.rows, &lo, &hi);
+  const int R = hi - lo;
+  const int w0 = lo + (int)((int64_t)R * warp / kCWarps), w1 = lo + (int)((int64_t)R * (warp + 1) / kCWarps);
+  uint64_t top = 0;
+  bool nan = false;
+  if (mode == 1) {  // the maximum only
+#pragma unroll 1
+    for (int r = w0 + lane; r < w1; r += 32) {
+      const float v = __ldcg(G.out + r);
+      nan |= v != v;
+      const uint64_t k = v != v ? 0ull : cand_key(v, r);
+      top = k > top ? k : top;
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      const uint64_t o = shfl_xor64(top, m);
+      top = o > top ? o : top;
+    }
+  } else {
+#pragma unroll 1
+    for (int r0 = w0; r0 < w1; r0 += 32) {  // warp-uniform batches of 32 rows
+      const int r = r0 + lane;
+      const float v = r < w1 ? __ldcg(G.out + r) : 0.0f;
+      nan |= r < w1 && v != v;
+      uint64_t k = (r < w1 && v == v) ? cand_key(v, r) : 0ull;
+      k = warp_sort_desc(k, lane);
+      top = r0 == w0 ? k : warp_merge_desc(top, k, lane);
+    }
+  }
+  nan = __any_sync(0xffffffffu, nan);
+  lists[warp * 32 + lane] = top;
+  if (lane == 0) flags[warp] = nan;
+  csync();
+  if (mode == 2) {  // merge the warps' lists pairwise: 15 -> 8 -> 4 -> 2 -> 1
+    int count = kCWarps;
+#pragma unroll 1
+    for (int step = 8; step >= 1; step >>= 1) {
+      if (warp < step && warp + step < count) {
+        const uint64_t m = warp_merge_desc(lists[warp * 32 + lane], lists[(warp + step) * 32 + lane], lane);
+        __syncwarp();
+        lists[warp * 32 + lane] = m;
+      }
+      count = step;
+      csync();
+    }
+  }
+  if (warp == 0) {
+    bool any_nan = false;
+    uint64_t best = 0;
+#pragma unroll 1
+    for (int w = 0; w < kCWarps; ++w) {
+      any_nan |= flags[w] != 0;
+      if (mode == 1) best = lists[w * 32] > best ? lists[w * 32] : best;
+    }
+    if (mode == 2) best = lists[0];
+    if (lane == 0) {
+      P.cands.max_val[c] = best ? cand_value(best) : 0.0f;
+      P.cands.max_idx[c] = any_nan ? -2 : best ? cand_index(best) : -1;
+    }
+    if (mode == 2) {
+      // the list in index order: sort (index, value bits) ascending
+      const uint64_t k = lists[lane];
+      const uint64_t key2 = k ? ((uint64_t)(uint32_t)cand_index(k) << 32) | __float_as_uint(cand_value(k))
+                              : ~0ull;
+      const uint64_t sorted = ~warp_sort_desc(~key2, lane);
+      const bool pad = sorted == ~0ull;
+      P.cands.val[c * kCandK + lane] = pad ? 0.0f : __uint_as_float((uint32_t)sorted);
+      P.cands.idx[c * kCandK + lane] = pad ? -1 : (int32_t)(sorted >> 32);
+    }
+    if (lane == 0) st->cand_ok = mode;
+  }
+}
+
 template <uint32_t TM, int G>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -671,10 +805,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   for (int p = 0; p < P.nph; ++p) {
     const PhaseDev& ph = P.ph[p];
     const uint32_t target = (uint32_t)p * gridDim.x;
-    if (ph.kind == 0)
+    if (ph.kind == 0) {
       gemv_phase<TM>(P, ph, target, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
-    else
+      if (ph.cand && P.cands.val)  // the phase's reduction buffers are free again
+        cand_phase(P, ph, lane, warp, reinterpret_cast<uint64_t*>(red), reinterpret_cast<int*>(lim));
+    } else {
       attn_phase<G>(P, ph, target, &it, full, empty, desc, ring, scratch, flag, pos, tid, lane, warp);
+    }
     phase_signal(P, tid);
   }
 }
@@ -850,6 +987,7 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
     if (in[i].kind == 0) {
       int slot = 0;
       if (!plan_gemv(in[i].g, &ph[i], &slot)) return cudaErrorInvalidValue;
+      ph[i].cand = in[i].cand && in[i].g.nseg == 1 ? 1 : 0;
       need = std::max(need, slot);
       Umax = std::max(Umax, ph[i].U);
       redmax = std::max(redmax, ph[i].red_floats);
@@ -936,12 +1074,13 @@ void step_plan_free(StepPlan* p) {
 int step_plan_splits(const StepPlan* p) { return p ? p->splits : 0; }
 int step_plan_grid(const StepPlan* p) { return p ? p->grid : 0; }
 
-cudaError_t step_launch(const StepPlan* plan, const DecodeState* st, const float* rope, float eps,
-                        float* part, uint32_t* ctr, int32_t* err, cudaStream_t s) {
+cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope, float eps,
+                        float* part, uint32_t* ctr, int32_t* err, const LogitCands* cands, cudaStream_t s) {
   StepParams p{};
   p.ph = plan->dev;
   p.nph = plan->nph;
   p.st = st;
+  if (cands && cands->val && cands->ctas == plan->grid) p.cands = *cands;
   p.rope = rope;
   p.eps = eps;
   p.n_kv = plan->n_kv;

@@ -26,6 +26,22 @@ struct DecodeState {
   uint64_t seed;
   int32_t stop_ids[16];
   int32_t error;      // kernel error flags (bounded waits)
+  int32_t cand_ok;    // the pending logits' candidates (LogitCands): 0 none, 1 argmax, 2 argmax + top list
+};
+
+// Candidates the decode step's lm_head phase leaves beside the logits, per
+// CTA of the step kernel (its contiguous vocabulary rows): the first index of
+// its maximum, and (when sampling with 1 < top_k <= kCandK) its kCandK largest
+// logits, ties to the lower index, listed in index order (index -1: padding
+// for a CTA with fewer rows).  The sampler takes the argmax or the top-k
+// survivors from them instead of sweeping the whole vocabulary.
+constexpr int32_t kCandK = 32;
+struct LogitCands {
+  float* val;      // [ctas][kCandK] raw logits
+  int32_t* idx;    // [ctas][kCandK]
+  float* max_val;  // [ctas]
+  int32_t* max_idx;
+  int32_t ctas;
 };
 
 // ------------------------------------------------------------------ GEMV
@@ -106,6 +122,7 @@ struct StepPhaseIn {
   int32_t kind;  // 0 matrix-vector, 1 attention
   StepGemv g;
   StepAttn a;
+  int32_t cand;  // the lm_head phase: leave LogitCands of its output rows
 };
 struct StepPlan;
 // Plans the step's phases for `device` (shapes, ring, shared memory) and
@@ -120,8 +137,10 @@ int step_plan_grid(const StepPlan* p);
 size_t step_part_floats(const StepPlan* p);
 // One decode step: every phase of the plan in one cooperative launch.  ctr
 // (1 + the attention phases' head counters) must be zero when it starts.
-cudaError_t step_launch(const StepPlan* plan, const DecodeState* st, const float* rope, float eps,
-                        float* part, uint32_t* ctr, int32_t* err, cudaStream_t s);
+// cands (optional) receives the lm_head phase's candidates for the sampler
+// (ctas = step_plan_grid) and st->cand_ok says which were left.
+cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope, float eps,
+                        float* part, uint32_t* ctr, int32_t* err, const LogitCands* cands, cudaStream_t s);
 
 // ---------------------------------------------------------- prefill GEMM
 // OUT[t*ldo + r] (+)= sum_k X[t*K + k] * W[r, k], t < n.
@@ -277,6 +296,9 @@ struct SampleArgs {
   int32_t* const* out_ids_b;
   int32_t* const* n_out_b;
   int32_t nbatch;
+  // decode loop (optional): the step kernel's candidates of the pending
+  // logits, used when state->cand_ok says they fit the sampling options
+  LogitCands cands;
 };
 cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s);
 // state->pos += 1 when active (end of a decode step).
