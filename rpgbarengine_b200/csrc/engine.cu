@@ -210,7 +210,7 @@ struct Session {
   bool step_planned = false;
   float* step_part = nullptr;     // attention partials
   LogitCands cands{};             // the step kernel's lm_head candidates for the sampler
-  uint32_t* step_ctr = nullptr;   // step counter + per-layer head counters
+  uint32_t* step_ctr = nullptr;   // the step kernel's phase counter
   size_t step_ctr_bytes = 0;
   std::vector<void*> allocs;
   std::mutex mu;
@@ -758,8 +758,8 @@ void ensure_step_plan(Session* s) {
   const rpgc_model_config& c = m->c;
   const size_t lc = s->layer_cache_floats();
   const int32_t qd = c.n_heads * c.head_dim;
-  s->step_ctr_bytes = sizeof(uint32_t) * (1 + (size_t)c.n_layers * c.n_kv_heads);
-  s->step_ctr = s->alloc<uint32_t>(1 + (size_t)c.n_layers * c.n_kv_heads);
+  s->step_ctr_bytes = sizeof(uint32_t);
+  s->step_ctr = s->alloc<uint32_t>(1);
   std::vector<StepPhaseIn> ph;
   auto gemv_phase = [&](const float* x, int32_t K, const float* norm) {
     StepPhaseIn p;
@@ -789,7 +789,6 @@ void ensure_step_plan(Session* s) {
     a.a.kc = s->kc + l * lc;
     a.a.vc = s->vc + l * lc;
     a.a.out = s->attn;
-    a.a.head_ctr = s->step_ctr + 1 + (size_t)l * c.n_kv_heads;
     ph.push_back(a);
     StepPhaseIn o = gemv_phase(s->attn, qd, nullptr);
     o.g.seg[0] = seg_of(L.o, s->x, kAdd);

@@ -32,8 +32,8 @@
 // token's row is written into the cache and patched into the shared tile by
 // the owner split), online softmax over tiles streamed by the producer, merge
 // of 8 warps in shared memory, then the split's partial (o, max, sum per query
-// head) goes to global scratch; the last split of a head to arrive (counter
-// per head) merges all splits of that head in a fixed order.
+// head) goes to global scratch.  A merge phase follows: every CTA combines a
+// slice of the attention outputs from their heads' splits in a fixed order.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -64,6 +64,7 @@ constexpr uint32_t kMaxBarrierPolls = 1u << 22;
 constexpr int kRec = 132;                  // floats per attention partial record (16-byte multiple)
 constexpr int kMaxItems = 4;               // activation items per consumer thread (K <= 8 * 4 * 480)
 constexpr int kMaxNormItems = 2;           // ... with RMSNorm gains (the first round)
+constexpr int kPhaseBufOff = 640;          // two phase-table entries in shared memory
 static_assert(kMaxNormItems == 2 && kMaxItems % 2 == 0, "prologue rounds of two items");
 
 struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
@@ -74,7 +75,7 @@ struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
   int32_t cs;      // stages per reduction chunk
 };
 
-struct PhaseDev {
+struct alignas(16) PhaseDev {
   int32_t kind;    // 0 matrix-vector, 1 attention
   int32_t cand;    // lm_head: leave the sampler's candidates (LogitCands)
   int32_t nseg, K, U, S, nls, red_floats, half_bytes;
@@ -121,6 +122,10 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   return v;
 }
 
+// a[i] for i in {0, 1, 2} without indexing (keeps a register array out of
+// local memory)
+__device__ __forceinline__ int pick3(const int (&a)[3], int i) { return i == 0 ? a[0] : i == 1 ? a[1] : a[2]; }
+
 // Rows [lo, hi) of a segment owned by this CTA (balanced split over the grid).
 __device__ __forceinline__ void seg_rows(int32_t rows, int32_t* lo, int32_t* hi) {
   *lo = (int32_t)((uint32_t)rows * blockIdx.x / gridDim.x);
@@ -157,12 +162,6 @@ __device__ __forceinline__ void phase_signal(const StepParams& P, int tid) {
   if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
 }
 
-// Acquire-release add returning the old value (one round trip).
-__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // ============================================================== producer
 __device__ __forceinline__ void slot_acquire(uint64_t* empty, const RingPos& rp, int32_t* err) {
@@ -212,7 +211,7 @@ __device__ void producer(const StepParams& P, uint64_t* full, uint64_t* empty, S
           if (L.pair) bulk_g2s(dst + ph.half_bytes, reinterpret_cast<const void*>(b1), n1, &full[slot], pol);
         }
       }
-    } else {
+    } else if (ph.kind == 1) {
       const int item = (int)blockIdx.x;
       if (item >= P.n_kv * P.splits) continue;
       const int kh = item / P.splits, split = item % P.splits;
@@ -248,9 +247,9 @@ __device__ void producer(const StepParams& P, uint64_t* full, uint64_t* empty, S
 // (two float4 of x each, coalesced); the RMSNorm gains are loaded before the
 // phase barrier (they are constant), x after it (written by other CTAs, so
 // read through L2), every load of the thread in flight at once.
-__device__ __forceinline__ float gemv_prologue(const StepParams& P, const PhaseDev& ph, uint32_t target,
-                                               int tid, int lane, int warp, double* dred, uint4* lim,
-                                               float* ucon) {
+__device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDev& ph, uint32_t target,
+                                              int tid, int lane, int warp, double* dred, uint4* lim,
+                                              float* ucon) {
   const int K = ph.K, NI = K / 8, U = ph.U;
   const bool norm = ph.norm_w != nullptr;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -299,11 +298,17 @@ __device__ __forceinline__ float gemv_prologue(const StepParams& P, const PhaseD
     if (lane == 0) dred[warp] = ss;
   }
   csync();
-  if (!norm) return 1.0f;
+}
+
+// 1/rms of the phase input from the warps' sums of squares (double, fixed
+// order): needed only when the row totals are scaled, so it is taken after
+// the matrix work instead of delaying it.
+__device__ __forceinline__ float norm_factor(const StepParams& P, const PhaseDev& ph, const double* dred) {
+  if (!ph.norm_w) return 1.0f;
   double tot = 0.0;
-#pragma unroll 1
+#pragma unroll
   for (int w = 0; w < kCWarps; ++w) tot += dred[w];
-  return 1.0f / sqrtf((float)tot / (float)K + P.eps);
+  return 1.0f / sqrtf((float)tot / (float)ph.K + P.eps);
 }
 
 template <uint32_t TM>
@@ -311,8 +316,18 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
                                            uint64_t* full, uint64_t* empty, const SDesc* desc, uint32_t ring32,
                                            double* dred, uint4* lim, float* ucon, float* red, int tid, int lane,
                                            int warp) {
-  const float nscale = gemv_prologue(P, ph, target, tid, lane, warp, dred, lim, ucon);
+  gemv_prologue(P, ph, target, tid, lane, warp, dred, lim, ucon);
   const int U = ph.U, S = ph.S, Ur = U | 1, NS = P.stages;
+  // this CTA's rows of each logical segment, once per phase
+  int slo[3] = {0, 0, 0}, sn[3] = {0, 0, 0};
+#pragma unroll
+  for (int l = 0; l < 3; ++l)
+    if (l < ph.nls) {
+      int32_t lo, hi;
+      seg_rows(ph.ls[l].rows, &lo, &hi);
+      slo[l] = lo;
+      sn[l] = hi - lo;
+    }
   const int u = tid % U, s = tid / U;
   const bool busy = s < S;
   const UnitOff uo = unit_offsets(u);
@@ -343,26 +358,26 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
     stage_rows<TM>(type, sb + d.off0, L.pair ? sb + d.off1 : sb + d.off0, d.n, s, S, L.pair != 0, rb, u, Ur, uo,
                    act, nullptr, p0, p1);
   };
-  // row total of partial row pp, 4 threads per row, fixed order
-  auto row_total = [&](const float* pp, int q, bool live) {
+  // row total of partial row pp over tpr threads (4, 8 or 16 adjacent
+  // lanes), fixed order: deterministic for a phase shape
+  auto row_total = [&](const float* pp, int q, bool live, int tpr, float nscale) {
     float t = 0.0f;
     if (live) {
 #pragma unroll 4
-      for (int v = q; v < U; v += 4) t += pp[v];
+      for (int v = q; v < U; v += tpr) t += pp[v];
     }
-    t += __shfl_xor_sync(0xffffffffu, t, 1);
-    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    for (int m = 1; m < tpr; m <<= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
     return t * nscale;
   };
   if (ph.deferred) {
     int base = 0;
-#pragma unroll 1
-    for (int l = 0; l < ph.nls; ++l) {
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      if (l >= ph.nls) break;
       const SLSeg L = ph.ls[l];
-      int32_t lo, hi;
-      seg_rows(L.rows, &lo, &hi);
+      const int lo = slo[l], nrows = sn[l];
       const GemvSeg G = ph.seg[L.first];
-      const int nrows = hi - lo, nst = (nrows + L.m - 1) / L.m;
+      const int nst = (nrows + L.m - 1) / L.m;
 #pragma unroll 1
       for (int k = 0; k < nst; ++k, rp.advance(NS)) {
         const int slot = rp.slot;
@@ -375,51 +390,69 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
       }
       base += nrows * (L.pair + 1) * Ur;
     }
-    csync();
-    // one reduction over every segment's rows
+    // one reduction over every segment's rows: sum sid of segment l is row
+    // (pair ? sid / 2 : sid), half (pair ? sid % 2 : 0); tpr threads per sum
+    // (as many as fill the CTA once, at most 16)
     int total = 0;
-#pragma unroll 1
-    for (int l = 0; l < ph.nls; ++l) {
-      int32_t lo, hi;
-      seg_rows(ph.ls[l].rows, &lo, &hi);
-      total += (hi - lo) * (ph.ls[l].pair + 1);
-    }
-#pragma unroll 1
-    for (int b0 = 0; b0 < 4 * total; b0 += kNC) {
-      const int idx = b0 + tid, q = idx & 3;
-      int sid = idx >> 2, l = 0, bse = 0, lo = 0, hi = 0;
-      // segment of sum sid (at most three segments)
-#pragma unroll 1
-      for (; l < ph.nls; ++l) {
-        seg_rows(ph.ls[l].rows, &lo, &hi);
-        const int n = (hi - lo) * (ph.ls[l].pair + 1);
-        if (sid < n) break;
-        sid -= n;
-        bse += n * Ur;
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+      if (l < ph.nls) total += sn[l] * (ph.ls[l].pair + 1);
+    const int lg = total * 16 <= kNC ? 4 : total * 8 <= kNC ? 3 : 2, tpr = 1 << lg;
+    struct Sum {
+      int l, j, h, bse;
+      bool live;
+    };
+    auto locate = [&](int sid) {
+      Sum r{0, 0, 0, 0, false};
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        if (r.live || l >= ph.nls) continue;
+        const int pr = ph.ls[l].pair, n = sn[l] * (pr + 1);
+        if (sid < n) {
+          r = Sum{l, pr ? sid >> 1 : sid, pr ? sid & 1 : 0, r.bse, true};
+        } else {
+          sid -= n;
+          r.bse += n * Ur;
+        }
       }
-      const bool live = l < ph.nls;
-      const int ll = live ? l : 0;
-      const SLSeg& L = ph.ls[ll];
-      const int nrows = hi - lo;
-      const int j = L.pair ? sid >> 1 : sid, h = L.pair ? sid & 1 : 0;
-      const float t = row_total(red + bse + (h * nrows + j) * Ur, q, live);
-      const float other = __shfl_xor_sync(0xffffffffu, t, 4);  // up total for a pair's gate lane
-      if (live && q == 0 && h == 0) {
+      return r;
+    };
+    // the residual rows this thread adds to, loaded before the barrier
+    float resid = 0.0f;
+    {
+      const Sum a = locate(tid >> lg);
+      if (a.live && (tid & (tpr - 1)) == 0 && a.h == 0) {
+        const SLSeg& L = ph.ls[a.l];
         const GemvSeg& G = ph.seg[L.first];
-        const int32_t row = lo + j;
+        if (!L.pair && G.mode == kAdd) resid = __ldcg(G.out + pick3(slo, a.l) + a.j);
+      }
+    }
+    const float nscale = norm_factor(P, ph, dred);
+    csync();
+#pragma unroll 1
+    for (int b0 = 0; b0 < total * tpr; b0 += kNC) {
+      const int idx = b0 + tid, q = idx & (tpr - 1);
+      const Sum a = locate(idx >> lg);
+      const int ll = a.live ? a.l : 0;
+      const SLSeg& L = ph.ls[ll];
+      const float t = row_total(red + a.bse + (a.h * pick3(sn, ll) + a.j) * Ur, q, a.live, tpr, nscale);
+      const float other = __shfl_xor_sync(0xffffffffu, t, tpr);  // up total for a pair's gate lanes
+      if (a.live && q == 0 && a.h == 0) {
+        const GemvSeg& G = ph.seg[L.first];
+        const int32_t row = pick3(slo, ll) + a.j;
         if (L.pair) ph.seg[L.first + 1].out[row] = silu_mul(t, other);
-        else if (G.mode == kAdd) G.out[row] += t;
+        else if (G.mode == kAdd) G.out[row] = (b0 == 0 ? resid : __ldcg(G.out + row)) + t;
         else G.out[row] = t;
       }
     }
     *rpp = rp;
     return;
   }
+  const float nscale = norm_factor(P, ph, dred);
 #pragma unroll 1
   for (int l = 0; l < ph.nls; ++l) {
     const SLSeg L = ph.ls[l];
-    int32_t lo, hi;
-    seg_rows(L.rows, &lo, &hi);
+    const int32_t lo = pick3(slo, l), hi = lo + pick3(sn, l);
     const GemvSeg G = ph.seg[L.first];
     float* up_out = L.pair ? ph.seg[L.first + 1].out : nullptr;
     const int rb = (int)G.row_bytes, ck_rows = L.cs * L.m;
@@ -445,7 +478,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
       for (int b0 = 0; b0 < 4 * nsum; b0 += kNC) {
         const int idx = b0 + tid, q = idx & 3, sid = idx >> 2;
         const int j = L.pair ? sid >> 1 : sid, h = L.pair ? sid & 1 : 0;
-        const float t = row_total(rbuf + (h * ck_rows + j) * Ur, q, sid < nsum);
+        const float t = row_total(rbuf + (h * ck_rows + j) * Ur, q, sid < nsum, 4, nscale);
         const float other = __shfl_xor_sync(0xffffffffu, t, 4);
         if (sid < nsum && q == 0 && h == 0) {
           const int32_t row = chunk_r0 + j;
@@ -463,9 +496,9 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
 
 // Attention phase of one layer for a group of G query heads per kv head.
 template <int G>
-__device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, RingPos* rpp, uint64_t* full,
+__device__ __forceinline__ void attn_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, RingPos* rpp, uint64_t* full,
                                            uint64_t* empty, const SDesc* desc, uint8_t* ring, float* scratch,
-                                           int* flag, int pos, int tid, int lane, int warp) {
+                                           int pos, int tid, int lane, int warp) {
   constexpr int PB = 32 / G;
   const StepAttn& A = ph.a;
   const int item = (int)blockIdx.x, NS = P.stages;
@@ -604,36 +637,45 @@ __device__ __noinline__ void attn_phase(const StepParams& P, const PhaseDev& ph,
       }
     }
   }
-  csync();
-  if (tid == 0) {
-    int last = 0;
-    if (has_item) last = atom_add_acq_rel(A.head_ctr + kh, 1u) == (uint32_t)P.splits - 1u;
-    *flag = last;
+}
+
+// Merge phase after an attention phase: every split of a kv head has written
+// its partial (o, max, sum per query head), so output o of the n_kv * G * 128
+// attention outputs is combined from its head's splits in a fixed order
+// (max, then the rescaled sums).  Each CTA takes a contiguous slice of the
+// outputs; its loads are all independent (one L2 round trip).
+template <int G>
+__device__ __noinline__ void merge_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, int tid,
+                                         float* scratch) {
+  phase_wait(P, target, tid);
+  const int nout = P.n_kv * G * 128, S = P.splits;
+  const int o0 = (int)((int64_t)nout * blockIdx.x / gridDim.x), o1 = (int)((int64_t)nout * (blockIdx.x + 1) / gridDim.x);
+  const int n_o = o1 - o0;
+  // stage (output, split) -> (o, max, sum) with every load in flight at once
+  // (one L2 round trip), then combine from shared memory
+#pragma unroll 1
+  for (int i = tid; i < n_o * S; i += kNC) {
+    const int o = o0 + i / S, r = i % S;
+    const int kh = o / (G * 128), g = (o >> 7) % G, d = o & 127;
+    const float* rp = P.part + ((int64_t)kh * S + r) * (G * kRec) + g * kRec;
+    scratch[3 * i] = __ldcg(rp + d);
+    scratch[3 * i + 1] = __ldcg(rp + 128);
+    scratch[3 * i + 2] = __ldcg(rp + 129);
   }
   csync();
-  if (*flag) {  // every split of head kh has written its partial: merge them
-    // all partials of the head into shared memory at once (async copies
-    // through L2), then the merge from shared memory in a fixed order
-    float* hs = scratch;  // [splits][G][kRec]
-    const float* hp = P.part + (int64_t)kh * P.splits * (G * kRec);
-    const int nchunk = P.splits * G * kRec / 4;
 #pragma unroll 1
-    for (int c = tid; c < nchunk; c += kNC) cp_async16(hs + 4 * c, hp + 4 * c);
-    cp_async_wait_all();
-    csync();
-    for (int idx = tid; idx < G * 128; idx += kNC) {
-      const int g = idx >> 7, d = idx & 127;
-      float M = kNegBig;
-      for (int r = 0; r < P.splits; ++r) M = fmaxf(M, hs[(r * G + g) * kRec + 128]);
-      float O = 0.0f, Ls = 0.0f;
-      for (int r = 0; r < P.splits; ++r) {
-        const float* rp = hs + (r * G + g) * kRec;
-        const float f = expf(rp[128] - M);
-        O += rp[d] * f;
-        Ls += rp[129] * f;
-      }
-      A.out[(kh * G + g) * 128 + d] = O / Ls;
+  for (int i = tid; i < n_o; i += kNC) {
+    const float* sp = scratch + 3 * i * S;
+    float M = kNegBig;
+    for (int r = 0; r < S; ++r) M = fmaxf(M, sp[3 * r + 1]);
+    float O = 0.0f, Ls = 0.0f;
+    for (int r = 0; r < S; ++r) {
+      const float f = expf(sp[3 * r + 1] - M);
+      O += sp[3 * r] * f;
+      Ls += sp[3 * r + 2] * f;
     }
+    const int o = o0 + i, kh = o / (G * 128), g = (o >> 7) % G, d = o & 127;
+    ph.a.out[(kh * G + g) * 128 + d] = O / Ls;
   }
 }
 
@@ -776,7 +818,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   uint64_t* empty = full + kMaxStages;                            // [kMaxStages]
   SDesc* desc = reinterpret_cast<SDesc*>(smem + 128);             // [kMaxStages]
   double* dred = reinterpret_cast<double*>(smem + 384);           // [16]
-  int* flag = reinterpret_cast<int*>(smem + 512);
+  // the consumers' copies of the phase table entries: phase p in pbuf[p & 1]
+  // (the table lives in global memory, and with the ring taking nearly all of
+  // the SM's shared memory L1 is too small to keep it)
+  PhaseDev* pbuf = reinterpret_cast<PhaseDev*>(smem + kPhaseBufOff);
   float* ucon = reinterpret_cast<float*>(smem + P.ucon_off);
   uint4* lim = reinterpret_cast<uint4*>(smem + P.lim_off);
   float* red = reinterpret_cast<float*>(smem + P.red_off);
@@ -801,17 +846,31 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   }
   const uint32_t ring32 = smem_u32(ring);
   RingPos it;
+  constexpr int kPhaseChunks = (int)(sizeof(PhaseDev) / 16);
+  if (tid < kPhaseChunks) {
+    cp_async16(reinterpret_cast<uint4*>(pbuf) + tid, reinterpret_cast<const uint4*>(P.ph) + tid);
+    cp_async_wait_all();
+  }
+  csync();
 #pragma unroll 1
   for (int p = 0; p < P.nph; ++p) {
-    const PhaseDev& ph = P.ph[p];
+    const PhaseDev& ph = pbuf[p & 1];
     const uint32_t target = (uint32_t)p * gridDim.x;
+    // the next phase's entry arrives while this phase runs; the copy is
+    // waited for before this phase's closing barrier
+    if (tid < kPhaseChunks && p + 1 < P.nph)
+      cp_async16(reinterpret_cast<uint4*>(pbuf + ((p + 1) & 1)) + tid,
+                 reinterpret_cast<const uint4*>(P.ph + p + 1) + tid);
     if (ph.kind == 0) {
       gemv_phase<TM>(P, ph, target, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
       if (ph.cand && P.cands.val)  // the phase's reduction buffers are free again
         cand_phase(P, ph, lane, warp, reinterpret_cast<uint64_t*>(red), reinterpret_cast<int*>(lim));
+    } else if (ph.kind == 1) {
+      attn_phase<G>(P, ph, target, &it, full, empty, desc, ring, scratch, pos, tid, lane, warp);
     } else {
-      attn_phase<G>(P, ph, target, &it, full, empty, desc, ring, scratch, flag, pos, tid, lane, warp);
+      merge_phase<G>(P, ph, target, tid, scratch);
     }
+    if (tid < kPhaseChunks) cp_async_wait_all();
     phase_signal(P, tid);
   }
 }
@@ -979,22 +1038,29 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
   if (n <= 0 || n_kv <= 0 || n_heads % n_kv) return cudaErrorInvalidValue;
   const int G = n_heads / n_kv;
   if (G != 1 && G != 2 && G != 4 && G != 8) return cudaErrorInvalidValue;
-  std::vector<PhaseDev> ph((size_t)n);
+  // each attention phase is followed by its merge phase
+  int nph = n;
+  for (int i = 0; i < n; ++i) nph += in[i].kind == 1 ? 1 : 0;
+  std::vector<PhaseDev> ph((size_t)nph);
   int need = 0, Umax = 0, redmax = 0;
   uint32_t mask = 0;
-  for (int i = 0; i < n; ++i) {
-    std::memset(&ph[i], 0, sizeof(PhaseDev));
+  for (int i = 0, o = 0; i < n; ++i, ++o) {
+    std::memset(&ph[o], 0, sizeof(PhaseDev));
     if (in[i].kind == 0) {
       int slot = 0;
-      if (!plan_gemv(in[i].g, &ph[i], &slot)) return cudaErrorInvalidValue;
-      ph[i].cand = in[i].cand && in[i].g.nseg == 1 ? 1 : 0;
+      if (!plan_gemv(in[i].g, &ph[o], &slot)) return cudaErrorInvalidValue;
+      ph[o].cand = in[i].cand && in[i].g.nseg == 1 ? 1 : 0;
       need = std::max(need, slot);
-      Umax = std::max(Umax, ph[i].U);
-      redmax = std::max(redmax, ph[i].red_floats);
+      Umax = std::max(Umax, ph[o].U);
+      redmax = std::max(redmax, ph[o].red_floats);
       for (int k = 0; k < in[i].g.nseg; ++k) mask |= type_mask(in[i].g.seg[k].type);
     } else {
-      ph[i].kind = 1;
-      ph[i].a = in[i].a;
+      ph[o].kind = 1;
+      ph[o].a = in[i].a;
+      ++o;
+      std::memset(&ph[o], 0, sizeof(PhaseDev));
+      ph[o].kind = 2;
+      ph[o].a = in[i].a;
     }
   }
   StepPlan* P = new StepPlan();
@@ -1004,21 +1070,21 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
   P->splits = P->grid / n_kv;
   P->max_seq = max_seq;
   P->mask = mask;
-  P->nph = n;
+  P->nph = nph;
   if (P->splits < 1) {
     delete P;
     return cudaErrorInvalidValue;
   }
   Geometry& g = P->geo;
-  g.ucon_off = 640;
+  g.ucon_off = kPhaseBufOff + (int)((2 * sizeof(PhaseDev) + 127) & ~size_t(127));
   g.lim_off = g.ucon_off + ((20 * Umax + 127) & ~127);
   g.red_off = g.lim_off + 192 * Umax;
   int end = g.red_off + ((2 * redmax * 4 + 127) & ~127);
   const int attn_scratch = (G * 128 + kAttnWarps * G * 128 + 2 * kAttnWarps * G) * 4;
   end = std::max(end, g.lim_off + ((attn_scratch + 127) & ~127));
-  // the merge stages every split's partial of a head in the same region
-  const int per_split = G * kRec * 4;
-  P->splits = std::min(P->splits, std::max(1, (end - g.lim_off) / per_split));
+  // the merge phase stages (output, split) triples of its slice of outputs
+  const int merge_scratch = ((n_kv * G * 128 + P->grid - 1) / P->grid) * P->splits * 12;
+  end = std::max(end, g.lim_off + ((merge_scratch + 127) & ~127));
   g.ring_off = (end + 127) & ~127;
   const int stage_bytes = std::max(need, 2 * 16 * 512);  // an attention tile holds 16 positions at least
   g.stage_bytes = stage_bytes;
@@ -1032,7 +1098,7 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
   g.smem = g.ring_off + g.stages * stage_bytes;
   // second pass: a segment whose rows of one CTA fit one slot takes one
   // stage; a phase whose partials fit both buffers reduces once at its end
-  for (int i = 0; i < n; ++i) {
+  for (int i = 0; i < nph; ++i) {
     PhaseDev& d = ph[i];
     if (d.kind != 0) continue;
     int total = 0;
@@ -1053,9 +1119,9 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
     delete P;
     return cudaErrorInvalidValue;
   }
-  cudaError_t e = cudaMalloc(&P->dev, sizeof(PhaseDev) * (size_t)n);
+  cudaError_t e = cudaMalloc(&P->dev, sizeof(PhaseDev) * (size_t)nph);
   if (e == cudaSuccess)
-    e = cudaMemcpy(P->dev, ph.data(), sizeof(PhaseDev) * (size_t)n, cudaMemcpyHostToDevice);
+    e = cudaMemcpy(P->dev, ph.data(), sizeof(PhaseDev) * (size_t)nph, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     if (P->dev) cudaFree(P->dev);
     delete P;

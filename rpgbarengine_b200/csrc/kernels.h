@@ -116,7 +116,6 @@ struct StepAttn {
   float* kc;            // this layer's caches [n_kv][max_seq][128]
   float* vc;
   float* out;           // [n_heads][128]
-  uint32_t* head_ctr;   // [n_kv] split arrival counters (zero before the step)
 };
 struct StepPhaseIn {
   int32_t kind;  // 0 matrix-vector, 1 attention
@@ -136,7 +135,7 @@ int step_plan_grid(const StepPlan* p);
 // Attention partial scratch (floats) of a plan.
 size_t step_part_floats(const StepPlan* p);
 // One decode step: every phase of the plan in one cooperative launch.  ctr
-// (1 + the attention phases' head counters) must be zero when it starts.
+// (the phase counter, one word) must be zero when it starts.
 // cands (optional) receives the lm_head phase's candidates for the sampler
 // (ctas = step_plan_grid) and st->cand_ok says which were left.
 cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope, float eps,
