@@ -93,8 +93,8 @@ class Clocks:
 # same kernel on the same matrices): gate 14.08 MB, down 20.56 MB.
 # DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
 # dram__bytes_write.sum, the 4B Q4_K_M-mix model, 512-token prompt, context 516)
-STEP_TRAFFIC = 2_832_019_712  # dram read + write of one step_kernel launch, ncu, context 514
-STEP_TRAFFIC_CTX = 514
+STEP_TRAFFIC = 2_795_648_512  # dram read + write of one step_kernel launch, ncu, context 516
+STEP_TRAFFIC_CTX = 516
 
 
 def decode_bytes_per_token(shape, ctx: int) -> float:

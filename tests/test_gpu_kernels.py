@@ -86,7 +86,11 @@ def test_matvec_activation_edge_values(orc):
 @pytest.mark.parametrize("ty", TYPES)
 @pytest.mark.parametrize("rows,cols,n", [(6144, 2048, 64), (2048, 6144, 64), (9728, 2560, 64),
                                          (37, 512, 11), (5, 768, 9),
-                                         (300, 12288, 8)])  # the 8B down projection's input width
+                                         (300, 12288, 8),  # the 8B down projection's input width
+                                         # prefill sizes: two or three 256-token tiles, a partly
+                                         # live last tile, ragged rows, split K
+                                         (9728, 2560, 512), (333, 2560, 300), (1000, 4096, 700),
+                                         (2560, 9728, 512)])
 def test_matmul_row_gate(orc, ty, rows, cols, n):
     w = legal_random(ty, rows, cols, rows + cols + n)
     X = np.random.default_rng(n).standard_normal((n, cols)).astype(np.float32)
