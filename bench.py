@@ -88,12 +88,10 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# DRAM bytes (read + write) per launch of the roofline kernel, from one ncu
-# capture of each shape (gpu__time_duration / dram__bytes_*.sum pass of the
-# same kernel on the same matrices): gate 14.08 MB, down 20.56 MB.
 # DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
-# dram__bytes_write.sum, the 4B Q4_K_M-mix model, 512-token prompt, context 516)
-STEP_TRAFFIC = 2_795_648_512  # dram read + write of one step_kernel launch, ncu, context 516
+# dram__bytes_write.sum; the 4B Q4_K_M-mix model after the 512-token prompt,
+# attention over 516 keys)
+STEP_TRAFFIC = 2_795_648_512
 STEP_TRAFFIC_CTX = 516
 
 
@@ -236,6 +234,7 @@ def run_gpu(args):
         cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
                "sample": "timed at N=1 only" if world > 1 else "skipped (--skip-cpu)"}
     e2e_tok = e2e_steps * 2 * decode_n * world / e2e_s
+    _, bf16, _ = peaks()
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -260,6 +259,14 @@ def run_gpu(args):
         "prefill_tok_s": round(prefill_tok_s, 1),
         "prefill_ms": round(pre_ms / args.steps, 3),
         "prefill_tflops": round(prefill_flops / (pre_ms / args.steps / 1e3) / 1e12, 2),
+        "prefill_roofline": {"bound": "tensor",
+                             "achieved": round(prefill_flops / (pre_ms / args.steps / 1e3) / 1e12, 2),
+                             "peak": bf16, "unit": "TFLOP/s",
+                             "frac": round(prefill_flops / (pre_ms / args.steps / 1e3) / 1e12 / bf16, 4),
+                             "peak_source": src,
+                             "flops": "useful: 2 x the weight MACs of the prompt's tokens, causal "
+                                      "attention, one lm_head row; the fp16 hi/lo matmuls issue three "
+                                      "MMAs per useful MAC"},
         "greedy_tok_s": round(decode_n * args.steps * world / (greedy_ms / 1e3), 2),
         "sampled_tok_s": round(decode_n * args.steps * world / (sampled_ms / 1e3), 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
