@@ -407,8 +407,11 @@ def run_tp8b(args):
         "config": {"workload": "config4: qwen3-8b q8_0, 4096-tok prefill + 128 greedy decode, "
                                f"tensor parallel x{world}",
                    "model": shape.name, "global_batch": 1, "seq_len": TP_PROMPT + TP_DECODE,
-                   "parallelism": f"tp{world} (column-split q/k/v/gate/up, row-split o/down, "
-                                  "NCCL all-reduce; vocabulary-split lm_head, all-gather)",
+                   "parallelism": (f"tp{world} (column-split q/k/v/gate/up, row-split o/down; decode: "
+                                   "partial rows stored into every rank's inbox by the step kernel "
+                                   "over peer memory, summed in rank order, vocabulary-split lm_head "
+                                   "rows written to every rank; prefill: NCCL all-reduce / all-gather)"
+                                   if world > 1 else "tp1 (one GPU, no communication)"),
                    "weights": "raw Q8_0 blocks in HBM", "kv": "fp32",
                    "l2": "inputs > L2: 8.04 GB of weights re-streamed every decode step",
                    "seed_weights": SEED_WEIGHTS, "seed_prompt": SEED_PROMPT},
@@ -418,8 +421,10 @@ def run_tp8b(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(hbm * world, 1),
                      "unit": "GB/s", "frac": round(achieved / (hbm * world), 4), "traffic": None,
                      "peak_source": src + f" copy bandwidth x {world} GPUs",
-                     "kernel": "whole decode step (per-launch kernels + NCCL all-reduce per "
-                               "row-split matmul)",
+                     "kernel": ("whole decode step: the persistent step kernel on every rank, "
+                                "two peer-memory exchanges per layer and one for the logits, no "
+                                "collective call" if world > 1 else
+                                "whole decode step: the persistent step kernel"),
                      "algorithmic_bytes_per_launch": int(bytes_tok),
                      "launch_us": round(per_tok_s * 1e6, 2),
                      "timing": "CUDA events on the session stream, max over ranks"},

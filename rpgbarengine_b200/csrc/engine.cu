@@ -213,6 +213,7 @@ struct Session {
   uint32_t* step_ctr = nullptr;   // the step kernel's phase counter
   size_t step_ctr_bytes = 0;
   std::vector<void*> allocs;
+  std::vector<void*> ipc_mapped;  // tensor parallelism: peers' step-kernel buffers mapped here
   std::mutex mu;
 
   template <typename T>
@@ -228,6 +229,7 @@ struct Session {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     if (step_graph) cudaGraphExecDestroy(step_graph);
+    for (void* p : ipc_mapped) cudaIpcCloseMemHandle(p);
     step_plan_free(step_plan);
     for (void* p : allocs) cudaFree(p);
     if (st_host) cudaFreeHost(st_host);
@@ -747,14 +749,62 @@ bool step_kernel_enabled() {
   return !(e && e[0] == '0' && e[1] == 0);
 }
 
+// Every rank's address of two device allocations of every rank (this rank's
+// own at its index): the IPC handles all-gathered over the model's
+// communicator, the peers' mapped with peer access.  The mappings are closed
+// with the session.
+void tp_map_peers(Session* s, void* a_own, void* b_own, std::vector<void*>* a_all, std::vector<void*>* b_all) {
+  const Model* m = s->m;
+  const int W = m->tp_world, R = m->tp_rank;
+  cudaIpcMemHandle_t own[2];
+  CK(cudaIpcGetMemHandle(&own[0], a_own));
+  CK(cudaIpcGetMemHandle(&own[1], b_own));
+  const size_t hb = sizeof(own);
+  std::vector<cudaIpcMemHandle_t> all((size_t)2 * W);
+  char* dev = nullptr;
+  CK(cudaMalloc(&dev, hb * (W + 1)));
+  try {
+    CK(cudaMemcpyAsync(dev + hb * W, own, hb, cudaMemcpyHostToDevice, s->stream));
+    const ncclResult_t r = nccl_api()->all_gather(dev + hb * W, dev, hb, ncclChar, m->comm, s->stream);
+    if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclAllGather: %s", nccl_api()->error_string(r));
+    CK(cudaMemcpyAsync(all.data(), dev, hb * W, cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+  } catch (...) {
+    cudaFree(dev);
+    throw;
+  }
+  cudaFree(dev);
+  a_all->assign(W, nullptr);
+  b_all->assign(W, nullptr);
+  for (int r = 0; r < W; ++r) {
+    if (r == R) {
+      (*a_all)[r] = a_own;
+      (*b_all)[r] = b_own;
+      continue;
+    }
+    for (int k = 0; k < 2; ++k) {
+      void* p = nullptr;
+      CK(cudaIpcOpenMemHandle(&p, all[(size_t)2 * r + k], cudaIpcMemLazyEnablePeerAccess));
+      s->ipc_mapped.push_back(p);
+      (k ? *b_all : *a_all)[r] = p;
+    }
+  }
+}
+
 // Plans the persistent decode step of a session once (device allocations:
 // call outside graph capture).  Leaves step_plan null when the model's block
-// types or shapes are outside the step kernel, or it is disabled.
+// types or shapes are outside the step kernel, or it is disabled.  Under
+// tensor parallelism every rank plans at the same call (the peers' buffers
+// are exchanged over the communicator); the o and down projections leave
+// partial rows in every rank's inbox, the phase after each sums them onto
+// the residual, and the vocabulary-split lm_head writes its rows into every
+// rank's logits, so the decode step runs no collective call.
 void ensure_step_plan(Session* s) {
   if (s->step_planned) return;
   s->step_planned = true;
-  if (!step_kernel_enabled() || s->m->tp_world > 1) return;  // collectives run between launches
+  if (!step_kernel_enabled()) return;
   const Model* m = s->m;
+  const bool tp = m->tp_world > 1;
   const rpgc_model_config& c = m->c;
   const size_t lc = s->layer_cache_floats();
   const int32_t qd = c.n_heads * c.head_dim;
@@ -770,6 +820,9 @@ void ensure_step_plan(Session* s) {
     p.g.norm_w = norm;
     return p;
   };
+  // under tensor parallelism the row-split projections store partial rows
+  // (exchanged), otherwise they add into the residual
+  const int32_t res_mode = tp ? kStore : kAdd;
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m->layers[l];
     StepPhaseIn q = gemv_phase(s->x, c.hidden, L.attn_norm);
@@ -777,6 +830,7 @@ void ensure_step_plan(Session* s) {
     q.g.seg[1] = seg_of(L.k, s->k, kStore);
     q.g.seg[2] = seg_of(L.v, s->v, kStore);
     q.g.nseg = 3;
+    q.x_sum = tp && l > 0;
     ph.push_back(q);
     StepPhaseIn a;
     std::memset(&a, 0, sizeof(a));
@@ -791,29 +845,55 @@ void ensure_step_plan(Session* s) {
     a.a.out = s->attn;
     ph.push_back(a);
     StepPhaseIn o = gemv_phase(s->attn, qd, nullptr);
-    o.g.seg[0] = seg_of(L.o, s->x, kAdd);
+    o.g.seg[0] = seg_of(L.o, s->x, res_mode);
     o.g.nseg = 1;
+    o.xchg = tp ? 1 : 0;
     ph.push_back(o);
     StepPhaseIn f = gemv_phase(s->x, c.hidden, L.ffn_norm);
     f.g.seg[0] = seg_of(L.gate, s->gate, kSwiGLU);
     f.g.seg[1] = seg_of(L.up, s->gate, kStore);
     f.g.nseg = 2;
+    f.x_sum = tp;
     ph.push_back(f);
     StepPhaseIn d = gemv_phase(s->gate, c.intermediate, nullptr);
-    d.g.seg[0] = seg_of(L.down, s->x, kAdd);
+    d.g.seg[0] = seg_of(L.down, s->x, res_mode);
     d.g.nseg = 1;
+    d.xchg = tp ? 1 : 0;
     ph.push_back(d);
   }
   StepPhaseIn h = gemv_phase(s->x, c.hidden, m->out_norm);
-  h.g.seg[0] = seg_of(m->lm_head, s->logits, kStore);
+  h.g.seg[0] = seg_of(m->lm_head, tp ? s->logits_part : s->logits, kStore);
   h.g.nseg = 1;
-  h.cand = 1;
+  h.cand = tp ? 0 : 1;
+  h.x_sum = tp;
+  h.xchg = tp ? 2 : 0;
   ph.push_back(h);
+  StepTp spec{m->tp_rank, m->tp_world, c.hidden, (int64_t)m->tp_rank * m->lm_head.rows};
   StepPlan* plan = nullptr;
-  if (step_plan_create(ph.data(), (int)ph.size(), c.n_heads, c.n_kv_heads, s->max_seq, s->device, &plan) !=
-      cudaSuccess) {
+  if (step_plan_create(ph.data(), (int)ph.size(), c.n_heads, c.n_kv_heads, s->max_seq, s->device, &plan,
+                       tp ? &spec : nullptr) != cudaSuccess) {
     cudaGetLastError();
     return;
+  }
+  if (tp) {
+    // every rank reaches this call (the same forward or generate on every
+    // rank); a rank whose plan failed above fails the exchange's peers too
+    std::vector<void*> arenas, outs;
+    try {
+      tp_map_peers(s, step_plan_tp_arena(plan), s->logits, &arenas, &outs);
+    } catch (...) {
+      step_plan_free(plan);
+      throw;
+    }
+    std::vector<float*> outf(outs.size());
+    for (size_t r = 0; r < outs.size(); ++r) outf[r] = static_cast<float*>(outs[r]);
+    if (step_plan_tp_bind(plan, arenas.data(), outf.data()) != cudaSuccess) {
+      step_plan_free(plan);
+      fail(RPGC_E_CUDA, "binding the tensor-parallel decode step failed");
+    }
+    s->step_plan = plan;
+    s->step_part = s->alloc<float>(step_part_floats(plan));
+    return;  // candidates: the sampler sweeps the gathered logits
   }
   s->step_plan = plan;
   s->step_part = s->alloc<float>(step_part_floats(plan));

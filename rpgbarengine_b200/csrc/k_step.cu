@@ -80,10 +80,19 @@ struct alignas(16) PhaseDev {
   int32_t cand;    // lm_head: leave the sampler's candidates (LogitCands)
   int32_t nseg, K, U, S, nls, red_floats, half_bytes;
   int32_t deferred;  // 1: every partial of the phase fits the buffers: one reduction at the end
+  // tensor parallelism (StepParams::tp_world > 1)
+  int32_t x_sum;     // input = xr_prev + the ranks' partial rows of exchange x_xk (rank order)
+  int32_t x_xk;
+  int32_t xchg;      // 1: partial rows to every rank's inbox; 2: rows to every rank's output copy
+  int32_t xchg_k;    // this phase's exchange number in the launch
   GemvSeg seg[3];
   SLSeg ls[3];
   const float* x;
   const float* norm_w;
+  const float* inbox;    // x_sum: this rank's inbox of the exchange [world][K]
+  const float* xr_prev;  // x_sum: the residual before the exchange
+  float* xr_next;        // x_sum: the residual after it (each CTA writes its rows)
+  float* xdst[kMaxTp];   // xchg: every rank's destination for this rank's rows
   StepAttn a;
 };
 
@@ -99,6 +108,13 @@ struct StepParams {
   float* part;      // [n_kv][splits][G][kRec]: o[128], max, sum, 2 pad
   uint32_t* ctr;    // step counter
   int32_t* err;
+  // tensor parallelism: exchanges per launch, this rank's arrival counter
+  // (every rank's CTAs add one per exchange) and every rank's (mapped), and
+  // this rank's launch counter (grid per launch)
+  int32_t tp_world, n_xchg;
+  unsigned long long* xctr;
+  unsigned long long* xctr_rank[kMaxTp];
+  unsigned long long* launches;
   int32_t stages, stage_bytes, tile_pos, attn_half;
   int32_t ucon_off, lim_off, red_off, ring_off;  // shared-memory carve-up
 };
@@ -157,9 +173,44 @@ __device__ __forceinline__ void phase_wait(const StepParams& P, uint32_t target,
 
 // Release add: the barrier orders every consumer's stores of the phase before
 // thread 0's release, which is cumulative at GPU scope (no separate fence).
-__device__ __forceinline__ void phase_signal(const StepParams& P, int tid) {
+// An exchange phase first adds one to every rank's arrival counter with a
+// release at system scope, which covers the CTA's stores to the peers.
+__device__ __forceinline__ void phase_signal(const StepParams& P, const PhaseDev& ph, int tid) {
   csync();  // every consumer's output of this phase is written
-  if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
+  if (tid == 0) {
+    if (ph.xchg)
+      for (int r = 0; r < P.tp_world; ++r)
+        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r]) : "memory");
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
+  }
+}
+
+// Bounded wait (thread 0 of the consumers) until every rank's CTAs have
+// signalled exchange k of launch L, then release the other consumers.  The
+// acquire at system scope makes the peers' stores before their signals
+// visible to this CTA.  A wait gives up after ~2 s (a rank that never
+// signals: the error flag is set and the step runs on, so the host sees
+// RPGC_E_TIMEOUT), and once any wait of the launch has given up the others
+// give up within 256 polls.
+constexpr uint32_t kMaxXchgPolls = 1u << 21;
+__device__ __forceinline__ void xchg_wait(const StepParams& P, unsigned long long L, int k, int tid) {
+  if (tid == 0) {
+    const unsigned long long target =
+        (L * (unsigned long long)P.n_xchg + (unsigned long long)k + 1ull) * (unsigned long long)P.tp_world * gridDim.x;
+    uint32_t i = 0;
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(P.xctr) : "memory");
+      if (v >= target) break;
+      ++i;
+      if (i > kMaxXchgPolls || ((i & 255u) == 0 && (*reinterpret_cast<volatile int32_t*>(P.err) & kErrTimeout))) {
+        atomicOr(P.err, kErrTimeout);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  csync();
 }
 
 
@@ -243,13 +294,34 @@ __device__ void producer(const StepParams& P, uint64_t* full, uint64_t* empty, S
 }
 
 // ============================================================== consumers
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// Elements e..e+3 of an exchange's input: the residual before it plus the
+// ranks' partial rows summed in rank order (the same sum on every rank).
+__device__ __forceinline__ float4 xsum4(const StepParams& P, const PhaseDev& ph, int e) {
+  float4 s = __ldcg(reinterpret_cast<const float4*>(ph.inbox + e));
+  for (int r = 1; r < P.tp_world; ++r)
+    s = add4(s, __ldcg(reinterpret_cast<const float4*>(ph.inbox + (size_t)r * ph.K + e)));
+  return add4(__ldcg(reinterpret_cast<const float4*>(ph.xr_prev + e)), s);
+}
+
+// The elements of e..e+7 in [lo, hi) into dst.
+__device__ __forceinline__ void write_owned(float* dst, int e, float4 a, float4 c, int lo, int hi) {
+  const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (e + j >= lo && e + j < hi) dst[e + j] = v[j];
+}
+
 // Input vector of a matrix-vector phase.  Thread t quantises items t + NC b
 // (two float4 of x each, coalesced); the RMSNorm gains are loaded before the
 // phase barrier (they are constant), x after it (written by other CTAs, so
 // read through L2), every load of the thread in flight at once.
 __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDev& ph, uint32_t target,
-                                              int tid, int lane, int warp, double* dred, uint4* lim,
-                                              float* ucon) {
+                                              unsigned long long L, int tid, int lane, int warp, double* dred,
+                                              uint4* lim, float* ucon) {
   const int K = ph.K, NI = K / 8, U = ph.U;
   const bool norm = ph.norm_w != nullptr;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -263,7 +335,13 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
       g1[b] = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + 2 * i + 1);
     }
   }
-  phase_wait(P, target, tid);
+  int own_lo = 0, own_hi = 0;  // tensor parallel: this CTA's rows of the new residual
+  if (ph.x_sum) {
+    xchg_wait(P, L, ph.x_xk, tid);
+    seg_rows(K, &own_lo, &own_hi);
+  } else {
+    phase_wait(P, target, tid);
+  }
   double ss = 0.0;
   // two items per round, both rounds' loads in flight before any use
 #pragma unroll 1
@@ -273,8 +351,20 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int i = (b0 + k) * kNC + tid;
-      v0[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
-      v1[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
+      if (ph.x_sum) {
+        v0[k] = i < NI ? xsum4(P, ph, 8 * i) : zero;
+        v1[k] = i < NI ? xsum4(P, ph, 8 * i + 4) : zero;
+      } else {
+        v0[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
+        v1[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
+      }
+    }
+    if (ph.x_sum && ph.xr_next) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int i = (b0 + k) * kNC + tid;
+        if (i < NI) write_owned(ph.xr_next, 8 * i, v0[k], v1[k], own_lo, own_hi);
+      }
     }
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -311,12 +401,23 @@ __device__ __forceinline__ float norm_factor(const StepParams& P, const PhaseDev
   return 1.0f / sqrtf((float)tot / (float)ph.K + P.eps);
 }
 
+// A stored row total: into the segment's output, or for an exchange phase
+// into every rank's destination (plain stores, peers' memory included).
+__device__ __forceinline__ void out_row(const StepParams& P, const PhaseDev& ph, const GemvSeg& G, int32_t row,
+                                        float t) {
+  if (ph.xchg) {
+    for (int r = 0; r < P.tp_world; ++r) ph.xdst[r][row] = t;
+  } else {
+    G.out[row] = t;
+  }
+}
+
 template <uint32_t TM>
-__device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& ph, uint32_t target, RingPos* rpp,
-                                           uint64_t* full, uint64_t* empty, const SDesc* desc, uint32_t ring32,
-                                           double* dred, uint4* lim, float* ucon, float* red, int tid, int lane,
-                                           int warp) {
-  gemv_prologue(P, ph, target, tid, lane, warp, dred, lim, ucon);
+__device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& ph, uint32_t target,
+                                           unsigned long long L, RingPos* rpp, uint64_t* full, uint64_t* empty,
+                                           const SDesc* desc, uint32_t ring32, double* dred, uint4* lim, float* ucon,
+                                           float* red, int tid, int lane, int warp) {
+  gemv_prologue(P, ph, target, L, tid, lane, warp, dred, lim, ucon);
   const int U = ph.U, S = ph.S, Ur = U | 1, NS = P.stages;
   // this CTA's rows of each logical segment, once per phase
   int slo[3] = {0, 0, 0}, sn[3] = {0, 0, 0};
@@ -442,7 +543,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
         const int32_t row = pick3(slo, ll) + a.j;
         if (L.pair) ph.seg[L.first + 1].out[row] = silu_mul(t, other);
         else if (G.mode == kAdd) G.out[row] = (b0 == 0 ? resid : __ldcg(G.out + row)) + t;
-        else G.out[row] = t;
+        else out_row(P, ph, G, row, t);
       }
     }
     *rpp = rp;
@@ -484,7 +585,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
           const int32_t row = chunk_r0 + j;
           if (L.pair) up_out[row] = silu_mul(t, other);
           else if (G.mode == kAdd) G.out[row] += t;
-          else G.out[row] = t;
+          else out_row(P, ph, G, row, t);
         }
       }
       chunk0 = k + 1;
@@ -851,7 +952,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     cp_async16(reinterpret_cast<uint4*>(pbuf) + tid, reinterpret_cast<const uint4*>(P.ph) + tid);
     cp_async_wait_all();
   }
+  // tensor parallelism: this launch's number (every CTA of a launch adds
+  // one, and a launch starts after the previous one ended)
+  unsigned long long* launch_s = reinterpret_cast<unsigned long long*>(smem + 512);
+  if (P.tp_world > 1 && tid == 0) *launch_s = atomicAdd(P.launches, 1ull) / gridDim.x;
   csync();
+  const unsigned long long L = P.tp_world > 1 ? *launch_s : 0ull;
 #pragma unroll 1
   for (int p = 0; p < P.nph; ++p) {
     const PhaseDev& ph = pbuf[p & 1];
@@ -862,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       cp_async16(reinterpret_cast<uint4*>(pbuf + ((p + 1) & 1)) + tid,
                  reinterpret_cast<const uint4*>(P.ph + p + 1) + tid);
     if (ph.kind == 0) {
-      gemv_phase<TM>(P, ph, target, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
+      gemv_phase<TM>(P, ph, target, L, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
       if (ph.cand && P.cands.val)  // the phase's reduction buffers are free again
         cand_phase(P, ph, lane, warp, reinterpret_cast<uint64_t*>(red), reinterpret_cast<int*>(lim));
     } else if (ph.kind == 1) {
@@ -871,8 +977,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       merge_phase<G>(P, ph, target, tid, scratch);
     }
     if (tid < kPhaseChunks) cp_async_wait_all();
-    phase_signal(P, tid);
+    phase_signal(P, ph, tid);
   }
+  // tensor parallelism: the last exchange (every rank's rows of the output)
+  // has arrived before the kernel ends, so the launches after it read it whole
+  if (P.tp_world > 1 && blockIdx.x == 0) xchg_wait(P, L, P.n_xchg - 1, tid);
 }
 
 // ------------------------------------------------------------------ host
@@ -1026,16 +1135,35 @@ struct StepPlan {
   uint32_t mask = 0;
   int grid = 0, n_kv = 0, G = 0, splits = 0;
   int64_t max_seq = 0;
+  // tensor parallelism: the arena every rank maps (arrival counter, launch
+  // counter, two exchange inboxes [world][hidden], two residual buffers), the
+  // phase table kept on the host until every rank's arena is bound
+  StepTp tp{0, 1, 0, 0};
+  uint8_t* arena = nullptr;
+  int n_xchg = 0;
+  std::vector<PhaseDev> table;
+  unsigned long long* xctr_rank[kMaxTp] = {};
+  bool bound = true;
 };
+
+namespace {
+constexpr size_t kArenaHead = 256;  // arrival counter at 0, launch counter at 8
+size_t inbox_off(const StepTp& t, int slot) { return kArenaHead + (size_t)slot * t.world * t.hidden * 4; }
+size_t xr_off(const StepTp& t, int i) { return inbox_off(t, 2) + (size_t)i * t.hidden * 4; }
+size_t arena_bytes(const StepTp& t) { return xr_off(t, 2); }
+}  // namespace
 
 size_t step_part_floats(const StepPlan* p) {
   return p ? (size_t)p->n_kv * p->splits * p->G * kRec : 0;
 }
 
 cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv, int64_t max_seq,
-                             int device, StepPlan** out) {
+                             int device, StepPlan** out, const StepTp* tp) {
   *out = nullptr;
   if (n <= 0 || n_kv <= 0 || n_heads % n_kv) return cudaErrorInvalidValue;
+  const bool tpm = tp && tp->world > 1;
+  if (tpm && (tp->world > kMaxTp || tp->rank < 0 || tp->rank >= tp->world || tp->hidden <= 0 || tp->hidden % 8))
+    return cudaErrorInvalidValue;
   const int G = n_heads / n_kv;
   if (G != 1 && G != 2 && G != 4 && G != 8) return cudaErrorInvalidValue;
   // each attention phase is followed by its merge phase
@@ -1049,7 +1177,15 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
     if (in[i].kind == 0) {
       int slot = 0;
       if (!plan_gemv(in[i].g, &ph[o], &slot)) return cudaErrorInvalidValue;
-      ph[o].cand = in[i].cand && in[i].g.nseg == 1 ? 1 : 0;
+      ph[o].cand = in[i].cand && in[i].g.nseg == 1 && !tpm ? 1 : 0;
+      if (tpm) {
+        ph[o].x_sum = in[i].x_sum;
+        ph[o].xchg = in[i].xchg;
+        if (in[i].xchg && (in[i].g.nseg != 1 || in[i].g.seg[0].mode != kStore)) return cudaErrorInvalidValue;
+        if (in[i].x_sum && in[i].g.K != tp->hidden) return cudaErrorInvalidValue;
+      } else if (in[i].x_sum || in[i].xchg) {
+        return cudaErrorInvalidValue;
+      }
       need = std::max(need, slot);
       Umax = std::max(Umax, ph[o].U);
       redmax = std::max(redmax, ph[o].red_floats);
@@ -1119,6 +1255,63 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
     delete P;
     return cudaErrorInvalidValue;
   }
+  if (tpm) {
+    // exchange k of a launch: inbox slot k & 1; the residual before it is the
+    // phase's own input (the embedding) for k = 0, else buffer (k - 1) & 1,
+    // and the residual after it goes to buffer k & 1
+    P->tp = *tp;
+    int k = 0, last = -1;
+    for (int i = 0, o = 0; i < n; ++i, ++o) {
+      PhaseDev& d = ph[o];
+      if (in[i].kind != 0) {
+        ++o;
+        continue;
+      }
+      if (d.x_sum) {
+        if (last < 0) {
+          delete P;
+          return cudaErrorInvalidValue;  // no exchange before it
+        }
+        d.x_xk = last;
+      }
+      if (d.xchg) {
+        d.xchg_k = k;
+        last = k++;
+      }
+    }
+    P->n_xchg = k;
+    int max_xk = -1;  // the last exchange whose sum a later phase reads
+    for (const PhaseDev& d : ph)
+      if (d.kind == 0 && d.x_sum) max_xk = std::max(max_xk, d.x_xk);
+    if (k == 0 || !ph[nph - 1].xchg) {  // the last phase gathers the output to every rank
+      delete P;
+      return cudaErrorInvalidValue;
+    }
+    cudaError_t e = cudaMalloc(&P->arena, arena_bytes(P->tp));
+    if (e == cudaSuccess) e = cudaMemset(P->arena, 0, arena_bytes(P->tp));
+    if (e != cudaSuccess) {
+      if (P->arena) cudaFree(P->arena);
+      delete P;
+      return e;
+    }
+    for (int i = 0, o = 0; i < n; ++i, ++o) {
+      PhaseDev& d = ph[o];
+      if (in[i].kind != 0) {
+        ++o;
+        continue;
+      }
+      if (d.x_sum) {
+        const int x = d.x_xk;
+        d.inbox = reinterpret_cast<const float*>(P->arena + inbox_off(P->tp, x & 1));
+        d.xr_prev = x == 0 ? in[i].g.x : reinterpret_cast<const float*>(P->arena + xr_off(P->tp, (x - 1) & 1));
+        d.xr_next = x < max_xk ? reinterpret_cast<float*>(P->arena + xr_off(P->tp, x & 1)) : nullptr;
+      }
+    }
+    P->table = ph;
+    P->bound = false;
+    *out = P;
+    return cudaSuccess;
+  }
   cudaError_t e = cudaMalloc(&P->dev, sizeof(PhaseDev) * (size_t)nph);
   if (e == cudaSuccess)
     e = cudaMemcpy(P->dev, ph.data(), sizeof(PhaseDev) * (size_t)nph, cudaMemcpyHostToDevice);
@@ -1134,7 +1327,37 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
 void step_plan_free(StepPlan* p) {
   if (!p) return;
   if (p->dev) cudaFree(p->dev);
+  if (p->arena) cudaFree(p->arena);
   delete p;
+}
+
+void* step_plan_tp_arena(const StepPlan* p) { return p ? p->arena : nullptr; }
+
+cudaError_t step_plan_tp_bind(StepPlan* p, void* const* arenas, float* const* outputs) {
+  if (!p || p->bound || !p->arena) return cudaErrorInvalidValue;
+  const StepTp& t = p->tp;
+  for (int r = 0; r < t.world; ++r) {
+    if (!arenas[r] || !outputs[r]) return cudaErrorInvalidValue;
+    p->xctr_rank[r] = static_cast<unsigned long long*>(arenas[r]);
+  }
+  for (PhaseDev& d : p->table) {
+    if (d.kind != 0 || !d.xchg) continue;
+    for (int r = 0; r < t.world; ++r)
+      d.xdst[r] = d.xchg == 1
+                      ? reinterpret_cast<float*>(static_cast<uint8_t*>(arenas[r]) + inbox_off(t, d.xchg_k & 1)) +
+                            (size_t)t.rank * t.hidden
+                      : outputs[r] + t.gather_offset;
+  }
+  cudaError_t e = cudaMalloc(&p->dev, sizeof(PhaseDev) * p->table.size());
+  if (e == cudaSuccess)
+    e = cudaMemcpy(p->dev, p->table.data(), sizeof(PhaseDev) * p->table.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (p->dev) cudaFree(p->dev);
+    p->dev = nullptr;
+    return e;
+  }
+  p->bound = true;
+  return cudaSuccess;
 }
 
 int step_plan_splits(const StepPlan* p) { return p ? p->splits : 0; }
@@ -1142,9 +1365,17 @@ int step_plan_grid(const StepPlan* p) { return p ? p->grid : 0; }
 
 cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope, float eps,
                         float* part, uint32_t* ctr, int32_t* err, const LogitCands* cands, cudaStream_t s) {
+  if (!plan->bound) return cudaErrorInvalidValue;
   StepParams p{};
   p.ph = plan->dev;
   p.nph = plan->nph;
+  p.tp_world = plan->tp.world;
+  p.n_xchg = plan->n_xchg;
+  if (plan->tp.world > 1) {
+    p.xctr = reinterpret_cast<unsigned long long*>(plan->arena);
+    p.launches = reinterpret_cast<unsigned long long*>(plan->arena + 8);
+    for (int r = 0; r < plan->tp.world; ++r) p.xctr_rank[r] = plan->xctr_rank[r];
+  }
   p.st = st;
   if (cands && cands->val && cands->ctas == plan->grid) p.cands = *cands;
   p.rope = rope;

@@ -122,13 +122,35 @@ struct StepPhaseIn {
   StepGemv g;
   StepAttn a;
   int32_t cand;  // the lm_head phase: leave LogitCands of its output rows
+  // Tensor parallelism (a plan created with a StepTp): the input is the
+  // residual plus the sum of every rank's partial rows of the last exchange
+  // (x_sum), and / or the outputs go to every rank (xchg 1: partial rows into
+  // each rank's inbox, summed by the next phase; 2: rows into each rank's
+  // copy of the whole output at this rank's row offset).
+  int32_t x_sum;
+  int32_t xchg;
 };
+// Tensor-parallel shape of a step plan: this rank, the rank count, the
+// residual width (the rows every exchange carries) and, for the gathered
+// last phase, this rank's row offset in the whole output.
+struct StepTp {
+  int32_t rank, world;
+  int32_t hidden;
+  int64_t gather_offset;
+};
+constexpr int kMaxTp = 8;
 struct StepPlan;
 // Plans the step's phases for `device` (shapes, ring, shared memory) and
 // uploads the phase table; fails (cudaErrorInvalidValue) for block types or
 // shapes the step kernel does not take, so the caller keeps per-launch kernels.
 cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv, int64_t max_seq,
-                             int device, StepPlan** out);
+                             int device, StepPlan** out, const StepTp* tp = nullptr);
+// Tensor-parallel plans: the device allocation every rank must map (the
+// exchange inboxes and counters), and the binding of every rank's mapping of
+// it and of its whole-output buffer (indexed by rank, this rank's own
+// included); the plan launches only after the binding.
+void* step_plan_tp_arena(const StepPlan* p);
+cudaError_t step_plan_tp_bind(StepPlan* p, void* const* arenas, float* const* outputs);
 void step_plan_free(StepPlan* p);
 int step_plan_splits(const StepPlan* p);
 int step_plan_grid(const StepPlan* p);
