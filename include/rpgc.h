@@ -104,15 +104,29 @@ RPGC_API int32_t rpgc_model_upload(int device, const rpgc_model_config* cfg,
 /* Parses a GGUF v1-v3 file (src/gguf.cc:69-160), reads the qwen3.*
  * hyper-parameters (src/model.cc:159-211) and uploads it. */
 RPGC_API int32_t rpgc_model_load_gguf(int device, const char* path, int32_t max_pos);
-/* Tensor parallelism (the 8B shape: column-split q/k/v/gate/up and untied
- * output, row-split o and down, one NCCL all-reduce after each row-split
- * matmul, the logits' vocabulary slices all-gathered).  One process (or
- * thread) per GPU: one rank calls rpgc_tp_id (a 128-byte NCCL unique id),
- * every rank passes the same bytes with its rank to rpgc_model_upload_tp and
- * then makes the same session calls in the same order (each holds
- * collectives).  The tensor table is the whole model's; each rank uploads its
- * shard.  Needs libnccl.so.2 at run time. */
+/* Tensor parallelism (the 8B shape: row-split q/k/v/gate/up and untied
+ * output, column-split o and down).  Prefill: one NCCL all-reduce after each
+ * column-split matmul, the logits' vocabulary slices all-gathered.  Decode:
+ * the persistent step kernel of every rank stores its partial rows into every
+ * rank's inbox over peer memory (no collective call per token).  One process
+ * per GPU: one rank calls rpgc_tp_id (a 128-byte NCCL unique id), every rank
+ * passes the same bytes with its rank to rpgc_model_upload_tp and then makes
+ * the same session calls in the same order (each holds collectives or
+ * cross-rank waits).  The tensor table is the whole model's; each rank
+ * uploads its shard.  Needs libnccl.so.2 at run time. */
 RPGC_API int rpgc_tp_id(void* id, int64_t bytes);
+/* One rank's shard of a tensor-parallel model: its head, kv-head and
+ * intermediate counts, the row ranges [begin, end) it holds of attn_q,
+ * attn_k / attn_v, ffn_gate / ffn_up and the untied output (vocabulary), and
+ * the column ranges of attn_output and ffn_down.  Checks what
+ * rpgc_model_upload_tp checks of the shapes (every count divides by world);
+ * needs no device.  rpgc_model_upload_tp takes its ranges from here. */
+typedef struct rpgc_tp_shard {
+  int32_t n_heads, n_kv_heads, intermediate;
+  int64_t q_rows[2], kv_rows[2], ffn_rows[2], vocab_rows[2];
+  int64_t o_cols[2], down_cols[2];
+} rpgc_tp_shard;
+RPGC_API int rpgc_tp_shard_of(const rpgc_model_config* cfg, int32_t rank, int32_t world, rpgc_tp_shard* out);
 RPGC_API int32_t rpgc_model_upload_tp(int device, const rpgc_model_config* cfg,
                                       const rpgc_tensor* tensors, int32_t n_tensors, int32_t rank,
                                       int32_t world, const void* id);

@@ -54,6 +54,13 @@ class ModelConfig(C.Structure):
                 ("rope_theta", C.c_float), ("rms_eps", C.c_float)]
 
 
+class TpShard(C.Structure):
+    """rpgc_tp_shard: one rank's head counts and row / column ranges."""
+    _fields_ = [("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("intermediate", C.c_int32),
+                ("q_rows", C.c_int64 * 2), ("kv_rows", C.c_int64 * 2), ("ffn_rows", C.c_int64 * 2),
+                ("vocab_rows", C.c_int64 * 2), ("o_cols", C.c_int64 * 2), ("down_cols", C.c_int64 * 2)]
+
+
 class GenOpts(C.Structure):
     _fields_ = [("max_tokens", C.c_int32), ("stop_ids", C.POINTER(C.c_int32)),
                 ("n_stop", C.c_int32), ("temperature", C.c_float), ("top_k", C.c_int32),
@@ -97,6 +104,7 @@ def lib() -> C.CDLL:
         "rpgc_device_count": ([], C.c_int),
         "rpgc_model_upload": ([C.c_int, C.POINTER(ModelConfig), C.POINTER(Tensor), i32], i32),
         "rpgc_tp_id": ([C.c_void_p, C.c_int64], C.c_int),
+        "rpgc_tp_shard_of": ([C.POINTER(ModelConfig), i32, i32, C.POINTER(TpShard)], C.c_int),
         "rpgc_model_upload_tp": ([C.c_int, C.POINTER(ModelConfig), C.POINTER(Tensor), i32, i32, i32,
                                   C.c_void_p], i32),
         "rpgc_model_load_gguf": ([C.c_int, C.c_char_p, i32], i32),
@@ -364,6 +372,21 @@ def generate_batch(sessions, max_tokens: int, stop_ids=(), temperature: float = 
     _check(lib().rpgc_generate_batch(C.cast(handles, C.c_void_p), n, C.byref(o), out.ctypes.data,
                                      n_out.ctypes.data))
     return [out[i, : n_out[i]].copy() for i in range(n)]
+
+
+def tp_shard(shape, rank: int, world: int) -> dict:
+    """Rank `rank`'s shard of a `world`-way tensor-parallel model of `shape`
+    (rpgc_tp_shard_of, the ranges rpgc_model_upload_tp uploads): head counts
+    and [begin, end) row / column ranges per matrix kind.  Needs no device."""
+    cfg = ModelConfig(shape.n_layers, shape.hidden, shape.n_heads, shape.n_kv_heads, shape.head_dim,
+                      shape.intermediate, shape.vocab, shape.context_length, shape.context_length,
+                      shape.rope_theta, shape.rms_eps)
+    out = TpShard()
+    _check(lib().rpgc_tp_shard_of(C.byref(cfg), rank, world, C.byref(out)))
+    d = {k: getattr(out, k) for k in ("n_heads", "n_kv_heads", "intermediate")}
+    for k in ("q_rows", "kv_rows", "ffn_rows", "vocab_rows", "o_cols", "down_cols"):
+        d[k] = (int(getattr(out, k)[0]), int(getattr(out, k)[1]))
+    return d
 
 
 def tp_unique_id() -> bytes:

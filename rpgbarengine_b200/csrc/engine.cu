@@ -386,6 +386,34 @@ void upload_pieces(uint8_t* blob, const std::vector<Piece>& pieces, int device) 
   if (failed) fail(RPGC_E_CUDA, "model upload: %s", err.c_str());
 }
 
+// Rank `rank`'s shard of a tensor-parallel model (world ranks): whole heads,
+// kv heads, intermediate rows and vocabulary rows, an equal contiguous range
+// per rank in rank order.
+rpgc_tp_shard tp_shard_of(const rpgc_model_config& c, int32_t rank, int32_t world) {
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    fail(RPGC_E_ARG, "tensor-parallel rank %d of %d", rank, world);
+  if (c.n_heads <= 0 || c.n_kv_heads <= 0 || c.intermediate <= 0 || c.vocab <= 0 || c.head_dim <= 0)
+    fail(RPGC_E_ARG, "incomplete model config");
+  if (world > 1 && (c.n_heads % world || c.n_kv_heads % world || c.intermediate % world || c.vocab % world))
+    fail(RPGC_E_ARG, "heads %d, kv heads %d, intermediate %d and vocab %d must divide by %d ranks",
+         c.n_heads, c.n_kv_heads, c.intermediate, c.vocab, world);
+  rpgc_tp_shard t{};
+  t.n_heads = c.n_heads / world;
+  t.n_kv_heads = c.n_kv_heads / world;
+  t.intermediate = c.intermediate / world;
+  auto range = [&](int64_t per, int64_t* r) {
+    r[0] = per * rank;
+    r[1] = per * (rank + 1);
+  };
+  range((int64_t)t.n_heads * c.head_dim, t.q_rows);
+  range((int64_t)t.n_kv_heads * c.head_dim, t.kv_rows);
+  range(t.intermediate, t.ffn_rows);
+  range(c.vocab / world, t.vocab_rows);
+  range((int64_t)t.n_heads * c.head_dim, t.o_cols);
+  range(t.intermediate, t.down_cols);
+  return t;
+}
+
 // Uploads the model, or with world > 1 rank `rank`'s tensor-parallel shard:
 // q/k/v/gate/up and the untied output split by rows (heads, intermediate
 // rows, vocabulary), o and down by columns (the same block range of every
@@ -406,15 +434,11 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
       fail(RPGC_E_ARG, "GQA group %d unsupported (1, 2, 4 or 8)", g);
   }
   if (c.hidden % 256 || c.intermediate % 32) fail(RPGC_E_ARG, "hidden/intermediate not block aligned");
-  if (world < 1 || world > 64 || rank < 0 || rank >= world)
-    fail(RPGC_E_ARG, "tensor-parallel rank %d of %d", rank, world);
-  if (world > 1 && (c.n_heads % world || c.n_kv_heads % world || c.intermediate % world || c.vocab % world))
-    fail(RPGC_E_ARG, "heads %d, kv heads %d, intermediate %d and vocab %d must divide by %d ranks",
-         c.n_heads, c.n_kv_heads, c.intermediate, c.vocab, world);
+  const rpgc_tp_shard sh = tp_shard_of(c, rank, world);
   rpgc_model_config cl = c;  // this rank's shapes
-  cl.n_heads /= world;
-  cl.n_kv_heads /= world;
-  cl.intermediate /= world;
+  cl.n_heads = sh.n_heads;
+  cl.n_kv_heads = sh.n_kv_heads;
+  cl.intermediate = sh.intermediate;
   if (!gemv_supported(c.hidden, true) || !gemv_supported(cl.intermediate, false) ||
       !gemv_supported((int64_t)cl.n_heads * c.head_dim, false))
     fail(RPGC_E_ARG, "decode kernels need hidden, intermediate and heads*head_dim to be multiples of "
@@ -476,17 +500,15 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
     piece_of[t] = pieces.size();
     pieces.push_back(pc);
   };
-  auto rows_of = [&](const rpgc_tensor* t) {  // this rank's row range
-    const int64_t r = t->dims[1] / world;
-    add(t, world > 1 ? 1 : 0, r * rank, r * (rank + 1));
+  auto rows_of = [&](const rpgc_tensor* t, const int64_t* r) {  // this rank's row range
+    add(t, world > 1 ? 1 : 0, r[0], r[1]);
   };
-  auto cols_of = [&](const rpgc_tensor* t) {  // this rank's column range
-    const int64_t k = t->dims[0] / world;
+  auto cols_of = [&](const rpgc_tensor* t, const int64_t* k) {  // this rank's column range
     int64_t be = 0, bb = 0;
-    if (!ggml_block(t->type, &be, &bb) || k % be)
-      fail(RPGC_E_ARG, "tensor %s: %lld columns per rank split a %lld-element block", t->name,
-           (long long)k, (long long)be);
-    add(t, world > 1 ? 2 : 0, k * rank, k * (rank + 1));
+    if (!ggml_block(t->type, &be, &bb) || k[0] % be || k[1] % be)
+      fail(RPGC_E_ARG, "tensor %s: the columns per rank (%lld) split a %lld-element block", t->name,
+           (long long)(k[1] - k[0]), (long long)be);
+    add(t, world > 1 ? 2 : 0, k[0], k[1]);
   };
   const rpgc_tensor* emb = require("token_embd.weight");
   check_matrix(emb, c.vocab, H);
@@ -494,7 +516,7 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
   const rpgc_tensor* out = find("output.weight");
   if (out) {
     check_matrix(out, c.vocab, H);
-    rows_of(out);
+    rows_of(out, sh.vocab_rows);
   }
   const rpgc_tensor* onorm = require("output_norm.weight");
   check_norm(onorm, H);
@@ -529,13 +551,13 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
     check_matrix(t.u, F, H);
     check_matrix(t.d, H, F);
     for (const rpgc_tensor* x : {t.an, t.fn, t.qn, t.kn}) add(x, 0, 0, 0);
-    rows_of(t.q);
-    rows_of(t.k);
-    rows_of(t.v);
-    cols_of(t.o);
-    rows_of(t.g);
-    rows_of(t.u);
-    cols_of(t.d);
+    rows_of(t.q, sh.q_rows);
+    rows_of(t.k, sh.kv_rows);
+    rows_of(t.v, sh.kv_rows);
+    cols_of(t.o, sh.o_cols);
+    rows_of(t.g, sh.ffn_rows);
+    rows_of(t.u, sh.ffn_rows);
+    cols_of(t.d, sh.down_cols);
   }
   size_t total = 0;
   for (Piece& pc : pieces) {
@@ -574,8 +596,8 @@ int32_t upload(int device, const rpgc_model_config& cfg, const rpgc_tensor* tens
     model->lm_head = mat(out);
   } else {  // tied: this rank's vocabulary rows of the embedding table
     model->lm_head = model->embd;
-    model->lm_head.rows = c.vocab / world;
-    model->lm_head.w = model->embd.w + (int64_t)rank * model->lm_head.rows * model->embd.row_bytes;
+    model->lm_head.rows = sh.vocab_rows[1] - sh.vocab_rows[0];
+    model->lm_head.w = model->embd.w + sh.vocab_rows[0] * model->embd.row_bytes;
   }
   model->out_norm = vec(onorm);
   model->layers.resize(c.n_layers);
@@ -1743,6 +1765,14 @@ int rpgc_tp_id(void* id, int64_t bytes) {
     const ncclResult_t r = api->get_id(&u);
     if (r != ncclSuccess) fail(RPGC_E_CUDA, "ncclGetUniqueId: %s", api->error_string(r));
     std::memcpy(id, &u, sizeof(u));
+    return RPGC_OK;
+  });
+}
+
+int rpgc_tp_shard_of(const rpgc_model_config* cfg, int32_t rank, int32_t world, rpgc_tp_shard* out) {
+  return guard([&] {
+    if (!cfg || !out) fail(RPGC_E_ARG, "null argument");
+    *out = tp_shard_of(*cfg, rank, world);
     return RPGC_OK;
   });
 }
