@@ -175,12 +175,15 @@ __device__ __forceinline__ void phase_wait(const StepParams& P, uint32_t target,
 // thread 0's release, which is cumulative at GPU scope (no separate fence).
 // An exchange phase first adds one to every rank's arrival counter with a
 // release at system scope, which covers the CTA's stores to the peers.
+template <bool TP>
 __device__ __forceinline__ void phase_signal(const StepParams& P, const PhaseDev& ph, int tid) {
   csync();  // every consumer's output of this phase is written
   if (tid == 0) {
-    if (ph.xchg)
-      for (int r = 0; r < P.tp_world; ++r)
-        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r]) : "memory");
+    if constexpr (TP) {
+      if (ph.xchg)
+        for (int r = 0; r < P.tp_world; ++r)
+          asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r]) : "memory");
+    }
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
   }
 }
@@ -319,6 +322,7 @@ __device__ __forceinline__ void write_owned(float* dst, int e, float4 a, float4 
 // (two float4 of x each, coalesced); the RMSNorm gains are loaded before the
 // phase barrier (they are constant), x after it (written by other CTAs, so
 // read through L2), every load of the thread in flight at once.
+template <bool TP>
 __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDev& ph, uint32_t target,
                                               unsigned long long L, int tid, int lane, int warp, double* dred,
                                               uint4* lim, float* ucon) {
@@ -336,7 +340,8 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
     }
   }
   int own_lo = 0, own_hi = 0;  // tensor parallel: this CTA's rows of the new residual
-  if (ph.x_sum) {
+  const bool xs = TP && ph.x_sum;
+  if (xs) {
     xchg_wait(P, L, ph.x_xk, tid);
     seg_rows(K, &own_lo, &own_hi);
   } else {
@@ -351,7 +356,7 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int i = (b0 + k) * kNC + tid;
-      if (ph.x_sum) {
+      if (xs) {
         v0[k] = i < NI ? xsum4(P, ph, 8 * i) : zero;
         v1[k] = i < NI ? xsum4(P, ph, 8 * i + 4) : zero;
       } else {
@@ -359,7 +364,7 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
         v1[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
       }
     }
-    if (ph.x_sum && ph.xr_next) {
+    if (xs && ph.xr_next) {
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int i = (b0 + k) * kNC + tid;
@@ -403,21 +408,22 @@ __device__ __forceinline__ float norm_factor(const StepParams& P, const PhaseDev
 
 // A stored row total: into the segment's output, or for an exchange phase
 // into every rank's destination (plain stores, peers' memory included).
+template <bool TP>
 __device__ __forceinline__ void out_row(const StepParams& P, const PhaseDev& ph, const GemvSeg& G, int32_t row,
                                         float t) {
-  if (ph.xchg) {
+  if (TP && ph.xchg) {
     for (int r = 0; r < P.tp_world; ++r) ph.xdst[r][row] = t;
   } else {
     G.out[row] = t;
   }
 }
 
-template <uint32_t TM>
+template <uint32_t TM, bool TP>
 __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& ph, uint32_t target,
                                            unsigned long long L, RingPos* rpp, uint64_t* full, uint64_t* empty,
                                            const SDesc* desc, uint32_t ring32, double* dred, uint4* lim, float* ucon,
                                            float* red, int tid, int lane, int warp) {
-  gemv_prologue(P, ph, target, L, tid, lane, warp, dred, lim, ucon);
+  gemv_prologue<TP>(P, ph, target, L, tid, lane, warp, dred, lim, ucon);
   const int U = ph.U, S = ph.S, Ur = U | 1, NS = P.stages;
   // this CTA's rows of each logical segment, once per phase
   int slo[3] = {0, 0, 0}, sn[3] = {0, 0, 0};
@@ -543,7 +549,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
         const int32_t row = pick3(slo, ll) + a.j;
         if (L.pair) ph.seg[L.first + 1].out[row] = silu_mul(t, other);
         else if (G.mode == kAdd) G.out[row] = (b0 == 0 ? resid : __ldcg(G.out + row)) + t;
-        else out_row(P, ph, G, row, t);
+        else out_row<TP>(P, ph, G, row, t);
       }
     }
     *rpp = rp;
@@ -585,7 +591,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
           const int32_t row = chunk_r0 + j;
           if (L.pair) up_out[row] = silu_mul(t, other);
           else if (G.mode == kAdd) G.out[row] += t;
-          else out_row(P, ph, G, row, t);
+          else out_row<TP>(P, ph, G, row, t);
         }
       }
       chunk0 = k + 1;
@@ -912,7 +918,7 @@ __device__ __noinline__ void cand_phase(const StepParams& P, const PhaseDev& ph,
   }
 }
 
-template <uint32_t TM, int G>
+template <uint32_t TM, int G, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);             // [kMaxStages]
@@ -955,9 +961,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   // tensor parallelism: this launch's number (every CTA of a launch adds
   // one, and a launch starts after the previous one ended)
   unsigned long long* launch_s = reinterpret_cast<unsigned long long*>(smem + 512);
-  if (P.tp_world > 1 && tid == 0) *launch_s = atomicAdd(P.launches, 1ull) / gridDim.x;
+  if constexpr (TP) {
+    if (tid == 0) *launch_s = atomicAdd(P.launches, 1ull) / gridDim.x;
+  }
   csync();
-  const unsigned long long L = P.tp_world > 1 ? *launch_s : 0ull;
+  const unsigned long long L = TP ? *launch_s : 0ull;
 #pragma unroll 1
   for (int p = 0; p < P.nph; ++p) {
     const PhaseDev& ph = pbuf[p & 1];
@@ -968,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       cp_async16(reinterpret_cast<uint4*>(pbuf + ((p + 1) & 1)) + tid,
                  reinterpret_cast<const uint4*>(P.ph + p + 1) + tid);
     if (ph.kind == 0) {
-      gemv_phase<TM>(P, ph, target, L, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
+      gemv_phase<TM, TP>(P, ph, target, L, &it, full, empty, desc, ring32, dred, lim, ucon, red, tid, lane, warp);
       if (ph.cand && P.cands.val)  // the phase's reduction buffers are free again
         cand_phase(P, ph, lane, warp, reinterpret_cast<uint64_t*>(red), reinterpret_cast<int*>(lim));
     } else if (ph.kind == 1) {
@@ -977,11 +985,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       merge_phase<G>(P, ph, target, tid, scratch);
     }
     if (tid < kPhaseChunks) cp_async_wait_all();
-    phase_signal(P, ph, tid);
+    phase_signal<TP>(P, ph, tid);
   }
   // tensor parallelism: the last exchange (every rank's rows of the output)
   // has arrived before the kernel ends, so the launches after it read it whole
-  if (P.tp_world > 1 && blockIdx.x == 0) xchg_wait(P, L, P.n_xchg - 1, tid);
+  if constexpr (TP) {
+    if (blockIdx.x == 0) xchg_wait(P, L, P.n_xchg - 1, tid);
+  }
 }
 
 // ------------------------------------------------------------------ host
@@ -1058,13 +1068,13 @@ int sms_of(int dev) {
   return n > 0 ? n : 148;
 }
 
-template <uint32_t TM, int G>
+template <uint32_t TM, int G, bool TP>
 cudaError_t launch_g(const StepParams& p, int grid, int smem, cudaStream_t s) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && configured[dev] < smem) {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel<TM, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<TM, G, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
@@ -1078,50 +1088,54 @@ cudaError_t launch_g(const StepParams& p, int grid, int smem, cudaStream_t s) {
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, step_kernel<TM, G>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, step_kernel<TM, G, TP>, p);
   if (e == cudaSuccess) count_launches(1);
   return e;
 }
 
 // Whether one CTA of the instantiation fits an SM with `smem` bytes.
-template <uint32_t TM, int G>
+template <uint32_t TM, int G, bool TP>
 bool fits_g(int smem) {
-  if (cudaFuncSetAttribute(step_kernel<TM, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+  if (cudaFuncSetAttribute(step_kernel<TM, G, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel<TM, G>, kThreads, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel<TM, G, TP>, kThreads, smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
   return n >= 1;
 }
 
-template <uint32_t TM>
+template <uint32_t TM, bool TP>
 bool fits_tm(int G, int smem) {
   switch (G) {
-    case 1: return fits_g<TM, 1>(smem);
-    case 2: return fits_g<TM, 2>(smem);
-    case 4: return fits_g<TM, 4>(smem);
-    case 8: return fits_g<TM, 8>(smem);
+    case 1: return fits_g<TM, 1, TP>(smem);
+    case 2: return fits_g<TM, 2, TP>(smem);
+    case 4: return fits_g<TM, 4, TP>(smem);
+    case 8: return fits_g<TM, 8, TP>(smem);
     default: return false;
   }
 }
 
-bool fits(uint32_t mask, int G, int smem) {
-  if ((mask & ~(kMQ4K | kMQ6K)) == 0) return fits_tm<kMQ4K | kMQ6K>(G, smem);
-  if (mask == kMQ80) return fits_tm<kMQ80>(G, smem);
-  return fits_tm<kMQ4K | kMQ6K | kMQ80>(G, smem);
+// Instantiations: one per block-type mix and query group; the
+// tensor-parallel kernel (exchanges compiled in) for all-Q8_0 models and for
+// any mix.
+bool fits(uint32_t mask, int G, int smem, bool tp) {
+  if (tp) return mask == kMQ80 ? fits_tm<kMQ80, true>(G, smem) : fits_tm<kMQ4K | kMQ6K | kMQ80, true>(G, smem);
+  if ((mask & ~(kMQ4K | kMQ6K)) == 0) return fits_tm<kMQ4K | kMQ6K, false>(G, smem);
+  if (mask == kMQ80) return fits_tm<kMQ80, false>(G, smem);
+  return fits_tm<kMQ4K | kMQ6K | kMQ80, false>(G, smem);
 }
 
-template <uint32_t TM>
+template <uint32_t TM, bool TP>
 cudaError_t launch_tm(const StepParams& p, int G, int grid, int smem, cudaStream_t s) {
   switch (G) {
-    case 1: return launch_g<TM, 1>(p, grid, smem, s);
-    case 2: return launch_g<TM, 2>(p, grid, smem, s);
-    case 4: return launch_g<TM, 4>(p, grid, smem, s);
-    case 8: return launch_g<TM, 8>(p, grid, smem, s);
+    case 1: return launch_g<TM, 1, TP>(p, grid, smem, s);
+    case 2: return launch_g<TM, 2, TP>(p, grid, smem, s);
+    case 4: return launch_g<TM, 4, TP>(p, grid, smem, s);
+    case 8: return launch_g<TM, 8, TP>(p, grid, smem, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1251,7 +1265,7 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
         L.m = per_cta;
     }
   }
-  if (!fits(mask, G, g.smem)) {
+  if (!fits(mask, G, g.smem, tpm)) {
     delete P;
     return cudaErrorInvalidValue;
   }
@@ -1395,9 +1409,13 @@ cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope
   p.red_off = plan->geo.red_off;
   p.ring_off = plan->geo.ring_off;
   const uint32_t m = plan->mask;
-  if ((m & ~(kMQ4K | kMQ6K)) == 0) return launch_tm<kMQ4K | kMQ6K>(p, plan->G, plan->grid, plan->geo.smem, s);
-  if (m == kMQ80) return launch_tm<kMQ80>(p, plan->G, plan->grid, plan->geo.smem, s);
-  return launch_tm<kMQ4K | kMQ6K | kMQ80>(p, plan->G, plan->grid, plan->geo.smem, s);
+  if (plan->tp.world > 1) {
+    if (m == kMQ80) return launch_tm<kMQ80, true>(p, plan->G, plan->grid, plan->geo.smem, s);
+    return launch_tm<kMQ4K | kMQ6K | kMQ80, true>(p, plan->G, plan->grid, plan->geo.smem, s);
+  }
+  if ((m & ~(kMQ4K | kMQ6K)) == 0) return launch_tm<kMQ4K | kMQ6K, false>(p, plan->G, plan->grid, plan->geo.smem, s);
+  if (m == kMQ80) return launch_tm<kMQ80, false>(p, plan->G, plan->grid, plan->geo.smem, s);
+  return launch_tm<kMQ4K | kMQ6K | kMQ80, false>(p, plan->G, plan->grid, plan->geo.smem, s);
 }
 
 }  // namespace rpgc
