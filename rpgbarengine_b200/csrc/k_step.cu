@@ -615,12 +615,14 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, const PhaseDev& 
   if (has_item) attn_range(pos, P.splits, split, &c0, &c1);
   const bool owner = has_item && c0 <= pos && pos < c1;
   const float* cs = P.rope + (int64_t)pos * 128;
-  // scratch: qs[G][128] | wo[kAttnWarps][G][128] | wm[kAttnWarps][G] | wl[kAttnWarps][G] | cpart[G][130]
+  // scratch: qs[G][128] | wo[kAttnWarps][G][128] | wm[kAttnWarps][G] | wl[kAttnWarps][G] | kv_new[2][128]
+  // (the new token's k and v are kept in shared memory, not in registers
+  // across the tile loop, where they would push the kernel into spills)
   float* qs = scratch;
   float* wo = qs + G * 128;
   float* wm = wo + kAttnWarps * G * 128;
   float* wl = wm + kAttnWarps * G;
-  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  float* kv_new = wl + kAttnWarps * G;  // [2][128]: the new token's k and v (owner warp)
   // constants of the QK-norm and the rotation, before the phase barrier
   const float4 rc = __ldg(reinterpret_cast<const float4*>(cs + ((4 * lane) & 63)));
   const float4 rs = __ldg(reinterpret_cast<const float4*>(cs + 64 + ((4 * lane) & 63)));
@@ -634,9 +636,11 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, const PhaseDev& 
       reinterpret_cast<float4*>(qs + warp * 128)[lane] = v;
     }
     if (owner && warp == kAttnWarps) {  // the new token's k and v: into the cache
-      knew = __ldcg(reinterpret_cast<const float4*>(A.k_new + kh * 128) + lane);
+      float4 knew = __ldcg(reinterpret_cast<const float4*>(A.k_new + kh * 128) + lane);
       knew = attn::norm_rope_head_pre(knew, gk, rc, rs, P.eps, lane);
-      vnew = __ldcg(reinterpret_cast<const float4*>(A.v_new + kh * 128) + lane);
+      const float4 vnew = __ldcg(reinterpret_cast<const float4*>(A.v_new + kh * 128) + lane);
+      reinterpret_cast<float4*>(kv_new)[lane] = knew;
+      reinterpret_cast<float4*>(kv_new + 128)[lane] = vnew;
       const int64_t off = ((int64_t)kh * P.max_seq + pos) * 128 + 4 * lane;
       *reinterpret_cast<float4*>(A.kc + off) = knew;
       *reinterpret_cast<float4*>(A.vc + off) = vnew;
@@ -660,8 +664,8 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, const PhaseDev& 
     float* Ks = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes);
     float* Vs = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes + P.attn_half);
     if (owner && warp == kAttnWarps && pos >= t0 && pos < t0 + tn) {
-      reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = knew;
-      reinterpret_cast<float4*>(Vs + (pos - t0) * 128)[lane] = vnew;
+      reinterpret_cast<float4*>(Ks + (pos - t0) * 128)[lane] = reinterpret_cast<const float4*>(kv_new)[lane];
+      reinterpret_cast<float4*>(Vs + (pos - t0) * 128)[lane] = reinterpret_cast<const float4*>(kv_new + 128)[lane];
     }
     if (owner) csync();  // the patched row is visible to every scoring warp (CTA-uniform condition)
     if (warp < kAttnWarps) {
@@ -1230,7 +1234,7 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
   g.lim_off = g.ucon_off + ((20 * Umax + 127) & ~127);
   g.red_off = g.lim_off + 192 * Umax;
   int end = g.red_off + ((2 * redmax * 4 + 127) & ~127);
-  const int attn_scratch = (G * 128 + kAttnWarps * G * 128 + 2 * kAttnWarps * G) * 4;
+  const int attn_scratch = (G * 128 + kAttnWarps * G * 128 + 2 * kAttnWarps * G + 256) * 4;
   end = std::max(end, g.lim_off + ((attn_scratch + 127) & ~127));
   // the merge phase stages (output, split) triples of its slice of outputs
   const int merge_scratch = ((n_kv * G * 128 + P->grid - 1) / P->grid) * P->splits * 12;
