@@ -63,14 +63,30 @@ __device__ float counter_uniform(uint64_t seed, uint64_t counter) {
 }
 
 // ---- block reductions (1024 threads) ------------------------------------
-__device__ double block_sum_d(Smem& S, double v) {  // fixed pairing order
+// Fixed pairing order: element i takes i + st for st = NT/2, ..., 1 (the
+// same additions in the same order whatever the layout below).  The first
+// three levels run in shared memory; warp 0 does the rest in registers (its
+// lane l holds elements l + 32k, k < 4, then shuffles down for st < 32).
+__device__ double block_sum_d(Smem& S, double v) {
+  static_assert(NT == 1024, "three shared-memory levels leave 128 elements");
   S.dred[threadIdx.x] = v;
   __syncthreads();
-  for (int st = NT / 2; st > 0; st >>= 1) {
+  for (int st = NT / 2; st >= 128; st >>= 1) {
     if (threadIdx.x < st) S.dred[threadIdx.x] += S.dred[threadIdx.x + st];
     __syncthreads();
   }
-  const double r = S.dred[0];
+  if (threadIdx.x < 32) {
+    const int l = threadIdx.x;
+    double a0 = S.dred[l], a1 = S.dred[l + 32], a2 = S.dred[l + 64], a3 = S.dred[l + 96];
+    a0 += a2;  // st = 64
+    a1 += a3;
+    a0 += a1;  // st = 32
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a0 += __shfl_down_sync(0xffffffffu, a0, o);
+    if (l == 0) S.bcast_d[0] = a0;
+  }
+  __syncthreads();
+  const double r = S.bcast_d[0];
   __syncthreads();
   return r;
 }
@@ -123,21 +139,34 @@ __device__ int block_argmax(Smem& S, float v, int i) {
   __syncthreads();
   return r;
 }
-// exclusive prefix over threads (integers are exact, order irrelevant)
+// exclusive prefix over threads (integers are exact, order irrelevant): a
+// shuffle scan in each warp, then one over the 32 warp totals
 template <typename T>
 __device__ T block_excl_scan(T* buf, T v, T* total) {
-  buf[threadIdx.x] = v;
-  __syncthreads();
-  for (int off = 1; off < NT; off <<= 1) {
-    T add = threadIdx.x >= off ? buf[threadIdx.x - off] : T(0);
-    __syncthreads();
-    buf[threadIdx.x] += add;
-    __syncthreads();
+  static_assert(NT == 1024, "32 warps");
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  const T incl = buf[threadIdx.x];
-  *total = buf[NT - 1];
+  if (lane == 31) buf[w] = x;
   __syncthreads();
-  return incl - v;
+  if (w == 0) {
+    T t = buf[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    buf[32 + lane] = t;
+  }
+  __syncthreads();
+  const T off = w ? buf[32 + w - 1] : T(0);
+  *total = buf[63];
+  __syncthreads();
+  return off + x - v;
 }
 
 __device__ void clear_hist(Smem& S, bool sums) {
@@ -192,15 +221,40 @@ __device__ float kth_largest(Smem& S, const View& V, int m, int k) {
       S.cnt[0][tid] = c;
     }
     __syncthreads();
-    if (tid == 0) {
-      int above = 0, b = 255;
-      for (; b > 0; --b) {
-        const int c = (int)S.cnt[0][b];
-        if (above + c >= krem) break;
-        above += c;
+    if (tid < 32) {
+      // the highest bin b >= 1 whose count from b up reaches krem (0 if none)
+      // and the count above it: lane l holds bins 8l .. 8l+7
+      int c[8], tl = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = (int)S.cnt[0][8 * tid + j];
+        tl += c[j];
       }
-      S.bcast_i[1] = b;
-      S.bcast_i[2] = krem - above;
+      int sfx = tl;  // inclusive suffix over lanes l..31
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_down_sync(0xffffffffu, sfx, o);
+        if (tid + o < 32) sfx += y;
+      }
+      int run = sfx - tl, best = -1, best_above = 0;  // run: count of bins above the lane's
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {
+        const int b = 8 * tid + j;
+        if (b >= 1 && best < 0 && run + c[j] >= krem) {
+          best = b;
+          best_above = run;
+        }
+        run += c[j];
+      }
+      // the highest lane with a qualifying bin holds b*
+      const unsigned q = __ballot_sync(0xffffffffu, best >= 0);
+      const int src = q ? 31 - __clz((int)q) : 0;
+      const int b = q ? __shfl_sync(0xffffffffu, best, src) : 0;
+      const int above = q ? __shfl_sync(0xffffffffu, best_above, src) : __shfl_sync(0xffffffffu, sfx - c[0], 0);
+      if (tid == 0) {
+        S.bcast_i[1] = b;
+        S.bcast_i[2] = krem - above;
+      }
     }
     __syncthreads();
     prefix |= (uint32_t)S.bcast_i[1] << shift;
@@ -321,16 +375,42 @@ __device__ int sample_view(Smem& S, View V, float top_p, float u) {
         S.msum[0][tid] = s;
       }
       __syncthreads();
-      if (tid == 0) {
-        unsigned long long cum = below;
-        int b = 0;
-        for (; b < 256; ++b) {
-          if (cum + S.msum[0][b] > thr_fp) break;
-          cum += S.msum[0][b];
+      if (tid < 32) {
+        // the lowest bin b whose mass from below up to and including it
+        // exceeds thr_fp (256 if none): lane l holds bins 8l .. 8l+7
+        unsigned long long m8[8], tl = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          m8[j] = S.msum[0][8 * tid + j];
+          tl += m8[j];
         }
-        S.bcast_i[1] = b;
-        S.bcast_u[0] = cum;
-        S.bcast_i[3] = (b < 256) ? (int)S.cnt[0][b] : 0;
+        unsigned long long pre = tl;  // inclusive prefix over lanes 0..l
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned long long y = __shfl_up_sync(0xffffffffu, pre, o);
+          if (tid >= o) pre += y;
+        }
+        unsigned long long cum = below + (pre - tl);
+        int best = 256;
+        unsigned long long best_cum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (best == 256 && cum + m8[j] > thr_fp) {
+            best = 8 * tid + j;
+            best_cum = cum;
+          }
+          cum += m8[j];
+        }
+        const unsigned q = __ballot_sync(0xffffffffu, best < 256);
+        const int src = q ? __ffs((int)q) - 1 : 0;
+        const int b = q ? __shfl_sync(0xffffffffu, best, src) : 256;
+        const unsigned long long bc = __shfl_sync(0xffffffffu, best_cum, src);
+        const unsigned long long all = __shfl_sync(0xffffffffu, cum, 31);
+        if (tid == 0) {
+          S.bcast_i[1] = b;
+          S.bcast_u[0] = q ? bc : all;
+          S.bcast_i[3] = (b < 256) ? (int)S.cnt[0][b] : 0;
+        }
       }
       __syncthreads();
       const int b = S.bcast_i[1];

@@ -488,7 +488,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
 #pragma unroll 1
       for (int k = 0; k < nst; ++k, rp.advance(NS)) {
         const int slot = rp.slot;
-        mbar_wait_sleep(&full[slot], rp.parity, P.err);
+        mbar_wait(&full[slot], rp.parity, P.err);
         const SDesc d = desc[slot];
         const int jr0 = (int)d.r - lo;
         rows(d, slot, L, G.type, (int)G.row_bytes, red + base + jr0 * Ur, red + base + (nrows + jr0) * Ur);
@@ -569,7 +569,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
 #pragma unroll 1
     for (int k = 0; k < nst; ++k, rp.advance(NS)) {
       const int slot = rp.slot;
-      mbar_wait_sleep(&full[slot], rp.parity, P.err);
+      mbar_wait(&full[slot], rp.parity, P.err);
       const SDesc d = desc[slot];
       if (k == chunk0) chunk_r0 = (int32_t)d.r;
       const int jr0 = (k - chunk0) * L.m;
@@ -659,7 +659,7 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, const PhaseDev& 
   RingPos rp = *rpp;
   for (int t0 = c0; t0 < c1; t0 += P.tile_pos, rp.advance(NS)) {
     const int slot = rp.slot;
-    mbar_wait_sleep(&full[slot], rp.parity, P.err);
+    mbar_wait(&full[slot], rp.parity, P.err);
     const int tn = min(P.tile_pos, c1 - t0);
     float* Ks = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes);
     float* Vs = reinterpret_cast<float*>(ring + (size_t)slot * P.stage_bytes + P.attn_half);
