@@ -499,12 +499,14 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
     }
     // one reduction over every segment's rows: sum sid of segment l is row
     // (pair ? sid / 2 : sid), half (pair ? sid % 2 : 0); tpr threads per sum
-    // (as many as fill the CTA once, at most 16)
+    // (the most, up to 16, that still take every sum in one pass over the
+    // consumers: measured, a second pass costs more than longer serial sums)
     int total = 0;
 #pragma unroll
     for (int l = 0; l < 3; ++l)
       if (l < ph.nls) total += sn[l] * (ph.ls[l].pair + 1);
-    const int lg = total * 16 <= kNC ? 4 : total * 8 <= kNC ? 3 : 2, tpr = 1 << lg;
+    const int lg = total * 16 <= kNC ? 4 : total * 8 <= kNC ? 3 : total * 4 <= kNC ? 2 : total * 2 <= kNC ? 1 : 0,
+              tpr = 1 << lg;
     struct Sum {
       int l, j, h, bse;
       bool live;
