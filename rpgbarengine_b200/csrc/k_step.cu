@@ -65,6 +65,7 @@ constexpr int kRec = 132;                  // floats per attention partial recor
 constexpr int kMaxItems = 4;               // activation items per consumer thread (K <= 8 * 4 * 480)
 constexpr int kMaxNormItems = 2;           // ... with RMSNorm gains (the first round)
 constexpr int kPhaseBufOff = 640;          // two phase-table entries in shared memory
+constexpr int kCtrStride = 16;             // arrival counters 128 bytes apart (u64 words)
 static_assert(kMaxNormItems == 2 && kMaxItems % 2 == 0, "prologue rounds of two items");
 
 struct SLSeg {     // logical segment: one matrix, or a SwiGLU (gate, up) pair
@@ -111,8 +112,8 @@ struct StepParams {
   // tensor parallelism: exchanges per launch, this rank's arrival counter
   // (every rank's CTAs add one per exchange) and every rank's (mapped), and
   // this rank's launch counter (grid per launch)
-  int32_t tp_world, n_xchg;
-  unsigned long long* xctr;
+  int32_t tp_world, tp_rank, n_xchg;
+  unsigned long long* xctr;    // [kMaxTp][kCtrStride]: one counter per source rank
   unsigned long long* xctr_rank[kMaxTp];
   unsigned long long* launches;
   int32_t stages, stage_bytes, tile_pos, attn_half;
@@ -182,32 +183,37 @@ __device__ __forceinline__ void phase_signal(const StepParams& P, const PhaseDev
     if constexpr (TP) {
       if (ph.xchg)
         for (int r = 0; r < P.tp_world; ++r)
-          asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r]) : "memory");
+          asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r] + P.tp_rank * kCtrStride)
+                       : "memory");
     }
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.ctr) : "memory");
   }
 }
 
-// Bounded wait (thread 0 of the consumers) until every rank's CTAs have
-// signalled exchange k of launch L, then release the other consumers.  The
-// acquire at system scope makes the peers' stores before their signals
-// visible to this CTA.  A wait gives up after ~2 s (a rank that never
-// signals: the error flag is set and the step runs on, so the host sees
-// RPGC_E_TIMEOUT), and once any wait of the launch has given up the others
-// give up within 256 polls.
+// Bounded wait (warp 0 of the consumers, lane r watching source rank r's
+// counter) until every rank's CTAs have signalled exchange k of launch L,
+// then release the other consumers.  The acquires at system scope make the
+// peers' stores before their signals visible to this CTA.  A wait gives up
+// after ~2 s (a rank that never signals: the error flag is set and the step
+// runs on, so the host sees RPGC_E_TIMEOUT), and once any wait of the launch
+// has given up the others give up within 256 polls.
 constexpr uint32_t kMaxXchgPolls = 1u << 21;
 __device__ __forceinline__ void xchg_wait(const StepParams& P, unsigned long long L, int k, int tid) {
-  if (tid == 0) {
+  if (tid < 32) {
     const unsigned long long target =
-        (L * (unsigned long long)P.n_xchg + (unsigned long long)k + 1ull) * (unsigned long long)P.tp_world * gridDim.x;
+        (L * (unsigned long long)P.n_xchg + (unsigned long long)k + 1ull) * (unsigned long long)gridDim.x;
+    bool ok = tid >= P.tp_world;
     uint32_t i = 0;
     for (;;) {
-      unsigned long long v;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(P.xctr) : "memory");
-      if (v >= target) break;
-      ++i;
+      if (!ok) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(P.xctr + tid * kCtrStride) : "memory");
+        ok = v >= target;
+      }
+      if (__all_sync(0xffffffffu, ok)) break;
+      ++i;  // the same count on every lane
       if (i > kMaxXchgPolls || ((i & 255u) == 0 && (*reinterpret_cast<volatile int32_t*>(P.err) & kErrTimeout))) {
-        atomicOr(P.err, kErrTimeout);
+        if (tid == 0) atomicOr(P.err, kErrTimeout);
         break;
       }
       __nanosleep(256);
@@ -1167,7 +1173,10 @@ struct StepPlan {
 };
 
 namespace {
-constexpr size_t kArenaHead = 256;  // arrival counter at 0, launch counter at 8
+// arrival counters (one per source rank, 128 bytes apart) at 0, launch
+// counter at kMaxTp x 128
+constexpr size_t kLaunchOff = (size_t)kMaxTp * kCtrStride * 8;
+constexpr size_t kArenaHead = kLaunchOff + 256;
 size_t inbox_off(const StepTp& t, int slot) { return kArenaHead + (size_t)slot * t.world * t.hidden * 4; }
 size_t xr_off(const StepTp& t, int i) { return inbox_off(t, 2) + (size_t)i * t.hidden * 4; }
 size_t arena_bytes(const StepTp& t) { return xr_off(t, 2); }
@@ -1393,7 +1402,8 @@ cudaError_t step_launch(const StepPlan* plan, DecodeState* st, const float* rope
   p.n_xchg = plan->n_xchg;
   if (plan->tp.world > 1) {
     p.xctr = reinterpret_cast<unsigned long long*>(plan->arena);
-    p.launches = reinterpret_cast<unsigned long long*>(plan->arena + 8);
+    p.launches = reinterpret_cast<unsigned long long*>(plan->arena + kLaunchOff);
+    p.tp_rank = plan->tp.rank;
     for (int r = 0; r < plan->tp.world; ++r) p.xctr_rank[r] = plan->xctr_rank[r];
   }
   p.st = st;
