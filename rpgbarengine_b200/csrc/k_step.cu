@@ -90,10 +90,10 @@ struct alignas(16) PhaseDev {
   SLSeg ls[3];
   const float* x;
   const float* norm_w;
-  const float* inbox;    // x_sum: this rank's inbox of the exchange [world][K]
-  const float* xr_prev;  // x_sum: the residual before the exchange
-  float* xr_next;        // x_sum: the residual after it (each CTA writes its rows)
-  float* xdst[kMaxTp];   // xchg: every rank's destination for this rank's rows
+  const uint64_t* inbox;  // x_sum: this rank's inbox of the exchange [world][K], tagged words
+  const float* xr_prev;   // x_sum: the residual before the exchange
+  float* xr_next;         // x_sum: the residual after it (each CTA writes its rows)
+  void* xdst[kMaxTp];     // xchg: every rank's destination (1: tagged inbox words, 2: floats)
   StepAttn a;
 };
 
@@ -181,7 +181,14 @@ __device__ __forceinline__ void phase_signal(const StepParams& P, const PhaseDev
   csync();  // every consumer's output of this phase is written
   if (tid == 0) {
     if constexpr (TP) {
-      if (ph.xchg)
+      // partial rows (1) carry tags, so their arrival count is relaxed (the
+      // readers check every word); the gathered output (2) is plain floats
+      // read after the kernel: a release covering the CTA's peer stores
+      if (ph.xchg == 1)
+        for (int r = 0; r < P.tp_world; ++r)
+          asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r] + P.tp_rank * kCtrStride)
+                       : "memory");
+      else if (ph.xchg == 2)
         for (int r = 0; r < P.tp_world; ++r)
           asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xctr_rank[r] + P.tp_rank * kCtrStride)
                        : "memory");
@@ -307,12 +314,49 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
+// Tag of exchange k of launch L (inboxes start at 0xFFFFFFFF, which the
+// next 2^32 exchanges do not reach).
+__device__ __forceinline__ uint32_t xtag(const StepParams& P, unsigned long long L, int k) {
+  return (uint32_t)(L * (unsigned long long)P.n_xchg + (unsigned long long)k + 1ull);
+}
+
+// Exchange words: the float's bits in the low half, the exchange's tag in
+// the high half, stored and loaded 64 bits at a time at system scope
+// (single-copy atomic), so a word showing the expected tag holds its value.
+__device__ __forceinline__ void st_xword(void* p, float v, uint32_t tag) {
+  const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// Four words at p (16-byte aligned) -> float4; whether every tag is `tag`.
+__device__ __forceinline__ bool ld_xwords4(const uint64_t* p, uint32_t tag, float4* v) {
+  uint64_t w0, w1, w2, w3;
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w2), "=l"(w3) : "l"(p + 2) : "memory");
+  *v = make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1), __uint_as_float((uint32_t)w2),
+                   __uint_as_float((uint32_t)w3));
+  return ((uint32_t)(w0 >> 32) == tag) & ((uint32_t)(w1 >> 32) == tag) & ((uint32_t)(w2 >> 32) == tag) &
+         ((uint32_t)(w3 >> 32) == tag);
+}
+
 // Elements e..e+3 of an exchange's input: the residual before it plus the
-// ranks' partial rows summed in rank order (the same sum on every rank).
-__device__ __forceinline__ float4 xsum4(const StepParams& P, const PhaseDev& ph, int e) {
-  float4 s = __ldcg(reinterpret_cast<const float4*>(ph.inbox + e));
-  for (int r = 1; r < P.tp_world; ++r)
-    s = add4(s, __ldcg(reinterpret_cast<const float4*>(ph.inbox + (size_t)r * ph.K + e)));
+// ranks' partial rows summed in rank order (the same sum on every rank).  A
+// partial's words are polled until they carry the exchange's tag (the
+// arrival count that let this phase start is relaxed, so a peer's store may
+// land after it); bounded, the error flag set on expiry.
+__device__ __forceinline__ float4 xsum4(const StepParams& P, const PhaseDev& ph, int e, uint32_t tag) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < P.tp_world; ++r) {
+    float4 v;
+    uint32_t n = 0;
+    while (!ld_xwords4(ph.inbox + (size_t)r * ph.K + e, tag, &v)) {
+      if (++n > kMaxBarrierPolls || ((n & 255u) == 0 && (*reinterpret_cast<volatile int32_t*>(P.err) & kErrTimeout))) {
+        atomicOr(P.err, kErrTimeout);
+        break;
+      }
+      __nanosleep(32);
+    }
+    s = r ? add4(s, v) : v;
+  }
   return add4(__ldcg(reinterpret_cast<const float4*>(ph.xr_prev + e)), s);
 }
 
@@ -363,8 +407,8 @@ __device__ __forceinline__ void gemv_prologue(const StepParams& P, const PhaseDe
     for (int k = 0; k < 2; ++k) {
       const int i = (b0 + k) * kNC + tid;
       if (xs) {
-        v0[k] = i < NI ? xsum4(P, ph, 8 * i) : zero;
-        v1[k] = i < NI ? xsum4(P, ph, 8 * i + 4) : zero;
+        v0[k] = i < NI ? xsum4(P, ph, 8 * i, xtag(P, L, ph.x_xk)) : zero;
+        v1[k] = i < NI ? xsum4(P, ph, 8 * i + 4, xtag(P, L, ph.x_xk)) : zero;
       } else {
         v0[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i) : zero;
         v1[k] = i < NI ? __ldcg(reinterpret_cast<const float4*>(ph.x) + 2 * i + 1) : zero;
@@ -416,9 +460,12 @@ __device__ __forceinline__ float norm_factor(const StepParams& P, const PhaseDev
 // into every rank's destination (plain stores, peers' memory included).
 template <bool TP>
 __device__ __forceinline__ void out_row(const StepParams& P, const PhaseDev& ph, const GemvSeg& G, int32_t row,
-                                        float t) {
-  if (TP && ph.xchg) {
-    for (int r = 0; r < P.tp_world; ++r) ph.xdst[r][row] = t;
+                                        float t, unsigned long long L) {
+  if (TP && ph.xchg == 1) {
+    const uint32_t tag = xtag(P, L, ph.xchg_k);
+    for (int r = 0; r < P.tp_world; ++r) st_xword(static_cast<uint64_t*>(ph.xdst[r]) + row, t, tag);
+  } else if (TP && ph.xchg == 2) {
+    for (int r = 0; r < P.tp_world; ++r) static_cast<float*>(ph.xdst[r])[row] = t;
   } else {
     G.out[row] = t;
   }
@@ -426,10 +473,10 @@ __device__ __forceinline__ void out_row(const StepParams& P, const PhaseDev& ph,
 
 template <uint32_t TM, bool TP>
 __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& ph, uint32_t target,
-                                           unsigned long long L, RingPos* rpp, uint64_t* full, uint64_t* empty,
+                                           unsigned long long launch, RingPos* rpp, uint64_t* full, uint64_t* empty,
                                            const SDesc* desc, uint32_t ring32, double* dred, uint4* lim, float* ucon,
                                            float* red, int tid, int lane, int warp) {
-  gemv_prologue<TP>(P, ph, target, L, tid, lane, warp, dred, lim, ucon);
+  gemv_prologue<TP>(P, ph, target, launch, tid, lane, warp, dred, lim, ucon);
   const int U = ph.U, S = ph.S, Ur = U | 1, NS = P.stages;
   // this CTA's rows of each logical segment, once per phase
   int slo[3] = {0, 0, 0}, sn[3] = {0, 0, 0};
@@ -557,7 +604,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
         const int32_t row = pick3(slo, ll) + a.j;
         if (L.pair) ph.seg[L.first + 1].out[row] = silu_mul(t, other);
         else if (G.mode == kAdd) G.out[row] = (b0 == 0 ? resid : __ldcg(G.out + row)) + t;
-        else out_row<TP>(P, ph, G, row, t);
+        else out_row<TP>(P, ph, G, row, t, launch);
       }
     }
     *rpp = rp;
@@ -599,7 +646,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, const PhaseDev& 
           const int32_t row = chunk_r0 + j;
           if (L.pair) up_out[row] = silu_mul(t, other);
           else if (G.mode == kAdd) G.out[row] += t;
-          else out_row<TP>(P, ph, G, row, t);
+          else out_row<TP>(P, ph, G, row, t, launch);
         }
       }
       chunk0 = k + 1;
@@ -1177,7 +1224,7 @@ namespace {
 // counter at kMaxTp x 128
 constexpr size_t kLaunchOff = (size_t)kMaxTp * kCtrStride * 8;
 constexpr size_t kArenaHead = kLaunchOff + 256;
-size_t inbox_off(const StepTp& t, int slot) { return kArenaHead + (size_t)slot * t.world * t.hidden * 4; }
+size_t inbox_off(const StepTp& t, int slot) { return kArenaHead + (size_t)slot * t.world * t.hidden * 8; }
 size_t xr_off(const StepTp& t, int i) { return inbox_off(t, 2) + (size_t)i * t.hidden * 4; }
 size_t arena_bytes(const StepTp& t) { return xr_off(t, 2); }
 }  // namespace
@@ -1318,6 +1365,8 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
     }
     cudaError_t e = cudaMalloc(&P->arena, arena_bytes(P->tp));
     if (e == cudaSuccess) e = cudaMemset(P->arena, 0, arena_bytes(P->tp));
+    if (e == cudaSuccess)  // inbox words: tag 0xFFFFFFFF, no exchange's
+      e = cudaMemset(P->arena + inbox_off(P->tp, 0), 0xFF, inbox_off(P->tp, 2) - inbox_off(P->tp, 0));
     if (e != cudaSuccess) {
       if (P->arena) cudaFree(P->arena);
       delete P;
@@ -1331,7 +1380,7 @@ cudaError_t step_plan_create(const StepPhaseIn* in, int n, int n_heads, int n_kv
       }
       if (d.x_sum) {
         const int x = d.x_xk;
-        d.inbox = reinterpret_cast<const float*>(P->arena + inbox_off(P->tp, x & 1));
+        d.inbox = reinterpret_cast<const uint64_t*>(P->arena + inbox_off(P->tp, x & 1));
         d.xr_prev = x == 0 ? in[i].g.x : reinterpret_cast<const float*>(P->arena + xr_off(P->tp, (x - 1) & 1));
         d.xr_next = x < max_xk ? reinterpret_cast<float*>(P->arena + xr_off(P->tp, x & 1)) : nullptr;
       }
@@ -1372,10 +1421,10 @@ cudaError_t step_plan_tp_bind(StepPlan* p, void* const* arenas, float* const* ou
   for (PhaseDev& d : p->table) {
     if (d.kind != 0 || !d.xchg) continue;
     for (int r = 0; r < t.world; ++r)
-      d.xdst[r] = d.xchg == 1
-                      ? reinterpret_cast<float*>(static_cast<uint8_t*>(arenas[r]) + inbox_off(t, d.xchg_k & 1)) +
-                            (size_t)t.rank * t.hidden
-                      : outputs[r] + t.gather_offset;
+      d.xdst[r] = d.xchg == 1 ? static_cast<void*>(reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(arenas[r]) +
+                                                                               inbox_off(t, d.xchg_k & 1)) +
+                                                   (size_t)t.rank * t.hidden)
+                              : static_cast<void*>(outputs[r] + t.gather_offset);
   }
   cudaError_t e = cudaMalloc(&p->dev, sizeof(PhaseDev) * p->table.size());
   if (e == cudaSuccess)
