@@ -91,7 +91,7 @@ class Clocks:
 # DRAM bytes of one step_kernel launch (ncu dram__bytes_read.sum +
 # dram__bytes_write.sum; the 4B Q4_K_M-mix model after the 512-token prompt,
 # attention over 516 keys)
-STEP_TRAFFIC = 2_795_648_512
+STEP_TRAFFIC = 2_784_180_480
 STEP_TRAFFIC_CTX = 516
 
 
