@@ -212,7 +212,9 @@ RPGC_API int rpgc_generate_batch(const int32_t* sessions, int32_t n, const rpgc_
  * its own options, stop ids and max_tokens).  Each call returns when its
  * batch ends, with its own ids and status; a call that arrives while a
  * batch runs joins the next one.  A call alone after the window decodes
- * unbatched.  Calls that are not eligible (no pending logits, less room
+ * unbatched: with batching on, a call that no other caller joins waits up to
+ * window_us before it starts (the price of the gathering; keep window_us
+ * small, or leave batching off for a single caller).  Calls that are not eligible (no pending logits, less room
  * than max_tokens, invalid options) run unbatched and report their errors
  * as before.  Batched tokens match an unbatched call's within the parity
  * tolerance (the matmuls run on the tensor cores).  max_batch 0 or 1 turns
