@@ -6,12 +6,14 @@
 // (src/kv_cache.cc:29-33), AttentionFromCache with a softmax over [0, pos]
 // (src/qwen3.cc:79-117).
 #include <cooperative_groups.h>
+#include <cstdlib>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "attn_dev.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_dev.cuh"
 
 namespace rpgc {
 namespace {
@@ -541,6 +543,255 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) 
   }
 }
 
+// --------------------------------------------------------------- prefill, tcgen05
+// The same attention (same split, same 2^14 probability scale) on the
+// 5th-generation tensor cores (tcgen05, TMEM accumulators).  One CTA
+// of 8 warps per (head, 128-query tile), heaviest tiles first.  All warps
+// stage operands; query row t is TMEM lane t of both accumulators, and
+// threads t and t + 128 share it (keys 0-31 and 32-63 of each tile, columns
+// 0-63 and 64-127 of the output).  Q gets its QK-norm and RoPE as it is staged
+// and stays in shared memory as hi/lo halves.  Per 64-key tile:
+//   1. the CTA stages K [64 keys][128 dims] and V^T [128 dims][64 keys] as
+//      fp16 hi/lo in K-major tiles with the 128-byte swizzle (V is transposed
+//      as it is staged, so that both products read K-major operands);
+//   2. one thread issues S = Q K^T (M = 128, N = 64; 8 k16 steps over the
+//      dims x 3 products) into TMEM columns [0, 64);
+//   3. a row's two threads read its S row back, mask it (keys past the row's
+//      position or past the chunk), update the running max and sums, and
+//      write P = exp(s - max) 2^14 as an fp16 hi/lo row;
+//   4. they rescale the row of the output accumulator O (TMEM columns
+//      [64, 192)) by c = exp(old max - new max), unless no row of the warp
+//      changed its max;
+//   5. one thread issues O += P V (M = 128, N = 128; 4 k16 steps over the
+//      keys x 3 products).
+// Every stage completes before the next overwrites what it read (the commits'
+// barriers and the CTA barriers between the phases), so one buffer of each
+// operand suffices; all mbarrier waits are bounded.
+constexpr int TQ = 128;
+constexpr int kQPanel = TQ * 128;   // one 64-dim panel of Q: 128 rows x 128 B
+constexpr int kKPanel = KT * 128;   // one 64-dim panel of K: 64 rows x 128 B
+constexpr int kVTile = HD * 128;    // V^T: 128 dim rows x 64 keys (128 B)
+constexpr int kPTile = TQ * 128;    // P: 128 query rows x 64 keys
+constexpr int kTcBytes = 4 * kQPanel + 4 * kKPanel + 2 * kVTile + 2 * kPTile;
+constexpr int kTcSmem = kTcBytes + 1024 + 1024;  // + barriers, + alignment slack
+constexpr uint32_t kTcCols = 256;                // S: [0, 64), O: [64, 192)
+// instruction descriptors: fp16 x fp16 -> fp32, both K-major, M = 128
+constexpr uint32_t kIdS = (1u << 4) | ((uint32_t)(KT >> 3) << 17) | ((uint32_t)(TQ >> 4) << 24);
+constexpr uint32_t kIdO = (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(TQ >> 4) << 24);
+
+__global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs a) {
+  using namespace tc;
+  extern __shared__ uint8_t tsm_raw[];
+  uint8_t* sb = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Qh = sb;                     // 2 panels
+  uint8_t* Ql = Qh + 2 * kQPanel;
+  uint8_t* Kh = Ql + 2 * kQPanel;       // 2 panels
+  uint8_t* Kl = Kh + 2 * kKPanel;
+  uint8_t* Vh = Kl + 2 * kKPanel;
+  uint8_t* Vl = Vh + kVTile;
+  uint8_t* Ph = Vl + kVTile;
+  uint8_t* Pl = Ph + kPTile;
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sb + kTcBytes);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
+
+  const int h = blockIdx.x;
+  const int64_t qt0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * TQ;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.n_heads / a.n_kv, kh = h / G;
+  const float scale = 1.0f / sqrtf((float)HD);
+  const int64_t qpos0 = a.pos0 + qt0;
+  const int64_t nq = min((int64_t)TQ, a.n - qt0);
+  const int64_t key_end = qpos0 + nq;  // keys [0, key_end)
+  const float* kb = a.kc + (int64_t)kh * a.max_seq * HD;
+  const float* vb = a.vc + (int64_t)kh * a.max_seq * HD;
+
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // ---- Q: warp w stages rows w, w + 8, ...; lane l holds dims 4l .. 4l + 3
+  // (rows past the chunk are zeros)
+  for (int row = warp; row < TQ; row += 8) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < nq) {  // warp-uniform: the norm's reduction has every lane
+      v = *reinterpret_cast<const float4*>(a.q + ((qt0 + row) * a.n_heads + h) * HD + 4 * lane);
+      if (a.q_norm) v = norm_rope_head(v, a.q_norm, a.rope + (qpos0 + row) * HD, a.eps, lane);
+    }
+    uint32_t h0, l0, h1, l1;
+    split2(v.x, v.y, &h0, &l0);
+    split2(v.z, v.w, &h1, &l1);
+    const int d = 4 * lane;
+    const uint32_t off = (uint32_t)((d >> 6) * kQPanel) + swz(row, (d & 63) >> 3) + (uint32_t)((d & 7) * 2);
+    *reinterpret_cast<uint2*>(Qh + off) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(Ql + off) = make_uint2(l0, l1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's lane quarter
+  const int r = (warp & 3) * 32 + lane, hf = warp >> 2;  // query row = TMEM lane; key / column half
+  __shared__ float red[2][TQ];  // the two halves' maxima, at the end their sums
+  const int64_t qp = qpos0 + r;
+  float m = kNegBig, l = 0.0f;
+  uint32_t ph = 0;
+
+  for (int64_t k0 = 0; k0 < key_end; k0 += KT) {
+    // ---- 1. all eight warps stage, every load of the tile in flight before
+    // the first conversion: K as 4 items of (key, 8 dims) per thread; V^T as
+    // one 8-key x 4-dim block per thread (warp = 8-key chunk, lane = 4 dims),
+    // transposed in registers into 4 rows of 8 keys
+    {
+      float4 kx[8], vx[8];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int idx = it * 256 + tid, j = idx >> 4, c = idx & 15;
+        const bool ok = k0 + j < key_end;
+        const float4* kp = reinterpret_cast<const float4*>(kb + (k0 + (ok ? j : 0)) * HD + 8 * c);
+        kx[2 * it] = ok ? kp[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        kx[2 * it + 1] = ok ? kp[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t key = k0 + 8 * warp + i;
+        vx[i] = key < key_end ? *reinterpret_cast<const float4*>(vb + key * HD + 4 * lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int idx = it * 256 + tid, j = idx >> 4, c = idx & 15;
+        const float kv[8] = {kx[2 * it].x, kx[2 * it].y, kx[2 * it].z, kx[2 * it].w,
+                             kx[2 * it + 1].x, kx[2 * it + 1].y, kx[2 * it + 1].z, kx[2 * it + 1].w};
+        uint4 hi, lo;
+        split8(kv, &hi, &lo);
+        const uint32_t off = (uint32_t)((c >> 3) * kKPanel) + swz(j, c & 7);
+        *reinterpret_cast<uint4*>(Kh + off) = hi;
+        *reinterpret_cast<uint4*>(Kl + off) = lo;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float vv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vv[i] = e == 0 ? vx[i].x : e == 1 ? vx[i].y : e == 2 ? vx[i].z : vx[i].w;
+        uint4 hi, lo;
+        split8(vv, &hi, &lo);
+        const int d = 4 * lane + e;
+        *reinterpret_cast<uint4*>(Vh + swz(d, warp)) = hi;
+        *reinterpret_cast<uint4*>(Vl + swz(d, warp)) = lo;
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMAs
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // ---- 2. S = Q K^T
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const int pn = kk >> 2, ko = (kk & 3) * 32;
+        const uint64_t qh = sdesc(Qh + pn * kQPanel + ko), ql = sdesc(Ql + pn * kQPanel + ko);
+        const uint64_t bh = sdesc(Kh + pn * kKPanel + ko), bl = sdesc(Kl + pn * kKPanel + ko);
+        mma_f16(tmem, qh, bh, kIdS, kk > 0 ? 1u : 0u);
+        mma_f16(tmem, qh, bl, kIdS, 1u);
+        mma_f16(tmem, ql, bh, kIdS, 1u);
+      }
+      mma_commit(bar_s);
+    }
+    mbar_wait_sleep(bar_s, ph, a.err);
+    tc_fence_after();
+    // ---- 3. scale, causal mask, online softmax; P = exp(s - max) 2^14 as hi/lo.
+    // Warp w takes keys 32 (w / 4) .. + 31 of its quarter's rows: the two
+    // halves' maxima meet in shared memory, each keeps the running sum of
+    // its half (rescaled alike), and each rescales its half of O's columns.
+    float sv[32];
+    tmem_ld32(tl + (uint32_t)(32 * hf), sv);
+    float mx = kNegBig;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int64_t key = k0 + 32 * hf + j;
+      if (key <= qp && key < key_end) mx = fmaxf(mx, sv[j] * scale);
+    }
+    red[hf][r] = mx;
+    __syncthreads();
+    const float mn = fmaxf(m, fmaxf(red[0][r], red[1][r])), corr = expf(m - mn);
+    m = mn;
+    l *= corr;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float p8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t key = k0 + 32 * hf + 8 * c + i;
+        const float pv = (key <= qp && key < key_end) ? expf(sv[8 * c + i] * scale - mn) : 0.0f;
+        l += pv;
+        p8[i] = pv * kPScale;
+      }
+      uint4 hi, lo;
+      split8(p8, &hi, &lo);
+      *reinterpret_cast<uint4*>(Ph + swz(r, 4 * hf + c)) = hi;
+      *reinterpret_cast<uint4*>(Pl + swz(r, 4 * hf + c)) = lo;
+    }
+    // ---- 4. rescale this half row of O (nothing to rescale before the first tile)
+    if (k0 > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        float t[32];
+        const uint32_t col = 64 + (uint32_t)(64 * hf + 32 * q);
+        tmem_ld32(tl + col, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] *= corr;
+        tmem_st32(tl + col, t);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMAs
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // ---- 5. O += P V
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk) {
+        const int ko = kk * 32;
+        const uint64_t pa = sdesc(Ph + ko), pl = sdesc(Pl + ko), vh = sdesc(Vh + ko), vl = sdesc(Vl + ko);
+        mma_f16(tmem + 64, pa, vh, kIdO, (k0 > 0 || kk > 0) ? 1u : 0u);
+        mma_f16(tmem + 64, pa, vl, kIdO, 1u);
+        mma_f16(tmem + 64, pl, vh, kIdO, 1u);
+      }
+      mma_commit(bar_o);
+    }
+    mbar_wait_sleep(bar_o, ph, a.err);
+    tc_fence_after();
+    ph ^= 1u;  // the next tile's first CTA barrier orders these S and O reads before its MMAs
+  }
+  red[hf][r] = l;
+  __syncthreads();
+  const float inv = 1.0f / ((red[0][r] + red[1][r]) * kPScale);
+  float4* op = r < nq ? reinterpret_cast<float4*>(a.out + ((qt0 + r) * a.n_heads + h) * HD + 64 * hf) : nullptr;
+#pragma unroll 1
+  for (int q = 0; q < 2; ++q) {
+    float t[32];
+    tmem_ld32(tl + 64 + (uint32_t)(64 * hf + 32 * q), t);  // warp-wide: every lane loads
+    if (op)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        op[8 * q + i] = make_float4(t[4 * i] * inv, t[4 * i + 1] * inv, t[4 * i + 2] * inv, t[4 * i + 3] * inv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
 }  // namespace
 
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s) {
@@ -648,21 +899,45 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t s) {
   }
 }
 
-cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
-  if (a.hd != HD || a.n_heads % a.n_kv || a.n <= 0) return cudaErrorInvalidValue;
+namespace {
+
+cudaError_t launch_prefill_mma(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)4 * KT * KP * sizeof(__half);
-  static int configured = -1;
+  static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured != dev) {
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    configured = dev;
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
   dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + QT - 1) / QT));
   attn_prefill_kernel<<<grid, 128, smem, s>>>(a);
-  const cudaError_t e_ = cudaGetLastError();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_tc(const AttnArgs& a, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + TQ - 1) / TQ));
+  attn_prefill_tc_kernel<<<grid, 256, kTcSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// RPGC_ATTN_TC=1 (read at every call) selects the tcgen05 kernel; the
+// default is the mma.sync kernel, which is faster on the 512-token prefill.
+cudaError_t attn_prefill_launch(const AttnArgs& a, cudaStream_t s) {
+  if (a.hd != HD || a.n_kv <= 0 || a.n_heads % a.n_kv || a.n <= 0) return cudaErrorInvalidValue;
+  const char* tc = getenv("RPGC_ATTN_TC");
+  const cudaError_t e_ = (tc && tc[0] == '1') ? launch_prefill_tc(a, s) : launch_prefill_mma(a, s);
   if (e_ == cudaSuccess) count_launches(1);
   return e_;
 }

@@ -35,9 +35,12 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_dev.cuh"
 
 namespace rpgc {
 namespace {
+
+using namespace tc;
 
 constexpr int TMt = 256;  // tokens per CTA
 constexpr int TKt = 64;   // K per stage (one 128-byte swizzle row of fp16)
@@ -83,36 +86,6 @@ struct GemmArgs {
   const float* glu;       // ks == 1, optional: OUT = silu(glu) * (X W^T), glu in OUT's layout
 };
 
-// ------------------------------------------------------------ tcgen05 glue
-// Shared-memory matrix descriptor, K-major with 128-byte swizzle: start
-// address, stride between 8-row groups 1024 B, descriptor version 1.
-__device__ __forceinline__ uint64_t sdesc(const void* p) {
-  const uint64_t a = smem_u32(p);
-  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) |
-         (2ull << 61);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
   asm volatile(
@@ -120,39 +93,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "%3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
-}
-
-// 16 consecutive TMEM columns of this warp's 32 lanes -> 16 registers.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // ------------------------------------------------------------ dequant
@@ -280,26 +220,6 @@ __device__ __forceinline__ void convert16(uint32_t type, const uint32_t* r, cons
     }
   }
 }
-
-// fp16 hi/lo split of 8 values packed for a 16-byte store: hi = fp16(v)
-// (round to nearest), lo = fp16(v - hi), where v - hi is exact in fp32.
-__device__ __forceinline__ void split8(const float* v, uint4* hi, uint4* lo) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 ph = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-    const float2 f = __half22float2(ph);
-    const __half2 pl = __floats2half2_rn(v[2 * i] - f.x, v[2 * i + 1] - f.y);
-    h[i] = *reinterpret_cast<const uint32_t*>(&ph);
-    l[i] = *reinterpret_cast<const uint32_t*>(&pl);
-  }
-  *hi = make_uint4(h[0], h[1], h[2], h[3]);
-  *lo = make_uint4(l[0], l[1], l[2], l[3]);
-}
-
-// Byte offset of 16-byte chunk c of row r in a K-major tile with 128-byte
-// rows and the 128-byte swizzle (chunk index XOR row mod 8).
-__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 template <int TN>
 __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_h,
