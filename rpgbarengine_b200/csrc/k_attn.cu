@@ -545,55 +545,59 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) 
 
 // --------------------------------------------------------------- prefill, tcgen05
 // The same attention (same split, same 2^14 probability scale) on the
-// 5th-generation tensor cores (tcgen05, TMEM accumulators).  One CTA
-// of 8 warps per (head, 128-query tile), heaviest tiles first.  All warps
-// stage operands; query row t is TMEM lane t of both accumulators, and
-// threads t and t + 128 share it (keys 0-31 and 32-63 of each tile, columns
-// 0-63 and 64-127 of the output).  Q gets its QK-norm and RoPE as it is staged
-// and stays in shared memory as hi/lo halves.  Per 64-key tile:
-//   1. the CTA stages K [64 keys][128 dims] and V^T [128 dims][64 keys] as
-//      fp16 hi/lo in K-major tiles with the 128-byte swizzle (V is transposed
-//      as it is staged, so that both products read K-major operands);
-//   2. one thread issues S = Q K^T (M = 128, N = 64; 8 k16 steps over the
-//      dims x 3 products) into TMEM columns [0, 64);
-//   3. a row's two threads read its S row back, mask it (keys past the row's
-//      position or past the chunk), update the running max and sums, and
-//      write P = exp(s - max) 2^14 as an fp16 hi/lo row;
-//   4. they rescale the row of the output accumulator O (TMEM columns
-//      [64, 192)) by c = exp(old max - new max), unless no row of the warp
+// 5th-generation tensor cores (tcgen05, TMEM accumulators).  One CTA of 8
+// warps per (head, 128-query tile), heaviest tiles first.  All warps stage
+// operands; query row t is TMEM lane t of the accumulators, and threads t and
+// t + 128 share it (keys 0-31 and 32-63 of each tile, columns 0-63 and 64-127
+// of the output).  Q gets its QK-norm and RoPE as it is staged and stays in
+// shared memory as hi/lo halves; K, V^T and P are fp16 hi/lo K-major tiles
+// with the 128-byte swizzle (V is transposed as it is staged, so that both
+// products read K-major operands).  Per 64-key tile i, pipelined so that the
+// tensor core works while the CUDA cores stage and run the softmax:
+//   A. stage K(i + 1) and V(i) (two buffers of each);
+//   B. one thread issues S(i + 1) = Q K(i + 1)^T (M = 128, N = 64; 8 k16
+//      steps x 3 products) into the other of two TMEM S buffers;
+//   C. wait for S(i) (issued one tile earlier);
+//   D. a row's two threads read its S(i) row, mask it (keys past the row's
+//      position or past the chunk), update the running max and sums and form
+//      P = exp(s - max) 2^14 in registers -- while the tensor core runs
+//      O += P(i - 1) V(i - 1) and S(i + 1);
+//   E. wait for that product, write P(i) as an fp16 hi/lo row, rescale the
+//      row of O (TMEM) by exp(old max - new max) unless no row of the warp
 //      changed its max;
-//   5. one thread issues O += P V (M = 128, N = 128; 4 k16 steps over the
-//      keys x 3 products).
-// Every stage completes before the next overwrites what it read (the commits'
-// barriers and the CTA barriers between the phases), so one buffer of each
-// operand suffices; all mbarrier waits are bounded.
+//   F. one thread issues O += P(i) V(i) (M = 128, N = 128; 4 k16 steps x 3
+//      products).
+// Each S buffer has its own mbarrier and each barrier completes once before
+// it is waited on; all waits are bounded.
 constexpr int TQ = 128;
-constexpr int kQPanel = TQ * 128;   // one 64-dim panel of Q: 128 rows x 128 B
-constexpr int kKPanel = KT * 128;   // one 64-dim panel of K: 64 rows x 128 B
-constexpr int kVTile = HD * 128;    // V^T: 128 dim rows x 64 keys (128 B)
-constexpr int kPTile = TQ * 128;    // P: 128 query rows x 64 keys
-constexpr int kTcBytes = 4 * kQPanel + 4 * kKPanel + 2 * kVTile + 2 * kPTile;
-constexpr int kTcSmem = kTcBytes + 1024 + 1024;  // + barriers, + alignment slack
-constexpr uint32_t kTcCols = 256;                // S: [0, 64), O: [64, 192)
+constexpr int kQPanel = TQ * 128;     // one 64-dim panel of Q: 128 rows x 128 B
+constexpr int kKPanel = KT * 128;     // one 64-dim panel of K: 64 rows x 128 B
+constexpr int kKBuf = 4 * kKPanel;    // Kh and Kl, 2 panels each
+constexpr int kVTile = HD * 128;      // V^T: 128 dim rows x 64 keys (128 B)
+constexpr int kVBuf = 2 * kVTile;     // Vh and Vl
+constexpr int kPTile = TQ * 128;      // P: 128 query rows x 64 keys
+constexpr int kTcBytes = 4 * kQPanel + 2 * kKBuf + 2 * kVBuf + 2 * kPTile;
+constexpr int kTcSmem = kTcBytes + 1024 + 64;  // + alignment slack, + barriers
+constexpr uint32_t kTcCols = 256;  // S buffers at columns 0 and 192 (64 each), O at 64 (128)
 // instruction descriptors: fp16 x fp16 -> fp32, both K-major, M = 128
 constexpr uint32_t kIdS = (1u << 4) | ((uint32_t)(KT >> 3) << 17) | ((uint32_t)(TQ >> 4) << 24);
 constexpr uint32_t kIdO = (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(TQ >> 4) << 24);
+static_assert(kTcSmem + 2 * TQ * 4 <= 227 * 1024, "attention smem");
 
 __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs a) {
   using namespace tc;
   extern __shared__ uint8_t tsm_raw[];
   uint8_t* sb = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* Qh = sb;                     // 2 panels
+  uint8_t* Qh = sb;                 // 2 panels
   uint8_t* Ql = Qh + 2 * kQPanel;
-  uint8_t* Kh = Ql + 2 * kQPanel;       // 2 panels
-  uint8_t* Kl = Kh + 2 * kKPanel;
-  uint8_t* Vh = Kl + 2 * kKPanel;
-  uint8_t* Vl = Vh + kVTile;
-  uint8_t* Ph = Vl + kVTile;
+  uint8_t* Kb = Ql + 2 * kQPanel;   // [2] x (Kh 2 panels, Kl 2 panels)
+  uint8_t* Vb = Kb + 2 * kKBuf;     // [2] x (Vh, Vl)
+  uint8_t* Ph = Vb + 2 * kVBuf;
   uint8_t* Pl = Ph + kPTile;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sb + kTcBytes);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sb + kTcBytes);  // [2], one per S buffer
+  uint64_t* bar_o = bar_s + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 3);
+  __shared__ float red[2][TQ];  // the two halves' maxima, at the end their sums
 
   const int h = blockIdx.x;
   const int64_t qt0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * TQ;
@@ -603,11 +607,13 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
   const int64_t qpos0 = a.pos0 + qt0;
   const int64_t nq = min((int64_t)TQ, a.n - qt0);
   const int64_t key_end = qpos0 + nq;  // keys [0, key_end)
-  const float* kb = a.kc + (int64_t)kh * a.max_seq * HD;
-  const float* vb = a.vc + (int64_t)kh * a.max_seq * HD;
+  const int T = (int)((key_end + KT - 1) / KT);  // key tiles
+  const float* kbase = a.kc + (int64_t)kh * a.max_seq * HD;
+  const float* vbase = a.vc + (int64_t)kh * a.max_seq * HD;
 
   if (tid == 0) {
-    mbar_init(bar_s, 1);
+    mbar_init(&bar_s[0], 1);
+    mbar_init(&bar_s[1], 1);
     mbar_init(bar_o, 1);
     fence_barrier_init();
   }
@@ -617,54 +623,73 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // ---- Q: warp w stages rows w, w + 8, ...; lane l holds dims 4l .. 4l + 3
-  // (rows past the chunk are zeros)
-  for (int row = warp; row < TQ; row += 8) {
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < nq) {  // warp-uniform: the norm's reduction has every lane
-      v = *reinterpret_cast<const float4*>(a.q + ((qt0 + row) * a.n_heads + h) * HD + 4 * lane);
-      if (a.q_norm) v = norm_rope_head(v, a.q_norm, a.rope + (qpos0 + row) * HD, a.eps, lane);
+  // ---- Q: warp w stages rows w + 8 u (u = 0..15) in two batches of 8, every
+  // load of a batch (q, the position's cosines and sines) in flight before the
+  // first norm; lane l holds dims 4l .. 4l + 3 (rows past the chunk are zeros)
+  {
+    const float4 gq = a.q_norm ? *reinterpret_cast<const float4*>(a.q_norm + 4 * lane) : make_float4(1.f, 1.f, 1.f, 1.f);
+    const int ci = (4 * lane) & 63;
+#pragma unroll 1
+    for (int bt = 0; bt < 2; ++bt) {
+      float4 qv[8], cv[8], sn[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int row = warp + 8 * (8 * bt + u);
+        qv[u] = cv[u] = sn[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < nq) {
+          qv[u] = *reinterpret_cast<const float4*>(a.q + ((qt0 + row) * a.n_heads + h) * HD + 4 * lane);
+          if (a.q_norm) {
+            const float* cs = a.rope + (qpos0 + row) * HD;
+            cv[u] = *reinterpret_cast<const float4*>(cs + ci);
+            sn[u] = *reinterpret_cast<const float4*>(cs + 64 + ci);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int row = warp + 8 * (8 * bt + u);
+        float4 v = qv[u];
+        if (row < nq && a.q_norm) v = norm_rope_head_pre(v, gq, cv[u], sn[u], a.eps, lane);  // warp-uniform
+        uint32_t h0, l0, h1, l1;
+        split2(v.x, v.y, &h0, &l0);
+        split2(v.z, v.w, &h1, &l1);
+        const int d = 4 * lane;
+        const uint32_t off = (uint32_t)((d >> 6) * kQPanel) + swz(row, (d & 63) >> 3) + (uint32_t)((d & 7) * 2);
+        *reinterpret_cast<uint2*>(Qh + off) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(Ql + off) = make_uint2(l0, l1);
+      }
     }
-    uint32_t h0, l0, h1, l1;
-    split2(v.x, v.y, &h0, &l0);
-    split2(v.z, v.w, &h1, &l1);
-    const int d = 4 * lane;
-    const uint32_t off = (uint32_t)((d >> 6) * kQPanel) + swz(row, (d & 63) >> 3) + (uint32_t)((d & 7) * 2);
-    *reinterpret_cast<uint2*>(Qh + off) = make_uint2(h0, h1);
-    *reinterpret_cast<uint2*>(Ql + off) = make_uint2(l0, l1);
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's lane quarter
-  const int r = (warp & 3) * 32 + lane, hf = warp >> 2;  // query row = TMEM lane; key / column half
-  __shared__ float red[2][TQ];  // the two halves' maxima, at the end their sums
-  const int64_t qp = qpos0 + r;
-  float m = kNegBig, l = 0.0f;
-  uint32_t ph = 0;
 
-  for (int64_t k0 = 0; k0 < key_end; k0 += KT) {
-    // ---- 1. all eight warps stage, every load of the tile in flight before
-    // the first conversion: K as 4 items of (key, 8 dims) per thread; V^T as
-    // one 8-key x 4-dim block per thread (warp = 8-key chunk, lane = 4 dims),
-    // transposed in registers into 4 rows of 8 keys
-    {
-      float4 kx[8], vx[8];
+  // K of tile kt into buffer kt & 1 (4 items of (key, 8 dims) per thread) and
+  // V^T of tile vt into buffer vt & 1 (one 8-key x 4-dim block per thread:
+  // warp = 8-key chunk, lane = 4 dims, transposed in registers); every load
+  // in flight before the first conversion.  A tile index < 0 or >= T skips.
+  auto stage = [&](int kt, int vt) {
+    float4 kx[8], vx[8];
+    const bool dok = kt >= 0 && kt < T, dov = vt >= 0 && vt < T;
+    const int64_t k0 = (int64_t)kt * KT, v0 = (int64_t)vt * KT;
+    if (dok) {
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
         const int idx = it * 256 + tid, j = idx >> 4, c = idx & 15;
         const bool ok = k0 + j < key_end;
-        const float4* kp = reinterpret_cast<const float4*>(kb + (k0 + (ok ? j : 0)) * HD + 8 * c);
+        const float4* kp = reinterpret_cast<const float4*>(kbase + (k0 + (ok ? j : 0)) * HD + 8 * c);
         kx[2 * it] = ok ? kp[0] : make_float4(0.f, 0.f, 0.f, 0.f);
         kx[2 * it + 1] = ok ? kp[1] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    }
+    if (dov) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int64_t key = k0 + 8 * warp + i;
-        vx[i] = key < key_end ? *reinterpret_cast<const float4*>(vb + key * HD + 4 * lane)
+        const int64_t key = v0 + 8 * warp + i;
+        vx[i] = key < key_end ? *reinterpret_cast<const float4*>(vbase + key * HD + 4 * lane)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    }
+    if (dok) {
+      uint8_t* Kh = Kb + (kt & 1) * kKBuf;
+      uint8_t* Kl = Kh + 2 * kKPanel;
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
         const int idx = it * 256 + tid, j = idx >> 4, c = idx & 15;
@@ -676,6 +701,10 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
         *reinterpret_cast<uint4*>(Kh + off) = hi;
         *reinterpret_cast<uint4*>(Kl + off) = lo;
       }
+    }
+    if (dov) {
+      uint8_t* Vh = Vb + (vt & 1) * kVBuf;
+      uint8_t* Vl = Vh + kVTile;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float vv[8];
@@ -688,31 +717,51 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
         *reinterpret_cast<uint4*>(Vl + swz(d, warp)) = lo;
       }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMAs
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    // ---- 2. S = Q K^T
-    if (tid == 0) {
+  };
+  // S(t) = Q K(t)^T into S buffer t & 1 (one thread)
+  auto issue_s = [&](uint32_t tmem, int t) {
+    const uint8_t* Kh = Kb + (t & 1) * kKBuf;
+    const uint8_t* Kl = Kh + 2 * kKPanel;
+    const uint32_t d = tmem + (uint32_t)((t & 1) * 192);
 #pragma unroll
-      for (int kk = 0; kk < HD / 16; ++kk) {
-        const int pn = kk >> 2, ko = (kk & 3) * 32;
-        const uint64_t qh = sdesc(Qh + pn * kQPanel + ko), ql = sdesc(Ql + pn * kQPanel + ko);
-        const uint64_t bh = sdesc(Kh + pn * kKPanel + ko), bl = sdesc(Kl + pn * kKPanel + ko);
-        mma_f16(tmem, qh, bh, kIdS, kk > 0 ? 1u : 0u);
-        mma_f16(tmem, qh, bl, kIdS, 1u);
-        mma_f16(tmem, ql, bh, kIdS, 1u);
-      }
-      mma_commit(bar_s);
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      const int pn = kk >> 2, ko = (kk & 3) * 32;
+      const uint64_t qh = sdesc(Qh + pn * kQPanel + ko), ql = sdesc(Ql + pn * kQPanel + ko);
+      const uint64_t bh = sdesc(Kh + pn * kKPanel + ko), bl = sdesc(Kl + pn * kKPanel + ko);
+      mma_f16(d, qh, bh, kIdS, kk > 0 ? 1u : 0u);
+      mma_f16(d, qh, bl, kIdS, 1u);
+      mma_f16(d, ql, bh, kIdS, 1u);
     }
-    mbar_wait_sleep(bar_s, ph, a.err);
+    mma_commit(&bar_s[t & 1]);
+  };
+
+  stage(0, -1);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // Q and K(0) visible to the MMAs
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's lane quarter
+  const int r = (warp & 3) * 32 + lane, hf = warp >> 2;  // query row = TMEM lane; key / column half
+  const int64_t qp = qpos0 + r;
+  if (tid == 0) issue_s(tmem, 0);
+  float m = kNegBig, l = 0.0f;
+
+  for (int i = 0; i < T; ++i) {
+    const int64_t k0 = (int64_t)i * KT;
+    // ---- A, B. K(i + 1) and V(i); S(i + 1).  K buffer (i + 1) & 1 was read by
+    // S(i - 1), waited for in the previous pass; V buffer i & 1 by PV(i - 2).
+    stage(i + 1, i);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();  // also: every thread is done with S buffer (i + 1) & 1 and with red
     tc_fence_after();
-    // ---- 3. scale, causal mask, online softmax; P = exp(s - max) 2^14 as hi/lo.
-    // Warp w takes keys 32 (w / 4) .. + 31 of its quarter's rows: the two
-    // halves' maxima meet in shared memory, each keeps the running sum of
-    // its half (rescaled alike), and each rescales its half of O's columns.
+    if (tid == 0 && i + 1 < T) issue_s(tmem, i + 1);
+    // ---- C, D. S(i): scale, causal mask, online softmax into registers
+    mbar_wait_sleep(&bar_s[i & 1], (uint32_t)(i >> 1) & 1u, a.err);
+    tc_fence_after();
     float sv[32];
-    tmem_ld32(tl + (uint32_t)(32 * hf), sv);
+    tmem_ld32(tl + (uint32_t)((i & 1) * 192 + 32 * hf), sv);
     float mx = kNegBig;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -725,29 +774,32 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
     m = mn;
     l *= corr;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float p8[8];
+    for (int j = 0; j < 32; ++j) {
+      const int64_t key = k0 + 32 * hf + j;
+      const float pv = (key <= qp && key < key_end) ? expf(sv[j] * scale - mn) : 0.0f;
+      l += pv;
+      sv[j] = pv * kPScale;
+    }
+    // ---- E. PV(i - 1) done: P(i) into shared memory, O's row rescaled
+    if (i > 0) {
+      mbar_wait_sleep(bar_o, (uint32_t)(i - 1) & 1u, a.err);
+      tc_fence_after();
+    }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int64_t key = k0 + 32 * hf + 8 * c + i;
-        const float pv = (key <= qp && key < key_end) ? expf(sv[8 * c + i] * scale - mn) : 0.0f;
-        l += pv;
-        p8[i] = pv * kPScale;
-      }
+    for (int c = 0; c < 4; ++c) {
       uint4 hi, lo;
-      split8(p8, &hi, &lo);
+      split8(sv + 8 * c, &hi, &lo);
       *reinterpret_cast<uint4*>(Ph + swz(r, 4 * hf + c)) = hi;
       *reinterpret_cast<uint4*>(Pl + swz(r, 4 * hf + c)) = lo;
     }
-    // ---- 4. rescale this half row of O (nothing to rescale before the first tile)
-    if (k0 > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {
+    if (i > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {
 #pragma unroll 1
       for (int q = 0; q < 2; ++q) {
         float t[32];
         const uint32_t col = 64 + (uint32_t)(64 * hf + 32 * q);
         tmem_ld32(tl + col, t);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] *= corr;
+        for (int j = 0; j < 32; ++j) t[j] *= corr;
         tmem_st32(tl + col, t);
       }
     }
@@ -755,22 +807,23 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ---- 5. O += P V
+    // ---- F. O += P(i) V(i)
     if (tid == 0) {
+      const uint8_t* Vh = Vb + (i & 1) * kVBuf;
+      const uint8_t* Vl = Vh + kVTile;
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
         const int ko = kk * 32;
         const uint64_t pa = sdesc(Ph + ko), pl = sdesc(Pl + ko), vh = sdesc(Vh + ko), vl = sdesc(Vl + ko);
-        mma_f16(tmem + 64, pa, vh, kIdO, (k0 > 0 || kk > 0) ? 1u : 0u);
+        mma_f16(tmem + 64, pa, vh, kIdO, (i > 0 || kk > 0) ? 1u : 0u);
         mma_f16(tmem + 64, pa, vl, kIdO, 1u);
         mma_f16(tmem + 64, pl, vh, kIdO, 1u);
       }
       mma_commit(bar_o);
     }
-    mbar_wait_sleep(bar_o, ph, a.err);
-    tc_fence_after();
-    ph ^= 1u;  // the next tile's first CTA barrier orders these S and O reads before its MMAs
   }
+  mbar_wait_sleep(bar_o, (uint32_t)(T - 1) & 1u, a.err);
+  tc_fence_after();
   red[hf][r] = l;
   __syncthreads();
   const float inv = 1.0f / ((red[0][r] + red[1][r]) * kPScale);
@@ -781,8 +834,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
     tmem_ld32(tl + 64 + (uint32_t)(64 * hf + 32 * q), t);  // warp-wide: every lane loads
     if (op)
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        op[8 * q + i] = make_float4(t[4 * i] * inv, t[4 * i + 1] * inv, t[4 * i + 2] * inv, t[4 * i + 3] * inv);
+      for (int j = 0; j < 8; ++j)
+        op[8 * q + j] = make_float4(t[4 * j] * inv, t[4 * j + 1] * inv, t[4 * j + 2] * inv, t[4 * j + 3] * inv);
   }
   tc_fence_before();
   __syncthreads();
