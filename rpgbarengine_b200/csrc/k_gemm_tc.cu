@@ -251,6 +251,11 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
   const int nmb = g.n - t0 > 128 ? 2 : 1;        // 128-token halves holding live tokens
   const int kc0 = (int)((int64_t)nk_all * blockIdx.z / g.ks);  // this CTA's stages
   const int nk = (int)((int64_t)nk_all * (blockIdx.z + 1) / g.ks) - kc0;
+  // Launched as a programmatic dependent: the set-up, the TMEM allocation and
+  // the weight stages (which no kernel writes) overlap the previous kernel's
+  // tail; X (warp 0) and the epilogue's reads and writes wait for it.  The
+  // next kernel may start its own set-up as soon as every CTA here has begun.
+  grid_dep_launch();
 
   if (tid == 0) {
     for (int s = 0; s < kStg; ++s) {
@@ -276,6 +281,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (X tiles)
     if (lane == 0) {
+      grid_dep_wait();  // X is the previous kernel's output
       for (int c = 0; c < nk; ++c) {
         const int s = c % kStg;
         if (c >= kStg) mbar_wait_sleep(&empty[s], (uint32_t)(c / kStg - 1) & 1u, g.err);
@@ -363,6 +369,7 @@ __global__ void __launch_bounds__(Tile<TN>::kThreads, 1) gemm_tc_kernel(const __
     // 32 (w % 4) .. + 31 only, so the nq warps with one w % 4 share that
     // quarter of both token halves mb (the first eight warps take one
     // (half, quarter) each, the others none)
+    grid_dep_wait();  // OUT, the partial sums, glu and the row scales belong to earlier kernels
     mbar_wait_sleep(acc_full, 0, g.err);
     tc_fence_after();
     const int ew = warp - 2, quarter = warp & 3, nq = (kDeqWarps - (ew & 3) + 3) >> 2;
@@ -446,6 +453,7 @@ __global__ void __launch_bounds__(NT, 1) split_rows_kernel(const float* __restri
                                                          int64_t K, float eps, __half* __restrict__ xh,
                                                          __half* __restrict__ xl, float* __restrict__ inv_scale) {
   extern __shared__ __align__(16) float vrow[];  // [K]
+  grid_dep_launch();  // the matmul after this split may begin its set-up and weight stages
   constexpr int NW = NT / 32;
   __shared__ double dred[NW];
   __shared__ float red[NW];
@@ -643,8 +651,17 @@ cudaError_t launch_tile(const CUtensorMap& mh, const CUtensorMap& ml, const Gemm
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  gemm_tc_kernel<TN><<<grid, Tile<TN>::kThreads, Tile<TN>::kSmem, s>>>(mh, ml, g);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(Tile<TN>::kThreads);
+  cfg.dynamicSmemBytes = Tile<TN>::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TN>, mh, ml, g);
 }
 
 // Split-K factor for a tile shape: enough K partitions to fill the GPU
