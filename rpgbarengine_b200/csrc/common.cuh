@@ -205,6 +205,25 @@ RPGC_DEV uint64_t policy_evict_first() {
 RPGC_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 RPGC_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Launch with programmatic stream serialisation: the kernel may be scheduled
+// while the previous kernel in the stream finishes, and must execute
+// grid_dep_wait() before it touches memory that kernel reads or writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Unaligned little-endian 32-bit word from shared memory built from the two
 // aligned words around it.
 RPGC_DEV uint32_t lds_u32(const uint8_t* p) {

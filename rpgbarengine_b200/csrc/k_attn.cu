@@ -334,6 +334,7 @@ __device__ __forceinline__ void ldsm4_t(uint32_t addr, uint32_t* r) {
 }
 
 __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const AttnArgs a) {
+  grid_dep_wait();  // launched as a programmatic dependent: q and the cache come from earlier kernels
   extern __shared__ __align__(16) __half hsm[];
   __half* Kh = hsm;            // [KT][KP]
   __half* Kl = Kh + KT * KP;
@@ -585,6 +586,7 @@ constexpr uint32_t kIdO = (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(
 static_assert(kTcSmem + 2 * TQ * 4 <= 227 * 1024, "attention smem");
 
 __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs a) {
+  grid_dep_wait();  // launched as a programmatic dependent: q and the cache come from earlier kernels
   using namespace tc;
   extern __shared__ uint8_t tsm_raw[];
   uint8_t* sb = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
@@ -850,8 +852,7 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_tc_kernel(const AttnArgs 
 cudaError_t qkv_rope_launch(const QkvArgs& a, cudaStream_t s) {
   if (a.hd > 256 || (a.hd & 31) || a.n <= 0) return cudaErrorInvalidValue;
   dim3 grid((unsigned)a.n, (unsigned)(a.kv_only ? a.n_kv : a.n_heads + a.n_kv));
-  qkv_rope_kernel<<<grid, a.hd, 0, s>>>(a);
-  const cudaError_t e_ = cudaGetLastError();
+  const cudaError_t e_ = launch_pdl(qkv_rope_kernel, grid, dim3((unsigned)a.hd), 0, s, a);  // waits first thing
   if (e_ == cudaSuccess) count_launches(1);
   return e_;
 }
@@ -965,8 +966,7 @@ cudaError_t launch_prefill_mma(const AttnArgs& a, cudaStream_t s) {
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
   dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + QT - 1) / QT));
-  attn_prefill_kernel<<<grid, 128, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(attn_prefill_kernel, grid, dim3(128), smem, s, a);
 }
 
 cudaError_t launch_prefill_tc(const AttnArgs& a, cudaStream_t s) {
@@ -979,8 +979,7 @@ cudaError_t launch_prefill_tc(const AttnArgs& a, cudaStream_t s) {
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
   dim3 grid((unsigned)a.n_heads, (unsigned)((a.n + TQ - 1) / TQ));
-  attn_prefill_tc_kernel<<<grid, 256, kTcSmem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(attn_prefill_tc_kernel, grid, dim3(256), (size_t)kTcSmem, s, a);
 }
 
 }  // namespace

@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(NT, 1) split_rows_kernel(const float* __restri
                                                          __half* __restrict__ xl, float* __restrict__ inv_scale) {
   extern __shared__ __align__(16) float vrow[];  // [K]
   grid_dep_launch();  // the matmul after this split may begin its set-up and weight stages
+  grid_dep_wait();    // launched as a programmatic dependent: the rows are the previous kernel's
   constexpr int NW = NT / 32;
   __shared__ double dred[NW];
   __shared__ float red[NW];
@@ -549,11 +550,9 @@ cudaError_t split_rows_launch(const float* A, const float* B, int64_t n, int64_t
   }
   // a few hundred rows or more fill the GPU at 256 threads a row; fewer
   // (a batched decode step's session rows) take 1024 threads a row
-  if (n >= 256)
-    split_rows_kernel<MODE, 256><<<(unsigned)n, 256, smem, s>>>(A, B, K, eps, xh, xl, inv);
-  else
-    split_rows_kernel<MODE, 1024><<<(unsigned)n, 1024, smem, s>>>(A, B, K, eps, xh, xl, inv);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      n >= 256 ? launch_pdl(split_rows_kernel<MODE, 256>, dim3((unsigned)n), dim3(256), (size_t)smem, s, A, B, K, eps, xh, xl, inv)
+               : launch_pdl(split_rows_kernel<MODE, 1024>, dim3((unsigned)n), dim3(1024), (size_t)smem, s, A, B, K, eps, xh, xl, inv);
   if (e == cudaSuccess) count_launches(1);
   return e;
 }
@@ -564,6 +563,7 @@ cudaError_t split_rows_launch(const float* A, const float* B, int64_t n, int64_t
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int ks,
                                                             int64_t n, int64_t rows, float* out,
                                                             int64_t ldo, int accumulate, int vec) {
+  grid_dep_wait();  // launched as a programmatic dependent of the matmul
   const int64_t total = n * rows;
   if (vec) {
     const int64_t i = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
@@ -770,9 +770,8 @@ cudaError_t launch_group(GemmMat* mat, int nmat, int64_t K, const float* X, int6
                      (reinterpret_cast<uintptr_t>(mat[i].out) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(mpart[i]) & 15) == 0;
     const int64_t threads = vec ? (total + 3) / 4 : total;
-    splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
-        mpart[i], (int)ks, n, mat[i].rows, mat[i].out, mat[i].ldo, accumulate ? 1 : 0, vec ? 1 : 0);
-    e = cudaGetLastError();
+    e = launch_pdl(splitk_reduce_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, s, (const float*)mpart[i],
+                   (int)ks, n, mat[i].rows, mat[i].out, mat[i].ldo, accumulate ? 1 : 0, vec ? 1 : 0);
     if (e != cudaSuccess) return e;
     count_launches(1);
   }
