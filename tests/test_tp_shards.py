@@ -5,8 +5,8 @@ matrices the way the upload does (whole rows of q/k/v/gate/up/output; for o
 and down the same block range of every row), dequantises its slices with the
 oracle and computes its part of every projection.  The gathered row slices
 must equal the unsharded products, and the all-reduced partial sums of the
-column-split projections must match them to fp32 rounding.  Reference split:
-SURVEY's tensor-parallel layout of src/qwen3.cc:119-206's matrices."""
+column-split projections must match them to fp32 rounding.  The matrices
+split are those of the reference's layer (src/qwen3.cc:119-206)."""
 import os
 import socket
 
